@@ -1,0 +1,145 @@
+// g4_common.cuh — device helpers shared by every g4cuda kernel (sm_100a only).
+//
+// Conventions:
+//   - Bit-exactness: the reference is built -std=c11, so no a*b+c contraction;
+//     every place whose rounding must match uses the explicit __f*_rn
+//     intrinsics, and FMAs appear only where the reference uses FMA intrinsics.
+//   - Every spin (mbarrier waits, tickets) is bounded by a %globaltimer budget;
+//     on expiry the kernel records an error code in the context's device error
+//     word and returns, leaving the CUDA context usable.
+//   - Kernels are launched with programmatic dependent launch: anything that
+//     reads the previous kernel's output sits after griddep_wait().
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#ifndef __CUDACC__
+#error "g4_common.cuh is CUDA-only"
+#endif
+
+#define G4_DEV __device__ __forceinline__
+
+
+// ~2 s wall budget for any single wait.
+#define G4_WAIT_NS 2000000000ull
+
+G4_DEV uint64_t g4_globaltimer() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+G4_DEV void g4_set_error(int *err, int code) {
+    if (err) atomicCAS(err, 0, code);
+}
+
+// ---- programmatic dependent launch --------------------------------------
+G4_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+G4_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---- mbarrier + bulk async copy (TMA engine, 1-D) ------------------------
+G4_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+G4_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+G4_DEV void mbar_fence_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
+
+G4_DEV void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+G4_DEV void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.release.cta.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+G4_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cta.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+// Bounded wait on phase `parity`; returns false (and records `code`) on timeout.
+G4_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    uint64_t t0 = g4_globaltimer();
+    while (!mbar_try_wait(bar, parity)) {
+        if (g4_globaltimer() - t0 > G4_WAIT_NS) {
+            g4_set_error(err, code);
+            return false;
+        }
+    }
+    return true;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` (bytes, 16-B multiples,
+// both addresses 16-B aligned). Weights are streamed once per token, so they are
+// marked evict-first in L2.
+G4_DEV void bulk_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+G4_DEV uint64_t l2_policy_evict_first() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+G4_DEV uint64_t l2_policy_evict_last() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+
+// Named barrier among the first `threads` threads (consumer warps only).
+G4_DEV void bar_sync(int id, int threads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory"); }
+
+// ---- exact integer / float helpers --------------------------------------
+G4_DEV int dp4a(uint32_t a, uint32_t b, int c) { return __dp4a((int)a, (int)b, c); }
+
+G4_DEV float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
+
+// gemma4.c:265-279: scale = max|x| / 127 (IEEE divide), inv = 1/scale,
+// q = rintf(x * inv) (round-half-even), zero group -> scale 0, q 0.
+G4_DEV float quant_scale(float amax) { return __fdiv_rn(amax, 127.0f); }
+G4_DEV float quant_inv(float scale) { return scale > 0.0f ? __frcp_rn(scale) : 0.0f; }
+G4_DEV int quant_one(float x, float inv) { return __float2int_rn(__fmul_rn(x, inv)); }
+
+// gemma4.c:360-373 rmsnorm tail: inv_rms = 1 / sqrtf(ss / n + eps);
+// out = w * (inv_rms * x). The sum of squares itself is reduced in parallel,
+// so only this tail is bit-exact.
+G4_DEV float rms_inv(float ss, float width, float eps) {
+    return __frcp_rn(__fsqrt_rn(__fadd_rn(__fdiv_rn(ss, width), eps)));
+}
+G4_DEV float rms_apply(float x, float inv, float w) { return __fmul_rn(w, __fmul_rn(inv, x)); }
+
+// gemma4.c:310-331 geglu element: LUT GELU with linear interpolation, times up.
+G4_DEV float geglu_one(float x, float up, const float *__restrict__ table, int size, float lo, float hi, float scale) {
+    if (x <= lo) {
+        x = table[0];
+    } else if (!(x >= hi)) {
+        float pos = __fmul_rn(__fsub_rn(x, lo), scale);
+        int idx = (int)pos;
+        float frac = __fsub_rn(pos, (float)idx);
+        float t0 = table[idx];
+        float t1 = idx + 1 < size ? table[idx + 1] : t0;
+        x = __fadd_rn(t0, __fmul_rn(frac, __fsub_rn(t1, t0)));
+    }
+    return __fmul_rn(x, up);
+}
+
+// ---- reductions -----------------------------------------------------------
+G4_DEV float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+G4_DEV float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}

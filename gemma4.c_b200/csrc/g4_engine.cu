@@ -1,0 +1,862 @@
+// g4_engine.cu — context, model upload, forward/logits orchestration, C ABI.
+//
+// Replaces gemma4.c's forward (gemma4.c:463-509) and logits (:512-522) and
+// the state they use (InferenceState, :157-167). The host side of this file
+// only sequences kernels; all arithmetic runs on the device.
+//
+// Paths:
+//   - T = 1 (decode): 8 kernels per layer, every int8 projection a GEMV with
+//     its RMSNorm/residual/quantise producer fused into the prologue and its
+//     GeGLU consumer fused into the epilogue; captured once into a CUDA graph
+//     whose kernels read the token and position from device memory; PDL lets
+//     each GEMV stream its weights while its predecessor drains.
+//   - T = 2..4: same GEMVs, attention through the chunk kernels.
+//   - T > 4 (prefill chunks): row kernels + GEMM + chunk attention.
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <vector>
+
+#include "../../include/g4cuda.h"
+#include "g4_format.h"
+#include "g4_internal.h"
+
+cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl);
+cudaError_t g4_launch_gemm_simt(const GemmArgs &a, cudaStream_t st, bool pdl);
+bool g4_gemm_tc_supported(const GemmArgs &a);
+cudaError_t g4_launch_topk(const float *x, int n, int k, float *part_v, int *part_i, float *vals, int *ids,
+                           cudaStream_t st);
+
+namespace {
+
+constexpr int kMaxT = G4_BATCH;
+constexpr int kSplits = 148;   // decode attention splits (one CTA per SM)
+constexpr int kQkvStride = G4_HEADS * G4_HD_GLOBAL + 2 * G4_HD_GLOBAL;   // 5120
+constexpr int kMaxFfn = 12288;
+
+struct Layer {
+    DMat qkv, o, gu, down, pleg, plep;
+    const float *in_norm, *post_attn, *pre_ffn, *post_ffn, *post_ple, *q_norm, *k_norm, *scalar;
+    const float *rope_cos, *rope_sin;
+    int hd, pairs, global, owner, has_kv, qw, ffn;
+    float *kcache, *vcache;
+    int ring;
+};
+
+}  // namespace
+
+struct g4_ctx {
+    int device = 0, num_sms = 148;
+    cudaStream_t st = nullptr;
+    uint8_t *arena = nullptr;
+    size_t arena_bytes = 0, arena_used = 0;
+    DMat embed{}, embed_ple{}, pmp{};
+    const float *final_norm = nullptr, *ple_norm = nullptr, *gelu = nullptr;
+    Layer L[G4_NUM_LAYERS];
+    // activations / state
+    uint8_t *state = nullptr;
+    float *res[2] = {nullptr, nullptr};
+    int cur = 0;
+    int8_t *xq = nullptr;
+    float *xs = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *gu = nullptr, *pg = nullptr;
+    float *pli = nullptr, *ple_emb = nullptr, *ple_u = nullptr, *logits = nullptr, *part = nullptr;
+    float *argmax_part = nullptr, *topk_v = nullptr;
+    int *argmax_out = nullptr, *topk_i = nullptr;
+    unsigned *ticket = nullptr;
+    int *err = nullptr, *tokens_d = nullptr, *pos_d = nullptr;
+    float *kv = nullptr;
+    size_t kv_bytes = 0;
+    // sequencing
+    int last_T = 0;
+    int logits_row_cached = -1;
+    bool use_graph = true, use_pdl = true;
+    int gemm_path = 0;
+    int layers = G4_NUM_LAYERS;   // layers to run (testing aid)
+    cudaGraphExec_t g_decode = nullptr;
+    int graph_cur = 0;
+    bool decode_warm = false;
+    char msg[512] = {0};
+};
+
+namespace {
+
+int fail(g4_ctx *c, int code, const char *fmt, ...) {
+    if (c) {
+        va_list ap;
+        va_start(ap, fmt);
+        vsnprintf(c->msg, sizeof(c->msg), fmt, ap);
+        va_end(ap);
+    }
+    return code;
+}
+
+#define CK(call)                                                                                     \
+    do {                                                                                             \
+        cudaError_t e_ = (call);                                                                     \
+        if (e_ != cudaSuccess)                                                                       \
+            return fail(c, e_ == cudaErrorMemoryAllocation ? G4_ERR_NOMEM : G4_ERR_CUDA, "%s: %s (%s:%d)", \
+                        #call, cudaGetErrorString(e_), __FILE__, __LINE__);                          \
+    } while (0)
+
+uint8_t *arena_take(g4_ctx *c, size_t bytes) {
+    size_t off = (c->arena_used + 255) & ~(size_t)255;
+    if (off + bytes > c->arena_bytes) return nullptr;
+    c->arena_used = off + bytes;
+    return c->arena + off;
+}
+
+struct Rec {
+    uint64_t data, scales;
+    int32_t shape[4];
+};
+
+// Resolve a record field (file offset, or a pointer into the same mapping after
+// gemma4.c:681-685's fix-up) to a host pointer inside the image.
+const uint8_t *resolve(const uint8_t *base, uint64_t bytes, uint64_t v, uint64_t need) {
+    if (!v) return nullptr;
+    uint64_t off = v;
+    if (v >= bytes) {
+        uintptr_t b = (uintptr_t)base;
+        if (v < b || v - b >= bytes) return nullptr;
+        off = v - b;
+    }
+    if (off + need > bytes) return nullptr;
+    return base + off;
+}
+
+struct HostMat {
+    const int8_t *w;
+    const uint16_t *s;
+    int N, K;
+};
+
+int get_mat(g4_ctx *c, const uint8_t *img, uint64_t bytes, const Rec *r, int idx, int N, int K, HostMat *out) {
+    const Rec &x = r[idx];
+    if (x.shape[0] != N || x.shape[1] != K)
+        return fail(c, G4_ERR_FORMAT, "record %d: shape %dx%d, expected %dx%d", idx, x.shape[0], x.shape[1], N, K);
+    out->w = (const int8_t *)resolve(img, bytes, x.data, (uint64_t)N * K);
+    out->s = (const uint16_t *)resolve(img, bytes, x.scales, (uint64_t)N * (K / 64) * 2);
+    out->N = N;
+    out->K = K;
+    if (!out->w || !out->s) return fail(c, G4_ERR_FORMAT, "record %d: data/scales outside the image", idx);
+    return G4_OK;
+}
+
+int get_vec(g4_ctx *c, const uint8_t *img, uint64_t bytes, const Rec *r, int idx, int n, const float **out) {
+    const Rec &x = r[idx];
+    if (x.shape[0] != n) return fail(c, G4_ERR_FORMAT, "record %d: length %d, expected %d", idx, x.shape[0], n);
+    *out = (const float *)resolve(img, bytes, x.data, (uint64_t)n * 4);
+    if (!*out) return fail(c, G4_ERR_FORMAT, "record %d: data outside the image", idx);
+    return G4_OK;
+}
+
+// Copy a packed host matrix into row-major device form, in chunks of whole
+// 16-row blocks through a staging buffer.
+int upload_mat(g4_ctx *c, const HostMat &hm, DMat dst, int row_offset, int row_mul, uint8_t *stage, size_t stage_bytes) {
+    const int K = hm.K, G = K / 64;
+    size_t per_row = (size_t)K + (size_t)G * 2;
+    int rows = (int)(stage_bytes / per_row) / 16 * 16;
+    if (rows < 16) return fail(c, G4_ERR_INVALID, "staging buffer too small");
+    uint8_t *sw = stage;
+    uint16_t *ss = (uint16_t *)(stage + (((size_t)rows * K + 255) & ~(size_t)255));
+    for (int r0 = 0; r0 < hm.N; r0 += rows) {
+        int nr = hm.N - r0 < rows ? hm.N - r0 : rows;
+        CK(cudaMemcpyAsync(sw, hm.w + (size_t)r0 * K, (size_t)nr * K, cudaMemcpyHostToDevice, c->st));
+        CK(cudaMemcpyAsync(ss, hm.s + (size_t)r0 * G, (size_t)nr * G * 2, cudaMemcpyHostToDevice, c->st));
+        CK(g4_launch_repack((const int8_t *)sw, ss, nr, K, (int8_t *)dst.w, (uint16_t *)dst.s, row_offset + r0 * row_mul,
+                            row_mul, c->st));
+        CK(cudaStreamSynchronize(c->st));
+    }
+    return G4_OK;
+}
+
+DMat alloc_mat(g4_ctx *c, int N, int K) {
+    DMat m{};
+    m.N = N;
+    m.K = K;
+    m.w = (const int8_t *)arena_take(c, (size_t)N * K);
+    m.s = (const uint16_t *)arena_take(c, (size_t)N * (K / 64) * 2);
+    return m;
+}
+
+const float *upload_vec(g4_ctx *c, const float *h, size_t n, int *rc) {
+    float *d = (float *)arena_take(c, n * 4);
+    if (!d) { *rc = G4_ERR_NOMEM; return nullptr; }
+    cudaError_t e = cudaMemcpyAsync(d, h, n * 4, cudaMemcpyHostToDevice, c->st);
+    if (e != cudaSuccess) *rc = G4_ERR_CUDA;
+    return d;
+}
+
+size_t mat_bytes(int N, int K) { return (((size_t)N * K + 255) & ~(size_t)255) + (((size_t)N * (K / 64) * 2 + 255) & ~(size_t)255); }
+
+int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
+    if (bytes < G4_WEIGHTS_OFFSET + (uint64_t)G4_NUM_RECORDS * G4_RECORD_BYTES || memcmp(img, "MOG", 4) != 0)
+        return fail(c, G4_ERR_FORMAT, "not a gemma4.c model image (magic \"MOG\")");
+    const Rec *r = (const Rec *)(img + G4_WEIGHTS_OFFSET);
+
+    CK(cudaSetDevice(c->device));
+    CK(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, c->device));
+    CK(cudaStreamCreateWithFlags(&c->st, cudaStreamNonBlocking));
+
+    // ---- collect host views + validate geometry ----
+    HostMat embed, eple, pmp;
+    int rc;
+    if ((rc = get_mat(c, img, bytes, r, G4_R_EMBED, G4_VOCAB, G4_HIDDEN, &embed))) return rc;
+    if ((rc = get_mat(c, img, bytes, r, G4_R_EMBED_PER_LAYER, G4_VOCAB, G4_NUM_LAYERS * G4_PLE, &eple))) return rc;
+    if ((rc = get_mat(c, img, bytes, r, G4_R_PLE_MODEL_PROJ, G4_NUM_LAYERS * G4_PLE, G4_HIDDEN, &pmp))) return rc;
+    struct HL {
+        HostMat q, k, v, o, gate, up, down, pleg, plep;
+        const float *vec[8];
+        const float *cosv, *sinv;
+        int pairs;
+    } hl[G4_NUM_LAYERS];
+    size_t total = mat_bytes(G4_VOCAB, G4_HIDDEN) + mat_bytes(G4_VOCAB, G4_NUM_LAYERS * G4_PLE) +
+                   mat_bytes(G4_NUM_LAYERS * G4_PLE, G4_HIDDEN);
+    for (int l = 0; l < G4_NUM_LAYERS; l++) {
+        const int global = g4_layer_is_global(l), hd = global ? G4_HD_GLOBAL : G4_HD_SLIDING;
+        const int kv = l < G4_NUM_KV_LAYERS, ffn = kv ? 6144 : 12288, qw = G4_HEADS * hd;
+        HL &x = hl[l];
+        if ((rc = get_mat(c, img, bytes, r, G4_R_LAYER(l, G4_L_Q_PROJ), qw, G4_HIDDEN, &x.q))) return rc;
+        if (kv) {
+            if ((rc = get_mat(c, img, bytes, r, G4_R_LAYER(l, G4_L_K_PROJ), hd, G4_HIDDEN, &x.k))) return rc;
+            if ((rc = get_mat(c, img, bytes, r, G4_R_LAYER(l, G4_L_V_PROJ), hd, G4_HIDDEN, &x.v))) return rc;
+        } else if (r[G4_R_LAYER(l, G4_L_K_PROJ)].data || r[G4_R_LAYER(l, G4_L_V_PROJ)].data) {
+            return fail(c, G4_ERR_FORMAT, "layer %d: unexpected K/V weights on a shared-cache layer", l);
+        }
+        if ((rc = get_mat(c, img, bytes, r, G4_R_LAYER(l, G4_L_O_PROJ), G4_HIDDEN, qw, &x.o))) return rc;
+        if ((rc = get_mat(c, img, bytes, r, G4_R_LAYER(l, G4_L_GATE), ffn, G4_HIDDEN, &x.gate))) return rc;
+        if ((rc = get_mat(c, img, bytes, r, G4_R_LAYER(l, G4_L_UP), ffn, G4_HIDDEN, &x.up))) return rc;
+        if ((rc = get_mat(c, img, bytes, r, G4_R_LAYER(l, G4_L_DOWN), G4_HIDDEN, ffn, &x.down))) return rc;
+        if ((rc = get_mat(c, img, bytes, r, G4_R_LAYER(l, G4_L_PLE_GATE), G4_PLE, G4_HIDDEN, &x.pleg))) return rc;
+        if ((rc = get_mat(c, img, bytes, r, G4_R_LAYER(l, G4_L_PLE_PROJ), G4_HIDDEN, G4_PLE, &x.plep))) return rc;
+        const int vidx[8] = {G4_L_INPUT_NORM, G4_L_POST_ATTN_NORM, G4_L_PRE_FFN_NORM, G4_L_POST_FFN_NORM,
+                             G4_L_POST_PLE_NORM, G4_L_Q_NORM, G4_L_K_NORM, G4_L_LAYER_SCALAR};
+        const int vlen[8] = {G4_HIDDEN, G4_HIDDEN, G4_HIDDEN, G4_HIDDEN, G4_HIDDEN, hd, hd, 1};
+        for (int i = 0; i < 8; i++) {
+            x.vec[i] = nullptr;
+            if (i == 6 && !kv) continue;
+            if ((rc = get_vec(c, img, bytes, r, G4_R_LAYER(l, vidx[i]), vlen[i], &x.vec[i]))) return rc;
+        }
+        const Rec &rcos = r[G4_R_LAYER(l, G4_L_ROPE_COS)], &rsin = r[G4_R_LAYER(l, G4_L_ROPE_SIN)];
+        x.pairs = rcos.shape[1];
+        const int want_pairs = global ? 64 : 128;
+        if (rcos.shape[0] != G4_MAX_CONTEXT || x.pairs != want_pairs || rsin.shape[1] != x.pairs ||
+            rsin.shape[0] != G4_MAX_CONTEXT)
+            return fail(c, G4_ERR_FORMAT, "layer %d: rope table shape", l);
+        x.cosv = (const float *)resolve(img, bytes, rcos.data, (uint64_t)G4_MAX_CONTEXT * x.pairs * 4);
+        x.sinv = (const float *)resolve(img, bytes, rsin.data, (uint64_t)G4_MAX_CONTEXT * x.pairs * 4);
+        if (!x.cosv || !x.sinv) return fail(c, G4_ERR_FORMAT, "layer %d: rope tables outside the image", l);
+        total += mat_bytes(qw + (kv ? 2 * hd : 0), G4_HIDDEN) + mat_bytes(G4_HIDDEN, qw) + mat_bytes(2 * ffn, G4_HIDDEN) +
+                 mat_bytes(G4_HIDDEN, ffn) + mat_bytes(G4_PLE, G4_HIDDEN) + mat_bytes(G4_HIDDEN, G4_PLE) +
+                 8 * 4 * 1024 + 2 * 256;
+    }
+    const float *final_norm, *ple_norm, *gelu;
+    if ((rc = get_vec(c, img, bytes, r, G4_R_NORM, G4_HIDDEN, &final_norm))) return rc;
+    if ((rc = get_vec(c, img, bytes, r, G4_R_PLE_PROJ_NORM, G4_PLE, &ple_norm))) return rc;
+    const Rec &rg = r[G4_R_GELU];
+    if (rg.shape[0] != 4096 || rg.shape[1] != -8 || rg.shape[2] != 8)
+        return fail(c, G4_ERR_FORMAT, "gelu table shape (%d,%d,%d)", rg.shape[0], rg.shape[1], rg.shape[2]);
+    gelu = (const float *)resolve(img, bytes, rg.data, 4096 * 4);
+    if (!gelu) return fail(c, G4_ERR_FORMAT, "gelu table outside the image");
+    total += 2 * (size_t)G4_MAX_CONTEXT * (128 + 64) * 4 + 64 * 1024;
+
+    // ---- device allocation ----
+    c->arena_bytes = total + (1 << 20);
+    CK(cudaMalloc(&c->arena, c->arena_bytes));
+    c->embed = alloc_mat(c, G4_VOCAB, G4_HIDDEN);
+    c->embed_ple = alloc_mat(c, G4_VOCAB, G4_NUM_LAYERS * G4_PLE);
+    c->pmp = alloc_mat(c, G4_NUM_LAYERS * G4_PLE, G4_HIDDEN);
+    for (int l = 0; l < G4_NUM_LAYERS; l++) {
+        Layer &Y = c->L[l];
+        HL &x = hl[l];
+        Y.global = g4_layer_is_global(l);
+        Y.hd = Y.global ? G4_HD_GLOBAL : G4_HD_SLIDING;
+        Y.has_kv = l < G4_NUM_KV_LAYERS;
+        Y.owner = g4_cache_owner(l);
+        Y.ffn = x.gate.N;
+        Y.qw = G4_HEADS * Y.hd;
+        Y.pairs = x.pairs;
+        Y.qkv = alloc_mat(c, Y.qw + (Y.has_kv ? 2 * Y.hd : 0), G4_HIDDEN);
+        Y.o = alloc_mat(c, G4_HIDDEN, Y.qw);
+        Y.gu = alloc_mat(c, 2 * Y.ffn, G4_HIDDEN);
+        Y.down = alloc_mat(c, G4_HIDDEN, Y.ffn);
+        Y.pleg = alloc_mat(c, G4_PLE, G4_HIDDEN);
+        Y.plep = alloc_mat(c, G4_HIDDEN, G4_PLE);
+    }
+    if (!c->embed.w || !c->L[G4_NUM_LAYERS - 1].plep.s) return fail(c, G4_ERR_NOMEM, "weight arena too small");
+
+    // ---- upload + repack ----
+    const size_t stage_bytes = 256u << 20;
+    uint8_t *stage = nullptr;
+    CK(cudaMalloc(&stage, stage_bytes));
+    auto up = [&](const HostMat &hm, DMat d, int off, int mul) { return upload_mat(c, hm, d, off, mul, stage, stage_bytes); };
+    rc = up(embed, c->embed, 0, 1);
+    if (!rc) rc = up(eple, c->embed_ple, 0, 1);
+    if (!rc) rc = up(pmp, c->pmp, 0, 1);
+    for (int l = 0; l < G4_NUM_LAYERS && !rc; l++) {
+        Layer &Y = c->L[l];
+        HL &x = hl[l];
+        rc = up(x.q, Y.qkv, 0, 1);
+        if (!rc && Y.has_kv) rc = up(x.k, Y.qkv, Y.qw, 1);
+        if (!rc && Y.has_kv) rc = up(x.v, Y.qkv, Y.qw + Y.hd, 1);
+        if (!rc) rc = up(x.o, Y.o, 0, 1);
+        if (!rc) rc = up(x.gate, Y.gu, 0, 2);
+        if (!rc) rc = up(x.up, Y.gu, 1, 2);
+        if (!rc) rc = up(x.down, Y.down, 0, 1);
+        if (!rc) rc = up(x.pleg, Y.pleg, 0, 1);
+        if (!rc) rc = up(x.plep, Y.plep, 0, 1);
+    }
+    cudaFree(stage);
+    if (rc) return rc;
+    int vr = G4_OK;
+    const float *rope_dev[4] = {nullptr, nullptr, nullptr, nullptr};
+    for (int l = 0; l < G4_NUM_LAYERS; l++) {
+        Layer &Y = c->L[l];
+        HL &x = hl[l];
+        Y.in_norm = upload_vec(c, x.vec[0], G4_HIDDEN, &vr);
+        Y.post_attn = upload_vec(c, x.vec[1], G4_HIDDEN, &vr);
+        Y.pre_ffn = upload_vec(c, x.vec[2], G4_HIDDEN, &vr);
+        Y.post_ffn = upload_vec(c, x.vec[3], G4_HIDDEN, &vr);
+        Y.post_ple = upload_vec(c, x.vec[4], G4_HIDDEN, &vr);
+        Y.q_norm = upload_vec(c, x.vec[5], Y.hd, &vr);
+        Y.k_norm = Y.has_kv ? upload_vec(c, x.vec[6], Y.hd, &vr) : nullptr;
+        Y.scalar = upload_vec(c, x.vec[7], 1, &vr);
+        const int ti = Y.global ? 2 : 0;
+        if (!rope_dev[ti]) {
+            rope_dev[ti] = upload_vec(c, x.cosv, (size_t)G4_MAX_CONTEXT * x.pairs, &vr);
+            rope_dev[ti + 1] = upload_vec(c, x.sinv, (size_t)G4_MAX_CONTEXT * x.pairs, &vr);
+        }
+        Y.rope_cos = rope_dev[ti];
+        Y.rope_sin = rope_dev[ti + 1];
+    }
+    c->final_norm = upload_vec(c, final_norm, G4_HIDDEN, &vr);
+    c->ple_norm = upload_vec(c, ple_norm, G4_PLE, &vr);
+    c->gelu = upload_vec(c, gelu, 4096, &vr);
+    if (vr) return fail(c, vr, "uploading vectors failed");
+    CK(cudaStreamSynchronize(c->st));
+
+    // ---- state ----
+    struct { void **p; size_t bytes; } bufs[] = {
+        {(void **)&c->res[0], (size_t)kMaxT * G4_HIDDEN * 4},
+        {(void **)&c->res[1], (size_t)kMaxT * G4_HIDDEN * 4},
+        {(void **)&c->xq, (size_t)kMaxT * kMaxFfn},
+        {(void **)&c->xs, (size_t)kMaxT * kMaxFfn / 64 * 4},
+        {(void **)&c->qkv, (size_t)kMaxT * kQkvStride * 4},
+        {(void **)&c->attn, (size_t)kMaxT * G4_HEADS * G4_HD_GLOBAL * 4},
+        {(void **)&c->h, (size_t)kMaxT * G4_HIDDEN * 4},
+        {(void **)&c->gu, (size_t)kMaxT * kMaxFfn * 4},
+        {(void **)&c->pg, (size_t)kMaxT * G4_PLE * 4},
+        {(void **)&c->pli, (size_t)kMaxT * G4_NUM_LAYERS * G4_PLE * 4},
+        {(void **)&c->ple_emb, (size_t)kMaxT * G4_NUM_LAYERS * G4_PLE * 4},
+        {(void **)&c->ple_u, (size_t)kMaxT * G4_NUM_LAYERS * G4_PLE * 4},
+        {(void **)&c->logits, (size_t)G4_VOCAB * 4},
+        {(void **)&c->part, (size_t)kSplits * G4_HEADS * (G4_HD_GLOBAL + 4) * 4},
+        {(void **)&c->argmax_part, (size_t)1024 * 4 * 2 * 4},
+        {(void **)&c->topk_v, (size_t)1024 * 64 * 4},
+        {(void **)&c->topk_i, (size_t)1024 * 64 * 4},
+        {(void **)&c->argmax_out, 64},
+        {(void **)&c->ticket, 64},
+        {(void **)&c->err, 64},
+        {(void **)&c->tokens_d, (size_t)kMaxT * 4},
+        {(void **)&c->pos_d, 64},
+    };
+    size_t st_total = 0;
+    for (auto &b : bufs) st_total += (b.bytes + 255) & ~(size_t)255;
+    CK(cudaMalloc(&c->state, st_total));
+    CK(cudaMemset(c->state, 0, st_total));
+    size_t off = 0;
+    for (auto &b : bufs) {
+        *b.p = c->state + off;
+        off += (b.bytes + 255) & ~(size_t)255;
+    }
+    // KV rings: 12 sliding (owners 0-3, 5-8, 10-13) + 3 global (owners 4, 9, 14)
+    const size_t sl = (size_t)2 * G4_SLIDING_RING * G4_HD_SLIDING * 4, gl = (size_t)2 * G4_MAX_CONTEXT * G4_HD_GLOBAL * 4;
+    c->kv_bytes = 12 * sl + 3 * gl;
+    CK(cudaMalloc(&c->kv, c->kv_bytes));
+    CK(cudaMemset(c->kv, 0, c->kv_bytes));
+    for (int l = 0; l < G4_NUM_LAYERS; l++) {
+        Layer &Y = c->L[l];
+        const int o = Y.owner;
+        if (Y.global) {
+            Y.ring = G4_MAX_CONTEXT;
+            Y.kcache = (float *)((uint8_t *)c->kv + 12 * sl + (size_t)(o / 5) * gl);
+        } else {
+            Y.ring = G4_SLIDING_RING;
+            Y.kcache = (float *)((uint8_t *)c->kv + (size_t)((o / 5) * 4 + o % 5) * sl);
+        }
+        Y.vcache = Y.kcache + (size_t)Y.ring * Y.hd;
+    }
+    CK(cudaStreamSynchronize(c->st));
+    return G4_OK;
+}
+
+// ---------------------------------------------------------------------------
+// launch sequences
+
+struct Seq {
+    g4_ctx *c;
+    bool pdl;
+    cudaError_t e = cudaSuccess;
+    void ck(cudaError_t x) { if (e == cudaSuccess && x != cudaSuccess) e = x; }
+};
+
+GemvArgs gemv_base(g4_ctx *c, const DMat &m, int T) {
+    GemvArgs a{};
+    a.m = m;
+    a.T = T;
+    a.eps = G4_RMS_EPS;
+    a.gelu = c->gelu;
+    a.err = c->err;
+    g4_gemv_plan(a, c->num_sms);
+    return a;
+}
+
+void gemv(Seq &q, GemvArgs &a, int pro, int epi) {
+    g4_gemv_plan(a, q.c->num_sms);
+    int units = a.m.N / a.row_gran;
+    int grid = units < q.c->num_sms ? units : q.c->num_sms;
+    q.ck(g4_launch_gemv(a, pro, epi, grid, q.c->st, q.pdl));
+}
+
+void gemm(Seq &q, const DMat &m, int T, int epi, float *out, int out_stride, const float *u, int u_stride) {
+    g4_ctx *c = q.c;
+    GemmArgs a{};
+    a.m = m;
+    a.T = T;
+    a.xq = c->xq;
+    a.xs = c->xs;
+    a.epi = epi;
+    a.out = out;
+    a.out_stride = out_stride;
+    a.ple_u = u;
+    a.u_stride = u_stride;
+    a.gelu = c->gelu;
+    a.err = c->err;
+    if (c->gemm_path == 1 || !g4_gemm_tc_supported(a) || c->gemm_path == -1)
+        q.ck(g4_launch_gemm_simt(a, c->st, q.pdl));
+    else
+        q.ck(g4_launch_gemm_tc(a, c->st, q.pdl));
+}
+
+AttnArgs attn_base(g4_ctx *c, const Layer &Y, int T, int start_pos, const int *pos_dev) {
+    AttnArgs a{};
+    a.hd = Y.hd;
+    a.pairs = Y.pairs;
+    a.window = Y.global ? 0 : G4_SLIDING_WINDOW;
+    a.mask = Y.ring - 1;
+    a.T = T;
+    a.start_pos = start_pos;
+    a.pos_dev = pos_dev;
+    a.qkv = c->qkv;
+    a.qkv_stride = kQkvStride;
+    a.has_kv = Y.has_kv;
+    a.q_norm = Y.q_norm;
+    a.k_norm = Y.k_norm;
+    a.rope_cos = Y.rope_cos;
+    a.rope_sin = Y.rope_sin;
+    a.kcache = Y.kcache;
+    a.vcache = Y.vcache;
+    a.part = c->part;
+    a.out = c->attn;
+    a.xq = c->xq;
+    a.xs = c->xs;
+    a.err = c->err;
+    return a;
+}
+
+// Decode path, T <= 4 tokens. pos_dev != NULL: positions and tokens come from
+// device memory (graph replay); otherwise from start_pos / tokens_d.
+cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev) {
+    Seq q{c, c->use_pdl};
+    int cur = 0;
+    const float emb_mult = sqrtf((float)G4_HIDDEN), ple_mult = sqrtf((float)G4_PLE);
+    {
+        GemvArgs a = gemv_base(c, c->pmp, T);
+        a.tokens = c->tokens_d;
+        a.embed = c->embed;
+        a.embed_ple = c->embed_ple;
+        a.ple_emb = c->ple_emb;
+        a.embed_mult = emb_mult;
+        a.ple_mult = ple_mult;
+        a.res_out = c->res[0];
+        a.out = c->pli;
+        a.out_stride = G4_NUM_LAYERS * G4_PLE;
+        gemv(q, a, PRO_EMBED_QUANT, EPI_STORE);
+        q.ck(g4_launch_ple_prep(c->pli, c->ple_emb, c->ple_norm, 1e-6f * G4_HIDDEN, 1.0f / sqrtf(2.0f), T, c->ple_u,
+                                c->st, q.pdl));
+    }
+    for (int l = 0; l < c->layers; l++) {
+        const Layer &Y = c->L[l];
+        // K1: q|k|v with the input norm (and the previous layer's PLE residual update)
+        {
+            GemvArgs a = gemv_base(c, Y.qkv, T);
+            a.out = c->qkv;
+            a.out_stride = kQkvStride;
+            a.w_pre = Y.in_norm;
+            if (l == 0) {
+                a.src = c->res[cur];
+                a.src_stride = G4_HIDDEN;
+                gemv(q, a, PRO_NORM_QUANT, EPI_STORE);
+            } else {
+                const Layer &P = c->L[l - 1];
+                a.src = c->h;
+                a.src_stride = G4_HIDDEN;
+                a.w_post = P.post_ple;
+                a.scalar = P.scalar;
+                a.res_in = c->res[cur];
+                a.res_out = c->res[cur ^ 1];
+                cur ^= 1;
+                gemv(q, a, PRO_RES_NORM_QUANT, EPI_STORE);
+            }
+        }
+        // attention
+        AttnArgs at = attn_base(c, Y, T, start_pos, pos_dev);
+        if (T == 1) {
+            q.ck(g4_launch_attn_decode(at, kSplits, c->st, q.pdl));
+            q.ck(g4_launch_attn_combine(at, kSplits, c->st, q.pdl));
+        } else {
+            q.ck(g4_launch_qkv_post(at, c->st, q.pdl));
+            q.ck(g4_launch_attn_prefill(at, c->st, q.pdl));
+        }
+        // o_proj
+        {
+            GemvArgs a = gemv_base(c, Y.o, T);
+            a.out = c->h;
+            a.out_stride = G4_HIDDEN;
+            if (T == 1) {
+                a.xq_in = c->xq;
+                a.xs_in = c->xs;
+                gemv(q, a, PRO_LOADQ, EPI_STORE);
+            } else {
+                a.src = c->attn;
+                a.src_stride = Y.qw;
+                gemv(q, a, PRO_QUANT, EPI_STORE);
+            }
+        }
+        // gate|up with post-attn norm + residual + pre-ffn norm
+        {
+            GemvArgs a = gemv_base(c, Y.gu, T);
+            a.row_gran = 2;
+            a.src = c->h;
+            a.src_stride = G4_HIDDEN;
+            a.w_post = Y.post_attn;
+            a.res_in = c->res[cur];
+            a.res_out = c->res[cur ^ 1];
+            cur ^= 1;
+            a.w_pre = Y.pre_ffn;
+            a.out = c->gu;
+            a.out_stride = Y.ffn;
+            gemv(q, a, PRO_RES_NORM_QUANT, EPI_GEGLU_PAIR);
+        }
+        // down
+        {
+            GemvArgs a = gemv_base(c, Y.down, T);
+            a.src = c->gu;
+            a.src_stride = Y.ffn;
+            a.out = c->h;
+            a.out_stride = G4_HIDDEN;
+            gemv(q, a, PRO_QUANT, EPI_STORE);
+        }
+        // per-layer input gate with post-ffn norm + residual
+        {
+            GemvArgs a = gemv_base(c, Y.pleg, T);
+            a.src = c->h;
+            a.src_stride = G4_HIDDEN;
+            a.w_post = Y.post_ffn;
+            a.res_in = c->res[cur];
+            a.res_out = c->res[cur ^ 1];
+            cur ^= 1;
+            a.out = c->pg;
+            a.out_stride = G4_PLE;
+            a.ple_u = c->ple_u + l * G4_PLE;
+            a.u_stride = G4_NUM_LAYERS * G4_PLE;
+            gemv(q, a, PRO_RES_QUANT, EPI_PLE);
+        }
+        // per-layer projection
+        {
+            GemvArgs a = gemv_base(c, Y.plep, T);
+            a.src = c->pg;
+            a.src_stride = G4_PLE;
+            a.out = c->h;
+            a.out_stride = G4_HIDDEN;
+            gemv(q, a, PRO_QUANT, EPI_STORE);
+        }
+    }
+    const Layer &Z = c->L[c->layers - 1];
+    q.ck(g4_launch_rows_norm(3, c->h, T, Z.post_ple, c->res[cur], c->res[cur ^ 1], Z.scalar, nullptr, G4_RMS_EPS,
+                             nullptr, nullptr, c->st, q.pdl));
+    cur ^= 1;
+    c->cur = cur;
+    return q.e;
+}
+
+cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos) {
+    Seq q{c, c->use_pdl};
+    int cur = 0;
+    q.ck(g4_launch_rows_embed(c->tokens_d, T, c->embed, c->embed_ple, sqrtf((float)G4_HIDDEN), sqrtf((float)G4_PLE),
+                              c->res[0], c->ple_emb, c->err, c->st, q.pdl));
+    q.ck(g4_launch_rows_quant(c->res[0], G4_HIDDEN, T, G4_HIDDEN, c->xq, c->xs, c->st, q.pdl));
+    gemm(q, c->pmp, T, EPI_STORE, c->pli, G4_NUM_LAYERS * G4_PLE, nullptr, 0);
+    q.ck(g4_launch_ple_prep(c->pli, c->ple_emb, c->ple_norm, 1e-6f * G4_HIDDEN, 1.0f / sqrtf(2.0f), T, c->ple_u, c->st,
+                            q.pdl));
+    for (int l = 0; l < c->layers; l++) {
+        const Layer &Y = c->L[l];
+        if (l == 0) {
+            q.ck(g4_launch_rows_norm(0, c->res[cur], T, nullptr, nullptr, nullptr, nullptr, Y.in_norm, G4_RMS_EPS, c->xq,
+                                     c->xs, c->st, q.pdl));
+        } else {
+            const Layer &P = c->L[l - 1];
+            q.ck(g4_launch_rows_norm(1, c->h, T, P.post_ple, c->res[cur], c->res[cur ^ 1], P.scalar, Y.in_norm,
+                                     G4_RMS_EPS, c->xq, c->xs, c->st, q.pdl));
+            cur ^= 1;
+        }
+        gemm(q, Y.qkv, T, EPI_STORE, c->qkv, kQkvStride, nullptr, 0);
+        AttnArgs at = attn_base(c, Y, T, start_pos, nullptr);
+        q.ck(g4_launch_qkv_post(at, c->st, q.pdl));
+        q.ck(g4_launch_attn_prefill(at, c->st, q.pdl));
+        q.ck(g4_launch_rows_quant(c->attn, Y.qw, T, Y.qw, c->xq, c->xs, c->st, q.pdl));
+        gemm(q, Y.o, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
+        q.ck(g4_launch_rows_norm(1, c->h, T, Y.post_attn, c->res[cur], c->res[cur ^ 1], nullptr, Y.pre_ffn, G4_RMS_EPS,
+                                 c->xq, c->xs, c->st, q.pdl));
+        cur ^= 1;
+        gemm(q, Y.gu, T, EPI_GEGLU_PAIR, c->gu, Y.ffn, nullptr, 0);
+        q.ck(g4_launch_rows_quant(c->gu, Y.ffn, T, Y.ffn, c->xq, c->xs, c->st, q.pdl));
+        gemm(q, Y.down, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
+        q.ck(g4_launch_rows_norm(2, c->h, T, Y.post_ffn, c->res[cur], c->res[cur ^ 1], nullptr, nullptr, G4_RMS_EPS,
+                                 c->xq, c->xs, c->st, q.pdl));
+        cur ^= 1;
+        gemm(q, Y.pleg, T, EPI_PLE, c->pg, G4_PLE, c->ple_u + l * G4_PLE, G4_NUM_LAYERS * G4_PLE);
+        q.ck(g4_launch_rows_quant(c->pg, G4_PLE, T, G4_PLE, c->xq, c->xs, c->st, q.pdl));
+        gemm(q, Y.plep, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
+    }
+    const Layer &Z = c->L[c->layers - 1];
+    q.ck(g4_launch_rows_norm(3, c->h, T, Z.post_ple, c->res[cur], c->res[cur ^ 1], Z.scalar, nullptr, G4_RMS_EPS,
+                             nullptr, nullptr, c->st, q.pdl));
+    cur ^= 1;
+    c->cur = cur;
+    return q.e;
+}
+
+int check_device_error(g4_ctx *c) {
+    int e = 0;
+    cudaError_t ce = cudaMemcpyAsync(&e, c->err, 4, cudaMemcpyDeviceToHost, c->st);
+    if (ce == cudaSuccess) ce = cudaStreamSynchronize(c->st);
+    if (ce != cudaSuccess) return fail(c, G4_ERR_CUDA, "device: %s", cudaGetErrorString(ce));
+    if (e) {
+        cudaMemsetAsync(c->err, 0, 4, c->st);
+        cudaStreamSynchronize(c->st);
+        const char *what = e == G4D_BAD_TOKEN ? "token id outside the vocabulary"
+                           : e == G4D_TIMEOUT_FULL || e == G4D_TIMEOUT_EMPTY ? "kernel wait timed out"
+                                                                              : "kernel error";
+        return fail(c, G4_ERR_DEVICE, "device reported error %d: %s", e, what);
+    }
+    return G4_OK;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------------------
+// C ABI
+
+extern "C" {
+
+const char *g4_strerror(int code) {
+    switch (code) {
+    case G4_OK: return "ok";
+    case G4_ERR_INVALID: return "invalid argument";
+    case G4_ERR_FORMAT: return "bad model image";
+    case G4_ERR_CUDA: return "CUDA error";
+    case G4_ERR_NOMEM: return "out of memory";
+    case G4_ERR_DEVICE: return "device-side error";
+    case G4_ERR_STATE: return "call out of sequence";
+    default: return "unknown error";
+    }
+}
+
+const char *g4_last_error(g4_ctx *c) { return c ? c->msg : "no context"; }
+
+static char g_open_msg[512];
+
+int g4_open(const void *image, uint64_t bytes, int device, g4_ctx **out) {
+    if (!out) return G4_ERR_INVALID;
+    *out = nullptr;
+    if (!image || device < 0) return G4_ERR_INVALID;
+    g4_ctx *c = new g4_ctx();
+    c->device = device;
+    int rc = open_impl(c, (const uint8_t *)image, bytes);
+    if (rc) {
+        snprintf(g_open_msg, sizeof(g_open_msg), "%s", c->msg);
+        g4_close(c);
+        return rc;
+    }
+    *out = c;
+    return G4_OK;
+}
+
+const char *g4_open_error(void) { return g_open_msg; }
+
+int g4_open_file(const char *path, int device, g4_ctx **out) {
+    if (!path || !out) return G4_ERR_INVALID;
+    FILE *f = fopen(path, "rb");
+    if (!f) return G4_ERR_INVALID;
+    fseek(f, 0, SEEK_END);
+    long long n = ftell(f);
+    fseek(f, 0, SEEK_SET);
+    uint8_t *buf = (uint8_t *)malloc((size_t)n);
+    if (!buf) { fclose(f); return G4_ERR_NOMEM; }
+    size_t got = fread(buf, 1, (size_t)n, f);
+    fclose(f);
+    int rc = got == (size_t)n ? g4_open(buf, (uint64_t)n, device, out) : G4_ERR_FORMAT;
+    free(buf);
+    return rc;
+}
+
+int g4_close(g4_ctx *c) {
+    if (!c) return G4_ERR_INVALID;
+    if (c->st) cudaStreamSynchronize(c->st);
+    if (c->g_decode) cudaGraphExecDestroy(c->g_decode);
+    if (c->arena) cudaFree(c->arena);
+    if (c->state) cudaFree(c->state);
+    if (c->kv) cudaFree(c->kv);
+    if (c->st) cudaStreamDestroy(c->st);
+    delete c;
+    return G4_OK;
+}
+
+int g4_set_option(g4_ctx *c, int option, int value) {
+    if (!c) return G4_ERR_INVALID;
+    switch (option) {
+    case G4_OPT_GRAPHS: c->use_graph = value != 0; break;
+    case G4_OPT_PDL:
+        c->use_pdl = value != 0;
+        if (c->g_decode) { cudaGraphExecDestroy(c->g_decode); c->g_decode = nullptr; }
+        break;
+    case G4_OPT_GEMM_PATH: c->gemm_path = value; break;
+    case G4_OPT_LAYERS:
+        if (value < 1 || value > G4_NUM_LAYERS) return fail(c, G4_ERR_INVALID, "layers %d out of range", value);
+        c->layers = value;
+        if (c->g_decode) { cudaGraphExecDestroy(c->g_decode); c->g_decode = nullptr; }
+        break;
+    default: return fail(c, G4_ERR_INVALID, "unknown option %d", option);
+    }
+    return G4_OK;
+}
+
+int g4_forward(g4_ctx *c, const int *tokens, size_t count, int start_pos) {
+    if (!c) return G4_ERR_INVALID;
+    if (!tokens || count < 1 || count > (size_t)kMaxT || start_pos < 0 ||
+        (long long)start_pos + (long long)count > G4_MAX_CONTEXT)
+        return fail(c, G4_ERR_INVALID, "forward: count %zu start_pos %d out of range", count, start_pos);
+    for (size_t i = 0; i < count; i++)
+        if (tokens[i] < 0 || tokens[i] >= G4_VOCAB) return fail(c, G4_ERR_INVALID, "forward: token %d out of range", tokens[i]);
+    cudaSetDevice(c->device);
+    const int T = (int)count;
+    CK(cudaMemcpyAsync(c->tokens_d, tokens, count * 4, cudaMemcpyHostToDevice, c->st));
+    cudaError_t e;
+    if (T == 1 && c->use_graph) {
+        CK(cudaMemcpyAsync(c->pos_d, &start_pos, 4, cudaMemcpyHostToDevice, c->st));
+        if (!c->g_decode) {
+            if (!c->decode_warm) {
+                // first call runs eagerly (sets kernel attributes), later calls replay the graph
+                e = enqueue_small(c, 1, start_pos, c->pos_d);
+                if (e) return fail(c, G4_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
+                c->decode_warm = true;
+                c->graph_cur = c->cur;
+                c->last_T = T;
+                return G4_OK;
+            }
+            cudaGraph_t g = nullptr;
+            CK(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
+            e = enqueue_small(c, 1, start_pos, c->pos_d);
+            cudaError_t e2 = cudaStreamEndCapture(c->st, &g);
+            if (e || e2) {
+                if (g) cudaGraphDestroy(g);
+                return fail(c, G4_ERR_CUDA, "decode capture: %s", cudaGetErrorString(e ? e : e2));
+            }
+            e = cudaGraphInstantiate(&c->g_decode, g, 0);
+            cudaGraphDestroy(g);
+            if (e) return fail(c, G4_ERR_CUDA, "graph instantiate: %s", cudaGetErrorString(e));
+            c->graph_cur = c->cur;
+        }
+        CK(cudaGraphLaunch(c->g_decode, c->st));
+        c->cur = c->graph_cur;
+    } else if (T <= 4) {
+        e = enqueue_small(c, T, start_pos, nullptr);
+        if (e) return fail(c, G4_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
+    } else {
+        e = enqueue_prefill(c, T, start_pos);
+        if (e) return fail(c, G4_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e));
+    }
+    c->last_T = T;
+    return G4_OK;
+}
+
+int g4_logits(g4_ctx *c, size_t row, float *out, int *argmax) {
+    if (!c) return G4_ERR_INVALID;
+    if (c->last_T == 0 || row >= (size_t)c->last_T)
+        return fail(c, G4_ERR_STATE, "logits: row %zu not computed by the last forward (%d rows)", row, c->last_T);
+    cudaSetDevice(c->device);
+    GemvArgs a = gemv_base(c, c->embed, 1);
+    a.src = c->res[c->cur] + row * G4_HIDDEN;
+    a.src_stride = G4_HIDDEN;
+    a.w_pre = c->final_norm;
+    a.out = c->logits;
+    a.out_stride = G4_VOCAB;
+    a.argmax_part = c->argmax_part;
+    a.argmax_out = c->argmax_out;
+    a.ticket = c->ticket;
+    Seq q{c, c->use_pdl};
+    gemv(q, a, PRO_NORM_QUANT, EPI_LOGITS);
+    if (q.e) return fail(c, G4_ERR_CUDA, "logits launch: %s", cudaGetErrorString(q.e));
+    if (out) CK(cudaMemcpyAsync(out, c->logits, (size_t)G4_VOCAB * 4, cudaMemcpyDeviceToHost, c->st));
+    if (argmax) CK(cudaMemcpyAsync(argmax, c->argmax_out, 4, cudaMemcpyDeviceToHost, c->st));
+    return check_device_error(c);
+}
+
+int g4_topk(g4_ctx *c, size_t row, int k, float *values, int *ids) {
+    if (!c || !values || !ids || k < 1 || k > 64) return G4_ERR_INVALID;
+    int rc = g4_logits(c, row, nullptr, nullptr);
+    if (rc) return rc;
+    CK(g4_launch_topk(c->logits, G4_VOCAB, k, c->topk_v, c->topk_i, c->topk_v + 1024 * 32, c->topk_i + 1024 * 32,
+                      c->st));
+    CK(cudaMemcpyAsync(values, c->topk_v + 1024 * 32, (size_t)k * 4, cudaMemcpyDeviceToHost, c->st));
+    CK(cudaMemcpyAsync(ids, c->topk_i + 1024 * 32, (size_t)k * 4, cudaMemcpyDeviceToHost, c->st));
+    return check_device_error(c);
+}
+
+int g4_sync(g4_ctx *c) {
+    if (!c) return G4_ERR_INVALID;
+    cudaSetDevice(c->device);
+    return check_device_error(c);
+}
+
+int g4_read_residual(g4_ctx *c, size_t rows, float *out) {
+    if (!c || !out || rows > (size_t)kMaxT) return G4_ERR_INVALID;
+    cudaSetDevice(c->device);
+    CK(cudaMemcpyAsync(out, c->res[c->cur], rows * G4_HIDDEN * 4, cudaMemcpyDeviceToHost, c->st));
+    return check_device_error(c);
+}
+
+int g4_read_cache(g4_ctx *c, int layer, int which, int slot0, int nslots, float *out) {
+    if (!c || !out || layer < 0 || layer >= G4_NUM_LAYERS || nslots < 0) return G4_ERR_INVALID;
+    const Layer &Y = c->L[layer];
+    if (slot0 < 0 || slot0 + nslots > Y.ring) return G4_ERR_INVALID;
+    cudaSetDevice(c->device);
+    const float *src = (which ? Y.vcache : Y.kcache) + (size_t)slot0 * Y.hd;
+    CK(cudaMemcpyAsync(out, src, (size_t)nslots * Y.hd * 4, cudaMemcpyDeviceToHost, c->st));
+    return check_device_error(c);
+}
+
+void *g4_stream(g4_ctx *c) { return c ? (void *)c->st : nullptr; }
+
+int g4_device_bytes(g4_ctx *c, uint64_t *weights, uint64_t *total) {
+    if (!c) return G4_ERR_INVALID;
+    if (weights) *weights = c->arena_used;
+    if (total) *total = c->arena_bytes + c->kv_bytes;
+    return G4_OK;
+}
+
+}  // extern "C"

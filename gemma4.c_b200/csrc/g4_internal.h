@@ -1,0 +1,162 @@
+// g4_internal.h — structures shared by the g4cuda kernels and the host engine.
+//
+// Device weight layout (repacked once at load from the file's 16-row-block
+// layout, exporter.py:304-316):
+//   - every int8 matrix is row-major W[N][K] (K contiguous), so a row is one
+//     contiguous byte run for the decode GEMV's bulk copies and K-major tiles
+//     for the prefill GEMM;
+//   - its FP16 scales are row-major S[N][K/64];
+//   - fused matrices: QKV rows are q | k | v concatenated (layers 0-14), and
+//     gate/up rows are interleaved (row 2i = gate i, 2i+1 = up i) so one
+//     GEMV/GEMM produces both halves of every GeGLU pair.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "g4_format.h"
+
+// Device-side error codes written to the context's error word (reported by the
+// host as G4_ERR_DEVICE).
+enum : int {
+    G4D_OK = 0,
+    G4D_TIMEOUT_FULL = 1,   // consumer waited too long for a weight stage
+    G4D_TIMEOUT_EMPTY = 2,  // producer waited too long for a free stage
+    G4D_BAD_TOKEN = 3,      // token id outside the vocabulary
+    G4D_BAD_SHAPE = 4,
+};
+
+struct DMat {
+    const int8_t *w;     // [N][K]
+    const uint16_t *s;   // [N][K/64] fp16 bits
+    int N, K;
+};
+
+// ---- GEMV (decode, T <= 4 tokens) ------------------------------------------
+enum GemvPro : int {
+    PRO_QUANT = 0,          // x = src
+    PRO_LOADQ = 1,          // xq/xs already quantised in global memory
+    PRO_NORM_QUANT = 2,     // x = rmsnorm(src, w_pre)
+    PRO_RES_NORM_QUANT = 3, // r' = (res_in + rmsnorm(src, w_post)) * scalar; x = rmsnorm(r', w_pre)
+    PRO_RES_QUANT = 4,      // r' = res_in + rmsnorm(src, w_post); x = r'
+    PRO_EMBED_QUANT = 5,    // x = embed(token) * sqrt(1536) (written to res_out); PLE rows gathered
+};
+enum GemvEpi : int {
+    EPI_STORE = 0,      // out[t][n] = acc
+    EPI_GEGLU_PAIR = 1, // interleaved gate/up rows: out[t][n/2] = geglu(gate, up)
+    EPI_PLE = 2,        // out[t][n] = geglu(acc, u[t][n])
+    EPI_LOGITS = 3,     // out[t][n] = 30 tanh(acc/30) and argmax over n
+};
+
+struct GemvArgs {
+    DMat m;
+    int T;
+    int rb;                 // rows per batch (stage = rb rows x kc bytes)
+    int kc;                 // K-chunk bytes per stage
+    int row_gran;           // row split granularity (1 or 2)
+    // prologue
+    const float *src;       // [T][src_stride]
+    int src_stride;
+    const int8_t *xq_in;    // PRO_LOADQ: [T][K]
+    const float *xs_in;     //            [T][K/64]
+    const float *w_post;    // norm weights
+    const float *w_pre;
+    const float *res_in;    // [T][1536]
+    float *res_out;         // written by block 0
+    const float *scalar;    // layer_scalar (device), NULL = 1
+    const int *tokens;      // PRO_EMBED_QUANT
+    DMat embed;             //   token embedding table (row-major)
+    DMat embed_ple;         //   per-layer embedding table
+    float *ple_emb;         //   [T][8960] gathered, x16
+    float embed_mult, ple_mult;
+    float eps;
+    // epilogue
+    float *out;
+    int out_stride;
+    const float *ple_u;     // EPI_PLE: [T][u_stride]
+    int u_stride;
+    const float *gelu;      // 4096-entry table
+    float *argmax_part;     // EPI_LOGITS: [grid][T][2] (value, index as float bits)
+    int *argmax_out;        // [T]
+    unsigned *ticket;
+    int32_t *dots_out;      // optional debug: int32 per (t, n, g)
+    int *err;
+};
+
+// ---- GEMM (prefill, T > 4) -------------------------------------------------
+struct GemmArgs {
+    DMat m;
+    int T;
+    const int8_t *xq;       // [T][K]
+    const float *xs;        // [T][K/64]
+    int epi;                // GemvEpi subset: STORE, GEGLU_PAIR, PLE
+    float *out;
+    int out_stride;
+    const float *ple_u;
+    int u_stride;
+    const float *gelu;
+    int32_t *dots_out;      // optional debug
+    int *err;
+};
+
+// ---- attention ---------------------------------------------------------------
+struct AttnArgs {
+    int hd;                 // 256 or 512
+    int pairs;              // rotated pairs (128 sliding, 64 global)
+    int window;             // 512 for sliding layers, 0 = global
+    int mask;               // ring slots - 1
+    int T;                  // tokens in the chunk
+    int start_pos;          // host-side start (prefill) ...
+    const int *pos_dev;     // ... or device-side position (decode graphs); used when non-NULL
+    float *qkv;             // [T][qkv_stride]: q (heads*hd) [| k hd | v hd]
+    int qkv_stride;
+    int has_kv;             // this layer owns (writes) the cache
+    const float *q_norm, *k_norm;
+    const float *rope_cos, *rope_sin;   // [131072][pairs]
+    float *kcache, *vcache;             // [ring][hd]
+    float *part;            // decode split partials [splits][8][hd + 4]: m, l, pad, pad, o[hd]
+    float *out;             // [T][8*hd]
+    int8_t *xq;             // decode combine: quantised output [8*hd]
+    float *xs;
+    int *err;
+};
+
+// ---- launchers (g4_*.cu) ---------------------------------------------------
+int g4_gemv_smem_bytes(const GemvArgs &a, int stages);
+void g4_gemv_plan(GemvArgs &a, int num_sms);
+cudaError_t g4_launch_gemv(const GemvArgs &a, int pro, int epi, int grid, cudaStream_t st, bool pdl);
+cudaError_t g4_launch_gemm(const GemmArgs &a, cudaStream_t st, bool pdl);
+cudaError_t g4_launch_attn_decode(const AttnArgs &a, int splits, cudaStream_t st, bool pdl);
+cudaError_t g4_launch_attn_combine(const AttnArgs &a, int splits, cudaStream_t st, bool pdl);
+cudaError_t g4_launch_qkv_post(const AttnArgs &a, cudaStream_t st, bool pdl);
+cudaError_t g4_launch_attn_prefill(const AttnArgs &a, cudaStream_t st, bool pdl);
+
+cudaError_t g4_launch_repack(const int8_t *packed_w, const uint16_t *packed_s, int N, int K, int8_t *w, uint16_t *s,
+                             int row_offset, int row_stride_mul, cudaStream_t st);
+cudaError_t g4_launch_rows_embed(const int *tokens, int T, DMat embed, DMat embed_ple, float mult, float ple_mult,
+                                 float *res, float *ple_emb, int *err, cudaStream_t st, bool pdl);
+cudaError_t g4_launch_rows_quant(const float *src, int src_stride, int T, int K, int8_t *xq, float *xs,
+                                 cudaStream_t st, bool pdl);
+// mode: 0 = norm+quant, 1 = res+norm+quant, 2 = res+quant, 3 = res finish (no quant)
+cudaError_t g4_launch_rows_norm(int mode, const float *src, int T, const float *w_post, const float *res_in,
+                                float *res_out, const float *scalar, const float *w_pre, float eps, int8_t *xq,
+                                float *xs, cudaStream_t st, bool pdl, float *y_out = nullptr);
+cudaError_t g4_launch_ple_prep(const float *pli, const float *ple_emb, const float *w, float eps, float scale, int T,
+                               float *u, cudaStream_t st, bool pdl);
+
+// Launch with (optional) programmatic dependent launch.
+template <typename... Args>
+cudaError_t g4_launch(void (*kern)(Args...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, bool pdl,
+                      Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}

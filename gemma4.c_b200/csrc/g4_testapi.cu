@@ -1,0 +1,215 @@
+// g4_testapi.cu — single-kernel C entry points (host buffers in and out) and
+// the logits top-k kernel.
+//
+// The g4k_* functions let parity tests drive one kernel at a time through the
+// C ABI on seeded inputs; each call allocates and frees its own device
+// buffers, so they are for testing, not for the hot path.
+#include <cuda_runtime.h>
+#include <math.h>
+
+#include <vector>
+
+#include "../../include/g4cuda.h"
+#include "g4_common.cuh"
+#include "g4_internal.h"
+
+cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl);
+cudaError_t g4_launch_gemm_simt(const GemmArgs &a, cudaStream_t st, bool pdl);
+bool g4_gemm_tc_supported(const GemmArgs &a);
+
+namespace {
+
+// Top-k in two passes: each CTA selects the k best of its slice (value
+// descending, id ascending on ties, gemma4.c:544-551), then one CTA merges.
+constexpr int kTopkThreads = 256;
+constexpr int kTopkSlice = 4096;
+
+__device__ void block_best(float v, int i, float *rv, int *ri, float *outv, int *outi) {
+    // reduce (v desc, i asc) over the block
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+        int i2 = __shfl_xor_sync(0xffffffffu, i, o);
+        if (v2 > v || (v2 == v && i2 < i)) { v = v2; i = i2; }
+    }
+    if (lane == 0) { rv[warp] = v; ri[warp] = i; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float bv = rv[0];
+        int bi = ri[0];
+        for (int w = 1; w < kTopkThreads / 32; w++)
+            if (rv[w] > bv || (rv[w] == bv && ri[w] < bi)) { bv = rv[w]; bi = ri[w]; }
+        *outv = bv;
+        *outi = bi;
+    }
+    __syncthreads();
+}
+
+// SLICE values per CTA; ids are explicit (xi) or the global index.
+template <int SLICE>
+__global__ void __launch_bounds__(kTopkThreads) k_topk_pass(const float *x, const int *xi, int n, int k, float *ov,
+                                                            int *oi) {
+    __shared__ float sv[SLICE];
+    __shared__ int si[SLICE];
+    __shared__ float rv[8];
+    __shared__ int ri[8];
+    __shared__ float bv;
+    __shared__ int bi;
+    const int base = blockIdx.x * SLICE;
+    for (int j = threadIdx.x; j < SLICE; j += kTopkThreads) {
+        const int g = base + j;
+        sv[j] = g < n ? x[g] : -INFINITY;
+        si[j] = g < n ? (xi ? xi[g] : g) : 0x7fffffff;
+    }
+    __syncthreads();
+    for (int r = 0; r < k; r++) {
+        float v = -INFINITY;
+        int i = 0x7fffffff, pos = -1;
+        for (int j = threadIdx.x; j < SLICE; j += kTopkThreads)
+            if (sv[j] > v || (sv[j] == v && si[j] < i)) { v = sv[j]; i = si[j]; pos = j; }
+        block_best(v, i, rv, ri, &bv, &bi);
+        if (pos >= 0 && i == bi) { sv[pos] = -INFINITY; si[pos] = 0x7fffffff; }
+        if (threadIdx.x == 0) {
+            ov[blockIdx.x * k + r] = bv;
+            oi[blockIdx.x * k + r] = bi;
+        }
+        __syncthreads();
+    }
+}
+
+struct DevBuf {
+    void *p = nullptr;
+    ~DevBuf() { if (p) cudaFree(p); }
+    cudaError_t alloc(size_t n) { return cudaMalloc(&p, n ? n : 16); }
+};
+
+#define TK(call)                                        \
+    do {                                                \
+        cudaError_t e_ = (call);                        \
+        if (e_ != cudaSuccess) return G4_ERR_CUDA;      \
+    } while (0)
+
+int num_sms() {
+    int dev = 0, n = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
+
+}  // namespace
+
+cudaError_t g4_launch_topk(const float *x, int n, int k, float *part_v, int *part_i, float *vals, int *ids,
+                           cudaStream_t st) {
+    // pass 1: 4096-value slices (64 CTAs for the vocabulary); pass 2: one CTA
+    // over the <= 64 x k candidates
+    constexpr int kSlice1 = 4096;
+    const int blocks = (n + kSlice1 - 1) / kSlice1;
+    const int m = blocks * k;
+    if (k < 1 || k > 64 || m > kTopkSlice) return cudaErrorInvalidValue;
+    k_topk_pass<kSlice1><<<blocks, kTopkThreads, 0, st>>>(x, nullptr, n, k, part_v, part_i);
+    k_topk_pass<kTopkSlice><<<1, kTopkThreads, 0, st>>>(part_v, part_i, m, k, vals, ids);
+    return cudaGetLastError();
+}
+
+extern "C" {
+
+int g4k_quantize(const float *x, int rows, int width, int8_t *q, float *s) {
+    if (!x || !q || !s || rows < 1 || width < 64 || width % 64) return G4_ERR_INVALID;
+    DevBuf dx, dq, ds;
+    TK(dx.alloc((size_t)rows * width * 4));
+    TK(dq.alloc((size_t)rows * width));
+    TK(ds.alloc((size_t)rows * width / 64 * 4));
+    TK(cudaMemcpy(dx.p, x, (size_t)rows * width * 4, cudaMemcpyHostToDevice));
+    TK(g4_launch_rows_quant((const float *)dx.p, width, rows, width, (int8_t *)dq.p, (float *)ds.p, 0, false));
+    TK(cudaMemcpy(q, dq.p, (size_t)rows * width, cudaMemcpyDeviceToHost));
+    TK(cudaMemcpy(s, ds.p, (size_t)rows * width / 64 * 4, cudaMemcpyDeviceToHost));
+    return G4_OK;
+}
+
+int g4k_rmsnorm_quant(const float *x, int rows, const float *w, float eps, float *y, int8_t *q, float *s) {
+    if (!x || !w || !q || !s || rows < 1) return G4_ERR_INVALID;
+    const int W = G4_HIDDEN;
+    DevBuf dx, dw, dy, dq, ds;
+    TK(dx.alloc((size_t)rows * W * 4));
+    TK(dw.alloc((size_t)W * 4));
+    TK(dy.alloc((size_t)rows * W * 4));
+    TK(dq.alloc((size_t)rows * W));
+    TK(ds.alloc((size_t)rows * W / 64 * 4));
+    TK(cudaMemcpy(dx.p, x, (size_t)rows * W * 4, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(dw.p, w, (size_t)W * 4, cudaMemcpyHostToDevice));
+    TK(g4_launch_rows_norm(0, (const float *)dx.p, rows, nullptr, nullptr, nullptr, nullptr, (const float *)dw.p, eps,
+                           (int8_t *)dq.p, (float *)ds.p, 0, false, (float *)dy.p));
+    if (y) TK(cudaMemcpy(y, dy.p, (size_t)rows * W * 4, cudaMemcpyDeviceToHost));
+    TK(cudaMemcpy(q, dq.p, (size_t)rows * W, cudaMemcpyDeviceToHost));
+    TK(cudaMemcpy(s, ds.p, (size_t)rows * W / 64 * 4, cudaMemcpyDeviceToHost));
+    return G4_OK;
+}
+
+int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, const int8_t *xq, const float *xs,
+               int T, int path, float *out, int32_t *dots) {
+    if (!w_packed || !s_packed || !xq || !xs || !out || N < 16 || N % 16 || K < 256 || K % 256 || T < 1 ||
+        T > G4_BATCH)
+        return G4_ERR_INVALID;
+    if (path == 0) path = T <= 4 ? 1 : 2;
+    if (path == 1 && T > 4) return G4_ERR_INVALID;
+    const int G = K / 64;
+    DevBuf pw, ps, w, s, dxq, dxs, dout, ddots, derr, dticket;
+    TK(pw.alloc((size_t)N * K));
+    TK(ps.alloc((size_t)N * G * 2));
+    TK(w.alloc((size_t)N * K));
+    TK(s.alloc((size_t)N * G * 2));
+    TK(dxq.alloc((size_t)T * K));
+    TK(dxs.alloc((size_t)T * G * 4));
+    TK(dout.alloc((size_t)T * N * 4));
+    TK(derr.alloc(64));
+    TK(cudaMemset(derr.p, 0, 64));
+    if (dots) TK(ddots.alloc((size_t)T * N * G * 4));
+    TK(cudaMemcpy(pw.p, w_packed, (size_t)N * K, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(ps.p, s_packed, (size_t)N * G * 2, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(dxq.p, xq, (size_t)T * K, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(dxs.p, xs, (size_t)T * G * 4, cudaMemcpyHostToDevice));
+    TK(g4_launch_repack((const int8_t *)pw.p, (const uint16_t *)ps.p, N, K, (int8_t *)w.p, (uint16_t *)s.p, 0, 1, 0));
+    DMat m{(const int8_t *)w.p, (const uint16_t *)s.p, N, K};
+    if (path == 1) {
+        GemvArgs a{};
+        a.m = m;
+        a.T = T;
+        a.xq_in = (const int8_t *)dxq.p;
+        a.xs_in = (const float *)dxs.p;
+        a.out = (float *)dout.p;
+        a.out_stride = N;
+        a.dots_out = (int32_t *)ddots.p;
+        a.err = (int *)derr.p;
+        a.eps = G4_RMS_EPS;
+        g4_gemv_plan(a, num_sms());
+        int units = N / a.row_gran, grid = units < num_sms() ? units : num_sms();
+        TK(g4_launch_gemv(a, PRO_LOADQ, EPI_STORE, grid, 0, false));
+    } else {
+        GemmArgs a{};
+        a.m = m;
+        a.T = T;
+        a.xq = (const int8_t *)dxq.p;
+        a.xs = (const float *)dxs.p;
+        a.epi = EPI_STORE;
+        a.out = (float *)dout.p;
+        a.out_stride = N;
+        a.dots_out = (int32_t *)ddots.p;
+        a.err = (int *)derr.p;
+        if (path == 3) {
+            if (!g4_gemm_tc_supported(a)) return G4_ERR_INVALID;
+            TK(g4_launch_gemm_tc(a, 0, false));
+        } else {
+            TK(g4_launch_gemm_simt(a, 0, false));
+        }
+    }
+    TK(cudaDeviceSynchronize());
+    int err = 0;
+    TK(cudaMemcpy(&err, derr.p, 4, cudaMemcpyDeviceToHost));
+    if (err) return G4_ERR_DEVICE;
+    TK(cudaMemcpy(out, dout.p, (size_t)T * N * 4, cudaMemcpyDeviceToHost));
+    if (dots) TK(cudaMemcpy(dots, ddots.p, (size_t)T * N * G * 4, cudaMemcpyDeviceToHost));
+    return G4_OK;
+}
+
+}  // extern "C"

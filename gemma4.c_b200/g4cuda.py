@@ -1,0 +1,229 @@
+"""Python binding of libg4cuda.so (include/g4cuda.h) via ctypes.
+
+Mirrors the reference's hot-path interface — `forward(tokens, start_pos)` and
+`logits(row)` of gemma4.c:463 and gemma4.c:512 — on a device context, plus the
+single-kernel entry points the parity tests drive. No torch: device memory,
+streams and kernels all live inside the C library.
+
+Importing this module never falls back to a CPU path: if the shared library
+is missing, `load()` raises.
+"""
+import ctypes as C
+import os
+import re
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+LIB_PATH = os.path.join(HERE, "libg4cuda.so")
+HEADER = os.path.join(ROOT, "include", "g4cuda.h")
+
+VOCAB = 262144
+HIDDEN = 1536
+NUM_LAYERS = 35
+MAX_CONTEXT = 131072
+G4_OK = 0
+ERRORS = {-1: "G4_ERR_INVALID", -2: "G4_ERR_FORMAT", -3: "G4_ERR_CUDA", -4: "G4_ERR_NOMEM",
+          -5: "G4_ERR_DEVICE", -6: "G4_ERR_STATE"}
+OPT_GRAPHS, OPT_PDL, OPT_GEMM_PATH = 1, 2, 3
+SYN_GROUP_SCALES, SYN_RANDOM_NORMS = 1, 2
+
+_f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+_i8p = np.ctypeslib.ndpointer(np.int8, flags="C_CONTIGUOUS")
+_i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+_u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+
+
+class G4Error(RuntimeError):
+    def __init__(self, code, msg=""):
+        self.code = code
+        super().__init__(f"{ERRORS.get(code, code)}: {msg}")
+
+
+_lib = None
+
+
+def load(path=LIB_PATH):
+    """Load libg4cuda.so once; raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(path):
+        raise FileNotFoundError(f"{path} not built: run `make -C gemma4.c_b200` or __graft_entry__.build()")
+    L = C.CDLL(path)
+    vp = C.c_void_p
+    L.g4_open.argtypes = [vp, C.c_uint64, C.c_int, C.POINTER(vp)]
+    L.g4_open_file.argtypes = [C.c_char_p, C.c_int, C.POINTER(vp)]
+    L.g4_open_error.restype = C.c_char_p
+    L.g4_close.argtypes = [vp]
+    L.g4_forward.argtypes = [vp, _i32p, C.c_size_t, C.c_int]
+    L.g4_logits.argtypes = [vp, C.c_size_t, vp, vp]
+    L.g4_topk.argtypes = [vp, C.c_size_t, C.c_int, _f32p, _i32p]
+    L.g4_sync.argtypes = [vp]
+    L.g4_last_error.argtypes = [vp]
+    L.g4_last_error.restype = C.c_char_p
+    L.g4_strerror.restype = C.c_char_p
+    L.g4_set_option.argtypes = [vp, C.c_int, C.c_int]
+    L.g4_read_residual.argtypes = [vp, C.c_size_t, _f32p]
+    L.g4_read_cache.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
+    L.g4_stream.argtypes = [vp]
+    L.g4_stream.restype = vp
+    L.g4_device_bytes.argtypes = [vp, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
+    L.g4synth_image_bytes.restype = C.c_uint64
+    L.g4synth_fill.argtypes = [vp, C.c_uint64, C.c_uint64, C.c_uint]
+    L.g4synth_write_file.argtypes = [C.c_char_p, C.c_uint64, C.c_uint]
+    L.g4k_quantize.argtypes = [_f32p, C.c_int, C.c_int, _i8p, _f32p]
+    L.g4k_linear.argtypes = [_i8p, _u16p, C.c_int, C.c_int, _i8p, _f32p, C.c_int, C.c_int, _f32p, vp]
+    L.g4k_rmsnorm_quant.argtypes = [_f32p, C.c_int, _f32p, C.c_float, vp, _i8p, _f32p]
+    _lib = L
+    return L
+
+
+def header_symbols(header=HEADER):
+    """Function names declared in include/g4cuda.h."""
+    text = open(header).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(g4[a-z0-9_]*)\s*\(", text)))
+
+
+def _check(code, ctx=None):
+    if code != G4_OK:
+        L = load()
+        msg = L.g4_last_error(ctx).decode() if ctx else L.g4_strerror(code).decode()
+        raise G4Error(code, msg)
+
+
+# ---------------------------------------------------------------------------
+# synthetic model images
+
+def aligned_empty(nbytes, align=4096):
+    """Page-aligned uint8 buffer (the reference's AVX-512 path needs 64-byte
+    aligned tensors, which a mapped file gives and a plain numpy array may not)."""
+    raw = np.empty(nbytes + align, np.uint8)
+    off = (-raw.ctypes.data) % align
+    return raw[off:off + nbytes]
+
+
+def synth_image(seed=0, flags=0):
+    """A seeded random-init Gemma 4 E2B image in the gemma4.c .bin layout."""
+    L = load()
+    n = L.g4synth_image_bytes()
+    img = aligned_empty(n)
+    _check(L.g4synth_fill(img.ctypes.data, n, seed, flags))
+    return img
+
+
+# ---------------------------------------------------------------------------
+# the model context
+
+class Model:
+    """A device context: forward/logits exactly as gemma4.c's hot path."""
+
+    def __init__(self, image=None, path=None, device=0):
+        L = self.L = load()
+        h = C.c_void_p()
+        if path is not None:
+            rc = L.g4_open_file(path.encode(), device, C.byref(h))
+        else:
+            rc = L.g4_open(image.ctypes.data, image.nbytes, device, C.byref(h))
+        if rc != G4_OK:
+            raise G4Error(rc, L.g4_open_error().decode())
+        self.h = h
+
+    def set_option(self, option, value):
+        _check(self.L.g4_set_option(self.h, option, int(value)), self.h)
+
+    def forward(self, tokens, start_pos):
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        _check(self.L.g4_forward(self.h, tokens, tokens.size, int(start_pos)), self.h)
+
+    def logits(self, row=0, want_logits=True):
+        out = np.empty(VOCAB, np.float32) if want_logits else None
+        am = C.c_int(-1)
+        _check(self.L.g4_logits(self.h, row, out.ctypes.data if out is not None else None, C.byref(am)), self.h)
+        return out, am.value
+
+    def topk(self, row, k):
+        v = np.empty(k, np.float32)
+        i = np.empty(k, np.int32)
+        _check(self.L.g4_topk(self.h, row, k, v, i), self.h)
+        return v, i
+
+    def sync(self):
+        _check(self.L.g4_sync(self.h), self.h)
+
+    def residual(self, rows):
+        out = np.empty((rows, HIDDEN), np.float32)
+        _check(self.L.g4_read_residual(self.h, rows, out), self.h)
+        return out
+
+    def cache(self, layer, which, slot0, nslots, head_dim):
+        out = np.empty((nslots, head_dim), np.float32)
+        _check(self.L.g4_read_cache(self.h, layer, which, slot0, nslots, out), self.h)
+        return out
+
+    def stream(self):
+        return self.L.g4_stream(self.h)
+
+    def device_bytes(self):
+        w, t = C.c_uint64(), C.c_uint64()
+        _check(self.L.g4_device_bytes(self.h, C.byref(w), C.byref(t)), self.h)
+        return w.value, t.value
+
+    def close(self):
+        if self.h:
+            self.L.g4_close(self.h)
+            self.h = None
+
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        self.close()
+
+
+# ---------------------------------------------------------------------------
+# single-kernel entry points
+
+def pack_matrix(w, s):
+    """Row-major int8 [N][K] + scales [N][K/64] (fp16 bits) -> the .bin packed
+    layout (exporter.py:304-316): [N/16][K/64][16 chunks][16 rows][4]."""
+    N, K = w.shape
+    G = K // 64
+    wp = w.reshape(N // 16, 16, G, 16, 4).transpose(0, 2, 3, 1, 4).reshape(-1)
+    sp = s.reshape(N // 16, 16, G).transpose(0, 2, 1).reshape(-1)
+    return np.ascontiguousarray(wp, np.int8), np.ascontiguousarray(sp, np.uint16)
+
+
+def quantize(x):
+    L = load()
+    x = np.ascontiguousarray(x, np.float32)
+    rows, width = x.shape
+    q = np.empty((rows, width), np.int8)
+    s = np.empty((rows, width // 64), np.float32)
+    _check(L.g4k_quantize(x, rows, width, q, s))
+    return q, s
+
+
+def linear(w_packed, s_packed, N, K, xq, xs, path=0, want_dots=False):
+    L = load()
+    xq = np.ascontiguousarray(xq, np.int8)
+    xs = np.ascontiguousarray(xs, np.float32)
+    T = xq.shape[0]
+    out = np.empty((T, N), np.float32)
+    dots = np.empty((T, N, K // 64), np.int32) if want_dots else None
+    _check(L.g4k_linear(w_packed, s_packed, N, K, xq, xs, T, path, out,
+                        dots.ctypes.data if dots is not None else None))
+    return out, dots
+
+
+def rmsnorm_quant(x, w, eps=1e-6):
+    L = load()
+    x = np.ascontiguousarray(x, np.float32)
+    rows = x.shape[0]
+    y = np.empty_like(x)
+    q = np.empty((rows, HIDDEN), np.int8)
+    s = np.empty((rows, HIDDEN // 64), np.float32)
+    _check(L.g4k_rmsnorm_quant(x, rows, np.ascontiguousarray(w, np.float32), eps, y.ctypes.data, q, s))
+    return y, q, s

@@ -1,0 +1,113 @@
+/*
+ * g4cuda.h — C ABI of libg4cuda.so, the B200 (sm_100a) implementation of
+ * gemma4.c's transformer forward path.
+ *
+ * The library replaces the two hot-path functions a gemma4.c host calls:
+ *
+ *   void   forward(Model*, InferenceState*, const int *tokens, size_t n, int start_pos)
+ *            (gemma4.c:463)  ->  g4_forward
+ *   float *logits(Model*, InferenceState*, size_t token_row)
+ *            (gemma4.c:512)  ->  g4_logits (+ g4_topk for the sampling loop,
+ *                                gemma4.c:536-561)
+ *
+ * The model stays in gemma4.c's .bin layout (exporter.py); g4_open takes the
+ * mapped file (records holding file offsets, or already fixed-up pointers into
+ * the same mapping, gemma4.c:681-685) and builds the device copy and the
+ * device-resident FP32 KV caches, which replace InferenceState.
+ *
+ * Conventions: plain C types only; every function returns G4_OK (0) or a
+ * negative G4_ERR_* code and never aborts. Calls on one context must come from
+ * one host thread at a time. g4_forward is asynchronous (stream ordered);
+ * device-side failures surface at the next synchronising call (g4_logits,
+ * g4_topk, g4_sync, reads).
+ */
+#ifndef G4CUDA_H
+#define G4CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define G4_OK 0
+#define G4_ERR_INVALID (-1)  /* bad argument (null pointer, range, token id) */
+#define G4_ERR_FORMAT (-2)   /* model image rejected (magic, record, shape) */
+#define G4_ERR_CUDA (-3)     /* CUDA runtime error */
+#define G4_ERR_NOMEM (-4)    /* device or pinned allocation failed */
+#define G4_ERR_DEVICE (-5)   /* a kernel reported an error (wait timeout, bad token) */
+#define G4_ERR_STATE (-6)    /* call out of sequence (e.g. logits of a row not computed) */
+
+typedef struct g4_ctx g4_ctx;
+
+/* Upload a model image (the whole .bin mapping, `bytes` long) to `device`.
+ * Replaces main's mmap + pointer fix-up + calloc(InferenceState)
+ * (gemma4.c:673-686). The image is only read during the call. */
+int g4_open(const void *image, uint64_t bytes, int device, g4_ctx **out);
+/* Same, reading the file at `path`. */
+int g4_open_file(const char *path, int device, g4_ctx **out);
+int g4_close(g4_ctx *ctx);
+/* Message for the last failed g4_open / g4_open_file in this process. */
+const char *g4_open_error(void);
+
+/* forward (gemma4.c:463-509): run `count` tokens (1..512, the reference's
+ * BATCH_SIZE) at positions start_pos..start_pos+count-1, updating the KV caches
+ * and the per-row residual stream. Position semantics are the reference's:
+ * chunks must be called in order and start_pos + count <= 131072. */
+int g4_forward(g4_ctx *ctx, const int *tokens, size_t count, int start_pos);
+
+/* logits (gemma4.c:512-522) of residual row `row` (< count of the last
+ * forward): final RMSNorm, int8 lm_head over the tied embedding, 30*tanh(x/30).
+ * `out` (262144 floats, may be NULL) receives the logits and `argmax` (may be
+ * NULL) the greedy token (first maximum, gemma4.c:537-541). Synchronises. */
+int g4_logits(g4_ctx *ctx, size_t row, float *out, int *argmax);
+
+/* Top-k (k <= 64) of the logits of `row`, descending, ties to the lower id:
+ * the candidate list of gemma4.c:544-551. Synchronises. */
+int g4_topk(g4_ctx *ctx, size_t row, int k, float *values, int *ids);
+
+/* Wait for queued work; returns any device-side error. */
+int g4_sync(g4_ctx *ctx);
+
+/* Message for the last error on this context (never NULL). */
+const char *g4_last_error(g4_ctx *ctx);
+const char *g4_strerror(int code);
+
+/* Options (g4_set_option): */
+#define G4_OPT_GRAPHS 1      /* capture single-token decode in a CUDA graph (default 1) */
+#define G4_OPT_PDL 2         /* programmatic dependent launch between kernels (default 1) */
+#define G4_OPT_GEMM_PATH 3   /* prefill GEMM: 0 auto, 1 SIMT dp4a, 2 tcgen05 */
+#define G4_OPT_LAYERS 4      /* run only the first N layers (testing aid; default 35) */
+int g4_set_option(g4_ctx *ctx, int option, int value);
+
+/* ---- introspection (tests, benchmarks) ---- */
+int g4_read_residual(g4_ctx *ctx, size_t rows, float *out);          /* [rows][1536] */
+/* `nslots` ring slots of the K (which=0) or V (which=1) cache `layer` reads. */
+int g4_read_cache(g4_ctx *ctx, int layer, int which, int slot0, int nslots, float *out);
+void *g4_stream(g4_ctx *ctx);                 /* the context's cudaStream_t */
+int g4_device_bytes(g4_ctx *ctx, uint64_t *weights, uint64_t *total);
+
+/* ---- synthetic model images (benchmarks and parity tests) ----
+ * A seeded random-init Gemma 4 E2B in the exact .bin layout gemma4.c reads. */
+uint64_t g4synth_image_bytes(void);
+int g4synth_fill(uint8_t *image, uint64_t bytes, uint64_t seed, unsigned flags);
+int g4synth_write_file(const char *path, uint64_t seed, unsigned flags);
+
+/* ---- single-kernel entry points (host buffers in and out; each call
+ * allocates and frees its own device buffers on the current device) ---- */
+/* quantize (gemma4.c:265-279): x[rows][width] -> q[rows][width], s[rows][width/64] */
+int g4k_quantize(const float *x, int rows, int width, int8_t *q, float *s);
+/* matmul_int8 (gemma4.c:257-262) on a packed matrix (exporter.py:304-316 layout):
+ * out[T][N]; `dots` (may be NULL) receives the int32 of every (t, n, 64-group)
+ * as [T][N][K/64]. path: 0 auto, 1 decode GEMV (T <= 4), 2 SIMT GEMM,
+ * 3 tcgen05 GEMM. */
+int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, const int8_t *xq, const float *xs,
+               int T, int path, float *out, int32_t *dots);
+/* rmsnorm (gemma4.c:360-373) of hidden-width rows followed by quantize */
+int g4k_rmsnorm_quant(const float *x, int rows, const float *w, float eps, float *y, int8_t *q, float *s);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -27,7 +27,8 @@ G4_DEV int first_key(int p, int window) { return (window && p + 1 > window) ? p 
 // RMS-normalise (optional weight) and rotate one head vector held in shared
 // memory by one warp. x has HD floats.
 template <int HD>
-G4_DEV void norm_rope_warp(float *x, const float *w, const float *cosr, const float *sinr, int pairs, bool rope) {
+G4_DEV void norm_rope_warp(float *x, const float *w, const float *cosr, const float *sinr, int pairs, bool rope,
+                           bool strict = false) {
     const int lane = threadIdx.x & 31;
     float v[HD / 32];
     float ss = 0.0f;
@@ -36,7 +37,13 @@ G4_DEV void norm_rope_warp(float *x, const float *w, const float *cosr, const fl
         v[i] = x[lane + 32 * i];
         ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
     }
-    ss = warp_sum(ss);
+    if (strict) {
+        // reference order (gemma4.c:367-368): one lane, index order
+        ss = lane == 0 ? seq_sumsq(x, HD) : 0.0f;
+        ss = __shfl_sync(0xffffffffu, ss, 0);
+    } else {
+        ss = warp_sum(ss);
+    }
     const float inv = rms_inv(ss, (float)HD, 1e-6f);
 #pragma unroll
     for (int i = 0; i < HD / 32; i++) x[lane + 32 * i] = rms_apply(v[i], inv, w ? w[lane + 32 * i] : 1.0f);
@@ -68,7 +75,7 @@ __global__ void __launch_bounds__(32) k_qkv_post(const AttnArgs a) {
     __syncwarp();
     const float *cosr = a.rope_cos + (size_t)p * a.pairs, *sinr = a.rope_sin + (size_t)p * a.pairs;
     const float *w = which < kHeads ? a.q_norm : (which == kHeads ? a.k_norm : nullptr);
-    norm_rope_warp<HD>(x, w, cosr, sinr, a.pairs, which <= kHeads);
+    norm_rope_warp<HD>(x, w, cosr, sinr, a.pairs, which <= kHeads, a.strict != 0);
     float *dst = which < kHeads ? src
                  : which == kHeads ? a.kcache + (size_t)(p & a.mask) * HD
                                    : a.vcache + (size_t)(p & a.mask) * HD;
@@ -79,25 +86,72 @@ __global__ void __launch_bounds__(32) k_qkv_post(const AttnArgs a) {
 // Decode (T = 1) split-KV attention. Every CTA post-processes q (all heads)
 // and, on layers that own the cache, the new k/v; CTA 0 writes k/v to the
 // ring, and every CTA uses its own copy for key == pos. CTA c covers a slice of
-// the visible keys and writes (max, sum, unnormalised output) per head.
+// the visible keys (at least kMinSplit keys per slice) and writes (max, sum,
+// unnormalised output) per head. K/V tiles stream through a double-buffered
+// cp.async pipeline; warp h owns query head h, lanes own keys for the scores
+// and output dimensions for the value sum.
 constexpr int kTile = 32;
+constexpr int kMinSplit = 64;
+
+G4_DEV void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+G4_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+G4_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Key range of split `s` for position p; returns the number of active splits.
+G4_DEV int split_range(int p, int window, int splits, int s, int *k0, int *k1) {
+    const int kf = first_key(p, window), nk = p + 1 - kf;
+    int per = (nk + splits - 1) / splits;
+    per = per < kMinSplit ? kMinSplit : (per + 31) / 32 * 32;
+    *k0 = kf + s * per;
+    *k1 = min(p + 1, *k0 + per);
+    return (nk + per - 1) / per;
+}
 
 template <int HD>
-__global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
+struct DecodeCfg {
+    static constexpr int KT = HD == 512 ? 16 : 32;   // keys per tile
+    static constexpr int LPK = 32 / KT;              // lanes per key in the score phase
+    static constexpr int KS = HD + 4;                // padded K row (floats)
+    static constexpr size_t smem = (size_t)(kHeads * HD + 2 * HD + 2 * KT * KS + 2 * KT * HD) * 4;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a, int splits) {
+    using Cfg = DecodeCfg<HD>;
+    constexpr int KT = Cfg::KT, LPK = Cfg::LPK, KS = Cfg::KS;
     extern __shared__ __align__(16) float sm[];
     float *qn = sm;                       // [8][HD]
     float *kn = qn + kHeads * HD;         // [HD]
     float *vn = kn + HD;                  // [HD]
-    float *Ks = vn + HD;                  // [kTile][HD + 4]
-    float *Vs = Ks + kTile * (HD + 4);    // [kTile][HD]
+    float *Ks = vn + HD;                  // [2][KT][KS]
+    float *Vs = Ks + 2 * KT * KS;         // [2][KT][HD]
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     griddep_launch();
     griddep_wait();
     const int p = a.pos_dev ? *a.pos_dev : a.start_pos;
-    const float *cosr = a.rope_cos + (size_t)p * a.pairs, *sinr = a.rope_sin + (size_t)p * a.pairs;
+    int k0, k1;
+    const int active = split_range(p, a.window, splits, blockIdx.x, &k0, &k1);
+    if ((int)blockIdx.x >= active) return;
 
-    // q heads (warp h) and new k / v
+    // start streaming the first tile before the q/k/v post-processing
+    auto issue = [&](int tile, int buf) {
+        const int kt = k0 + tile * KT, nt = min(KT, k1 - kt);
+        for (int idx = threadIdx.x; idx < nt * (HD / 4); idx += 256) {
+            const int r = idx / (HD / 4), c4 = idx - r * (HD / 4);
+            const size_t slot = (size_t)((kt + r) & a.mask) * HD;
+            cp_async16(&Ks[(buf * KT + r) * KS + c4 * 4], a.kcache + slot + c4 * 4);
+            cp_async16(&Vs[(buf * KT + r) * HD + c4 * 4], a.vcache + slot + c4 * 4);
+        }
+        cp_async_commit();
+    };
+    const int ntiles = k1 > k0 ? (k1 - k0 + KT - 1) / KT : 0;
+    if (ntiles > 0) issue(0, 0);
+
+    const float *cosr = a.rope_cos + (size_t)p * a.pairs, *sinr = a.rope_sin + (size_t)p * a.pairs;
     for (int i = lane; i < HD; i += 32) qn[warp * HD + i] = a.qkv[warp * HD + i];
     __syncwarp();
     norm_rope_warp<HD>(qn + warp * HD, a.q_norm, cosr, sinr, a.pairs, true);
@@ -112,12 +166,8 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
             for (int i = lane; i < HD; i += 32) dst[i] = x[i];
         }
     }
+    if ((int)blockIdx.x >= active) return;   // CTA 0 of an idle split only wrote the cache
     __syncthreads();
-
-    const int k_first = first_key(p, a.window), nk = p + 1 - k_first;
-    int per = (nk + gridDim.x - 1) / gridDim.x;
-    per = (per + kTile - 1) / kTile * kTile;
-    const int k0 = k_first + blockIdx.x * per, k1 = min(p + 1, k0 + per);
 
     constexpr int NV = HD / 128;   // float4 output slices per lane
     float4 o[NV];
@@ -125,47 +175,48 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
     for (int i = 0; i < NV; i++) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     float m = -INFINITY, l = 0.0f;
     const float *q = qn + warp * HD;
+    const int key_lane = lane % KT, dpart = lane / KT;   // score phase: key and dimension part
 
-    for (int kt = k0; kt < k1; kt += kTile) {
-        const int nt = min(kTile, k1 - kt);
-        __syncthreads();
-        for (int idx = threadIdx.x; idx < kTile * (HD / 4); idx += 256) {
-            const int r = idx / (HD / 4), c4 = idx - r * (HD / 4);
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (r < nt) {
-                const int key = kt + r;
-                if (a.has_kv && key == p) {
-                    kv = *(const float4 *)&kn[c4 * 4];
-                    vv = *(const float4 *)&vn[c4 * 4];
-                } else {
-                    const size_t slot = (size_t)(key & a.mask) * HD;
-                    kv = __ldcg((const float4 *)(a.kcache + slot) + c4);
-                    vv = __ldcg((const float4 *)(a.vcache + slot) + c4);
-                }
-            }
-            *(float4 *)&Ks[r * (HD + 4) + c4 * 4] = kv;
-            *(float4 *)&Vs[r * HD + c4 * 4] = vv;
+    for (int t = 0; t < ntiles; t++) {
+        const int buf = t & 1, kt = k0 + t * KT, nt = min(KT, k1 - kt);
+        if (t + 1 < ntiles) {
+            issue(t + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
         __syncthreads();
-        // scores: lane = key
+        float *Kb = Ks + buf * KT * KS, *Vb = Vs + buf * KT * HD;
+        if (a.has_kv && p >= kt && p < kt + nt) {
+            // the new key/value: use this CTA's copy (CTA 0 may still be writing the ring slot)
+            const int r = p - kt;
+            for (int i = threadIdx.x; i < HD; i += 256) {
+                Kb[r * KS + i] = kn[i];
+                Vb[r * HD + i] = vn[i];
+            }
+            __syncthreads();
+        }
+        // scores: LPK lanes per key, each over HD/LPK dimensions
         float s = -INFINITY;
-        if (lane < nt) {
-            const float *kr = Ks + lane * (HD + 4);
+        {
+            const float *kr = Kb + key_lane * KS + dpart * (HD / LPK);
+            const float *qq = q + dpart * (HD / LPK);
             float acc = 0.0f;
 #pragma unroll 8
-            for (int d = 0; d < HD; d += 4) {
-                const float4 qq = *(const float4 *)&q[d], kk = *(const float4 *)&kr[d];
-                acc = fmaf(qq.x, kk.x, acc);
-                acc = fmaf(qq.y, kk.y, acc);
-                acc = fmaf(qq.z, kk.z, acc);
-                acc = fmaf(qq.w, kk.w, acc);
+            for (int d = 0; d < HD / LPK; d += 4) {
+                const float4 a4 = *(const float4 *)&qq[d], k4 = *(const float4 *)&kr[d];
+                acc = fmaf(a4.x, k4.x, acc);
+                acc = fmaf(a4.y, k4.y, acc);
+                acc = fmaf(a4.z, k4.z, acc);
+                acc = fmaf(a4.w, k4.w, acc);
             }
-            s = acc;
+            if (LPK == 2) acc += __shfl_xor_sync(0xffffffffu, acc, 16);
+            if (key_lane < nt) s = acc;
         }
         const float mt = warp_max(s);
         const float mn = fmaxf(m, mt);
         const float corr = (m == -INFINITY) ? 0.0f : expf(m - mn);
-        const float pj = (lane < nt) ? expf(s - mn) : 0.0f;
+        const float pj = (key_lane < nt && dpart == 0) ? expf(s - mn) : 0.0f;
         l = l * corr + warp_sum(pj);
         m = mn;
 #pragma unroll
@@ -174,7 +225,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
         }
         for (int jk = 0; jk < nt; jk++) {
             const float pk = __shfl_sync(0xffffffffu, pj, jk);
-            const float *vr = Vs + jk * HD + 4 * lane;
+            const float *vr = Vb + jk * HD + 4 * lane;
 #pragma unroll
             for (int i = 0; i < NV; i++) {
                 const float4 vv = *(const float4 *)&vr[128 * i];
@@ -184,6 +235,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
                 o[i].w = fmaf(pk, vv.w, o[i].w);
             }
         }
+        __syncthreads();
     }
     float *part = a.part + ((size_t)blockIdx.x * kHeads + warp) * (HD + 4);
     if (lane == 0) {
@@ -194,65 +246,114 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a) {
     for (int i = 0; i < NV; i++) *(float4 *)&part[4 + 4 * lane + 128 * i] = o[i];
 }
 
-// Combine split partials into the attention output and quantise it for
-// o_proj (gemma4.c:459). grid = 8*HD/256 CTAs of 256 threads; thread = one dim.
+// Combine the active split partials into the attention output and quantise it
+// for o_proj (gemma4.c:459). grid = 8*HD/256 CTAs of 256 threads; thread = one
+// output dimension.
 template <int HD>
 __global__ void __launch_bounds__(256) k_attn_combine(const AttnArgs a, int splits) {
-    extern __shared__ float wsm[];   // [splits] weights
+    __shared__ float wsm[256];
     __shared__ float red[8];
     __shared__ float tot;
     griddep_launch();
     griddep_wait();
+    const int p = a.pos_dev ? *a.pos_dev : a.start_pos;
+    int k0, k1;
+    const int active = split_range(p, a.window, splits, 0, &k0, &k1);
     const int per_head = HD / 256;
     const int h = blockIdx.x / per_head, d = (blockIdx.x % per_head) * 256 + threadIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // global max over splits
-    float mx = -INFINITY;
-    for (int s = threadIdx.x; s < splits; s += 256) mx = fmaxf(mx, a.part[((size_t)s * kHeads + h) * (HD + 4)]);
-    mx = warp_max(mx);
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
+    const size_t stride = (size_t)kHeads * (HD + 4);
+    const float *ph = a.part + (size_t)h * (HD + 4);
     if (threadIdx.x == 0) {
-        float v = red[0];
-        for (int i = 1; i < 8; i++) v = fmaxf(v, red[i]);
-        tot = v;
-    }
-    __syncthreads();
-    mx = tot;
-    float lsum = 0.0f;
-    for (int s = threadIdx.x; s < splits; s += 256) {
-        const float *pp = a.part + ((size_t)s * kHeads + h) * (HD + 4);
-        const float w = pp[0] == -INFINITY ? 0.0f : expf(pp[0] - mx);
-        wsm[s] = w;
-        lsum += w * pp[1];
-    }
-    lsum = warp_sum(lsum);
-    __syncthreads();
-    if (lane == 0) red[warp] = lsum;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float v = 0.0f;
-        for (int i = 0; i < 8; i++) v += red[i];
-        tot = v;
+        float mx = -INFINITY;
+        for (int s = 0; s < active; s++) mx = fmaxf(mx, ph[s * stride]);
+        float lsum = 0.0f;
+        for (int s = 0; s < active; s++) {
+            const float w = ph[s * stride] == -INFINITY ? 0.0f : expf(ph[s * stride] - mx);
+            wsm[s] = w;
+            lsum += w * ph[s * stride + 1];
+        }
+        tot = lsum;
     }
     __syncthreads();
     float o = 0.0f;
-    for (int s = 0; s < splits; s++) {
-        const float w = wsm[s];
-        if (w != 0.0f) o = fmaf(w, a.part[((size_t)s * kHeads + h) * (HD + 4) + 4 + d], o);
-    }
+    for (int s = 0; s < active; s++) o = fmaf(wsm[s], ph[s * stride + 4 + d], o);
     o = o / tot;
     const int col = h * HD + d;
     a.out[col] = o;
     // dynamic int8 quantisation of the 64-wide group this thread belongs to
     float amax = warp_max(fabsf(o));
-    __syncthreads();
     if (lane == 0) red[warp] = amax;
     __syncthreads();
     amax = fmaxf(red[warp & ~1], red[warp | 1]);
     const float sc = quant_scale(amax), inv = quant_inv(sc);
     a.xq[col] = (int8_t)quant_one(o, inv);
     if ((threadIdx.x & 63) == 0) a.xs[col >> 6] = sc;
+}
+
+// ---------------------------------------------------------------------------
+// Strict attention: the reference's exact floating-point order for one
+// (token, head) per CTA (gemma4.c:445-456): scores with its 16-lane FMA
+// pattern and reduction tree (attention_scores, :281-294), the sequential
+// running-max softmax with the host library's expf (:400-408), then every
+// output dimension as an FMA chain over the keys in order (weighted_value_sum,
+// :296-307). q must be post-processed (k_qkv_post, strict) and the chunk's
+// keys already in the ring. Used to demonstrate whole-model parity, not speed.
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_strict(const AttnArgs a) {
+    __shared__ float q[HD];
+    __shared__ float stat[2];
+    griddep_launch();
+    griddep_wait();
+    const int t = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+    const int p = (a.pos_dev ? *a.pos_dev : a.start_pos) + t;
+    const int first = first_key(p, a.window), n = p + 1 - first;
+    for (int i = tid; i < HD; i += 256) q[i] = a.qkv[(size_t)t * a.qkv_stride + h * HD + i];
+    __syncthreads();
+    float *sc = a.scores + ((size_t)t * kHeads + h) * a.score_stride;
+    for (int i = tid; i < n; i += 256) {
+        const float *k = a.kcache + (size_t)((first + i) & a.mask) * HD;
+        float s0[8], s1[8];
+#pragma unroll
+        for (int l = 0; l < 8; l++) { s0[l] = 0.0f; s1[l] = 0.0f; }
+        for (int j = 0; j < HD; j += 16) {
+#pragma unroll
+            for (int l = 0; l < 8; l++) {
+                s0[l] = __fmaf_rn(q[j + l], k[j + l], s0[l]);
+                s1[l] = __fmaf_rn(q[j + 8 + l], k[j + 8 + l], s1[l]);
+            }
+        }
+        float s8[8], s4[4];
+#pragma unroll
+        for (int l = 0; l < 8; l++) s8[l] = __fadd_rn(s0[l], s1[l]);
+#pragma unroll
+        for (int l = 0; l < 4; l++) s4[l] = __fadd_rn(s8[l], s8[l + 4]);
+        sc[i] = __fadd_rn(__fadd_rn(s4[0], s4[2]), __fadd_rn(s4[1], s4[3]));
+    }
+    __syncthreads();
+    if (tid == 0) {
+        float mx = sc[0], sum = 1.0f;
+        for (int i = 1; i < n; i++) {
+            const float v = sc[i];
+            if (v > mx) {
+                sum = __fadd_rn(__fmul_rn(sum, expf_host(__fsub_rn(mx, v))), 1.0f);
+                mx = v;
+            } else {
+                sum = __fadd_rn(sum, expf_host(__fsub_rn(v, mx)));
+            }
+        }
+        stat[0] = mx;
+        stat[1] = sum;
+    }
+    __syncthreads();
+    const float mx = stat[0], sum = stat[1];
+    for (int i = tid; i < n; i += 256) sc[i] = __fdiv_rn(expf_host(__fsub_rn(sc[i], mx)), sum);
+    __syncthreads();
+    for (int d = tid; d < HD; d += 256) {
+        float acc = 0.0f;
+        for (int i = 0; i < n; i++) acc = __fmaf_rn(sc[i], a.vcache[(size_t)((first + i) & a.mask) * HD + d], acc);
+        a.out[(size_t)t * (kHeads * HD) + h * HD + d] = acc;
+    }
 }
 
 // ---------------------------------------------------------------------------
@@ -315,17 +416,14 @@ __global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
     for (int kt = k_lo; kt <= k_hi; kt += kTile) {
         const int nt = min(kTile, k_hi + 1 - kt);
         __syncthreads();
-        for (int idx = tid; idx < kTile * (HD / 4); idx += 256) {
+        for (int idx = tid; idx < nt * (HD / 4); idx += 256) {
             const int r = idx / (HD / 4), c4 = idx - r * (HD / 4);
-            float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), vv = kv;
-            if (r < nt) {
-                const size_t slot = (size_t)((kt + r) & a.mask) * HD;
-                kv = __ldcg((const float4 *)(a.kcache + slot) + c4);
-                vv = __ldcg((const float4 *)(a.vcache + slot) + c4);
-            }
-            *(float4 *)&Ks[r * (HD + 4) + c4 * 4] = kv;
-            *(float4 *)&Vs[r * HD + c4 * 4] = vv;
+            const size_t slot = (size_t)((kt + r) & a.mask) * HD;
+            cp_async16(&Ks[r * (HD + 4) + c4 * 4], a.kcache + slot + c4 * 4);
+            cp_async16(&Vs[r * HD + c4 * 4], a.vcache + slot + c4 * 4);
         }
+        cp_async_commit();
+        cp_async_wait<0>();
         __syncthreads();
         // scores
         float s[2][2];
@@ -423,7 +521,6 @@ cudaError_t set_smem(K kern, size_t bytes) {
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
-size_t decode_smem(int hd) { return (size_t)(kHeads * hd + 2 * hd + kTile * (hd + 4) + kTile * hd) * 4; }
 size_t prefill_smem(int hd) { return (size_t)(kRows * hd + kTile * (hd + 4) + kTile * hd + kRows * 33 + 3 * kRows) * 4; }
 
 }  // namespace
@@ -436,25 +533,35 @@ cudaError_t g4_launch_qkv_post(const AttnArgs &a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t g4_launch_attn_decode(const AttnArgs &a, int splits, cudaStream_t st, bool pdl) {
-    const size_t smem = decode_smem(a.hd);
+    if (splits < 1 || splits > 256) return cudaErrorInvalidValue;
     if (a.hd == 256) {
+        const size_t smem = DecodeCfg<256>::smem;
         static bool once = false;
         if (!once) { cudaError_t e = set_smem(k_attn_decode<256>, smem); if (e) return e; once = true; }
-        return g4_launch(k_attn_decode<256>, dim3(splits), dim3(256), smem, st, pdl, a);
+        return g4_launch(k_attn_decode<256>, dim3(splits), dim3(256), smem, st, pdl, a, splits);
     }
     if (a.hd == 512) {
+        const size_t smem = DecodeCfg<512>::smem;
         static bool once = false;
         if (!once) { cudaError_t e = set_smem(k_attn_decode<512>, smem); if (e) return e; once = true; }
-        return g4_launch(k_attn_decode<512>, dim3(splits), dim3(256), smem, st, pdl, a);
+        return g4_launch(k_attn_decode<512>, dim3(splits), dim3(256), smem, st, pdl, a, splits);
     }
     return cudaErrorInvalidValue;
 }
 
 cudaError_t g4_launch_attn_combine(const AttnArgs &a, int splits, cudaStream_t st, bool pdl) {
-    const size_t smem = (size_t)splits * 4;
+    if (splits < 1 || splits > 256) return cudaErrorInvalidValue;
     const int grid = kHeads * a.hd / 256;
-    if (a.hd == 256) return g4_launch(k_attn_combine<256>, dim3(grid), dim3(256), smem, st, pdl, a, splits);
-    if (a.hd == 512) return g4_launch(k_attn_combine<512>, dim3(grid), dim3(256), smem, st, pdl, a, splits);
+    if (a.hd == 256) return g4_launch(k_attn_combine<256>, dim3(grid), dim3(256), 0, st, pdl, a, splits);
+    if (a.hd == 512) return g4_launch(k_attn_combine<512>, dim3(grid), dim3(256), 0, st, pdl, a, splits);
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t g4_launch_attn_strict(const AttnArgs &a, cudaStream_t st, bool pdl) {
+    if (!a.scores) return cudaErrorInvalidValue;
+    dim3 grid(a.T, kHeads);
+    if (a.hd == 256) return g4_launch(k_attn_strict<256>, grid, dim3(256), 0, st, pdl, a);
+    if (a.hd == 512) return g4_launch(k_attn_strict<512>, grid, dim3(256), 0, st, pdl, a);
     return cudaErrorInvalidValue;
 }
 

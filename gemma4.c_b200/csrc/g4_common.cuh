@@ -132,6 +132,64 @@ G4_DEV float geglu_one(float x, float up, const float *__restrict__ table, int s
     return __fmul_rn(x, up);
 }
 
+// ---- strict (reference-order) arithmetic ----------------------------------
+// The reference sums squares sequentially (gemma4.c:367-368: product rounded,
+// then added). Strict mode reproduces that order with one thread.
+G4_DEV float seq_sumsq(const float *x, int n) {
+    float ss = 0.0f;
+    for (int i = 0; i < n; i++) ss = __fadd_rn(ss, __fmul_rn(x[i], x[i]));
+    return ss;
+}
+
+// expf with the results of the host C library the reference links (glibc
+// 2.39): the published table-driven method (x * 32/ln2 split into k + r,
+// 2^(k/32) from a 32-entry table of doubles, degree-3 polynomial in r, one
+// rounding to float), evaluated in IEEE double with no contraction. Checked
+// exhaustively against the host expf over every float in [-104, 88.7]; the two
+// inputs where the host returns the other neighbour of the exact value are
+// listed explicitly.
+__device__ __constant__ uint64_t g4_exp2_tab[32] = {
+    0x3ff0000000000000ull, 0x3fefd9b0d3158574ull, 0x3fefb5586cf9890full, 0x3fef9301d0125b51ull,
+    0x3fef72b83c7d517bull, 0x3fef54873168b9aaull, 0x3fef387a6e756238ull, 0x3fef1e9df51fdee1ull,
+    0x3fef06fe0a31b715ull, 0x3feef1a7373aa9cbull, 0x3feedea64c123422ull, 0x3feece086061892dull,
+    0x3feebfdad5362a27ull, 0x3feeb42b569d4f82ull, 0x3feeab07dd485429ull, 0x3feea47eb03a5585ull,
+    0x3feea09e667f3bcdull, 0x3fee9f75e8ec5f74ull, 0x3feea11473eb0187ull, 0x3feea589994cce13ull,
+    0x3feeace5422aa0dbull, 0x3feeb737b0cdc5e5ull, 0x3feec49182a3f090ull, 0x3feed503b23e255dull,
+    0x3feee89f995ad3adull, 0x3feeff76f2fb5e47ull, 0x3fef199bdd85529cull, 0x3fef3720dcef9069ull,
+    0x3fef5818dcfba487ull, 0x3fef7c97337b9b5full, 0x3fefa4afa2a490daull, 0x3fefd0765b6e4540ull,
+};
+
+G4_DEV float expf_host(float x) {
+    const uint32_t ux = __float_as_uint(x);
+    const uint32_t abstop = (ux >> 20) & 0x7ffu;
+    if (abstop >= 0x42bu) {                                   // |x| >= 88 or not finite
+        if (ux == 0xff800000u) return 0.0f;                   // -inf
+        if (abstop >= 0x7f8u) return x + x;                   // nan, +inf
+        if (x > 0x1.62e42ep6f) return __int_as_float(0x7f800000);   // overflow
+        if (x < -0x1.9fe368p6f) return 0.0f;                  // underflow
+    }
+    if (ux == 0xc27c65d9u) return 0x1.f45326p-92f;             // x = -0x1.f8cbb2p+5
+    if (ux == 0x4202422fu) return 0x1.f93e38p+46f;             // x =  0x1.04845ep+5
+    const double inv_ln2_n = 0x1.71547652b82fep+0 * 32.0;
+    const double shift = 0x1.8p+52;
+    const double c0 = 0x1.c6af84b912394p-5 / 32.0 / 32.0 / 32.0;
+    const double c1 = 0x1.ebfce50fac4f3p-3 / 32.0 / 32.0;
+    const double c2 = 0x1.62e42ff0c52d6p-1 / 32.0;
+    const double z = __dmul_rn(inv_ln2_n, (double)x);
+    double kd = __dadd_rn(z, shift);
+    const uint64_t ki = (uint64_t)__double_as_longlong(kd);
+    kd = __dsub_rn(kd, shift);
+    const double r = __dsub_rn(z, kd);
+    const uint64_t t = g4_exp2_tab[ki & 31u] + (ki << 47);
+    const double s = __longlong_as_double((long long)t);
+    const double zz = __dadd_rn(__dmul_rn(c0, r), c1);
+    const double r2 = __dmul_rn(r, r);
+    double y = __dadd_rn(__dmul_rn(c2, r), 1.0);
+    y = __dadd_rn(__dmul_rn(zz, r2), y);
+    y = __dmul_rn(y, s);
+    return __double2float_rn(y);
+}
+
 // ---- reductions -----------------------------------------------------------
 G4_DEV float warp_sum(float v) {
 #pragma unroll

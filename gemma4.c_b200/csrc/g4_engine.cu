@@ -12,6 +12,7 @@
 //     each GEMV stream its weights while its predecessor drains.
 //   - T = 2..4: same GEMVs, attention through the chunk kernels.
 //   - T > 4 (prefill chunks): row kernels + GEMM + chunk attention.
+#include <cuda_profiler_api.h>
 #include <cuda_runtime.h>
 #include <stdarg.h>
 #include <stdio.h>
@@ -75,6 +76,9 @@ struct g4_ctx {
     bool use_graph = true, use_pdl = true;
     int gemm_path = 0;
     int layers = G4_NUM_LAYERS;   // layers to run (testing aid)
+    bool strict = false;          // reference-order reductions (bit-exact forward)
+    float *scores = nullptr;      // strict attention scratch
+    size_t scores_cap = 0;
     cudaGraphExec_t g_decode = nullptr;
     int graph_cur = 0;
     bool decode_warm = false;
@@ -410,14 +414,15 @@ GemvArgs gemv_base(g4_ctx *c, const DMat &m, int T) {
     a.eps = G4_RMS_EPS;
     a.gelu = c->gelu;
     a.err = c->err;
+    a.strict = c->strict;
     g4_gemv_plan(a, c->num_sms);
     return a;
 }
 
 void gemv(Seq &q, GemvArgs &a, int pro, int epi) {
-    g4_gemv_plan(a, q.c->num_sms);
-    int units = a.m.N / a.row_gran;
-    int grid = units < q.c->num_sms ? units : q.c->num_sms;
+    const int pairs = a.m.N / 2;
+    const int grid = pairs < q.c->num_sms ? pairs : q.c->num_sms;
+    g4_gemv_plan(a, grid);
     q.ck(g4_launch_gemv(a, pro, epi, grid, q.c->st, q.pdl));
 }
 
@@ -464,6 +469,9 @@ AttnArgs attn_base(g4_ctx *c, const Layer &Y, int T, int start_pos, const int *p
     a.xq = c->xq;
     a.xs = c->xs;
     a.err = c->err;
+    a.strict = c->strict;
+    a.scores = c->scores;
+    a.score_stride = start_pos + T;
     return a;
 }
 
@@ -486,7 +494,7 @@ cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev) {
         a.out_stride = G4_NUM_LAYERS * G4_PLE;
         gemv(q, a, PRO_EMBED_QUANT, EPI_STORE);
         q.ck(g4_launch_ple_prep(c->pli, c->ple_emb, c->ple_norm, 1e-6f * G4_HIDDEN, 1.0f / sqrtf(2.0f), T, c->ple_u,
-                                c->st, q.pdl));
+                                c->st, q.pdl, c->strict));
     }
     for (int l = 0; l < c->layers; l++) {
         const Layer &Y = c->L[l];
@@ -514,19 +522,20 @@ cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev) {
         }
         // attention
         AttnArgs at = attn_base(c, Y, T, start_pos, pos_dev);
-        if (T == 1) {
+        const bool fused_decode = T == 1 && !c->strict;
+        if (fused_decode) {
             q.ck(g4_launch_attn_decode(at, kSplits, c->st, q.pdl));
             q.ck(g4_launch_attn_combine(at, kSplits, c->st, q.pdl));
         } else {
             q.ck(g4_launch_qkv_post(at, c->st, q.pdl));
-            q.ck(g4_launch_attn_prefill(at, c->st, q.pdl));
+            q.ck(c->strict ? g4_launch_attn_strict(at, c->st, q.pdl) : g4_launch_attn_prefill(at, c->st, q.pdl));
         }
         // o_proj
         {
             GemvArgs a = gemv_base(c, Y.o, T);
             a.out = c->h;
             a.out_stride = G4_HIDDEN;
-            if (T == 1) {
+            if (fused_decode) {
                 a.xq_in = c->xq;
                 a.xs_in = c->xs;
                 gemv(q, a, PRO_LOADQ, EPI_STORE);
@@ -587,7 +596,7 @@ cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev) {
     }
     const Layer &Z = c->L[c->layers - 1];
     q.ck(g4_launch_rows_norm(3, c->h, T, Z.post_ple, c->res[cur], c->res[cur ^ 1], Z.scalar, nullptr, G4_RMS_EPS,
-                             nullptr, nullptr, c->st, q.pdl));
+                             nullptr, nullptr, c->st, q.pdl, nullptr, c->strict));
     cur ^= 1;
     c->cur = cur;
     return q.e;
@@ -601,32 +610,32 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos) {
     q.ck(g4_launch_rows_quant(c->res[0], G4_HIDDEN, T, G4_HIDDEN, c->xq, c->xs, c->st, q.pdl));
     gemm(q, c->pmp, T, EPI_STORE, c->pli, G4_NUM_LAYERS * G4_PLE, nullptr, 0);
     q.ck(g4_launch_ple_prep(c->pli, c->ple_emb, c->ple_norm, 1e-6f * G4_HIDDEN, 1.0f / sqrtf(2.0f), T, c->ple_u, c->st,
-                            q.pdl));
+                            q.pdl, c->strict));
     for (int l = 0; l < c->layers; l++) {
         const Layer &Y = c->L[l];
         if (l == 0) {
             q.ck(g4_launch_rows_norm(0, c->res[cur], T, nullptr, nullptr, nullptr, nullptr, Y.in_norm, G4_RMS_EPS, c->xq,
-                                     c->xs, c->st, q.pdl));
+                                     c->xs, c->st, q.pdl, nullptr, c->strict));
         } else {
             const Layer &P = c->L[l - 1];
             q.ck(g4_launch_rows_norm(1, c->h, T, P.post_ple, c->res[cur], c->res[cur ^ 1], P.scalar, Y.in_norm,
-                                     G4_RMS_EPS, c->xq, c->xs, c->st, q.pdl));
+                                     G4_RMS_EPS, c->xq, c->xs, c->st, q.pdl, nullptr, c->strict));
             cur ^= 1;
         }
         gemm(q, Y.qkv, T, EPI_STORE, c->qkv, kQkvStride, nullptr, 0);
         AttnArgs at = attn_base(c, Y, T, start_pos, nullptr);
         q.ck(g4_launch_qkv_post(at, c->st, q.pdl));
-        q.ck(g4_launch_attn_prefill(at, c->st, q.pdl));
+        q.ck(c->strict ? g4_launch_attn_strict(at, c->st, q.pdl) : g4_launch_attn_prefill(at, c->st, q.pdl));
         q.ck(g4_launch_rows_quant(c->attn, Y.qw, T, Y.qw, c->xq, c->xs, c->st, q.pdl));
         gemm(q, Y.o, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
         q.ck(g4_launch_rows_norm(1, c->h, T, Y.post_attn, c->res[cur], c->res[cur ^ 1], nullptr, Y.pre_ffn, G4_RMS_EPS,
-                                 c->xq, c->xs, c->st, q.pdl));
+                                 c->xq, c->xs, c->st, q.pdl, nullptr, c->strict));
         cur ^= 1;
         gemm(q, Y.gu, T, EPI_GEGLU_PAIR, c->gu, Y.ffn, nullptr, 0);
         q.ck(g4_launch_rows_quant(c->gu, Y.ffn, T, Y.ffn, c->xq, c->xs, c->st, q.pdl));
         gemm(q, Y.down, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
         q.ck(g4_launch_rows_norm(2, c->h, T, Y.post_ffn, c->res[cur], c->res[cur ^ 1], nullptr, nullptr, G4_RMS_EPS,
-                                 c->xq, c->xs, c->st, q.pdl));
+                                 c->xq, c->xs, c->st, q.pdl, nullptr, c->strict));
         cur ^= 1;
         gemm(q, Y.pleg, T, EPI_PLE, c->pg, G4_PLE, c->ple_u + l * G4_PLE, G4_NUM_LAYERS * G4_PLE);
         q.ck(g4_launch_rows_quant(c->pg, G4_PLE, T, G4_PLE, c->xq, c->xs, c->st, q.pdl));
@@ -634,7 +643,7 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos) {
     }
     const Layer &Z = c->L[c->layers - 1];
     q.ck(g4_launch_rows_norm(3, c->h, T, Z.post_ple, c->res[cur], c->res[cur ^ 1], Z.scalar, nullptr, G4_RMS_EPS,
-                             nullptr, nullptr, c->st, q.pdl));
+                             nullptr, nullptr, c->st, q.pdl, nullptr, c->strict));
     cur ^= 1;
     c->cur = cur;
     return q.e;
@@ -648,10 +657,12 @@ int check_device_error(g4_ctx *c) {
     if (e) {
         cudaMemsetAsync(c->err, 0, 4, c->st);
         cudaStreamSynchronize(c->st);
-        const char *what = e == G4D_BAD_TOKEN ? "token id outside the vocabulary"
-                           : e == G4D_TIMEOUT_FULL || e == G4D_TIMEOUT_EMPTY ? "kernel wait timed out"
-                                                                              : "kernel error";
-        return fail(c, G4_ERR_DEVICE, "device reported error %d: %s", e, what);
+        const int code = e & 0xff;
+        const char *what = code == G4D_BAD_TOKEN ? "token id outside the vocabulary"
+                           : code == G4D_TIMEOUT_FULL || code == G4D_TIMEOUT_EMPTY ? "kernel wait timed out"
+                                                                                    : "kernel error";
+        return fail(c, G4_ERR_DEVICE, "device reported error %d (stage %d, block %d): %s", code, (e >> 8) & 0xfff,
+                    (unsigned)e >> 20, what);
     }
     return G4_OK;
 }
@@ -721,6 +732,7 @@ int g4_close(g4_ctx *c) {
     if (c->arena) cudaFree(c->arena);
     if (c->state) cudaFree(c->state);
     if (c->kv) cudaFree(c->kv);
+    if (c->scores) cudaFree(c->scores);
     if (c->st) cudaStreamDestroy(c->st);
     delete c;
     return G4_OK;
@@ -735,6 +747,7 @@ int g4_set_option(g4_ctx *c, int option, int value) {
         if (c->g_decode) { cudaGraphExecDestroy(c->g_decode); c->g_decode = nullptr; }
         break;
     case G4_OPT_GEMM_PATH: c->gemm_path = value; break;
+    case G4_OPT_STRICT: c->strict = value != 0; break;
     case G4_OPT_LAYERS:
         if (value < 1 || value > G4_NUM_LAYERS) return fail(c, G4_ERR_INVALID, "layers %d out of range", value);
         c->layers = value;
@@ -754,9 +767,20 @@ int g4_forward(g4_ctx *c, const int *tokens, size_t count, int start_pos) {
         if (tokens[i] < 0 || tokens[i] >= G4_VOCAB) return fail(c, G4_ERR_INVALID, "forward: token %d out of range", tokens[i]);
     cudaSetDevice(c->device);
     const int T = (int)count;
+    if (c->strict) {
+        const size_t need = (size_t)T * G4_HEADS * ((size_t)start_pos + T) * 4;
+        if (need > c->scores_cap) {
+            CK(cudaStreamSynchronize(c->st));
+            if (c->scores) cudaFree(c->scores);
+            c->scores = nullptr;
+            c->scores_cap = 0;
+            CK(cudaMalloc(&c->scores, need));
+            c->scores_cap = need;
+        }
+    }
     CK(cudaMemcpyAsync(c->tokens_d, tokens, count * 4, cudaMemcpyHostToDevice, c->st));
     cudaError_t e;
-    if (T == 1 && c->use_graph) {
+    if (T == 1 && c->use_graph && !c->strict) {
         CK(cudaMemcpyAsync(c->pos_d, &start_pos, 4, cudaMemcpyHostToDevice, c->st));
         if (!c->g_decode) {
             if (!c->decode_warm) {
@@ -851,6 +875,11 @@ int g4_read_cache(g4_ctx *c, int layer, int which, int slot0, int nslots, float 
 }
 
 void *g4_stream(g4_ctx *c) { return c ? (void *)c->st : nullptr; }
+
+int g4_profiler_range(int on) {
+    cudaError_t e = on ? cudaProfilerStart() : cudaProfilerStop();
+    return e == cudaSuccess ? G4_OK : G4_ERR_CUDA;
+}
 
 int g4_device_bytes(g4_ctx *c, uint64_t *weights, uint64_t *total) {
     if (!c) return G4_ERR_INVALID;

@@ -17,7 +17,8 @@
 #include "g4_format.h"
 
 // Device-side error codes written to the context's error word (reported by the
-// host as G4_ERR_DEVICE).
+// host as G4_ERR_DEVICE). Wait timeouts also carry where they gave up:
+// bits 8-19 the stage index, bits 20-31 the CTA.
 enum : int {
     G4D_OK = 0,
     G4D_TIMEOUT_FULL = 1,   // consumer waited too long for a weight stage
@@ -81,6 +82,7 @@ struct GemvArgs {
     unsigned *ticket;
     int32_t *dots_out;      // optional debug: int32 per (t, n, g)
     int *err;
+    int strict;             // reference-order (sequential) RMSNorm sums
 };
 
 // ---- GEMM (prefill, T > 4) -------------------------------------------------
@@ -119,17 +121,22 @@ struct AttnArgs {
     int8_t *xq;             // decode combine: quantised output [8*hd]
     float *xs;
     int *err;
+    int strict;             // reference-order norms / softmax / value sums
+    float *scores;          // strict: [T][8][score_stride] scratch
+    int score_stride;
 };
 
 // ---- launchers (g4_*.cu) ---------------------------------------------------
 int g4_gemv_smem_bytes(const GemvArgs &a, int stages);
-void g4_gemv_plan(GemvArgs &a, int num_sms);
+// Fills the launch plan (rb = most rows one CTA owns) for a grid of `grid` CTAs.
+void g4_gemv_plan(GemvArgs &a, int grid);
 cudaError_t g4_launch_gemv(const GemvArgs &a, int pro, int epi, int grid, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_gemm(const GemmArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_decode(const AttnArgs &a, int splits, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_combine(const AttnArgs &a, int splits, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_qkv_post(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_prefill(const AttnArgs &a, cudaStream_t st, bool pdl);
+cudaError_t g4_launch_attn_strict(const AttnArgs &a, cudaStream_t st, bool pdl);
 
 cudaError_t g4_launch_repack(const int8_t *packed_w, const uint16_t *packed_s, int N, int K, int8_t *w, uint16_t *s,
                              int row_offset, int row_stride_mul, cudaStream_t st);
@@ -140,9 +147,9 @@ cudaError_t g4_launch_rows_quant(const float *src, int src_stride, int T, int K,
 // mode: 0 = norm+quant, 1 = res+norm+quant, 2 = res+quant, 3 = res finish (no quant)
 cudaError_t g4_launch_rows_norm(int mode, const float *src, int T, const float *w_post, const float *res_in,
                                 float *res_out, const float *scalar, const float *w_pre, float eps, int8_t *xq,
-                                float *xs, cudaStream_t st, bool pdl, float *y_out = nullptr);
+                                float *xs, cudaStream_t st, bool pdl, float *y_out = nullptr, int strict = 0);
 cudaError_t g4_launch_ple_prep(const float *pli, const float *ple_emb, const float *w, float eps, float scale, int T,
-                               float *u, cudaStream_t st, bool pdl);
+                               float *u, cudaStream_t st, bool pdl, int strict = 0);
 
 // Launch with (optional) programmatic dependent launch.
 template <typename... Args>

@@ -50,6 +50,27 @@ __device__ float block_sum256(float v, float *red) {
     return r;
 }
 
+// Sum of squares of a row held as v[i] at index tid + 256*i: block tree, or
+// (strict) one thread in index order through `buf` as gemma4.c:367-368 does.
+template <int PER>
+__device__ float sumsq_row(const float (&v)[PER], int strict, float *buf, float *red) {
+    const int tid = threadIdx.x;
+    if (!strict) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < PER; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+        return block_sum256(ss, red);
+    }
+#pragma unroll
+    for (int i = 0; i < PER; i++) buf[tid + 256 * i] = v[i];
+    __syncthreads();
+    if (tid == 0) red[0] = seq_sumsq(buf, PER * 256);
+    __syncthreads();
+    const float ss = red[0];
+    __syncthreads();
+    return ss;
+}
+
 // One warp per 64-group: x -> (q, scale) exactly as gemma4.c:265-279.
 __device__ void quant_group_warp(const float *src, int8_t *q, float *s) {
     const int lane = threadIdx.x & 31;
@@ -98,7 +119,7 @@ __global__ void __launch_bounds__(256) k_rows_quant(const float *src, int src_st
 __global__ void __launch_bounds__(256) k_rows_norm(int mode, const float *src, const float *w_post,
                                                    const float *res_in, float *res_out, const float *scalar,
                                                    const float *w_pre, float eps, int8_t *xq, float *xs,
-                                                   float *y_out) {
+                                                   float *y_out, int strict) {
     __shared__ float red[8];
     __shared__ __align__(16) float y[G4_HIDDEN];
     griddep_launch();
@@ -107,20 +128,15 @@ __global__ void __launch_bounds__(256) k_rows_norm(int mode, const float *src, c
     const int t = blockIdx.x, tid = threadIdx.x;
     const float *h = src + (size_t)t * G4_HIDDEN;
     float v[PER];
-    float ss = 0.0f;
 #pragma unroll
-    for (int i = 0; i < PER; i++) {
-        v[i] = h[tid + 256 * i];
-        ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-    }
-    ss = block_sum256(ss, red);
+    for (int i = 0; i < PER; i++) v[i] = h[tid + 256 * i];
+    const float ss = sumsq_row<PER>(v, strict, y, red);
     const float inv = rms_inv(ss, (float)G4_HIDDEN, eps);
     if (mode == 0) {
 #pragma unroll
         for (int i = 0; i < PER; i++) v[i] = rms_apply(v[i], inv, w_pre[tid + 256 * i]);
     } else {
         const float sc = scalar ? *scalar : 1.0f;
-        float ss2 = 0.0f;
 #pragma unroll
         for (int i = 0; i < PER; i++) {
             const int e = tid + 256 * i;
@@ -128,11 +144,10 @@ __global__ void __launch_bounds__(256) k_rows_norm(int mode, const float *src, c
             if (scalar) r = __fmul_rn(r, sc);
             res_out[(size_t)t * G4_HIDDEN + e] = r;
             v[i] = r;
-            ss2 = __fadd_rn(ss2, __fmul_rn(r, r));
         }
         if (mode == 3) return;
         if (mode == 1) {
-            ss2 = block_sum256(ss2, red);
+            const float ss2 = sumsq_row<PER>(v, strict, y, red);
             const float inv2 = rms_inv(ss2, (float)G4_HIDDEN, eps);
 #pragma unroll
             for (int i = 0; i < PER; i++) v[i] = rms_apply(v[i], inv2, w_pre[tid + 256 * i]);
@@ -151,14 +166,16 @@ __global__ void __launch_bounds__(256) k_rows_norm(int mode, const float *src, c
 
 // u[t][l][:] = (rmsnorm(pli[t][l][:], w, eps) + ple_emb[t][l][:]) * scale   (gemma4.c:474-477)
 __global__ void __launch_bounds__(256) k_ple_prep(const float *pli, const float *ple_emb, const float *w, float eps,
-                                                  float scale, float *u) {
+                                                  float scale, float *u, int strict) {
     __shared__ float red[8];
+    __shared__ float buf[G4_PLE];
     griddep_launch();
     griddep_wait();
     const size_t base = ((size_t)blockIdx.x * G4_NUM_LAYERS + blockIdx.y) * G4_PLE;
     const int i = threadIdx.x;
-    const float x = pli[base + i];
-    const float ss = block_sum256(__fmul_rn(x, x), red);
+    const float xv[1] = {pli[base + i]};
+    const float x = xv[0];
+    const float ss = sumsq_row<1>(xv, strict, buf, red);
     const float y = rms_apply(x, rms_inv(ss, (float)G4_PLE, eps), w[i]);
     u[base + i] = __fmul_rn(__fadd_rn(y, ple_emb[base + i]), scale);
 }
@@ -187,12 +204,13 @@ cudaError_t g4_launch_rows_quant(const float *src, int src_stride, int T, int K,
 
 cudaError_t g4_launch_rows_norm(int mode, const float *src, int T, const float *w_post, const float *res_in,
                                 float *res_out, const float *scalar, const float *w_pre, float eps, int8_t *xq,
-                                float *xs, cudaStream_t st, bool pdl, float *y_out) {
+                                float *xs, cudaStream_t st, bool pdl, float *y_out, int strict) {
     return g4_launch(k_rows_norm, dim3(T), dim3(256), 0, st, pdl, mode, src, w_post, res_in, res_out, scalar, w_pre,
-                     eps, xq, xs, y_out);
+                     eps, xq, xs, y_out, strict);
 }
 
 cudaError_t g4_launch_ple_prep(const float *pli, const float *ple_emb, const float *w, float eps, float scale, int T,
-                               float *u, cudaStream_t st, bool pdl) {
-    return g4_launch(k_ple_prep, dim3(T, G4_NUM_LAYERS), dim3(G4_PLE), 0, st, pdl, pli, ple_emb, w, eps, scale, u);
+                               float *u, cudaStream_t st, bool pdl, int strict) {
+    return g4_launch(k_ple_prep, dim3(T, G4_NUM_LAYERS), dim3(G4_PLE), 0, st, pdl, pli, ple_emb, w, eps, scale, u,
+                     strict);
 }

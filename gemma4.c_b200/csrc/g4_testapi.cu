@@ -6,6 +6,7 @@
 // buffers, so they are for testing, not for the hot path.
 #include <cuda_runtime.h>
 #include <math.h>
+#include <stdio.h>
 
 #include <vector>
 
@@ -182,8 +183,8 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
         a.dots_out = (int32_t *)ddots.p;
         a.err = (int *)derr.p;
         a.eps = G4_RMS_EPS;
-        g4_gemv_plan(a, num_sms());
-        int units = N / a.row_gran, grid = units < num_sms() ? units : num_sms();
+        const int grid = N / 2 < num_sms() ? N / 2 : num_sms();
+        g4_gemv_plan(a, grid);
         TK(g4_launch_gemv(a, PRO_LOADQ, EPI_STORE, grid, 0, false));
     } else {
         GemmArgs a{};
@@ -209,6 +210,69 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
     if (err) return G4_ERR_DEVICE;
     TK(cudaMemcpy(out, dout.p, (size_t)T * N * 4, cudaMemcpyDeviceToHost));
     if (dots) TK(cudaMemcpy(dots, ddots.p, (size_t)T * N * G * 4, cudaMemcpyDeviceToHost));
+    return G4_OK;
+}
+
+// Time the decode GEMV on an N x K matrix (random device-resident weights):
+// `copies` distinct weight sets are cycled so the working set exceeds L2, and
+// `iters` back-to-back launches are timed with CUDA events on one stream.
+// Reports the average launch duration and the algorithmic bytes per launch
+// (int8 weights + FP16 scales).
+int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch, double *bytes_per_launch) {
+    if (N < 2 || N % 2 || K % 256 || T < 1 || T > 4 || iters < 1 || !ms_per_launch) return G4_ERR_INVALID;
+    const int G = K / 64;
+    const size_t wbytes = (size_t)N * K + (size_t)N * G * 2;
+    int copies = (int)((512ull << 20) / wbytes) + 1;
+    if (copies > 64) copies = 64;
+    DevBuf w, xq, xs, out, err;
+    TK(w.alloc(wbytes * copies));
+    TK(xq.alloc((size_t)T * K));
+    TK(xs.alloc((size_t)T * G * 4));
+    TK(out.alloc((size_t)T * N * 4));
+    TK(err.alloc(64));
+    TK(cudaMemset(w.p, 1, wbytes * copies));
+    TK(cudaMemset(xq.p, 1, (size_t)T * K));
+    TK(cudaMemset(xs.p, 0, (size_t)T * G * 4));
+    TK(cudaMemset(err.p, 0, 64));
+    TK(cudaDeviceSynchronize());   // the memsets above must land before the timed stream reads the buffers
+    cudaStream_t st;
+    TK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    auto launch = [&](int i) {
+        const uint8_t *base = (const uint8_t *)w.p + (size_t)(i % copies) * wbytes;
+        GemvArgs a{};
+        a.m = DMat{(const int8_t *)base, (const uint16_t *)(base + (size_t)N * K), N, K};
+        a.T = T;
+        a.xq_in = (const int8_t *)xq.p;
+        a.xs_in = (const float *)xs.p;
+        a.out = (float *)out.p;
+        a.out_stride = N;
+        a.err = (int *)err.p;
+        const int grid = N / 2 < num_sms() ? N / 2 : num_sms();
+        g4_gemv_plan(a, grid);
+        return g4_launch_gemv(a, PRO_LOADQ, EPI_STORE, grid, st, pdl != 0);
+    };
+    for (int i = 0; i < 3; i++) TK(launch(i));
+    cudaEvent_t e0, e1;
+    TK(cudaEventCreate(&e0));
+    TK(cudaEventCreate(&e1));
+    TK(cudaEventRecord(e0, st));
+    for (int i = 0; i < iters; i++) TK(launch(i));
+    TK(cudaEventRecord(e1, st));
+    TK(cudaEventSynchronize(e1));
+    float ms = 0;
+    TK(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaStreamDestroy(st);
+    int derr = 0;
+    TK(cudaMemcpy(&derr, err.p, 4, cudaMemcpyDeviceToHost));
+    if (derr) {
+        fprintf(stderr, "g4_bench_gemv: device error %d stage %d block %d\n", derr & 0xff, (derr >> 8) & 0xfff,
+                (unsigned)derr >> 20);
+        return G4_ERR_DEVICE;
+    }
+    *ms_per_launch = ms / iters;
+    if (bytes_per_launch) *bytes_per_launch = (double)wbytes;
     return G4_OK;
 }
 

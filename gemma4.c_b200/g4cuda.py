@@ -76,6 +76,9 @@ def load(path=LIB_PATH):
     L.g4k_quantize.argtypes = [_f32p, C.c_int, C.c_int, _i8p, _f32p]
     L.g4k_linear.argtypes = [_i8p, _u16p, C.c_int, C.c_int, _i8p, _f32p, C.c_int, C.c_int, _f32p, vp]
     L.g4k_rmsnorm_quant.argtypes = [_f32p, C.c_int, _f32p, C.c_float, vp, _i8p, _f32p]
+    L.g4_bench_gemv.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
+                                C.POINTER(C.c_double)]
+    L.g4_profiler_range.argtypes = [C.c_int]
     _lib = L
     return L
 
@@ -216,6 +219,14 @@ def linear(w_packed, s_packed, N, K, xq, xs, path=0, want_dots=False):
     _check(L.g4k_linear(w_packed, s_packed, N, K, xq, xs, T, path, out,
                         dots.ctypes.data if dots is not None else None))
     return out, dots
+
+
+def bench_gemv(N, K, T=1, iters=200, pdl=True):
+    """(ms per launch, algorithmic bytes per launch) of the decode GEMV."""
+    L = load()
+    ms, by = C.c_float(), C.c_double()
+    _check(L.g4_bench_gemv(N, K, T, iters, int(pdl), C.byref(ms), C.byref(by)))
+    return ms.value, by.value
 
 
 def rmsnorm_quant(x, w, eps=1e-6):

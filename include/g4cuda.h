@@ -79,6 +79,11 @@ const char *g4_strerror(int code);
 #define G4_OPT_PDL 2         /* programmatic dependent launch between kernels (default 1) */
 #define G4_OPT_GEMM_PATH 3   /* prefill GEMM: 0 auto, 1 SIMT dp4a, 2 tcgen05 */
 #define G4_OPT_LAYERS 4      /* run only the first N layers (testing aid; default 35) */
+/* Reference-order arithmetic (default 0): RMSNorm sums of squares, attention
+ * scores, softmax and value sums are evaluated in gemma4.c's sequential order
+ * with the host C library's expf, so the whole forward reproduces the
+ * reference bit for bit (logits up to tanhf). Much slower; for verification. */
+#define G4_OPT_STRICT 5
 int g4_set_option(g4_ctx *ctx, int option, int value);
 
 /* ---- introspection (tests, benchmarks) ---- */
@@ -86,6 +91,8 @@ int g4_read_residual(g4_ctx *ctx, size_t rows, float *out);          /* [rows][1
 /* `nslots` ring slots of the K (which=0) or V (which=1) cache `layer` reads. */
 int g4_read_cache(g4_ctx *ctx, int layer, int which, int slot0, int nslots, float *out);
 void *g4_stream(g4_ctx *ctx);                 /* the context's cudaStream_t */
+/* Open (1) / close (0) the profiler capture range (ncu --profile-from-start off). */
+int g4_profiler_range(int on);
 int g4_device_bytes(g4_ctx *ctx, uint64_t *weights, uint64_t *total);
 
 /* ---- synthetic model images (benchmarks and parity tests) ----
@@ -104,6 +111,10 @@ int g4k_quantize(const float *x, int rows, int width, int8_t *q, float *s);
  * 3 tcgen05 GEMM. */
 int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, const int8_t *xq, const float *xs,
                int T, int path, float *out, int32_t *dots);
+/* Average duration of the decode GEMV on an N x K int8 matrix over `iters`
+ * launches (weights cycled through enough copies to exceed L2), and the
+ * algorithmic bytes (int8 weights + FP16 scales) one launch streams. */
+int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch, double *bytes_per_launch);
 /* rmsnorm (gemma4.c:360-373) of hidden-width rows followed by quantize */
 int g4k_rmsnorm_quant(const float *x, int rows, const float *w, float eps, float *y, int8_t *q, float *s);
 

@@ -1,0 +1,378 @@
+#!/usr/bin/env python3
+"""Benchmark of the gemma4.c forward path on B200 (libg4cuda.so).
+
+Headline (one JSON line on rank 0): decode tok/s at context 512, the
+reference's `./run --bench 512 128` decode figure (README.md:76) — one step is
+one token: forward(1 token) + logits, on the synthetic Gemma 4 E2B model of
+BASELINE config 1 (random-init weights in gemma4.c's .bin layout, seed 0; the
+real checkpoint is not available). Alongside: prefill tok/s at 512 and 16384,
+decode tok/s at 16384, the int8-GEMV roofline, and the reference CPU path timed
+on this host.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W]        # our CUDA path
+  python bench.py --impl reference [...]                     # the reference's CPU path
+  torchrun --nproc-per-node N bench.py --gpus N ...          # N replicas (weak scaling)
+
+value: device-resident decode — the step's token is already in device memory
+(g4_forward copies 8 bytes per step; the same fixed token id the reference
+benchmark feeds, gemma4.c:637-641) and logits are enqueued without readback;
+K steps timed with CUDA events on the library's stream between barriers, max
+over ranks. e2e: the greedy generation loop through the public C ABI — token
+id host->device, forward, logits with argmax device->host, next token from the
+argmax — every step.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "gemma4.c_b200"))
+
+PUBLISHED_DECODE_512 = 25.16   # README.md:76, tg128 @ d512, Ryzen 7 7700, 8 threads
+PREFILL = 512
+CTX_LONG = 16384
+
+
+def env_int(name, default):
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+class Dist:
+    """Process-group plumbing for N replicas: barrier and max over ranks."""
+
+    def __init__(self):
+        self.rank, self.world, self.local = env_int("RANK", 0), env_int("WORLD_SIZE", 1), env_int("LOCAL_RANK", 0)
+        self.pg = None
+        if self.world > 1:
+            import datetime
+
+            import torch
+            import torch.distributed as dist
+            self.torch, self.dist = torch, dist
+            backend = "nccl" if torch.cuda.is_available() else "gloo"
+            if backend == "nccl":
+                torch.cuda.set_device(self.local)
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            self.backend = backend
+            self.pg = True
+
+    def barrier(self):
+        if self.pg:
+            self.dist.barrier()
+
+    def max(self, v):
+        if not self.pg:
+            return v
+        t = self.torch.tensor([float(v)], dtype=self.torch.float64,
+                              device="cuda" if self.backend == "nccl" else "cpu")
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
+        return float(t.item())
+
+    def close(self):
+        if self.pg:
+            self.dist.barrier()
+            self.dist.destroy_process_group()
+
+
+class Clocks:
+    """nvidia-smi clock / throttle sampling over the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.device, self.proc, self.path = device, None, None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.device), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, mx, reasons = [], 0.0, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            for line in open(self.path):
+                f = [x.strip() for x in line.split(",")]
+                if len(f) < 9:
+                    continue
+                try:
+                    sm.append(float(f[1]))
+                    mx = max(mx, float(f[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, f[5:9]):
+                    if v.lower() == "active":
+                        reasons.add(n)
+            os.unlink(self.path)
+        except OSError:
+            return None
+        if not sm:
+            return None
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def prompt_ids(n, seed=0):
+    return np.random.default_rng(seed).integers(0, 262144, size=n).astype(np.int32)
+
+
+def cpu_reference_decode(img, max_seconds=10.0, max_steps=256, prompt=PREFILL):
+    """The unmodified reference (oracle/_ref) on this host: prefill `prompt`
+    tokens, then decode until max_seconds or max_steps. Returns a dict."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Reference
+    ref = Reference()
+    m = ref.open_model(img)
+    try:
+        ids = prompt_ids(prompt)
+        t0 = time.perf_counter()
+        for s in range(0, prompt, 512):
+            m.forward(ids[s:s + 512], s)
+        m.logits((prompt - 1) % 512)
+        t_pref = time.perf_counter() - t0
+        tok = np.array([2], np.int32)
+        steps, t0 = 0, time.perf_counter()
+        while steps < max_steps and time.perf_counter() - t0 < max_seconds:
+            m.forward(tok, prompt + steps)
+            m.logits(0)
+            steps += 1
+        dt = time.perf_counter() - t0
+        return {"prefill_tok_s": prompt / t_pref, "decode_tok_s": steps / dt, "steps": steps, "seconds": dt,
+                "cores": ref.threads(), "variant": ref.variant}
+    finally:
+        m.close()
+
+
+def run_reference_arm(args, dist):
+    """--impl reference: the reference's own CPU implementation of the path on
+    this host's cores (rank 0 only), same metric and workload."""
+    if dist.rank != 0:
+        return
+    import g4cuda as g4
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    from oracle import Reference
+    img = g4.synth_image(seed=0, flags=0)
+    ref = Reference()
+    m = ref.open_model(img)
+    ids = prompt_ids(PREFILL)
+    m.forward(ids, 0)
+    m.logits(PREFILL - 1)
+    tok = np.array([2], np.int32)
+    pos = PREFILL
+    for _ in range(args.warmup):
+        m.forward(tok, pos)
+        m.logits(0)
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        m.forward(tok, pos)
+        m.logits(0)
+        pos += 1
+    dt = time.perf_counter() - t0
+    v = args.steps / dt
+    line = {
+        "impl": "reference", "metric": "decode tok/s @ctx 512", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": v / PUBLISHED_DECODE_512, "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "decode after a 512-token prefill (gemma4.c --bench 512 K)",
+                   "model": "gemma4-E2B random-init (.bin layout, seed 0)", "global_batch": 1, "seq_len": PREFILL,
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": v, "unit": "tok/s", "cores": ref.threads(), "kind": "reference",
+                         "sample": f"{args.steps} decode steps after a {PREFILL}-token prefill ({ref.variant} build)"},
+        "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    m.close()
+    print(json.dumps(line), flush=True)
+
+
+def decode_timed(m, start, steps, warmup, dist, clocks=None, profile_range=False):
+    tok = np.array([2], np.int32)
+    pos = start
+    for _ in range(warmup):
+        m.forward(tok, pos)
+        m.logits_async(0)
+        pos += 1
+    m.sync()
+    dist.barrier()
+    if clocks:
+        clocks.start()
+    if profile_range:
+        m.L.g4_profiler_range(1)
+    m.mark(0)
+    for _ in range(steps):
+        m.forward(tok, pos)
+        m.logits_async(0)
+        pos += 1
+    m.mark(1)
+    if profile_range:
+        m.sync()
+        m.L.g4_profiler_range(0)
+    ms = m.elapsed(0, 1)
+    m.sync()
+    c = clocks.stop() if clocks else None
+    dist.barrier()
+    return dist.max(ms), pos, c
+
+
+def prefill_timed(m, n, reps, dist):
+    ids = prompt_ids(n)
+    times = []
+    for r in range(reps + 1):
+        m.sync()
+        dist.barrier()
+        m.mark(2)
+        for s in range(0, n, 512):
+            m.forward(ids[s:s + 512], s)
+        m.logits_async((n - 1) % 512)
+        m.mark(3)
+        ms = dist.max(m.elapsed(2, 3))
+        if r > 0 or reps == 0:
+            times.append(ms)
+    return n / (np.mean(times) / 1e3), float(np.mean(times))
+
+
+def run_ours(args, dist):
+    import g4cuda as g4
+    hbm_peak, peak_kind = peaks()
+    img = g4.synth_image(seed=0, flags=0)
+    m = g4.Model(img, device=dist.local)
+
+    # prefill @512 (also fills the cache for the decode run)
+    pre512, pre512_ms = prefill_timed(m, PREFILL, 2, dist)
+    # decode @512: the headline
+    clocks = Clocks(dist.local)
+    ms, pos, clk = decode_timed(m, PREFILL, args.steps, args.warmup, dist, clocks, args.profile_range)
+    value = dist.world * args.steps / (ms / 1e3)
+    per_step = ms / args.steps
+
+    # end to end through the C ABI: host token in, argmax out, greedy loop
+    tok = 2
+    m.sync()
+    dist.barrier()
+    t0 = time.perf_counter()
+    m.mark(4)
+    for _ in range(args.steps):
+        m.forward(np.array([tok], np.int32), pos)
+        _, tok = m.logits(0, want_logits=False)
+        pos += 1
+    m.mark(5)
+    wall = time.perf_counter() - t0
+    e2e_ms = dist.max(max(m.elapsed(4, 5), wall * 1e3))
+    e2e = dist.world * args.steps / (e2e_ms / 1e3)
+
+    # live kernel profile of one eager decode step: int8 GEMV class roofline
+    prof_ms, prof_bytes, prof_n = m.profile_decode(2, pos)
+    pos += 1
+    gemv_gbs = prof_bytes[0] / (prof_ms[0] / 1e3) / 1e9
+    traffic = None
+    try:
+        with open(os.path.join(ROOT, "profiles", "decode_gemv_traffic.json")) as f:
+            ratio = json.load(f)["dram_bytes_per_algorithmic_byte"]
+        traffic = prof_bytes[0] / prof_n[0] * ratio
+    except (OSError, KeyError, ValueError, ZeroDivisionError):
+        traffic = None
+    step_bytes = prof_bytes[0] + prof_bytes[1]
+
+    # long context: prefill 16384 then decode
+    long = {}
+    if not args.short:
+        pre_long, _ = prefill_timed(m, CTX_LONG, 0, dist)
+        ms_l, _, _ = decode_timed(m, CTX_LONG, max(8, args.steps // 2), 2, dist)
+        long = {"prefill_tok_s_16384": dist.world * pre_long,
+                "decode_tok_s_16384": dist.world * max(8, args.steps // 2) / (ms_l / 1e3)}
+
+    line = {
+        "metric": "decode tok/s @ctx 512", "value": value, "unit": "tok/s", "n_gpus": dist.world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": value / PUBLISHED_DECODE_512,
+        "dtype": "int8", "data": "synthetic",
+        "config": {"workload": "decode after a 512-token prefill (gemma4.c --bench 512 K); one step = "
+                               "forward(1 token) + logits",
+                   "model": "gemma4-E2B random-init (.bin layout, seed 0)", "global_batch": dist.world,
+                   "seq_len": PREFILL, "parallelism": f"replicas x{dist.world}",
+                   "l2": "weights streamed per step (2.35 GB) exceed L2 (126 MB)"},
+        "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
+        "gpu_launches": args.steps * m.launches_per_token(),
+        "roofline": {"bound": "hbm", "achieved": gemv_gbs, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": gemv_gbs / hbm_peak, "traffic": traffic,
+                     "kernel": "int8 decode GEMV (all projections of one token)", "peak_kind": peak_kind},
+        "step_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes / (per_step / 1e3) / 1e9,
+                          "frac": step_bytes / (per_step / 1e3) / 1e9 / hbm_peak},
+        "profile_ms": {"gemv": prof_ms[0], "attention": prof_ms[1], "other": prof_ms[2],
+                       "launches": prof_n},
+        "prefill_tok_s_512": dist.world * pre512,
+    }
+    line.update(long)
+    if clk:
+        line["clocks"] = clk
+    m.close()
+    if dist.rank == 0 and dist.world == 1 and not args.no_cpu_baseline:
+        cb = cpu_reference_decode(img)
+        line["cpu_baseline"] = {"value": cb["decode_tok_s"], "unit": "tok/s", "cores": cb["cores"],
+                                "kind": "reference",
+                                "sample": f"{cb['steps']} decode steps ({cb['seconds']:.1f} s) after a "
+                                          f"{PREFILL}-token prefill, {cb['variant']} build",
+                                "prefill_tok_s_512": cb["prefill_tok_s"]}
+    if dist.rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=128)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--short", action="store_true", help="skip the 16384-context runs")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-range", action="store_true",
+                    help="open the profiler capture range around the timed decode steps only "
+                         "(for ncu --profile-from-start off)")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)
+    if args.impl == "reference":
+        # the reference arm runs on rank 0's host cores only; other ranks exit at once
+        dist = Dist.__new__(Dist)
+        dist.rank, dist.world, dist.local, dist.pg = env_int("RANK", 0), env_int("WORLD_SIZE", 1), 0, None
+        run_reference_arm(args, dist)
+        return
+    dist = Dist()
+    try:
+        run_ours(args, dist)
+    finally:
+        dist.close()
+
+
+if __name__ == "__main__":
+    main()

@@ -82,6 +82,7 @@ struct g4_ctx {
     cudaGraphExec_t g_decode = nullptr;
     int graph_cur = 0;
     bool decode_warm = false;
+    cudaEvent_t events[16] = {};
     char msg[512] = {0};
 };
 
@@ -400,11 +401,35 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
 // ---------------------------------------------------------------------------
 // launch sequences
 
+// Per-kernel profile of one launch sequence: an event after every launch; with
+// launches serialised (no PDL), kernel i took ev[i] - ev[i-1].
+struct Prof {
+    static constexpr int kMax = 512;
+    cudaEvent_t ev[kMax + 1];
+    int cls[kMax];
+    double bytes[kMax];
+    int n = 0;
+};
+
 struct Seq {
     g4_ctx *c;
     bool pdl;
     cudaError_t e = cudaSuccess;
-    void ck(cudaError_t x) { if (e == cudaSuccess && x != cudaSuccess) e = x; }
+    Prof *prof = nullptr;
+    int next_cls = 2;          // 0 int8 weight GEMV, 1 attention, 2 other
+    double next_bytes = 0;
+    void tag(int cls, double bytes) { next_cls = cls; next_bytes = bytes; }
+    void ck(cudaError_t x) {
+        if (e == cudaSuccess && x != cudaSuccess) e = x;
+        if (prof && prof->n < Prof::kMax) {
+            cudaEventRecord(prof->ev[prof->n + 1], c->st);
+            prof->cls[prof->n] = next_cls;
+            prof->bytes[prof->n] = next_bytes;
+            prof->n++;
+        }
+        next_cls = 2;
+        next_bytes = 0;
+    }
 };
 
 GemvArgs gemv_base(g4_ctx *c, const DMat &m, int T) {
@@ -420,6 +445,7 @@ GemvArgs gemv_base(g4_ctx *c, const DMat &m, int T) {
 }
 
 void gemv(Seq &q, GemvArgs &a, int pro, int epi) {
+    q.tag(0, (double)a.m.N * a.m.K + (double)a.m.N * (a.m.K / 64) * 2);
     const int pairs = a.m.N / 2;
     const int grid = pairs < q.c->num_sms ? pairs : q.c->num_sms;
     g4_gemv_plan(a, grid);
@@ -477,8 +503,9 @@ AttnArgs attn_base(g4_ctx *c, const Layer &Y, int T, int start_pos, const int *p
 
 // Decode path, T <= 4 tokens. pos_dev != NULL: positions and tokens come from
 // device memory (graph replay); otherwise from start_pos / tokens_d.
-cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev) {
-    Seq q{c, c->use_pdl};
+cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev, Prof *prof = nullptr) {
+    Seq q{c, c->use_pdl && !prof};
+    q.prof = prof;
     int cur = 0;
     const float emb_mult = sqrtf((float)G4_HIDDEN), ple_mult = sqrtf((float)G4_PLE);
     {
@@ -524,7 +551,10 @@ cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev) {
         AttnArgs at = attn_base(c, Y, T, start_pos, pos_dev);
         const bool fused_decode = T == 1 && !c->strict;
         if (fused_decode) {
+            const int p = start_pos, kf = Y.global ? 0 : (p + 1 > G4_SLIDING_WINDOW ? p + 1 - G4_SLIDING_WINDOW : 0);
+            q.tag(1, (double)(p + 1 - kf) * Y.hd * 8);
             q.ck(g4_launch_attn_decode(at, kSplits, c->st, q.pdl));
+            q.tag(1, 0);
             q.ck(g4_launch_attn_combine(at, kSplits, c->st, q.pdl));
         } else {
             q.ck(g4_launch_qkv_post(at, c->st, q.pdl));
@@ -729,6 +759,8 @@ int g4_close(g4_ctx *c) {
     if (!c) return G4_ERR_INVALID;
     if (c->st) cudaStreamSynchronize(c->st);
     if (c->g_decode) cudaGraphExecDestroy(c->g_decode);
+    for (int i = 0; i < 16; i++)
+        if (c->events[i]) cudaEventDestroy(c->events[i]);
     if (c->arena) cudaFree(c->arena);
     if (c->state) cudaFree(c->state);
     if (c->kv) cudaFree(c->kv);
@@ -818,11 +850,33 @@ int g4_forward(g4_ctx *c, const int *tokens, size_t count, int start_pos) {
     return G4_OK;
 }
 
+static cudaError_t enqueue_logits(g4_ctx *c, size_t row, Prof *prof = nullptr) {
+    GemvArgs a = gemv_base(c, c->embed, 1);
+    a.src = c->res[c->cur] + row * G4_HIDDEN;
+    a.src_stride = G4_HIDDEN;
+    a.w_pre = c->final_norm;
+    a.out = c->logits;
+    a.out_stride = G4_VOCAB;
+    a.argmax_part = c->argmax_part;
+    a.argmax_out = c->argmax_out;
+    a.ticket = c->ticket;
+    Seq q{c, c->use_pdl && !prof};
+    q.prof = prof;
+    gemv(q, a, PRO_NORM_QUANT, EPI_LOGITS);
+    return q.e;
+}
+
 int g4_logits(g4_ctx *c, size_t row, float *out, int *argmax) {
     if (!c) return G4_ERR_INVALID;
     if (c->last_T == 0 || row >= (size_t)c->last_T)
         return fail(c, G4_ERR_STATE, "logits: row %zu not computed by the last forward (%d rows)", row, c->last_T);
     cudaSetDevice(c->device);
+    if (!out && !argmax) {
+        // nothing to return: enqueue only (the reference benchmark discards logits, gemma4.c:641)
+        cudaError_t e = enqueue_logits(c, row);
+        if (e) return fail(c, G4_ERR_CUDA, "logits launch: %s", cudaGetErrorString(e));
+        return G4_OK;
+    }
     GemvArgs a = gemv_base(c, c->embed, 1);
     a.src = c->res[c->cur] + row * G4_HIDDEN;
     a.src_stride = G4_HIDDEN;
@@ -875,6 +929,58 @@ int g4_read_cache(g4_ctx *c, int layer, int which, int slot0, int nslots, float 
 }
 
 void *g4_stream(g4_ctx *c) { return c ? (void *)c->st : nullptr; }
+
+int g4_mark(g4_ctx *c, int slot) {
+    if (!c || slot < 0 || slot >= 16) return G4_ERR_INVALID;
+    if (!c->events[slot]) CK(cudaEventCreate(&c->events[slot]));
+    CK(cudaEventRecord(c->events[slot], c->st));
+    return G4_OK;
+}
+
+int g4_elapsed(g4_ctx *c, int a, int b, float *ms) {
+    if (!c || !ms || a < 0 || b < 0 || a >= 16 || b >= 16 || !c->events[a] || !c->events[b]) return G4_ERR_INVALID;
+    CK(cudaEventSynchronize(c->events[b]));
+    CK(cudaEventElapsedTime(ms, c->events[a], c->events[b]));
+    return G4_OK;
+}
+
+int g4_profile_decode(g4_ctx *c, int token, int pos, float ms[3], double bytes[3], int launches[3]) {
+    if (!c || !ms || !bytes || !launches || token < 0 || token >= G4_VOCAB || pos < 0 || pos >= G4_MAX_CONTEXT)
+        return G4_ERR_INVALID;
+    cudaSetDevice(c->device);
+    Prof *pr = new Prof();
+    for (int i = 0; i <= Prof::kMax; i++) cudaEventCreate(&pr->ev[i]);
+    int rc = G4_OK;
+    cudaError_t e = cudaMemcpyAsync(c->tokens_d, &token, 4, cudaMemcpyHostToDevice, c->st);
+    if (!e) e = cudaMemcpyAsync(c->pos_d, &pos, 4, cudaMemcpyHostToDevice, c->st);
+    if (!e) e = cudaEventRecord(pr->ev[0], c->st);
+    if (!e) e = enqueue_small(c, 1, pos, nullptr, pr);
+    c->last_T = 1;
+    if (!e) e = enqueue_logits(c, 0, pr);
+    if (!e) e = cudaStreamSynchronize(c->st);
+    for (int k = 0; k < 3; k++) { ms[k] = 0; bytes[k] = 0; launches[k] = 0; }
+    if (e) rc = fail(c, G4_ERR_CUDA, "profile: %s", cudaGetErrorString(e));
+    else {
+        for (int i = 0; i < pr->n; i++) {
+            float t = 0;
+            cudaEventElapsedTime(&t, pr->ev[i], pr->ev[i + 1]);
+            ms[pr->cls[i]] += t;
+            bytes[pr->cls[i]] += pr->bytes[i];
+            launches[pr->cls[i]]++;
+        }
+    }
+    for (int i = 0; i <= Prof::kMax; i++) cudaEventDestroy(pr->ev[i]);
+    delete pr;
+    return rc ? rc : check_device_error(c);
+}
+
+int g4_launches_per_token(g4_ctx *c, int *n) {
+    if (!c || !n) return G4_ERR_INVALID;
+    // embed/PLE GEMV + PLE prep, 7 kernels per layer (qkv, attention, combine,
+    // o, gate|up, down, ple gate, ple proj => 8), final residual, logits
+    *n = 2 + 8 * c->layers + 1 + 1;
+    return G4_OK;
+}
 
 int g4_profiler_range(int on) {
     cudaError_t e = on ? cudaProfilerStart() : cudaProfilerStop();

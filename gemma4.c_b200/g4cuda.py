@@ -79,6 +79,11 @@ def load(path=LIB_PATH):
     L.g4_bench_gemv.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
                                 C.POINTER(C.c_double)]
     L.g4_profiler_range.argtypes = [C.c_int]
+    L.g4_mark.argtypes = [vp, C.c_int]
+    L.g4_elapsed.argtypes = [vp, C.c_int, C.c_int, C.POINTER(C.c_float)]
+    L.g4_profile_decode.argtypes = [vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_double),
+                                    C.POINTER(C.c_int)]
+    L.g4_launches_per_token.argtypes = [vp, C.POINTER(C.c_int)]
     _lib = L
     return L
 
@@ -168,6 +173,30 @@ class Model:
 
     def stream(self):
         return self.L.g4_stream(self.h)
+
+    def logits_async(self, row=0):
+        """Enqueue logits without reading them back (no synchronisation)."""
+        _check(self.L.g4_logits(self.h, row, None, None), self.h)
+
+    def mark(self, slot):
+        _check(self.L.g4_mark(self.h, slot), self.h)
+
+    def elapsed(self, a, b):
+        ms = C.c_float()
+        _check(self.L.g4_elapsed(self.h, a, b, C.byref(ms)), self.h)
+        return ms.value
+
+    def profile_decode(self, token, pos):
+        ms = (C.c_float * 3)()
+        by = (C.c_double * 3)()
+        n = (C.c_int * 3)()
+        _check(self.L.g4_profile_decode(self.h, token, pos, ms, by, n), self.h)
+        return list(ms), list(by), list(n)
+
+    def launches_per_token(self):
+        n = C.c_int()
+        _check(self.L.g4_launches_per_token(self.h, C.byref(n)), self.h)
+        return n.value
 
     def device_bytes(self):
         w, t = C.c_uint64(), C.c_uint64()

@@ -60,7 +60,9 @@ int g4_forward(g4_ctx *ctx, const int *tokens, size_t count, int start_pos);
 /* logits (gemma4.c:512-522) of residual row `row` (< count of the last
  * forward): final RMSNorm, int8 lm_head over the tied embedding, 30*tanh(x/30).
  * `out` (262144 floats, may be NULL) receives the logits and `argmax` (may be
- * NULL) the greedy token (first maximum, gemma4.c:537-541). Synchronises. */
+ * NULL) the greedy token (first maximum, gemma4.c:537-541). Synchronises,
+ * except when both are NULL: then the call only enqueues (the reference's
+ * benchmark computes logits it never reads, gemma4.c:641). */
 int g4_logits(g4_ctx *ctx, size_t row, float *out, int *argmax);
 
 /* Top-k (k <= 64) of the logits of `row`, descending, ties to the lower id:
@@ -94,6 +96,17 @@ void *g4_stream(g4_ctx *ctx);                 /* the context's cudaStream_t */
 /* Open (1) / close (0) the profiler capture range (ncu --profile-from-start off). */
 int g4_profiler_range(int on);
 int g4_device_bytes(g4_ctx *ctx, uint64_t *weights, uint64_t *total);
+/* CUDA-event timing on the context's stream: record slot (0..15), then the
+ * elapsed milliseconds between two recorded slots (waits for the later one). */
+int g4_mark(g4_ctx *ctx, int slot);
+int g4_elapsed(g4_ctx *ctx, int slot_a, int slot_b, float *ms);
+/* One single-token decode step at `pos` plus its logits, launched eagerly with
+ * an event after every kernel: per-class device time, algorithmic bytes and
+ * launch counts. Class 0: int8 weight GEMVs; 1: attention (+ combine); 2: rest.
+ * Advances the KV cache like g4_forward. */
+int g4_profile_decode(g4_ctx *ctx, int token, int pos, float ms[3], double bytes[3], int launches[3]);
+/* Kernels one single-token decode step (forward + logits) launches. */
+int g4_launches_per_token(g4_ctx *ctx, int *n);
 
 /* ---- synthetic model images (benchmarks and parity tests) ----
  * A seeded random-init Gemma 4 E2B in the exact .bin layout gemma4.c reads. */

@@ -8,6 +8,7 @@
 #include <math.h>
 #include <stdio.h>
 
+#include <mutex>
 #include <vector>
 
 #include "../../include/g4cuda.h"
@@ -100,6 +101,42 @@ int num_sms() {
 
 }  // namespace
 
+// ---------------------------------------------------------------------------
+// Top-k without any allocation, for hosts that must not allocate device
+// memory on their decode path. Its only scratch is the first pass's per-slice
+// candidate list, kept in a fixed array in the library's device image: each
+// GPU that loads the library reserves it (32 KB) until the process exits.
+constexpr int kNoAllocSlice = 4096;
+constexpr int kNoAllocMaxN = 64 * kNoAllocSlice;   // one 262144-entry vocabulary row
+constexpr int kNoAllocMaxK = 64;
+static __device__ __align__(256) float g_topk_cand_v[(kNoAllocMaxN / kNoAllocSlice) * kNoAllocMaxK];
+static __device__ __align__(256) int g_topk_cand_i[(kNoAllocMaxN / kNoAllocSlice) * kNoAllocMaxK];
+
+// Device addresses of the arrays above, resolved once per device. In host code
+// the array names only stand in for the symbols; kernels must be given these.
+struct NoAllocScratch {
+    bool ready = false;
+    float *v = nullptr;
+    int *i = nullptr;
+};
+static NoAllocScratch g_noalloc[64];
+static std::mutex g_noalloc_mu;
+
+static cudaError_t noalloc_scratch(int dev, NoAllocScratch *out) {
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    NoAllocScratch &s = g_noalloc[dev];
+    if (!s.ready) {
+        cudaError_t e = cudaGetSymbolAddress((void **)&s.v, g_topk_cand_v);
+        if (e != cudaSuccess) return e;
+        e = cudaGetSymbolAddress((void **)&s.i, g_topk_cand_i);
+        if (e != cudaSuccess) return e;
+        s.ready = true;
+    }
+    *out = s;
+    return cudaSuccess;
+}
+
 cudaError_t g4_launch_topk(const float *x, int n, int k, float *part_v, int *part_i, float *vals, int *ids,
                            cudaStream_t st) {
     // pass 1: 4096-value slices (64 CTAs for the vocabulary); pass 2: one CTA
@@ -114,6 +151,22 @@ cudaError_t g4_launch_topk(const float *x, int n, int k, float *part_v, int *par
 }
 
 extern "C" {
+
+int g4_topk_noalloc(const float *logits, int n, int k, float *values, int *ids, void *stream) {
+    if (!logits || !values || !ids || k < 1 || k > kNoAllocMaxK || n < k) return G4_ERR_INVALID;
+    if (n > kNoAllocMaxN) return G4_ERR_INVALID;   // beyond the fixed scratch
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return G4_ERR_CUDA;
+    NoAllocScratch s;
+    if (noalloc_scratch(dev, &s) != cudaSuccess) return G4_ERR_CUDA;
+    // pass 1 writes blocks * k candidates and pass 2 reads exactly those, so
+    // nothing in the shared scratch has to start at zero
+    const cudaStream_t st = (cudaStream_t)stream;
+    const int blocks = (n + kNoAllocSlice - 1) / kNoAllocSlice;
+    k_topk_pass<kNoAllocSlice><<<blocks, kTopkThreads, 0, st>>>(logits, nullptr, n, k, s.v, s.i);
+    k_topk_pass<kTopkSlice><<<1, kTopkThreads, 0, st>>>(s.v, s.i, blocks * k, k, values, ids);
+    return cudaGetLastError() == cudaSuccess ? G4_OK : G4_ERR_CUDA;
+}
 
 int g4k_quantize(const float *x, int rows, int width, int8_t *q, float *s) {
     if (!x || !q || !s || rows < 1 || width < 64 || width % 64) return G4_ERR_INVALID;

@@ -84,6 +84,7 @@ def load(path=LIB_PATH):
     L.g4_profile_decode.argtypes = [vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_double),
                                     C.POINTER(C.c_int)]
     L.g4_launches_per_token.argtypes = [vp, C.POINTER(C.c_int)]
+    L.g4_topk_noalloc.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp]
     _lib = L
     return L
 

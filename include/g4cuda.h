@@ -69,6 +69,25 @@ int g4_logits(g4_ctx *ctx, size_t row, float *out, int *argmax);
  * the candidate list of gemma4.c:544-551. Synchronises. */
 int g4_topk(g4_ctx *ctx, size_t row, int k, float *values, int *ids);
 
+/* Top-k (k <= 64) of n <= 262144 floats already in device memory, written to
+ * caller-provided device buffers `values`/`ids` on `stream` (a cudaStream_t;
+ * NULL = the default stream): the same selection as g4_topk (descending,
+ * ties to the lower index), but this entry point allocates nothing. It is for
+ * hosts that cannot call cudaMalloc on their decode path — frameworks that
+ * own every byte of device memory through their own pool, hosts that capture
+ * the decode loop into CUDA graphs (allocation is not allowed while a stream
+ * is being captured), and latency-critical loops that must not block in the
+ * allocator. It has no counterpart in the reference (which samples on the
+ * CPU).
+ * Its one piece of scratch is a fixed 32 KB array in the library's device
+ * image, which every GPU that loads the library keeps until exit; n above
+ * 262144 or k above 64 is rejected with G4_ERR_INVALID. The first call on a
+ * device looks up that array's device address, so make it before capturing a
+ * stream. All calls share the array: calls whose kernels overlap on the GPU
+ * (different streams, no ordering between them) race on it. Asynchronous: no
+ * synchronisation, results valid once the stream reaches them. */
+int g4_topk_noalloc(const float *logits, int n, int k, float *values, int *ids, void *stream);
+
 /* Wait for queued work; returns any device-side error. */
 int g4_sync(g4_ctx *ctx);
 

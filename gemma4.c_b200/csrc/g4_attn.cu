@@ -15,48 +15,9 @@
 // The softmax is computed online (running max and rescaled sum, the same
 // recurrence the reference uses) in a different summation order, so outputs
 // match within floating-point tolerance, not bit-for-bit.
-#include "g4_common.cuh"
-#include "g4_internal.h"
+#include "g4_attn_dev.cuh"
 
 namespace {
-
-constexpr int kHeads = G4_HEADS;
-
-G4_DEV int first_key(int p, int window) { return (window && p + 1 > window) ? p + 1 - window : 0; }
-
-// RMS-normalise (optional weight) and rotate one head vector held in shared
-// memory by one warp. x has HD floats.
-template <int HD>
-G4_DEV void norm_rope_warp(float *x, const float *w, const float *cosr, const float *sinr, int pairs, bool rope,
-                           bool strict = false) {
-    const int lane = threadIdx.x & 31;
-    float v[HD / 32];
-    float ss = 0.0f;
-#pragma unroll
-    for (int i = 0; i < HD / 32; i++) {
-        v[i] = x[lane + 32 * i];
-        ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-    }
-    if (strict) {
-        // reference order (gemma4.c:367-368): one lane, index order
-        ss = lane == 0 ? seq_sumsq(x, HD) : 0.0f;
-        ss = __shfl_sync(0xffffffffu, ss, 0);
-    } else {
-        ss = warp_sum(ss);
-    }
-    const float inv = rms_inv(ss, (float)HD, 1e-6f);
-#pragma unroll
-    for (int i = 0; i < HD / 32; i++) x[lane + 32 * i] = rms_apply(v[i], inv, w ? w[lane + 32 * i] : 1.0f);
-    __syncwarp();
-    if (rope) {
-        for (int jj = lane; jj < pairs; jj += 32) {
-            const float a0 = x[jj], b0 = x[jj + HD / 2], c = cosr[jj], s = sinr[jj];
-            x[jj] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(b0, s));
-            x[jj + HD / 2] = __fadd_rn(__fmul_rn(b0, c), __fmul_rn(a0, s));
-        }
-    }
-    __syncwarp();
-}
 
 // ---------------------------------------------------------------------------
 // q/k/v post-processing for a chunk of T tokens (prefill and small-T decode):
@@ -83,212 +44,27 @@ __global__ void __launch_bounds__(32) k_qkv_post(const AttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Decode (T = 1) split-KV attention. Every CTA post-processes q (all heads)
-// and, on layers that own the cache, the new k/v; CTA 0 writes k/v to the
-// ring, and every CTA uses its own copy for key == pos. CTA c covers a slice of
-// the visible keys (at least kMinSplit keys per slice) and writes (max, sum,
-// unnormalised output) per head. K/V tiles stream through a double-buffered
-// cp.async pipeline; warp h owns query head h, lanes own keys for the scores
-// and output dimensions for the value sum.
-constexpr int kTile = 32;
-constexpr int kMinSplit = 64;
-
-G4_DEV void cp_async16(void *dst, const void *src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
-}
-G4_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-G4_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
-// Key range of split `s` for position p; returns the number of active splits.
-G4_DEV int split_range(int p, int window, int splits, int s, int *k0, int *k1) {
-    const int kf = first_key(p, window), nk = p + 1 - kf;
-    int per = (nk + splits - 1) / splits;
-    per = per < kMinSplit ? kMinSplit : (per + 31) / 32 * 32;
-    *k0 = kf + s * per;
-    *k1 = min(p + 1, *k0 + per);
-    return (nk + per - 1) / per;
-}
-
+// Standalone decode kernels (one launch each) around the shared bodies.
 template <int HD>
 struct DecodeCfg {
-    static constexpr int KT = HD == 512 ? 16 : 32;   // keys per tile
-    static constexpr int LPK = 32 / KT;              // lanes per key in the score phase
-    static constexpr int KS = HD + 4;                // padded K row (floats)
-    static constexpr size_t smem = (size_t)(kHeads * HD + 2 * HD + 2 * KT * KS + 2 * KT * HD) * 4;
+    static constexpr int KT = DecodeKT<HD>::value;
+    static constexpr size_t smem = (size_t)decode_smem_floats(HD, KT) * 4;
 };
 
 template <int HD>
 __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a, int splits) {
-    using Cfg = DecodeCfg<HD>;
-    constexpr int KT = Cfg::KT, LPK = Cfg::LPK, KS = Cfg::KS;
     extern __shared__ __align__(16) float sm[];
-    float *qn = sm;                       // [8][HD]
-    float *kn = qn + kHeads * HD;         // [HD]
-    float *vn = kn + HD;                  // [HD]
-    float *Ks = vn + HD;                  // [2][KT][KS]
-    float *Vs = Ks + 2 * KT * KS;         // [2][KT][HD]
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
     griddep_launch();
     griddep_wait();
-    const int p = a.pos_dev ? *a.pos_dev : a.start_pos;
-    int k0, k1;
-    const int active = split_range(p, a.window, splits, blockIdx.x, &k0, &k1);
-    if ((int)blockIdx.x >= active) return;
-
-    // start streaming the first tile before the q/k/v post-processing
-    auto issue = [&](int tile, int buf) {
-        const int kt = k0 + tile * KT, nt = min(KT, k1 - kt);
-        for (int idx = threadIdx.x; idx < nt * (HD / 4); idx += 256) {
-            const int r = idx / (HD / 4), c4 = idx - r * (HD / 4);
-            const size_t slot = (size_t)((kt + r) & a.mask) * HD;
-            cp_async16(&Ks[(buf * KT + r) * KS + c4 * 4], a.kcache + slot + c4 * 4);
-            cp_async16(&Vs[(buf * KT + r) * HD + c4 * 4], a.vcache + slot + c4 * 4);
-        }
-        cp_async_commit();
-    };
-    const int ntiles = k1 > k0 ? (k1 - k0 + KT - 1) / KT : 0;
-    if (ntiles > 0) issue(0, 0);
-
-    const float *cosr = a.rope_cos + (size_t)p * a.pairs, *sinr = a.rope_sin + (size_t)p * a.pairs;
-    for (int i = lane; i < HD; i += 32) qn[warp * HD + i] = a.qkv[warp * HD + i];
-    __syncwarp();
-    norm_rope_warp<HD>(qn + warp * HD, a.q_norm, cosr, sinr, a.pairs, true);
-    if (a.has_kv && warp < 2) {
-        float *x = warp == 0 ? kn : vn;
-        const float *src = a.qkv + kHeads * HD + warp * HD;
-        for (int i = lane; i < HD; i += 32) x[i] = src[i];
-        __syncwarp();
-        norm_rope_warp<HD>(x, warp == 0 ? a.k_norm : nullptr, cosr, sinr, a.pairs, warp == 0);
-        if (blockIdx.x == 0) {
-            float *dst = (warp == 0 ? a.kcache : a.vcache) + (size_t)(p & a.mask) * HD;
-            for (int i = lane; i < HD; i += 32) dst[i] = x[i];
-        }
-    }
-    if ((int)blockIdx.x >= active) return;   // CTA 0 of an idle split only wrote the cache
-    __syncthreads();
-
-    constexpr int NV = HD / 128;   // float4 output slices per lane
-    float4 o[NV];
-#pragma unroll
-    for (int i = 0; i < NV; i++) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    float m = -INFINITY, l = 0.0f;
-    const float *q = qn + warp * HD;
-    const int key_lane = lane % KT, dpart = lane / KT;   // score phase: key and dimension part
-
-    for (int t = 0; t < ntiles; t++) {
-        const int buf = t & 1, kt = k0 + t * KT, nt = min(KT, k1 - kt);
-        if (t + 1 < ntiles) {
-            issue(t + 1, buf ^ 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
-        float *Kb = Ks + buf * KT * KS, *Vb = Vs + buf * KT * HD;
-        if (a.has_kv && p >= kt && p < kt + nt) {
-            // the new key/value: use this CTA's copy (CTA 0 may still be writing the ring slot)
-            const int r = p - kt;
-            for (int i = threadIdx.x; i < HD; i += 256) {
-                Kb[r * KS + i] = kn[i];
-                Vb[r * HD + i] = vn[i];
-            }
-            __syncthreads();
-        }
-        // scores: LPK lanes per key, each over HD/LPK dimensions
-        float s = -INFINITY;
-        {
-            const float *kr = Kb + key_lane * KS + dpart * (HD / LPK);
-            const float *qq = q + dpart * (HD / LPK);
-            float acc = 0.0f;
-#pragma unroll 8
-            for (int d = 0; d < HD / LPK; d += 4) {
-                const float4 a4 = *(const float4 *)&qq[d], k4 = *(const float4 *)&kr[d];
-                acc = fmaf(a4.x, k4.x, acc);
-                acc = fmaf(a4.y, k4.y, acc);
-                acc = fmaf(a4.z, k4.z, acc);
-                acc = fmaf(a4.w, k4.w, acc);
-            }
-            if (LPK == 2) acc += __shfl_xor_sync(0xffffffffu, acc, 16);
-            if (key_lane < nt) s = acc;
-        }
-        const float mt = warp_max(s);
-        const float mn = fmaxf(m, mt);
-        const float corr = (m == -INFINITY) ? 0.0f : expf(m - mn);
-        const float pj = (key_lane < nt && dpart == 0) ? expf(s - mn) : 0.0f;
-        l = l * corr + warp_sum(pj);
-        m = mn;
-#pragma unroll
-        for (int i = 0; i < NV; i++) {
-            o[i].x *= corr; o[i].y *= corr; o[i].z *= corr; o[i].w *= corr;
-        }
-        for (int jk = 0; jk < nt; jk++) {
-            const float pk = __shfl_sync(0xffffffffu, pj, jk);
-            const float *vr = Vb + jk * HD + 4 * lane;
-#pragma unroll
-            for (int i = 0; i < NV; i++) {
-                const float4 vv = *(const float4 *)&vr[128 * i];
-                o[i].x = fmaf(pk, vv.x, o[i].x);
-                o[i].y = fmaf(pk, vv.y, o[i].y);
-                o[i].z = fmaf(pk, vv.z, o[i].z);
-                o[i].w = fmaf(pk, vv.w, o[i].w);
-            }
-        }
-        __syncthreads();
-    }
-    float *part = a.part + ((size_t)blockIdx.x * kHeads + warp) * (HD + 4);
-    if (lane == 0) {
-        part[0] = m;
-        part[1] = l;
-    }
-#pragma unroll
-    for (int i = 0; i < NV; i++) *(float4 *)&part[4 + 4 * lane + 128 * i] = o[i];
+    attn_decode_split<HD, DecodeCfg<HD>::KT>(a, blockIdx.x, splits, sm);
 }
 
-// Combine the active split partials into the attention output and quantise it
-// for o_proj (gemma4.c:459). grid = 8*HD/256 CTAs of 256 threads; thread = one
-// output dimension.
 template <int HD>
 __global__ void __launch_bounds__(256) k_attn_combine(const AttnArgs a, int splits) {
-    __shared__ float wsm[256];
-    __shared__ float red[8];
-    __shared__ float tot;
+    __shared__ float wsm[256 + 16];
     griddep_launch();
     griddep_wait();
-    const int p = a.pos_dev ? *a.pos_dev : a.start_pos;
-    int k0, k1;
-    const int active = split_range(p, a.window, splits, 0, &k0, &k1);
-    const int per_head = HD / 256;
-    const int h = blockIdx.x / per_head, d = (blockIdx.x % per_head) * 256 + threadIdx.x;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const size_t stride = (size_t)kHeads * (HD + 4);
-    const float *ph = a.part + (size_t)h * (HD + 4);
-    if (threadIdx.x == 0) {
-        float mx = -INFINITY;
-        for (int s = 0; s < active; s++) mx = fmaxf(mx, ph[s * stride]);
-        float lsum = 0.0f;
-        for (int s = 0; s < active; s++) {
-            const float w = ph[s * stride] == -INFINITY ? 0.0f : expf(ph[s * stride] - mx);
-            wsm[s] = w;
-            lsum += w * ph[s * stride + 1];
-        }
-        tot = lsum;
-    }
-    __syncthreads();
-    float o = 0.0f;
-    for (int s = 0; s < active; s++) o = fmaf(wsm[s], ph[s * stride + 4 + d], o);
-    o = o / tot;
-    const int col = h * HD + d;
-    a.out[col] = o;
-    // dynamic int8 quantisation of the 64-wide group this thread belongs to
-    float amax = warp_max(fabsf(o));
-    if (lane == 0) red[warp] = amax;
-    __syncthreads();
-    amax = fmaxf(red[warp & ~1], red[warp | 1]);
-    const float sc = quant_scale(amax), inv = quant_inv(sc);
-    a.xq[col] = (int8_t)quant_one(o, inv);
-    if ((threadIdx.x & 63) == 0) a.xs[col >> 6] = sc;
+    attn_combine_part<HD>(a, blockIdx.x, splits, wsm);
 }
 
 // ---------------------------------------------------------------------------
@@ -360,6 +136,7 @@ __global__ void __launch_bounds__(256) k_attn_strict(const AttnArgs a) {
 // Prefill attention: CTA = 4 query tokens x 8 heads (32 rows) against key
 // tiles of 32, FP32 SIMT with online softmax. q must already be normalised and
 // rotated (k_qkv_post) and the chunk's keys already in the ring.
+constexpr int kTile = 32;             // keys per tile
 constexpr int kQT = 4;               // tokens per CTA
 constexpr int kRows = kQT * kHeads;  // 32 query rows
 

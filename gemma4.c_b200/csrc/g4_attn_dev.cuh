@@ -1,0 +1,257 @@
+// g4_attn_dev.cuh — attention device building blocks shared by the
+// standalone attention kernels (g4_attn.cu) and the persistent decode kernel
+// (g4_decode.cu).
+//
+// Reference: attention (gemma4.c:411-461), attention_scores (:281-294),
+// softmax (:400-408), weighted_value_sum (:296-307), rmsnorm of q/k/v
+// (:427,437,439) and apply_rope (:381-398).
+#pragma once
+#include "g4_common.cuh"
+#include "g4_internal.h"
+
+namespace {
+
+constexpr int kHeads = G4_HEADS;
+
+G4_DEV int first_key(int p, int window) { return (window && p + 1 > window) ? p + 1 - window : 0; }
+
+// RMS-normalise (optional weight) and rotate one head vector held in shared
+// memory by one warp. x has HD floats.
+template <int HD>
+G4_DEV void norm_rope_warp(float *x, const float *w, const float *cosr, const float *sinr, int pairs, bool rope,
+                           bool strict = false) {
+    const int lane = threadIdx.x & 31;
+    float v[HD / 32];
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < HD / 32; i++) {
+        v[i] = x[lane + 32 * i];
+        ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    }
+    if (strict) {
+        // reference order (gemma4.c:367-368): one lane, index order
+        ss = lane == 0 ? seq_sumsq(x, HD) : 0.0f;
+        ss = __shfl_sync(0xffffffffu, ss, 0);
+    } else {
+        ss = warp_sum(ss);
+    }
+    const float inv = rms_inv(ss, (float)HD, 1e-6f);
+#pragma unroll
+    for (int i = 0; i < HD / 32; i++) x[lane + 32 * i] = rms_apply(v[i], inv, w ? w[lane + 32 * i] : 1.0f);
+    __syncwarp();
+    if (rope) {
+        for (int jj = lane; jj < pairs; jj += 32) {
+            const float a0 = x[jj], b0 = x[jj + HD / 2], c = cosr[jj], s = sinr[jj];
+            x[jj] = __fsub_rn(__fmul_rn(a0, c), __fmul_rn(b0, s));
+            x[jj + HD / 2] = __fadd_rn(__fmul_rn(b0, c), __fmul_rn(a0, s));
+        }
+    }
+    __syncwarp();
+}
+
+
+constexpr int kMinSplit = 64;
+constexpr int kAttnThreads = 256;   // 8 warps: warp h owns query head h
+
+G4_DEV void attn_sync() { bar_sync(1, kAttnThreads); }
+
+G4_DEV void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+G4_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+G4_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Key range of split `s` for position p; returns the number of active splits.
+G4_DEV int split_range(int p, int window, int splits, int s, int *k0, int *k1) {
+    const int kf = first_key(p, window), nk = p + 1 - kf;
+    int per = (nk + splits - 1) / splits;
+    per = per < kMinSplit ? kMinSplit : (per + 31) / 32 * 32;
+    *k0 = kf + s * per;
+    *k1 = min(p + 1, *k0 + per);
+    return (nk + per - 1) / per;
+}
+
+// Keys per decode tile. The standalone decode kernel and the persistent decode
+// kernel use the same tile so that both give the same bits (the score lanes per
+// key and the online-softmax tile steps follow KT).
+template <int HD>
+struct DecodeKT {
+    static constexpr int value = HD == 512 ? 8 : 16;
+};
+
+// Shared-memory floats of one decode split with KT-key tiles (double buffered).
+__host__ __device__ constexpr int decode_smem_floats(int hd, int kt) {
+    return kHeads * hd + 2 * hd + 2 * kt * (hd + 4) + 2 * kt * hd;
+}
+
+// Decode (T = 1) split-KV attention for split `split` of `splits`, run by 256
+// threads (8 warps; warp h = query head h). The CTA post-processes q (all
+// heads) and, on layers that own the cache, the new k/v; CTA 0 of the grid
+// writes k/v to the ring, and every CTA uses its own copy for key == pos.
+// K/V tiles of KT keys stream through a double-buffered cp.async pipeline.
+// Writes (max, sum, unnormalised output) per head to a.part.
+template <int HD, int KT>
+G4_DEV void attn_decode_split(const AttnArgs &a, int split, int splits, float *sm) {
+    constexpr int LPK = 32 / KT, KS = HD + 4;
+    float *qn = sm;                       // [8][HD]
+    float *kn = qn + kHeads * HD;         // [HD]
+    float *vn = kn + HD;                  // [HD]
+    float *Ks = vn + HD;                  // [2][KT][KS]
+    float *Vs = Ks + 2 * KT * KS;         // [2][KT][HD]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int p = a.pos_dev ? *a.pos_dev : a.start_pos;
+    int k0, k1;
+    const int active = split_range(p, a.window, splits, split, &k0, &k1);
+    if (split >= active) return;
+
+    auto issue = [&](int tile, int buf) {
+        const int kt = k0 + tile * KT, nt = min(KT, k1 - kt);
+        for (int idx = tid; idx < nt * (HD / 4); idx += kAttnThreads) {
+            const int r = idx / (HD / 4), c4 = idx - r * (HD / 4);
+            const size_t slot = (size_t)((kt + r) & a.mask) * HD;
+            cp_async16(&Ks[(buf * KT + r) * KS + c4 * 4], a.kcache + slot + c4 * 4);
+            cp_async16(&Vs[(buf * KT + r) * HD + c4 * 4], a.vcache + slot + c4 * 4);
+        }
+        cp_async_commit();
+    };
+    const int ntiles = k1 > k0 ? (k1 - k0 + KT - 1) / KT : 0;
+    if (ntiles > 0) issue(0, 0);
+
+    const float *cosr = a.rope_cos + (size_t)p * a.pairs, *sinr = a.rope_sin + (size_t)p * a.pairs;
+    for (int i = lane; i < HD; i += 32) qn[warp * HD + i] = a.qkv[warp * HD + i];
+    __syncwarp();
+    norm_rope_warp<HD>(qn + warp * HD, a.q_norm, cosr, sinr, a.pairs, true);
+    if (a.has_kv && warp < 2) {
+        float *x = warp == 0 ? kn : vn;
+        const float *src = a.qkv + kHeads * HD + warp * HD;
+        for (int i = lane; i < HD; i += 32) x[i] = src[i];
+        __syncwarp();
+        norm_rope_warp<HD>(x, warp == 0 ? a.k_norm : nullptr, cosr, sinr, a.pairs, warp == 0);
+        if (split == 0) {
+            float *dst = (warp == 0 ? a.kcache : a.vcache) + (size_t)(p & a.mask) * HD;
+            for (int i = lane; i < HD; i += 32) dst[i] = x[i];
+        }
+    }
+    attn_sync();
+
+    constexpr int NV = HD / 128;   // float4 output slices per lane
+    float4 o[NV];
+#pragma unroll
+    for (int i = 0; i < NV; i++) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float m = -INFINITY, l = 0.0f;
+    const float *q = qn + warp * HD;
+    const int key_lane = lane % KT, dpart = lane / KT;   // score phase: key and dimension part
+
+    for (int t = 0; t < ntiles; t++) {
+        const int buf = t & 1, kt = k0 + t * KT, nt = min(KT, k1 - kt);
+        if (t + 1 < ntiles) {
+            issue(t + 1, buf ^ 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        attn_sync();
+        float *Kb = Ks + buf * KT * KS, *Vb = Vs + buf * KT * HD;
+        if (a.has_kv && p >= kt && p < kt + nt) {
+            // the new key/value: this CTA's copy (CTA 0 may still be writing the ring slot)
+            const int r = p - kt;
+            for (int i = tid; i < HD; i += kAttnThreads) {
+                Kb[r * KS + i] = kn[i];
+                Vb[r * HD + i] = vn[i];
+            }
+            attn_sync();
+        }
+        float s = -INFINITY;
+        {
+            const float *kr = Kb + key_lane * KS + dpart * (HD / LPK);
+            const float *qq = q + dpart * (HD / LPK);
+            float acc = 0.0f;
+#pragma unroll 8
+            for (int d = 0; d < HD / LPK; d += 4) {
+                const float4 a4 = *(const float4 *)&qq[d], k4 = *(const float4 *)&kr[d];
+                acc = fmaf(a4.x, k4.x, acc);
+                acc = fmaf(a4.y, k4.y, acc);
+                acc = fmaf(a4.z, k4.z, acc);
+                acc = fmaf(a4.w, k4.w, acc);
+            }
+#pragma unroll
+            for (int off = KT; off < 32; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+            if (key_lane < nt) s = acc;
+        }
+        const float mt = warp_max(s);
+        const float mn = fmaxf(m, mt);
+        const float corr = (m == -INFINITY) ? 0.0f : expf(m - mn);
+        const float pj = (key_lane < nt && dpart == 0) ? expf(s - mn) : 0.0f;
+        l = l * corr + warp_sum(pj);
+        m = mn;
+#pragma unroll
+        for (int i = 0; i < NV; i++) {
+            o[i].x *= corr; o[i].y *= corr; o[i].z *= corr; o[i].w *= corr;
+        }
+        for (int jk = 0; jk < nt; jk++) {
+            const float pk = __shfl_sync(0xffffffffu, pj, jk);
+            const float *vr = Vb + jk * HD + 4 * lane;
+#pragma unroll
+            for (int i = 0; i < NV; i++) {
+                const float4 vv = *(const float4 *)&vr[128 * i];
+                o[i].x = fmaf(pk, vv.x, o[i].x);
+                o[i].y = fmaf(pk, vv.y, o[i].y);
+                o[i].z = fmaf(pk, vv.z, o[i].z);
+                o[i].w = fmaf(pk, vv.w, o[i].w);
+            }
+        }
+        attn_sync();
+    }
+    float *part = a.part + ((size_t)split * kHeads + warp) * (HD + 4);
+    if (lane == 0) {
+        part[0] = m;
+        part[1] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < NV; i++) *(float4 *)&part[4 + 4 * lane + 128 * i] = o[i];
+}
+
+// Combine the active split partials into the attention output for 256 output
+// dimensions (combine block `blk` of 8*HD/256) and quantise them for o_proj
+// (gemma4.c:459). 256 threads, thread = one dimension. smem: 256 + 16 floats.
+template <int HD>
+G4_DEV void attn_combine_part(const AttnArgs &a, int blk, int splits, float *wsm) {
+    float *red = wsm + 256;
+    const int tid = threadIdx.x;
+    const int p = a.pos_dev ? *a.pos_dev : a.start_pos;
+    int k0, k1;
+    const int active = split_range(p, a.window, splits, 0, &k0, &k1);
+    const int per_head = HD / 256;
+    const int h = blk / per_head, d = (blk % per_head) * 256 + tid;
+    const int warp = tid >> 5, lane = tid & 31;
+    const size_t stride = (size_t)kHeads * (HD + 4);
+    const float *ph = a.part + (size_t)h * (HD + 4);
+    if (tid == 0) {
+        float mx = -INFINITY;
+        for (int s = 0; s < active; s++) mx = fmaxf(mx, ph[s * stride]);
+        float lsum = 0.0f;
+        for (int s = 0; s < active; s++) {
+            const float w = ph[s * stride] == -INFINITY ? 0.0f : expf(ph[s * stride] - mx);
+            wsm[s] = w;
+            lsum += w * ph[s * stride + 1];
+        }
+        red[8] = lsum;
+    }
+    attn_sync();
+    float o = 0.0f;
+    for (int s = 0; s < active; s++) o = fmaf(wsm[s], ph[s * stride + 4 + d], o);
+    o = o / red[8];
+    const int col = h * HD + d;
+    a.out[col] = o;
+    float amax = warp_max(fabsf(o));
+    if (lane == 0) red[warp] = amax;
+    attn_sync();
+    amax = fmaxf(red[warp & ~1], red[warp | 1]);
+    const float sc = quant_scale(amax), inv = quant_inv(sc);
+    a.xq[col] = (int8_t)quant_one(o, inv);
+    if ((tid & 63) == 0) a.xs[col >> 6] = sc;
+    attn_sync();
+}
+
+}  // namespace

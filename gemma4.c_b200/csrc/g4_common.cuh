@@ -74,6 +74,16 @@ G4_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
     return true;
 }
 
+// After a failed wait: give the bulk copies this CTA issued (stages
+// [0, issued), one single-use barrier each) time to land, bounded by one
+// overall deadline, so that none still writes shared memory when the CTA exits.
+G4_DEV void drain_stages(uint64_t *full, int issued) {
+    const uint64_t t0 = g4_globaltimer();
+    for (int c = 0; c < issued; c++)
+        while (!mbar_try_wait(&full[c], 0))
+            if (g4_globaltimer() - t0 > G4_WAIT_NS) return;
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` (bytes, 16-B multiples,
 // both addresses 16-B aligned). Weights are streamed once per token, so they are
 // marked evict-first in L2.

@@ -83,6 +83,14 @@ struct g4_ctx {
     int graph_cur = 0;
     bool decode_warm = false;
     cudaEvent_t events[16] = {};
+    // persistent single-token decode (g4_decode.cu)
+    bool persistent = false;         // G4_OPT_PERSISTENT
+    bool pending = false;            // a single-token forward waiting to be launched
+    DecodeOp *dec_fwd = nullptr, *dec_fwdlog = nullptr;
+    int n_fwd = 0, n_fwdlog = 0, dec_cur = 0, dec_layers = 0;
+    unsigned long long *bar = nullptr, *bar_base = nullptr;
+    std::vector<DecodeOp> dec_host;          // host copy of the forward+logits op list
+    unsigned long long *trace = nullptr;     // timeline buffer (g4_trace_decode)
     char msg[512] = {0};
 };
 
@@ -367,6 +375,7 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
         {(void **)&c->err, 64},
         {(void **)&c->tokens_d, (size_t)kMaxT * 4},
         {(void **)&c->pos_d, 64},
+        {(void **)&c->bar, 64},
     };
     size_t st_total = 0;
     for (auto &b : bufs) st_total += (b.bytes + 255) & ~(size_t)255;
@@ -394,6 +403,7 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
         }
         Y.vcache = Y.kcache + (size_t)Y.ring * Y.hd;
     }
+    c->bar_base = c->bar + 1;
     CK(cudaStreamSynchronize(c->st));
     return G4_OK;
 }
@@ -416,6 +426,7 @@ struct Seq {
     bool pdl;
     cudaError_t e = cudaSuccess;
     Prof *prof = nullptr;
+    std::vector<DecodeOp> *rec = nullptr;   // record the sequence as persistent-decode ops
     int next_cls = 2;          // 0 int8 weight GEMV, 1 attention, 2 other
     double next_bytes = 0;
     void tag(int cls, double bytes) { next_cls = cls; next_bytes = bytes; }
@@ -445,6 +456,16 @@ GemvArgs gemv_base(g4_ctx *c, const DMat &m, int T) {
 }
 
 void gemv(Seq &q, GemvArgs &a, int pro, int epi) {
+    if (q.rec) {
+        DecodeOp op{};
+        op.type = OP_GEMV;
+        op.pro = pro;
+        op.epi = epi;
+        op.barrier = 1;
+        op.g = a;
+        q.rec->push_back(op);
+        return;
+    }
     q.tag(0, (double)a.m.N * a.m.K + (double)a.m.N * (a.m.K / 64) * 2);
     const int pairs = a.m.N / 2;
     const int grid = pairs < q.c->num_sms ? pairs : q.c->num_sms;
@@ -503,9 +524,11 @@ AttnArgs attn_base(g4_ctx *c, const Layer &Y, int T, int start_pos, const int *p
 
 // Decode path, T <= 4 tokens. pos_dev != NULL: positions and tokens come from
 // device memory (graph replay); otherwise from start_pos / tokens_d.
-cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev, Prof *prof = nullptr) {
+cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev, Prof *prof = nullptr,
+                          std::vector<DecodeOp> *rec = nullptr) {
     Seq q{c, c->use_pdl && !prof};
     q.prof = prof;
+    q.rec = rec;
     int cur = 0;
     const float emb_mult = sqrtf((float)G4_HIDDEN), ple_mult = sqrtf((float)G4_PLE);
     {
@@ -520,8 +543,21 @@ cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev, P
         a.out = c->pli;
         a.out_stride = G4_NUM_LAYERS * G4_PLE;
         gemv(q, a, PRO_EMBED_QUANT, EPI_STORE);
-        q.ck(g4_launch_ple_prep(c->pli, c->ple_emb, c->ple_norm, 1e-6f * G4_HIDDEN, 1.0f / sqrtf(2.0f), T, c->ple_u,
-                                c->st, q.pdl, c->strict));
+        if (rec) {
+            DecodeOp op{};
+            op.type = OP_PLE_PREP;
+            op.barrier = 0;   // ple_u is first read by layer 0's per-layer gate, several barriers later
+            op.pli = c->pli;
+            op.ple_emb = c->ple_emb;
+            op.ple_norm = c->ple_norm;
+            op.ple_eps = 1e-6f * G4_HIDDEN;
+            op.ple_scale = 1.0f / sqrtf(2.0f);
+            op.ple_u = c->ple_u;
+            rec->push_back(op);
+        } else {
+            q.ck(g4_launch_ple_prep(c->pli, c->ple_emb, c->ple_norm, 1e-6f * G4_HIDDEN, 1.0f / sqrtf(2.0f), T,
+                                    c->ple_u, c->st, q.pdl, c->strict));
+        }
     }
     for (int l = 0; l < c->layers; l++) {
         const Layer &Y = c->L[l];
@@ -550,7 +586,15 @@ cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev, P
         // attention
         AttnArgs at = attn_base(c, Y, T, start_pos, pos_dev);
         const bool fused_decode = T == 1 && !c->strict;
-        if (fused_decode) {
+        if (fused_decode && rec) {
+            DecodeOp op{};
+            op.type = OP_ATTN;
+            op.barrier = 1;
+            op.at = at;
+            rec->push_back(op);
+            op.type = OP_COMBINE;
+            rec->push_back(op);
+        } else if (fused_decode) {
             const int p = start_pos, kf = Y.global ? 0 : (p + 1 > G4_SLIDING_WINDOW ? p + 1 - G4_SLIDING_WINDOW : 0);
             q.tag(1, (double)(p + 1 - kf) * Y.hd * 8);
             q.ck(g4_launch_attn_decode(at, kSplits, c->st, q.pdl));
@@ -625,8 +669,19 @@ cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev, P
         }
     }
     const Layer &Z = c->L[c->layers - 1];
-    q.ck(g4_launch_rows_norm(3, c->h, T, Z.post_ple, c->res[cur], c->res[cur ^ 1], Z.scalar, nullptr, G4_RMS_EPS,
-                             nullptr, nullptr, c->st, q.pdl, nullptr, c->strict));
+    if (rec) {
+        DecodeOp op{};
+        op.type = OP_FINISH;
+        op.fin_h = c->h;
+        op.fin_w = Z.post_ple;
+        op.fin_res_in = c->res[cur];
+        op.fin_res_out = c->res[cur ^ 1];
+        op.fin_scalar = Z.scalar;
+        rec->push_back(op);
+    } else {
+        q.ck(g4_launch_rows_norm(3, c->h, T, Z.post_ple, c->res[cur], c->res[cur ^ 1], Z.scalar, nullptr, G4_RMS_EPS,
+                                 nullptr, nullptr, c->st, q.pdl, nullptr, c->strict));
+    }
     cur ^= 1;
     c->cur = cur;
     return q.e;
@@ -679,6 +734,87 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos) {
     return q.e;
 }
 
+// Record the single-token step as persistent-decode op lists (forward only, and
+// forward + logits of row 0) and upload them; called once the context exists.
+void free_decode(g4_ctx *c) {
+    if (c->dec_fwd) cudaFree(c->dec_fwd);
+    if (c->dec_fwdlog) cudaFree(c->dec_fwdlog);
+    c->dec_fwd = c->dec_fwdlog = nullptr;
+    c->n_fwd = c->n_fwdlog = 0;
+    c->dec_layers = 0;
+    c->dec_host.clear();
+    if (c->trace) cudaFree(c->trace);
+    c->trace = nullptr;
+}
+
+int build_decode(g4_ctx *c) {
+    if (c->dec_fwd && c->dec_layers == c->layers) return G4_OK;
+    free_decode(c);
+    std::vector<DecodeOp> ops;
+    const int cur_save = c->cur;
+    cudaError_t e = enqueue_small(c, 1, 0, c->pos_d, nullptr, &ops);
+    c->dec_cur = c->cur;
+    c->cur = cur_save;
+    if (e) return fail(c, G4_ERR_CUDA, "decode op list: %s", cudaGetErrorString(e));
+    ops.back().barrier = 0;
+    std::vector<DecodeOp> withlog(ops);
+    // replace the last residual update by the lm_head GEMV whose prologue performs it
+    const DecodeOp fin = withlog.back();
+    DecodeOp lm{};
+    lm.type = OP_GEMV;
+    lm.pro = PRO_RES_NORM_QUANT;
+    lm.epi = EPI_LOGITS;
+    lm.g = gemv_base(c, c->embed, 1);
+    lm.g.src = fin.fin_h;
+    lm.g.src_stride = G4_HIDDEN;
+    lm.g.w_post = fin.fin_w;
+    lm.g.scalar = fin.fin_scalar;
+    lm.g.res_in = fin.fin_res_in;
+    lm.g.res_out = fin.fin_res_out;
+    lm.g.w_pre = c->final_norm;
+    lm.g.out = c->logits;
+    lm.g.out_stride = G4_VOCAB;
+    lm.g.argmax_part = c->argmax_part;
+    lm.g.argmax_out = c->argmax_out;
+    lm.g.ticket = c->ticket;
+    withlog.back() = lm;
+    if (g4_decode_max_stages(ops.data(), (int)ops.size(), c->num_sms) > (1 << 20) ||
+        g4_decode_max_stages(withlog.data(), (int)withlog.size(), c->num_sms) > (1 << 20) || c->num_sms < kSplits) {
+        c->persistent = false;   // geometry outside the persistent kernel's limits: keep the graph path
+        return G4_OK;
+    }
+    CK(cudaMalloc(&c->dec_fwd, ops.size() * sizeof(DecodeOp)));
+    CK(cudaMalloc(&c->dec_fwdlog, withlog.size() * sizeof(DecodeOp)));
+    CK(cudaMemcpy(c->dec_fwd, ops.data(), ops.size() * sizeof(DecodeOp), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(c->dec_fwdlog, withlog.data(), withlog.size() * sizeof(DecodeOp), cudaMemcpyHostToDevice));
+    c->n_fwd = (int)ops.size();
+    c->n_fwdlog = (int)withlog.size();
+    c->dec_layers = c->layers;
+    c->dec_host = withlog;
+    return G4_OK;
+}
+
+cudaError_t launch_decode(g4_ctx *c, bool with_logits, unsigned long long *trace = nullptr) {
+    DecodeParams p{};
+    p.trace = trace;
+    p.ops = with_logits ? c->dec_fwdlog : c->dec_fwd;
+    p.nops = with_logits ? c->n_fwdlog : c->n_fwd;
+    p.splits = kSplits;
+    p.bar = c->bar;
+    p.bar_base = c->bar_base;
+    p.err = c->err;
+    return g4_launch_decode(p, c->num_sms, c->st);
+}
+
+// Launch a deferred single-token forward on its own (without logits).
+int flush_pending(g4_ctx *c) {
+    if (!c->pending) return G4_OK;
+    c->pending = false;
+    cudaError_t e = launch_decode(c, false);
+    if (e) return fail(c, G4_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
+    return G4_OK;
+}
+
 int check_device_error(g4_ctx *c) {
     int e = 0;
     cudaError_t ce = cudaMemcpyAsync(&e, c->err, 4, cudaMemcpyDeviceToHost, c->st);
@@ -686,6 +822,7 @@ int check_device_error(g4_ctx *c) {
     if (ce != cudaSuccess) return fail(c, G4_ERR_CUDA, "device: %s", cudaGetErrorString(ce));
     if (e) {
         cudaMemsetAsync(c->err, 0, 4, c->st);
+        if (c->bar) cudaMemsetAsync(c->bar, 0, 16, c->st);   // a failed persistent step leaves them uneven
         cudaStreamSynchronize(c->st);
         const int code = e & 0xff;
         const char *what = code == G4D_BAD_TOKEN ? "token id outside the vocabulary"
@@ -757,7 +894,9 @@ int g4_open_file(const char *path, int device, g4_ctx **out) {
 
 int g4_close(g4_ctx *c) {
     if (!c) return G4_ERR_INVALID;
+    flush_pending(c);
     if (c->st) cudaStreamSynchronize(c->st);
+    free_decode(c);
     if (c->g_decode) cudaGraphExecDestroy(c->g_decode);
     for (int i = 0; i < 16; i++)
         if (c->events[i]) cudaEventDestroy(c->events[i]);
@@ -772,7 +911,10 @@ int g4_close(g4_ctx *c) {
 
 int g4_set_option(g4_ctx *c, int option, int value) {
     if (!c) return G4_ERR_INVALID;
+    int rc = flush_pending(c);
+    if (rc) return rc;
     switch (option) {
+    case G4_OPT_PERSISTENT: c->persistent = value != 0; break;
     case G4_OPT_GRAPHS: c->use_graph = value != 0; break;
     case G4_OPT_PDL:
         c->use_pdl = value != 0;
@@ -784,6 +926,8 @@ int g4_set_option(g4_ctx *c, int option, int value) {
         if (value < 1 || value > G4_NUM_LAYERS) return fail(c, G4_ERR_INVALID, "layers %d out of range", value);
         c->layers = value;
         if (c->g_decode) { cudaGraphExecDestroy(c->g_decode); c->g_decode = nullptr; }
+        CK(cudaStreamSynchronize(c->st));
+        free_decode(c);
         break;
     default: return fail(c, G4_ERR_INVALID, "unknown option %d", option);
     }
@@ -798,7 +942,13 @@ int g4_forward(g4_ctx *c, const int *tokens, size_t count, int start_pos) {
     for (size_t i = 0; i < count; i++)
         if (tokens[i] < 0 || tokens[i] >= G4_VOCAB) return fail(c, G4_ERR_INVALID, "forward: token %d out of range", tokens[i]);
     cudaSetDevice(c->device);
+    int rc = flush_pending(c);
+    if (rc) return rc;
     const int T = (int)count;
+    if (T == 1 && c->persistent && !c->strict) {
+        rc = build_decode(c);
+        if (rc) return rc;
+    }
     if (c->strict) {
         const size_t need = (size_t)T * G4_HEADS * ((size_t)start_pos + T) * 4;
         if (need > c->scores_cap) {
@@ -812,7 +962,12 @@ int g4_forward(g4_ctx *c, const int *tokens, size_t count, int start_pos) {
     }
     CK(cudaMemcpyAsync(c->tokens_d, tokens, count * 4, cudaMemcpyHostToDevice, c->st));
     cudaError_t e;
-    if (T == 1 && c->use_graph && !c->strict) {
+    if (T == 1 && c->persistent && !c->strict) {
+        // deferred: launched by the next call, fused with the lm_head when that call is g4_logits
+        CK(cudaMemcpyAsync(c->pos_d, &start_pos, 4, cudaMemcpyHostToDevice, c->st));
+        c->pending = true;
+        c->cur = c->dec_cur;
+    } else if (T == 1 && c->use_graph && !c->strict) {
         CK(cudaMemcpyAsync(c->pos_d, &start_pos, 4, cudaMemcpyHostToDevice, c->st));
         if (!c->g_decode) {
             if (!c->decode_warm) {
@@ -871,6 +1026,16 @@ int g4_logits(g4_ctx *c, size_t row, float *out, int *argmax) {
     if (c->last_T == 0 || row >= (size_t)c->last_T)
         return fail(c, G4_ERR_STATE, "logits: row %zu not computed by the last forward (%d rows)", row, c->last_T);
     cudaSetDevice(c->device);
+    if (c->pending) {
+        // one persistent launch: the deferred single-token forward and its logits
+        c->pending = false;
+        cudaError_t e = launch_decode(c, true);
+        if (e) return fail(c, G4_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
+        if (!out && !argmax) return G4_OK;
+        if (out) CK(cudaMemcpyAsync(out, c->logits, (size_t)G4_VOCAB * 4, cudaMemcpyDeviceToHost, c->st));
+        if (argmax) CK(cudaMemcpyAsync(argmax, c->argmax_out, 4, cudaMemcpyDeviceToHost, c->st));
+        return check_device_error(c);
+    }
     if (!out && !argmax) {
         // nothing to return: enqueue only (the reference benchmark discards logits, gemma4.c:641)
         cudaError_t e = enqueue_logits(c, row);
@@ -908,12 +1073,16 @@ int g4_topk(g4_ctx *c, size_t row, int k, float *values, int *ids) {
 int g4_sync(g4_ctx *c) {
     if (!c) return G4_ERR_INVALID;
     cudaSetDevice(c->device);
+    int rc = flush_pending(c);
+    if (rc) return rc;
     return check_device_error(c);
 }
 
 int g4_read_residual(g4_ctx *c, size_t rows, float *out) {
     if (!c || !out || rows > (size_t)kMaxT) return G4_ERR_INVALID;
     cudaSetDevice(c->device);
+    int rc = flush_pending(c);
+    if (rc) return rc;
     CK(cudaMemcpyAsync(out, c->res[c->cur], rows * G4_HIDDEN * 4, cudaMemcpyDeviceToHost, c->st));
     return check_device_error(c);
 }
@@ -923,15 +1092,23 @@ int g4_read_cache(g4_ctx *c, int layer, int which, int slot0, int nslots, float 
     const Layer &Y = c->L[layer];
     if (slot0 < 0 || slot0 + nslots > Y.ring) return G4_ERR_INVALID;
     cudaSetDevice(c->device);
+    int rc = flush_pending(c);
+    if (rc) return rc;
     const float *src = (which ? Y.vcache : Y.kcache) + (size_t)slot0 * Y.hd;
     CK(cudaMemcpyAsync(out, src, (size_t)nslots * Y.hd * 4, cudaMemcpyDeviceToHost, c->st));
     return check_device_error(c);
 }
 
-void *g4_stream(g4_ctx *c) { return c ? (void *)c->st : nullptr; }
+void *g4_stream(g4_ctx *c) {
+    if (!c) return nullptr;
+    flush_pending(c);   // work the caller enqueues next must follow the last forward
+    return (void *)c->st;
+}
 
 int g4_mark(g4_ctx *c, int slot) {
     if (!c || slot < 0 || slot >= 16) return G4_ERR_INVALID;
+    int rc = flush_pending(c);
+    if (rc) return rc;
     if (!c->events[slot]) CK(cudaEventCreate(&c->events[slot]));
     CK(cudaEventRecord(c->events[slot], c->st));
     return G4_OK;
@@ -944,10 +1121,76 @@ int g4_elapsed(g4_ctx *c, int a, int b, float *ms) {
     return G4_OK;
 }
 
+// Algorithmic bytes of one persistent-decode op at position pos.
+static double op_bytes(const g4_ctx *c, const DecodeOp &op, int pos) {
+    if (op.type == OP_GEMV) return (double)op.g.m.N * op.g.m.K + (double)op.g.m.N * (op.g.m.K / 64) * 2;
+    if (op.type == OP_ATTN) {
+        const int kf = op.at.window && pos + 1 > op.at.window ? pos + 1 - op.at.window : 0;
+        return (double)(pos + 1 - kf) * op.at.hd * 8;
+    }
+    (void)c;
+    return 0.0;
+}
+
+int g4_trace_decode(g4_ctx *c, int token, int pos, int cap, int *types, double *t_ns, int *nops) {
+    if (!c || !nops || token < 0 || token >= G4_VOCAB || pos < 0 || pos >= G4_MAX_CONTEXT || cap < 0 ||
+        (cap > 0 && (!types || !t_ns)))
+        return G4_ERR_INVALID;
+    cudaSetDevice(c->device);
+    if (int rc = flush_pending(c)) return rc;
+    if (!c->persistent || c->strict) return fail(c, G4_ERR_STATE, "trace: persistent decode is off");
+    if (int rc = build_decode(c)) return rc;
+    if (!c->persistent) return fail(c, G4_ERR_STATE, "trace: persistent decode unavailable on this device");
+    const int n = c->n_fwdlog;
+    const size_t tb = (size_t)(1 + 3 * n) * sizeof(unsigned long long);
+    if (!c->trace) CK(cudaMalloc(&c->trace, tb));
+    std::vector<unsigned long long> h(1 + 3 * n);
+    CK(cudaMemcpyAsync(c->tokens_d, &token, 4, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemcpyAsync(c->pos_d, &pos, 4, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemsetAsync(c->trace, 0, tb, c->st));
+    cudaError_t e = launch_decode(c, true, c->trace);
+    if (e) return fail(c, G4_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
+    c->last_T = 1;
+    c->cur = c->dec_cur;
+    CK(cudaMemcpyAsync(h.data(), c->trace, tb, cudaMemcpyDeviceToHost, c->st));
+    if (int rc = check_device_error(c)) return rc;
+    *nops = n;
+    for (int i = 0; i < n && i < cap; i++) {
+        types[i] = c->dec_host[i].type;
+        for (int k = 0; k < 3; k++) {
+            const unsigned long long t = h[1 + 3 * i + k];
+            t_ns[3 * i + k] = t ? (double)(t - h[0]) : -1.0;
+        }
+    }
+    return G4_OK;
+}
+
 int g4_profile_decode(g4_ctx *c, int token, int pos, float ms[3], double bytes[3], int launches[3]) {
     if (!c || !ms || !bytes || !launches || token < 0 || token >= G4_VOCAB || pos < 0 || pos >= G4_MAX_CONTEXT)
         return G4_ERR_INVALID;
     cudaSetDevice(c->device);
+    if (int rc0 = flush_pending(c)) return rc0;
+    if (c->persistent && !c->strict) {
+        // one traced persistent step: an op's time runs from the previous barrier exit to its own
+        if (int rc0 = build_decode(c)) return rc0;
+    }
+    if (c->persistent && !c->strict) {
+        std::vector<int> types(c->n_fwdlog);
+        std::vector<double> t(3 * (size_t)c->n_fwdlog);
+        int n = 0;
+        if (int rc0 = g4_trace_decode(c, token, pos, (int)types.size(), types.data(), t.data(), &n)) return rc0;
+        for (int k = 0; k < 3; k++) { ms[k] = 0; bytes[k] = 0; launches[k] = 0; }
+        double prev = 0.0;
+        for (int i = 0; i < n; i++) {
+            const int cls = types[i] == OP_GEMV ? 0 : (types[i] == OP_ATTN || types[i] == OP_COMBINE) ? 1 : 2;
+            const double end = t[3 * i + 2];
+            ms[cls] += (float)((end - prev) * 1e-6);
+            bytes[cls] += op_bytes(c, c->dec_host[i], pos);
+            launches[cls]++;
+            prev = end;
+        }
+        return G4_OK;
+    }
     Prof *pr = new Prof();
     for (int i = 0; i <= Prof::kMax; i++) cudaEventCreate(&pr->ev[i]);
     int rc = G4_OK;
@@ -978,7 +1221,7 @@ int g4_launches_per_token(g4_ctx *c, int *n) {
     if (!c || !n) return G4_ERR_INVALID;
     // embed/PLE GEMV + PLE prep, 7 kernels per layer (qkv, attention, combine,
     // o, gate|up, down, ple gate, ple proj => 8), final residual, logits
-    *n = 2 + 8 * c->layers + 1 + 1;
+    *n = (c->persistent && !c->strict) ? 1 : 2 + 8 * c->layers + 1 + 1;
     return G4_OK;
 }
 

@@ -1,0 +1,216 @@
+// g4_gemv_dev.cuh — device building blocks of the int8 GEMV consumers, shared
+// by the standalone decode GEMV (g4_gemv.cu) and the persistent decode kernel
+// (g4_decode.cu).
+//
+// Reference: quantize (gemma4.c:265-279), rmsnorm (:360-373), add_and_scale
+// (:375-378), embedding (:337-358), matmul_int8 (:192-262), geglu (:310-331),
+// logits soft-cap (:519) and greedy argmax (:537-541).
+#pragma once
+#include "g4_common.cuh"
+#include "g4_internal.h"
+
+namespace {
+
+constexpr int kWarps = 8;                   // consumer warps
+constexpr int kConsumers = kWarps * 32;
+
+// rows per weight stage: whole rows, an even number, ~16 KB
+__host__ __device__ inline int stage_rows(int K) {
+    int r = (16384 / K) & ~1;
+    return r < 2 ? 2 : r;
+}
+
+G4_DEV void csync() { bar_sync(1, kConsumers); }   // consumer-only barrier
+
+// Sum over the consumer threads; every consumer gets the result.
+__device__ float block_sum(float v, float *red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    v = warp_sum(v);
+    if (lane == 0) red[warp] = v;
+    csync();
+    float r = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kWarps; i++) r += red[i];
+    csync();
+    return r;
+}
+
+// Sum of squares of the hidden row whose values this thread holds at
+// e = tid + i * kConsumers: in parallel, or (strict) sequentially in index
+// order through shared memory exactly as gemma4.c:367-368 does.
+template <int PER>
+__device__ float row_sumsq(const float (&v)[PER], bool strict, float *vec, float *red) {
+    const int tid = threadIdx.x;
+    if (!strict) {
+        float ss = 0.0f;
+#pragma unroll
+        for (int i = 0; i < PER; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+        return block_sum(ss, red);
+    }
+#pragma unroll
+    for (int i = 0; i < PER; i++) vec[tid + i * kConsumers] = v[i];
+    csync();
+    if (tid == 0) red[0] = seq_sumsq(vec, PER * kConsumers);
+    csync();
+    const float ss = red[0];
+    csync();
+    return ss;
+}
+
+// Quantise `src` (K floats, shared or global) into xq/xs, one warp per 64-group.
+__device__ void quantize_row(const float *src, int K, int8_t *xq, float *xs) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int G = K / 64;
+    for (int g = warp; g < G; g += kWarps) {
+        float a = src[g * 64 + lane], b = src[g * 64 + 32 + lane];
+        float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
+        float s = quant_scale(amax);
+        float inv = quant_inv(s);
+        xq[g * 64 + lane] = (int8_t)quant_one(a, inv);
+        xq[g * 64 + 32 + lane] = (int8_t)quant_one(b, inv);
+        if (lane == 0) xs[g] = s;
+    }
+}
+
+template <int T, int PRO>
+__device__ void prologue(const GemvArgs &a, int8_t *xq, float *xs, float *vec, float *red) {
+    const int K = a.m.K, G = K / 64, tid = threadIdx.x;
+    if (PRO == PRO_LOADQ) {
+        const int4 *q4 = (const int4 *)a.xq_in;
+        int4 *d4 = (int4 *)xq;
+        for (int i = tid; i < T * K / 16; i += kConsumers) d4[i] = q4[i];
+        for (int i = tid; i < T * G; i += kConsumers) xs[i] = a.xs_in[i];
+        return;
+    }
+    if (PRO == PRO_QUANT) {
+        for (int t = 0; t < T; t++) quantize_row(a.src + (size_t)t * a.src_stride, K, xq + t * K, xs + t * G);
+        return;
+    }
+    // K == 1536 (hidden width) for all fused-norm prologues; 6 values per thread.
+    constexpr int PER = G4_HIDDEN / kConsumers;
+    for (int t = 0; t < T; t++) {
+        float y[PER];
+        if (PRO == PRO_EMBED_QUANT) {
+            int tok = a.tokens[t];
+            if (tok < 0 || tok >= a.embed.N) {
+                g4_set_error(a.err, G4D_BAD_TOKEN);
+                tok = 0;
+            }
+            const int8_t *wr = a.embed.w + (size_t)tok * G4_HIDDEN;
+            const uint16_t *sr = a.embed.s + (size_t)tok * (G4_HIDDEN / 64);
+#pragma unroll
+            for (int i = 0; i < PER; i++) {
+                const int e = tid + i * kConsumers;
+                const float sc = __fmul_rn(h2f(sr[e >> 6]), a.embed_mult);   // gemma4.c:350
+                y[i] = __fmul_rn((float)wr[e], sc);                          // gemma4.c:354
+                if (blockIdx.x == 0) a.res_out[t * G4_HIDDEN + e] = y[i];
+            }
+            // this CTA's slice of the per-layer embedding row (x16)
+            const int W = a.embed_ple.K;
+            const int per = (W + gridDim.x - 1) / gridDim.x;
+            const int e0 = blockIdx.x * per, e1 = min(W, e0 + per);
+            const int8_t *pw = a.embed_ple.w + (size_t)tok * W;
+            const uint16_t *ps = a.embed_ple.s + (size_t)tok * (W / 64);
+            for (int e = e0 + tid; e < e1; e += kConsumers)
+                a.ple_emb[(size_t)t * W + e] = __fmul_rn((float)pw[e], __fmul_rn(h2f(ps[e >> 6]), a.ple_mult));
+        } else {
+            const float *h = a.src + (size_t)t * a.src_stride;
+            float hv[PER];
+#pragma unroll
+            for (int i = 0; i < PER; i++) hv[i] = h[tid + i * kConsumers];
+            const float ss = row_sumsq<PER>(hv, a.strict, vec, red);
+            const float inv = rms_inv(ss, (float)G4_HIDDEN, a.eps);
+            if (PRO == PRO_NORM_QUANT) {
+#pragma unroll
+                for (int i = 0; i < PER; i++) y[i] = rms_apply(hv[i], inv, a.w_pre[tid + i * kConsumers]);
+            } else {
+                // residual update: r' = (r + rmsnorm(h, w_post)) * scalar (gemma4.c:485-486,496-497,505-506)
+                const float sc = a.scalar ? *a.scalar : 1.0f;
+#pragma unroll
+                for (int i = 0; i < PER; i++) {
+                    const int e = tid + i * kConsumers;
+                    float r = __fadd_rn(a.res_in[t * G4_HIDDEN + e], rms_apply(hv[i], inv, a.w_post[e]));
+                    if (a.scalar) r = __fmul_rn(r, sc);
+                    y[i] = r;
+                    if (blockIdx.x == 0) a.res_out[t * G4_HIDDEN + e] = r;
+                }
+                if (PRO == PRO_RES_NORM_QUANT) {
+                    const float ss2 = row_sumsq<PER>(y, a.strict, vec, red);
+                    const float inv2 = rms_inv(ss2, (float)G4_HIDDEN, a.eps);
+#pragma unroll
+                    for (int i = 0; i < PER; i++) y[i] = rms_apply(y[i], inv2, a.w_pre[tid + i * kConsumers]);
+                }
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < PER; i++) vec[tid + i * kConsumers] = y[i];
+        csync();
+        quantize_row(vec, G4_HIDDEN, xq + t * K, xs + t * G);
+        csync();
+    }
+}
+
+template <int EPI>
+__device__ __forceinline__ void epilogue_row(const GemvArgs &a, int t, int n, float v, float up, bool writer,
+                                             float &best_v, int &best_i) {
+    if (EPI == EPI_STORE) {
+        if (writer) a.out[(size_t)t * a.out_stride + n] = v;
+    } else if (EPI == EPI_GEGLU_PAIR) {
+        if (writer && (n & 1) == 0)
+            a.out[(size_t)t * a.out_stride + (n >> 1)] = geglu_one(v, up, a.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+    } else if (EPI == EPI_PLE) {
+        if (writer)
+            a.out[(size_t)t * a.out_stride + n] =
+                geglu_one(v, a.ple_u[(size_t)t * a.u_stride + n], a.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+    } else if (EPI == EPI_LOGITS) {
+        const float sv = __fmul_rn(30.0f, tanhf(__fdiv_rn(v, 30.0f)));   // gemma4.c:519
+        if (writer) a.out[(size_t)t * a.out_stride + n] = sv;
+        if (sv > best_v) { best_v = sv; best_i = n; }
+    }
+}
+
+// Exact int32 group dots and the ordered fp32 chain of one row pair held in
+// shared memory: lanes 0-15 take row A (wrow points at A + q*16 for them), lanes
+// 16-31 row B; 256 bytes per row per step, four 64-groups per step.
+template <int T>
+G4_DEV void pair_dot(const uint8_t *wrow, const uint16_t *srow, const int8_t *xq, const float *xs, int K, float (&acc)[T],
+                     int32_t *dots_row, size_t dots_t_stride) {
+    const int lane = threadIdx.x & 31, q = lane & 15, G = K >> 6, NC = K >> 8;
+#pragma unroll
+    for (int t = 0; t < T; t++) acc[t] = 0.0f;
+#pragma unroll 2
+    for (int step = 0; step < NC; step++) {
+        const uint4 w4 = *(const uint4 *)(wrow + step * 256);
+        const uint2 s2 = *(const uint2 *)(srow + step * 4);
+        const float ws0 = h2f((uint16_t)(s2.x & 0xFFFFu)), ws1 = h2f((uint16_t)(s2.x >> 16));
+        const float ws2 = h2f((uint16_t)(s2.y & 0xFFFFu)), ws3 = h2f((uint16_t)(s2.y >> 16));
+#pragma unroll
+        for (int t = 0; t < T; t++) {
+            const int4 x4 = *(const int4 *)(xq + t * K + step * 256 + q * 16);
+            int d = dp4a(w4.x, (uint32_t)x4.x, 0);
+            d = dp4a(w4.y, (uint32_t)x4.y, d);
+            d = dp4a(w4.z, (uint32_t)x4.z, d);
+            d = dp4a(w4.w, (uint32_t)x4.w, d);
+            d += __shfl_xor_sync(0xffffffffu, d, 1);
+            d += __shfl_xor_sync(0xffffffffu, d, 2);
+            const int base = lane & 16;
+            const int d0 = __shfl_sync(0xffffffffu, d, base);
+            const int d1 = __shfl_sync(0xffffffffu, d, base + 4);
+            const int d2 = __shfl_sync(0xffffffffu, d, base + 8);
+            const int d3 = __shfl_sync(0xffffffffu, d, base + 12);
+            const float4 xs4 = *(const float4 *)(xs + t * G + step * 4);
+            float v = acc[t];
+            v = __fmaf_rn(__int2float_rn(d0), __fmul_rn(ws0, xs4.x), v);
+            v = __fmaf_rn(__int2float_rn(d1), __fmul_rn(ws1, xs4.y), v);
+            v = __fmaf_rn(__int2float_rn(d2), __fmul_rn(ws2, xs4.z), v);
+            v = __fmaf_rn(__int2float_rn(d3), __fmul_rn(ws3, xs4.w), v);
+            acc[t] = v;
+            if (dots_row && q == 0) {
+                int32_t *dd = dots_row + (size_t)t * dots_t_stride + step * 4;
+                dd[0] = d0; dd[1] = d1; dd[2] = d2; dd[3] = d3;
+            }
+        }
+    }
+}
+
+}  // namespace

@@ -126,6 +126,46 @@ struct AttnArgs {
     int score_stride;
 };
 
+// ---- persistent decode step (g4_decode.cu) ---------------------------------
+enum DecodeOpType : int {
+    OP_GEMV = 0,       // GemvArgs g with (pro, epi)
+    OP_ATTN = 1,       // split-KV attention, AttnArgs at (CTA c = split c)
+    OP_COMBINE = 2,    // merge splits + quantise, CTA c = 256 output dims
+    OP_PLE_PREP = 3,   // per-layer inputs: CTA c = layer c
+    OP_FINISH = 4,     // last residual update (CTA 0)
+};
+
+struct DecodeOp {
+    int type, pro, epi, barrier;   // barrier: grid-wide barrier after the op
+    GemvArgs g;
+    AttnArgs at;
+    // OP_PLE_PREP
+    const float *pli, *ple_emb, *ple_norm;
+    float ple_eps, ple_scale;
+    float *ple_u;
+    // OP_FINISH: res_out = (res_in + rmsnorm(h, w)) * scalar
+    const float *fin_h, *fin_w, *fin_res_in, *fin_scalar;
+    float *fin_res_out;
+};
+
+struct DecodeParams {
+    const DecodeOp *ops;
+    int nops;
+    int splits;                       // attention splits (= grid)
+    unsigned long long *bar;          // grid-barrier arrival counter (monotonic)
+    unsigned long long *bar_base;     // its value when this launch starts
+    int *err;
+    // optional timeline (zeroed by the host): [0] latest CTA start, then per op o
+    // [1+3o] latest prologue end (GEMV), [2+3o] latest op end, [3+3o] latest
+    // barrier exit; %globaltimer nanoseconds
+    unsigned long long *trace;
+};
+
+size_t g4_decode_smem_bytes();
+cudaError_t g4_launch_decode(const DecodeParams &p, int grid, cudaStream_t st);
+// stages of every GEMV op this CTA streams (for sizing checks)
+int g4_decode_max_stages(const DecodeOp *ops, int nops, int grid);
+
 // ---- launchers (g4_*.cu) ---------------------------------------------------
 int g4_gemv_smem_bytes(const GemvArgs &a, int stages);
 // Fills the launch plan (rb = most rows one CTA owns) for a grid of `grid` CTAs.

@@ -26,7 +26,7 @@ MAX_CONTEXT = 131072
 G4_OK = 0
 ERRORS = {-1: "G4_ERR_INVALID", -2: "G4_ERR_FORMAT", -3: "G4_ERR_CUDA", -4: "G4_ERR_NOMEM",
           -5: "G4_ERR_DEVICE", -6: "G4_ERR_STATE"}
-OPT_GRAPHS, OPT_PDL, OPT_GEMM_PATH = 1, 2, 3
+OPT_GRAPHS, OPT_PDL, OPT_GEMM_PATH, OPT_LAYERS, OPT_STRICT, OPT_PERSISTENT = 1, 2, 3, 4, 5, 6
 SYN_GROUP_SCALES, SYN_RANDOM_NORMS = 1, 2
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
@@ -84,6 +84,8 @@ def load(path=LIB_PATH):
     L.g4_profile_decode.argtypes = [vp, C.c_int, C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_double),
                                     C.POINTER(C.c_int)]
     L.g4_launches_per_token.argtypes = [vp, C.POINTER(C.c_int)]
+    L.g4_trace_decode.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_double),
+                                  C.POINTER(C.c_int)]
     L.g4_topk_noalloc.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp]
     _lib = L
     return L
@@ -193,6 +195,15 @@ class Model:
         n = (C.c_int * 3)()
         _check(self.L.g4_profile_decode(self.h, token, pos, ms, by, n), self.h)
         return list(ms), list(by), list(n)
+
+    def trace_decode(self, token, pos, cap=512):
+        """Persistent decode step with a device timeline: (types[n], t_ns[n, 3])."""
+        types = (C.c_int * cap)()
+        t = (C.c_double * (3 * cap))()
+        n = C.c_int()
+        _check(self.L.g4_trace_decode(self.h, token, pos, cap, types, t, C.byref(n)), self.h)
+        k = min(n.value, cap)
+        return np.array(types[:k], np.int32), np.array(t[:3 * k], np.float64).reshape(k, 3)
 
     def launches_per_token(self):
         n = C.c_int()

@@ -105,6 +105,11 @@ const char *g4_strerror(int code);
  * with the host C library's expf, so the whole forward reproduces the
  * reference bit for bit (logits up to tanhf). Much slower; for verification. */
 #define G4_OPT_STRICT 5
+/* Single-token decode as ONE persistent cooperative kernel per step (default
+ * 0): g4_forward with one token is deferred; the next g4_logits launches the
+ * forward and the lm_head together, any other call launches the forward alone
+ * first. Same bits as the multi-kernel path. Not used in strict mode. */
+#define G4_OPT_PERSISTENT 6
 int g4_set_option(g4_ctx *ctx, int option, int value);
 
 /* ---- introspection (tests, benchmarks) ---- */
@@ -124,6 +129,16 @@ int g4_elapsed(g4_ctx *ctx, int slot_a, int slot_b, float *ms);
  * launch counts. Class 0: int8 weight GEMVs; 1: attention (+ combine); 2: rest.
  * Advances the KV cache like g4_forward. */
 int g4_profile_decode(g4_ctx *ctx, int token, int pos, float ms[3], double bytes[3], int launches[3]);
+/* One single-token step at `pos` (forward + logits) as the persistent kernel,
+ * with a device timeline: for op i (in launch order) types[i] is 0 int8 GEMV,
+ * 1 split attention, 2 split combine, 3 per-layer-input prep, 4 last residual
+ * update; t_ns[3i..3i+2] are nanoseconds from the latest CTA start until the
+ * latest CTA finished the op's prologue (GEMV only, else -1), the op, and the
+ * grid barrier after it. Advances the KV cache like g4_forward. *nops gets the
+ * op count; at most `cap` ops are written. G4_ERR_STATE if persistent decode
+ * is off (G4_OPT_PERSISTENT 0 or strict mode). With G4_OPT_PERSISTENT on,
+ * g4_profile_decode reports this timeline by class (ops, not kernels). */
+int g4_trace_decode(g4_ctx *ctx, int token, int pos, int cap, int *types, double *t_ns, int *nops);
 /* Kernels one single-token decode step (forward + logits) launches. */
 int g4_launches_per_token(g4_ctx *ctx, int *n);
 

@@ -84,6 +84,7 @@ def test_graph_replay_equals_eager(g4, image):
     outs = []
     for graphs in (1, 0):
         with g4.Model(image) as m:
+            m.set_option(g4.OPT_PERSISTENT, 0)
             m.set_option(1, graphs)
             m.forward(toks[:8], 0)
             for p in range(8, 12):

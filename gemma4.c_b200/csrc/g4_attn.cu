@@ -56,7 +56,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a, int split
     extern __shared__ __align__(16) float sm[];
     griddep_launch();
     griddep_wait();
-    attn_decode_split<HD, DecodeCfg<HD>::KT>(a, blockIdx.x, splits, sm);
+    attn_decode_split<HD, DecodeCfg<HD>::KT>(a, a.pos_dev ? *a.pos_dev : a.start_pos, blockIdx.x, splits, sm);
 }
 
 template <int HD>
@@ -64,7 +64,7 @@ __global__ void __launch_bounds__(256) k_attn_combine(const AttnArgs a, int spli
     __shared__ float wsm[256 + 16];
     griddep_launch();
     griddep_wait();
-    attn_combine_part<HD>(a, blockIdx.x, splits, wsm);
+    attn_combine_part<HD>(a, a.pos_dev ? *a.pos_dev : a.start_pos, blockIdx.x, splits, wsm);
 }
 
 // ---------------------------------------------------------------------------

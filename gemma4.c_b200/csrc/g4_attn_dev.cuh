@@ -50,7 +50,7 @@ G4_DEV void norm_rope_warp(float *x, const float *w, const float *cosr, const fl
 }
 
 
-constexpr int kMinSplit = 64;
+constexpr int kMinSplit = 8;
 constexpr int kAttnThreads = 256;   // 8 warps: warp h owns query head h
 
 G4_DEV void attn_sync() { bar_sync(1, kAttnThreads); }
@@ -66,7 +66,7 @@ G4_DEV void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : 
 G4_DEV int split_range(int p, int window, int splits, int s, int *k0, int *k1) {
     const int kf = first_key(p, window), nk = p + 1 - kf;
     int per = (nk + splits - 1) / splits;
-    per = per < kMinSplit ? kMinSplit : (per + 31) / 32 * 32;
+    per = per < kMinSplit ? kMinSplit : (per + 7) / 8 * 8;
     *k0 = kf + s * per;
     *k1 = min(p + 1, *k0 + per);
     return (nk + per - 1) / per;
@@ -77,22 +77,61 @@ G4_DEV int split_range(int p, int window, int splits, int s, int *k0, int *k1) {
 // key and the online-softmax tile steps follow KT).
 template <int HD>
 struct DecodeKT {
-    static constexpr int value = HD == 512 ? 8 : 16;
+    static constexpr int value = HD == 512 ? 4 : 8;
 };
+
+// RMS-normalise (optional weight) and rotate one head vector held in
+// registers by one warp: lane holds x[lane + 32 i], i < HD/32, so each rope
+// pair (j, j + HD/2) sits in one lane. The weight, cos and sin loads are issued
+// before any arithmetic so that they share one memory round trip with the
+// caller's loads of v.
+template <int HD>
+G4_DEV void norm_rope_regs(float (&v)[HD / 32], const float *w, const float *cosr, const float *sinr, int pairs,
+                           bool rope) {
+    constexpr int NI = HD / 32, NP = HD / 64;
+    const int lane = threadIdx.x & 31;
+    float wv[NI], cv[NP], sv[NP];
+#pragma unroll
+    for (int i = 0; i < NI; i++) wv[i] = w ? w[lane + 32 * i] : 1.0f;
+#pragma unroll
+    for (int i = 0; i < NP; i++) {
+        const int jj = lane + 32 * i;
+        const bool on = rope && jj < pairs;
+        cv[i] = on ? cosr[jj] : 1.0f;
+        sv[i] = on ? sinr[jj] : 0.0f;
+    }
+    float ss = 0.0f;
+#pragma unroll
+    for (int i = 0; i < NI; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+    ss = warp_sum(ss);
+    const float inv = rms_inv(ss, (float)HD, 1e-6f);
+#pragma unroll
+    for (int i = 0; i < NI; i++) v[i] = rms_apply(v[i], inv, wv[i]);
+    if (rope) {
+#pragma unroll
+        for (int i = 0; i < NP; i++) {
+            if (lane + 32 * i < pairs) {
+                const float a0 = v[i], b0 = v[i + NP];
+                v[i] = __fsub_rn(__fmul_rn(a0, cv[i]), __fmul_rn(b0, sv[i]));
+                v[i + NP] = __fadd_rn(__fmul_rn(b0, cv[i]), __fmul_rn(a0, sv[i]));
+            }
+        }
+    }
+}
 
 // Shared-memory floats of one decode split with KT-key tiles (double buffered).
 __host__ __device__ constexpr int decode_smem_floats(int hd, int kt) {
     return kHeads * hd + 2 * hd + 2 * kt * (hd + 4) + 2 * kt * hd;
 }
 
-// Decode (T = 1) split-KV attention for split `split` of `splits`, run by 256
+// Decode (T = 1) split-KV attention at position p for split `split` of `splits`, run by 256
 // threads (8 warps; warp h = query head h). The CTA post-processes q (all
 // heads) and, on layers that own the cache, the new k/v; CTA 0 of the grid
 // writes k/v to the ring, and every CTA uses its own copy for key == pos.
 // K/V tiles of KT keys stream through a double-buffered cp.async pipeline.
 // Writes (max, sum, unnormalised output) per head to a.part.
 template <int HD, int KT>
-G4_DEV void attn_decode_split(const AttnArgs &a, int split, int splits, float *sm) {
+__device__ __noinline__ void attn_decode_split(const AttnArgs &a, int p, int split, int splits, float *sm) {
     constexpr int LPK = 32 / KT, KS = HD + 4;
     float *qn = sm;                       // [8][HD]
     float *kn = qn + kHeads * HD;         // [HD]
@@ -100,7 +139,6 @@ G4_DEV void attn_decode_split(const AttnArgs &a, int split, int splits, float *s
     float *Ks = vn + HD;                  // [2][KT][KS]
     float *Vs = Ks + 2 * KT * KS;         // [2][KT][HD]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int p = a.pos_dev ? *a.pos_dev : a.start_pos;
     int k0, k1;
     const int active = split_range(p, a.window, splits, split, &k0, &k1);
     if (split >= active) return;
@@ -118,19 +156,28 @@ G4_DEV void attn_decode_split(const AttnArgs &a, int split, int splits, float *s
     const int ntiles = k1 > k0 ? (k1 - k0 + KT - 1) / KT : 0;
     if (ntiles > 0) issue(0, 0);
 
+    // q of head `warp`; k and v (warps 0, 1) when the layer owns its cache. All
+    // loads first, then the per-warp norm + rope in registers.
+    constexpr int NI = HD / 32;
     const float *cosr = a.rope_cos + (size_t)p * a.pairs, *sinr = a.rope_sin + (size_t)p * a.pairs;
-    for (int i = lane; i < HD; i += 32) qn[warp * HD + i] = a.qkv[warp * HD + i];
-    __syncwarp();
-    norm_rope_warp<HD>(qn + warp * HD, a.q_norm, cosr, sinr, a.pairs, true);
-    if (a.has_kv && warp < 2) {
+    const bool kv = a.has_kv && warp < 2;
+    float qv[NI], kvv[NI];
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        qv[i] = a.qkv[warp * HD + lane + 32 * i];
+        kvv[i] = kv ? a.qkv[(kHeads + warp) * HD + lane + 32 * i] : 0.0f;
+    }
+    norm_rope_regs<HD>(qv, a.q_norm, cosr, sinr, a.pairs, true);
+#pragma unroll
+    for (int i = 0; i < NI; i++) qn[warp * HD + lane + 32 * i] = qv[i];
+    if (kv) {
+        norm_rope_regs<HD>(kvv, warp == 0 ? a.k_norm : nullptr, cosr, sinr, a.pairs, warp == 0);
         float *x = warp == 0 ? kn : vn;
-        const float *src = a.qkv + kHeads * HD + warp * HD;
-        for (int i = lane; i < HD; i += 32) x[i] = src[i];
-        __syncwarp();
-        norm_rope_warp<HD>(x, warp == 0 ? a.k_norm : nullptr, cosr, sinr, a.pairs, warp == 0);
-        if (split == 0) {
-            float *dst = (warp == 0 ? a.kcache : a.vcache) + (size_t)(p & a.mask) * HD;
-            for (int i = lane; i < HD; i += 32) dst[i] = x[i];
+        float *dst = (warp == 0 ? a.kcache : a.vcache) + (size_t)(p & a.mask) * HD;
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            x[lane + 32 * i] = kvv[i];
+            if (split == 0) dst[lane + 32 * i] = kvv[i];
         }
     }
     attn_sync();
@@ -216,10 +263,9 @@ G4_DEV void attn_decode_split(const AttnArgs &a, int split, int splits, float *s
 // dimensions (combine block `blk` of 8*HD/256) and quantise them for o_proj
 // (gemma4.c:459). 256 threads, thread = one dimension. smem: 256 + 16 floats.
 template <int HD>
-G4_DEV void attn_combine_part(const AttnArgs &a, int blk, int splits, float *wsm) {
+__device__ __noinline__ void attn_combine_part(const AttnArgs &a, int p, int blk, int splits, float *wsm) {
     float *red = wsm + 256;
     const int tid = threadIdx.x;
-    const int p = a.pos_dev ? *a.pos_dev : a.start_pos;
     int k0, k1;
     const int active = split_range(p, a.window, splits, 0, &k0, &k1);
     const int per_head = HD / 256;
@@ -227,20 +273,38 @@ G4_DEV void attn_combine_part(const AttnArgs &a, int blk, int splits, float *wsm
     const int warp = tid >> 5, lane = tid & 31;
     const size_t stride = (size_t)kHeads * (HD + 4);
     const float *ph = a.part + (size_t)h * (HD + 4);
-    if (tid == 0) {
+    // this thread's values of the first splits are loaded before the weights
+    // exist, so that both loads share one memory round trip
+    constexpr int U = 16;
+    float pv[U];
+#pragma unroll
+    for (int u = 0; u < U; u++) pv[u] = u < active ? ph[u * stride + 4 + d] : 0.0f;
+    if (warp == 0) {
+        // split weights exp(m_s - max) and the total sum, lanes over splits (active <= 256)
         float mx = -INFINITY;
-        for (int s = 0; s < active; s++) mx = fmaxf(mx, ph[s * stride]);
+        for (int s = lane; s < active; s += 32) mx = fmaxf(mx, ph[s * stride]);
+        mx = warp_max(mx);
         float lsum = 0.0f;
-        for (int s = 0; s < active; s++) {
-            const float w = ph[s * stride] == -INFINITY ? 0.0f : expf(ph[s * stride] - mx);
+        for (int s = lane; s < active; s += 32) {
+            const float ms = ph[s * stride];
+            const float w = ms == -INFINITY ? 0.0f : expf(ms - mx);
             wsm[s] = w;
-            lsum += w * ph[s * stride + 1];
+            lsum = fmaf(w, ph[s * stride + 1], lsum);
         }
-        red[8] = lsum;
+        lsum = warp_sum(lsum);
+        if (lane == 0) red[8] = lsum;
     }
     attn_sync();
-    float o = 0.0f;
-    for (int s = 0; s < active; s++) o = fmaf(wsm[s], ph[s * stride + 4 + d], o);
+    float o = 0.0f;   // sum over splits in ascending order
+    for (int s0 = 0; s0 < active; s0 += U) {
+        if (s0 > 0) {
+#pragma unroll
+            for (int u = 0; u < U; u++) pv[u] = s0 + u < active ? ph[(s0 + u) * stride + 4 + d] : 0.0f;
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++)
+            if (s0 + u < active) o = fmaf(wsm[s0 + u], pv[u], o);
+    }
     o = o / red[8];
     const int col = h * HD + d;
     a.out[col] = o;

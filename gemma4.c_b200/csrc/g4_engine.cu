@@ -84,7 +84,7 @@ struct g4_ctx {
     bool decode_warm = false;
     cudaEvent_t events[16] = {};
     // persistent single-token decode (g4_decode.cu)
-    bool persistent = false;         // G4_OPT_PERSISTENT
+    bool persistent = true;          // G4_OPT_PERSISTENT
     bool pending = false;            // a single-token forward waiting to be launched
     DecodeOp *dec_fwd = nullptr, *dec_fwdlog = nullptr;
     int n_fwd = 0, n_fwdlog = 0, dec_cur = 0, dec_layers = 0;
@@ -800,6 +800,7 @@ cudaError_t launch_decode(g4_ctx *c, bool with_logits, unsigned long long *trace
     p.ops = with_logits ? c->dec_fwdlog : c->dec_fwd;
     p.nops = with_logits ? c->n_fwdlog : c->n_fwd;
     p.splits = kSplits;
+    p.pos = c->pos_d;
     p.bar = c->bar;
     p.bar_base = c->bar_base;
     p.err = c->err;
@@ -1142,9 +1143,9 @@ int g4_trace_decode(g4_ctx *c, int token, int pos, int cap, int *types, double *
     if (int rc = build_decode(c)) return rc;
     if (!c->persistent) return fail(c, G4_ERR_STATE, "trace: persistent decode unavailable on this device");
     const int n = c->n_fwdlog;
-    const size_t tb = (size_t)(1 + 3 * n) * sizeof(unsigned long long);
+    const size_t tb = (size_t)(1 + 6 * n) * sizeof(unsigned long long);
     if (!c->trace) CK(cudaMalloc(&c->trace, tb));
-    std::vector<unsigned long long> h(1 + 3 * n);
+    std::vector<unsigned long long> h(1 + 6 * n);
     CK(cudaMemcpyAsync(c->tokens_d, &token, 4, cudaMemcpyHostToDevice, c->st));
     CK(cudaMemcpyAsync(c->pos_d, &pos, 4, cudaMemcpyHostToDevice, c->st));
     CK(cudaMemsetAsync(c->trace, 0, tb, c->st));
@@ -1157,9 +1158,10 @@ int g4_trace_decode(g4_ctx *c, int token, int pos, int cap, int *types, double *
     *nops = n;
     for (int i = 0; i < n && i < cap; i++) {
         types[i] = c->dec_host[i].type;
-        for (int k = 0; k < 3; k++) {
-            const unsigned long long t = h[1 + 3 * i + k];
-            t_ns[3 * i + k] = t ? (double)(t - h[0]) : -1.0;
+        for (int k = 0; k < 6; k++) {
+            const unsigned long long t = h[1 + 6 * i + k];
+            if (k == 3) t_ns[6 * i + k] = (double)t;                     // a duration
+            else t_ns[6 * i + k] = t ? (double)t - (double)h[0] : -1.0;   // producer may start first
         }
     }
     return G4_OK;
@@ -1176,14 +1178,14 @@ int g4_profile_decode(g4_ctx *c, int token, int pos, float ms[3], double bytes[3
     }
     if (c->persistent && !c->strict) {
         std::vector<int> types(c->n_fwdlog);
-        std::vector<double> t(3 * (size_t)c->n_fwdlog);
+        std::vector<double> t(6 * (size_t)c->n_fwdlog);
         int n = 0;
         if (int rc0 = g4_trace_decode(c, token, pos, (int)types.size(), types.data(), t.data(), &n)) return rc0;
         for (int k = 0; k < 3; k++) { ms[k] = 0; bytes[k] = 0; launches[k] = 0; }
         double prev = 0.0;
         for (int i = 0; i < n; i++) {
             const int cls = types[i] == OP_GEMV ? 0 : (types[i] == OP_ATTN || types[i] == OP_COMBINE) ? 1 : 2;
-            const double end = t[3 * i + 2];
+            const double end = t[6 * i + 2];
             ms[cls] += (float)((end - prev) * 1e-6);
             bytes[cls] += op_bytes(c, c->dec_host[i], pos);
             launches[cls]++;

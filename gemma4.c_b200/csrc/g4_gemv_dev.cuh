@@ -57,18 +57,36 @@ __device__ float row_sumsq(const float (&v)[PER], bool strict, float *vec, float
     return ss;
 }
 
-// Quantise `src` (K floats, shared or global) into xq/xs, one warp per 64-group.
-__device__ void quantize_row(const float *src, int K, int8_t *xq, float *xs) {
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int G = K / 64;
-    for (int g = warp; g < G; g += kWarps) {
-        float a = src[g * 64 + lane], b = src[g * 64 + 32 + lane];
-        float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
-        float s = quant_scale(amax);
-        float inv = quant_inv(s);
-        xq[g * 64 + lane] = (int8_t)quant_one(a, inv);
-        xq[g * 64 + 32 + lane] = (int8_t)quant_one(b, inv);
-        if (lane == 0) xs[g] = s;
+// Quantise `src` (K floats, shared or global; 16-byte aligned) into xq/xs
+// (gemma4.c:265-279). All consumer threads work: thread t takes the float4s at
+// t + 256 j, so each 64-value group is one half-warp's 16 float4s; the group
+// maximum is a 4-step shuffle reduction (exact in any order). Loads are issued
+// U float4s ahead, so a global source costs ceil(K / (4 * 256 * U)) round trips.
+__device__ __noinline__ void quantize_row(const float *src, int K, int8_t *xq, float *xs) {
+    constexpr int U = 4;
+    const int tid = threadIdx.x, n4 = K >> 2;   // K % 128 == 0: a warp is all in or all out
+    const float4 *s4 = (const float4 *)src;
+    for (int i0 = tid; i0 < n4; i0 += kConsumers * U) {
+        float4 v[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = i0 + u * kConsumers;
+            v[u] = i < n4 ? s4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = i0 + u * kConsumers;
+            if (i - (tid & 31) >= n4) break;   // warp-uniform
+            float m = fmaxf(fmaxf(fabsf(v[u].x), fabsf(v[u].y)), fmaxf(fabsf(v[u].z), fabsf(v[u].w)));
+#pragma unroll
+            for (int o = 1; o < 16; o <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const float sc = quant_scale(m), inv = quant_inv(sc);
+            const uint32_t q = (uint32_t)(quant_one(v[u].x, inv) & 0xff) | ((uint32_t)(quant_one(v[u].y, inv) & 0xff) << 8) |
+                               ((uint32_t)(quant_one(v[u].z, inv) & 0xff) << 16) |
+                               ((uint32_t)(quant_one(v[u].w, inv) & 0xff) << 24);
+            ((uint32_t *)xq)[i] = q;
+            if ((tid & 15) == 0) xs[i >> 4] = sc;
+        }
     }
 }
 
@@ -87,7 +105,20 @@ __device__ void prologue(const GemvArgs &a, int8_t *xq, float *xs, float *vec, f
         return;
     }
     // K == 1536 (hidden width) for all fused-norm prologues; 6 values per thread.
+    // The norm weights and the scalar do not depend on earlier work: load them
+    // first, and each token row together with its residual row, so that the
+    // prologue waits for one memory round trip per row rather than five.
     constexpr int PER = G4_HIDDEN / kConsumers;
+    constexpr bool kRes = PRO == PRO_RES_NORM_QUANT || PRO == PRO_RES_QUANT;
+    constexpr bool kPre = PRO == PRO_NORM_QUANT || PRO == PRO_RES_NORM_QUANT;
+    float wpost[PER], wpre[PER];
+    float sc = 1.0f;
+#pragma unroll
+    for (int i = 0; i < PER; i++) {
+        wpost[i] = kRes ? a.w_post[tid + i * kConsumers] : 0.0f;
+        wpre[i] = kPre ? a.w_pre[tid + i * kConsumers] : 0.0f;
+    }
+    if (kRes && a.scalar) sc = *a.scalar;
     for (int t = 0; t < T; t++) {
         float y[PER];
         if (PRO == PRO_EMBED_QUANT) {
@@ -115,21 +146,23 @@ __device__ void prologue(const GemvArgs &a, int8_t *xq, float *xs, float *vec, f
                 a.ple_emb[(size_t)t * W + e] = __fmul_rn((float)pw[e], __fmul_rn(h2f(ps[e >> 6]), a.ple_mult));
         } else {
             const float *h = a.src + (size_t)t * a.src_stride;
-            float hv[PER];
+            float hv[PER], rv[PER];
 #pragma unroll
-            for (int i = 0; i < PER; i++) hv[i] = h[tid + i * kConsumers];
+            for (int i = 0; i < PER; i++) {
+                hv[i] = h[tid + i * kConsumers];
+                rv[i] = kRes ? a.res_in[t * G4_HIDDEN + tid + i * kConsumers] : 0.0f;
+            }
             const float ss = row_sumsq<PER>(hv, a.strict, vec, red);
             const float inv = rms_inv(ss, (float)G4_HIDDEN, a.eps);
             if (PRO == PRO_NORM_QUANT) {
 #pragma unroll
-                for (int i = 0; i < PER; i++) y[i] = rms_apply(hv[i], inv, a.w_pre[tid + i * kConsumers]);
+                for (int i = 0; i < PER; i++) y[i] = rms_apply(hv[i], inv, wpre[i]);
             } else {
                 // residual update: r' = (r + rmsnorm(h, w_post)) * scalar (gemma4.c:485-486,496-497,505-506)
-                const float sc = a.scalar ? *a.scalar : 1.0f;
 #pragma unroll
                 for (int i = 0; i < PER; i++) {
                     const int e = tid + i * kConsumers;
-                    float r = __fadd_rn(a.res_in[t * G4_HIDDEN + e], rms_apply(hv[i], inv, a.w_post[e]));
+                    float r = __fadd_rn(rv[i], rms_apply(hv[i], inv, wpost[i]));
                     if (a.scalar) r = __fmul_rn(r, sc);
                     y[i] = r;
                     if (blockIdx.x == 0) a.res_out[t * G4_HIDDEN + e] = r;
@@ -138,7 +171,7 @@ __device__ void prologue(const GemvArgs &a, int8_t *xq, float *xs, float *vec, f
                     const float ss2 = row_sumsq<PER>(y, a.strict, vec, red);
                     const float inv2 = rms_inv(ss2, (float)G4_HIDDEN, a.eps);
 #pragma unroll
-                    for (int i = 0; i < PER; i++) y[i] = rms_apply(y[i], inv2, a.w_pre[tid + i * kConsumers]);
+                    for (int i = 0; i < PER; i++) y[i] = rms_apply(y[i], inv2, wpre[i]);
                 }
             }
         }

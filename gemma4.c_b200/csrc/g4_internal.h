@@ -135,7 +135,7 @@ enum DecodeOpType : int {
     OP_FINISH = 4,     // last residual update (CTA 0)
 };
 
-struct DecodeOp {
+struct alignas(16) DecodeOp {
     int type, pro, epi, barrier;   // barrier: grid-wide barrier after the op
     GemvArgs g;
     AttnArgs at;
@@ -149,15 +149,17 @@ struct DecodeOp {
 };
 
 struct DecodeParams {
-    const DecodeOp *ops;
+    const DecodeOp *ops;             // 16-byte aligned
     int nops;
+    const int *pos;                  // the step's position (device)
     int splits;                       // attention splits (= grid)
     unsigned long long *bar;          // grid-barrier arrival counter (monotonic)
     unsigned long long *bar_base;     // its value when this launch starts
     int *err;
     // optional timeline (zeroed by the host): [0] latest CTA start, then per op o
-    // [1+3o] latest prologue end (GEMV), [2+3o] latest op end, [3+3o] latest
-    // barrier exit; %globaltimer nanoseconds
+    // at 1+6o: latest prologue end (GEMV), latest op end, latest barrier exit,
+    // longest stage wait of a consumer warp (ns), latest issue of the op's
+    // first stage, latest issue of its last stage; %globaltimer nanoseconds
     unsigned long long *trace;
 };
 

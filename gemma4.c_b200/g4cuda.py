@@ -197,13 +197,13 @@ class Model:
         return list(ms), list(by), list(n)
 
     def trace_decode(self, token, pos, cap=512):
-        """Persistent decode step with a device timeline: (types[n], t_ns[n, 3])."""
+        """Persistent decode step with a device timeline: (types[n], t_ns[n, 6])."""
         types = (C.c_int * cap)()
-        t = (C.c_double * (3 * cap))()
+        t = (C.c_double * (6 * cap))()
         n = C.c_int()
         _check(self.L.g4_trace_decode(self.h, token, pos, cap, types, t, C.byref(n)), self.h)
         k = min(n.value, cap)
-        return np.array(types[:k], np.int32), np.array(t[:3 * k], np.float64).reshape(k, 3)
+        return np.array(types[:k], np.int32), np.array(t[:6 * k], np.float64).reshape(k, 6)
 
     def launches_per_token(self):
         n = C.c_int()

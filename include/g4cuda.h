@@ -106,7 +106,7 @@ const char *g4_strerror(int code);
  * reference bit for bit (logits up to tanhf). Much slower; for verification. */
 #define G4_OPT_STRICT 5
 /* Single-token decode as ONE persistent cooperative kernel per step (default
- * 0): g4_forward with one token is deferred; the next g4_logits launches the
+ * 1): g4_forward with one token is deferred; the next g4_logits launches the
  * forward and the lm_head together, any other call launches the forward alone
  * first. Same bits as the multi-kernel path. Not used in strict mode. */
 #define G4_OPT_PERSISTENT 6
@@ -132,9 +132,11 @@ int g4_profile_decode(g4_ctx *ctx, int token, int pos, float ms[3], double bytes
 /* One single-token step at `pos` (forward + logits) as the persistent kernel,
  * with a device timeline: for op i (in launch order) types[i] is 0 int8 GEMV,
  * 1 split attention, 2 split combine, 3 per-layer-input prep, 4 last residual
- * update; t_ns[3i..3i+2] are nanoseconds from the latest CTA start until the
- * latest CTA finished the op's prologue (GEMV only, else -1), the op, and the
- * grid barrier after it. Advances the KV cache like g4_forward. *nops gets the
+ * update; t_ns[6i..6i+5] are, in nanoseconds from the latest CTA start, when
+ * the latest CTA finished the op's prologue (GEMV only, else -1), the op, and
+ * the grid barrier after it; then the longest time one consumer warp waited
+ * for the op's weights to land (a duration); then when the latest producer
+ * issued the op's first and its last weight stage (GEMV only, else -1). Advances the KV cache like g4_forward. *nops gets the
  * op count; at most `cap` ops are written. G4_ERR_STATE if persistent decode
  * is off (G4_OPT_PERSISTENT 0 or strict mode). With G4_OPT_PERSISTENT on,
  * g4_profile_decode reports this timeline by class (ops, not kernels). */

@@ -85,6 +85,8 @@ struct g4_ctx {
     cudaEvent_t events[16] = {};
     // persistent single-token decode (g4_decode.cu)
     bool persistent = true;          // G4_OPT_PERSISTENT
+    void *scales_t = nullptr;        // group-major fp32 weight scales (tensor-core GEMM)
+    size_t scales_t_bytes = 0;
     bool pending = false;            // a single-token forward waiting to be launched
     DecodeOp *dec_fwd = nullptr, *dec_fwdlog = nullptr;
     int n_fwd = 0, n_fwdlog = 0, dec_cur = 0, dec_layers = 0;
@@ -324,6 +326,26 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
     }
     cudaFree(stage);
     if (rc) return rc;
+    // group-major fp32 copies of the layer and per-layer-projection scales (tensor-core GEMM)
+    {
+        std::vector<DMat *> mats;
+        mats.push_back(&c->pmp);
+        for (int l = 0; l < G4_NUM_LAYERS; l++) {
+            Layer &Y = c->L[l];
+            for (DMat *m : {&Y.qkv, &Y.o, &Y.gu, &Y.down, &Y.pleg, &Y.plep}) mats.push_back(m);
+        }
+        size_t bytes = 0;
+        for (DMat *m : mats) bytes += ((size_t)m->N * (m->K / 64) * 4 + 255) & ~(size_t)255;
+        CK(cudaMalloc(&c->scales_t, bytes));
+        size_t off = 0;
+        for (DMat *m : mats) {
+            float *d = (float *)((uint8_t *)c->scales_t + off);
+            CK(g4_launch_scales_t(m->s, m->N, m->K, d, c->st));
+            m->sT = d;
+            off += ((size_t)m->N * (m->K / 64) * 4 + 255) & ~(size_t)255;
+        }
+        c->scales_t_bytes = bytes;
+    }
     int vr = G4_OK;
     const float *rope_dev[4] = {nullptr, nullptr, nullptr, nullptr};
     for (int l = 0; l < G4_NUM_LAYERS; l++) {
@@ -902,6 +924,7 @@ int g4_close(g4_ctx *c) {
     for (int i = 0; i < 16; i++)
         if (c->events[i]) cudaEventDestroy(c->events[i]);
     if (c->arena) cudaFree(c->arena);
+    if (c->scales_t) cudaFree(c->scales_t);
     if (c->state) cudaFree(c->state);
     if (c->kv) cudaFree(c->kv);
     if (c->scores) cudaFree(c->scores);

@@ -1,17 +1,363 @@
-// g4_gemm_tc.cu — prefill int8 GEMM on the 5th-generation tensor cores
-// (tcgen05, TMEM accumulators). Not yet enabled: every shape reports
-// "unsupported" and the engine uses the SIMT GEMM.
+// g4_gemm_tc.cu — prefill int8 GEMM on the 5th-generation tensor cores.
+//
+// Reference: matmul_int8 / matmul_block (gemma4.c:192-262) over T token rows:
+//   out[t][n] = fma-chain over groups g ascending of
+//               (float)(sum_{k in g} xq[t][k] * w[n][k])  *  (ws[n][g] * xs[t][g])
+// The int32 dot of every 64-wide group is exact on the tensor core; the fp32
+// chain runs on CUDA cores in the reference's order, so the result is
+// bit-identical to the GEMV and SIMT GEMM paths.
+//
+// One CTA computes a 128 (tokens) x 128 (outputs) tile (10 warps):
+//   warp 0      TMA producer: per K step of 128 bytes, a 128x128 int8 tile of
+//               the activations and of the weights (2-D tensor maps, 128-byte
+//               swizzle) plus the step's two groups of weight scales
+//               (transposed fp32 [G][N], 1-D bulk copies) into a 4-stage ring;
+//   warp 1      allocates 256 TMEM columns; one lane issues tcgen05.mma
+//               kind::i8 (M 128, N 128, K 32): two per 64-wide group, into one
+//               of two TMEM accumulators (int32), and commits each group;
+//   warps 2-9   epilogue: thread = token row (TMEM lane), warps 2-5 own
+//               columns 0-63 and warps 6-9 columns 64-127; per group they read
+//               the int32 dots from TMEM and advance their 64 fp32 chains,
+//               then apply the output epilogue (store, GEGLU pair, PLE gate).
+// Waits are bounded (mbar_wait); on a timeout every role leaves its loop, the
+// CTA drains the copies and MMAs it issued, and TMEM is freed.
+#include <cuda.h>
+
 #include "g4_common.cuh"
 #include "g4_internal.h"
 
+namespace {
+
+constexpr int kBM = 128, kBN = 128, kBK = 128;   // tile: tokens x outputs x K bytes per stage
+constexpr int kStages = 4;
+constexpr int kTileBytes = kBM * kBK;             // 16 KB (A and B alike)
+constexpr int kScaleBytes = 2 * kBN * 4;          // two groups of fp32 weight scales
+constexpr int kOffA = 0;
+constexpr int kOffB = kOffA + kStages * kTileBytes;
+constexpr int kOffS = kOffB + kStages * kTileBytes;
+constexpr int kOffBar = kOffS + kStages * kScaleBytes;
+// barriers: full[S], empty[S], tfull[2], tempty[2], then the TMEM address word
+constexpr int kSmemBytes = kOffBar + (2 * kStages + 4) * 8 + 16 + 1024;   // + 1 KB for alignment
+constexpr int kThreads = 320;
+constexpr int kEpiWarps = 8;
+constexpr int kTmemCols = 256;
+
+G4_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+G4_DEV void bulk_g2s_plain(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+// K-major operand tile of 128 rows x 128 bytes with the 128-byte swizzle:
+// 8-row atoms of 1 KB (stride byte offset), version 1, layout SWIZZLE_128B.
+G4_DEV uint64_t umma_desc(const void *tile, int kbyte) {
+    const uint32_t a = smem_u32(tile) + (uint32_t)kbyte;
+    return (uint64_t)((a >> 4) & 0x3FFF) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
+}
+// Instruction descriptor: S32 accumulate, signed int8 A and B, both K-major,
+// N = 128 (>> 3), M = 128 (>> 4).
+constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
+                            ((uint32_t)(kBM >> 4) << 24);
+
+G4_DEV void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, bool accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(da), "l"(db), "r"(kIdesc), "r"((uint32_t)accumulate)
+        : "memory");
+}
+G4_DEV void mma_commit(uint64_t *bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+G4_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+G4_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// 32 consecutive TMEM columns of this thread's lane (32x32b shape).
+G4_DEV void tmem_ld32(uint32_t taddr, int (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]),
+          "=r"(v[16]), "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]),
+          "=r"(v[24]), "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr)
+        : "memory");
+}
+G4_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+struct TcArgs {
+    int T, N, K;
+    const float *xs;        // [T][K/64] activation scales
+    const float *wsT;       // [K/64][N] weight scales, fp32
+    int epi;
+    float *out;
+    int out_stride;
+    const float *ple_u;
+    int u_stride;
+    const float *gelu;
+    int *err;
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const TcArgs p) {
+    extern __shared__ uint8_t smem_raw[];
+    // 1024-byte alignment for the swizzled tiles
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *full = (uint64_t *)(smem + kOffBar);
+    uint64_t *empty = full + kStages;
+    uint64_t *tfull = empty + kStages;
+    uint64_t *tempty = tfull + 2;
+    uint32_t *tmem_slot = (uint32_t *)(tempty + 2);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * kBN, t0 = blockIdx.y * kBM;
+    const int steps = p.K / kBK, G = p.K >> 6;
+    __shared__ int fail, issued, committed;
+
+    if (tid == 0) {
+        for (int s = 0; s < kStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1 + kEpiWarps);   // the MMA commit and every epilogue warp
+        }
+        for (int b = 0; b < 2; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], kEpiWarps);
+        }
+        mbar_fence_init();
+        fail = 0;
+        issued = 0;
+        committed = 0;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int k = 0;
+            for (; k < steps; k++) {
+                const int s = k % kStages, use = k / kStages;
+                if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | ((k & 0xfff) << 8))) {
+                    fail = 1;
+                    break;
+                }
+                mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + kScaleBytes);
+                tma_load_2d(smem + kOffA + s * kTileBytes, &map_a, k * kBK, t0, &full[s]);
+                tma_load_2d(smem + kOffB + s * kTileBytes, &map_b, k * kBK, n0, &full[s]);
+                for (int gi = 0; gi < 2; gi++)
+                    bulk_g2s_plain(smem + kOffS + s * kScaleBytes + gi * kBN * 4,
+                                   p.wsT + (size_t)(2 * k + gi) * p.N + n0, kBN * 4, &full[s]);
+            }
+            issued = k;
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int k = 0, gidx = 0;
+            bool ok = true;
+            for (; k < steps && ok; k++) {
+                const int s = k % kStages;
+                if (!mbar_wait(&full[s], (k / kStages) & 1, p.err, G4D_TIMEOUT_FULL | ((k & 0xfff) << 8))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                for (int gi = 0; gi < 2; gi++, gidx++) {
+                    const int b = gidx & 1, use = gidx >> 1;
+                    if (use > 0 && !mbar_wait(&tempty[b], (use - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | (0xffe << 8))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint8_t *ta = smem + kOffA + s * kTileBytes, *tb = smem + kOffB + s * kTileBytes;
+                    for (int kk = 0; kk < 2; kk++) {
+                        const int kb = gi * 64 + kk * 32;
+                        mma_i8(tmem + b * kBN, umma_desc(ta, kb), umma_desc(tb, kb), kk != 0);
+                    }
+                    mma_commit(&tfull[b]);
+                }
+                if (!ok) break;
+                mma_commit(&empty[s]);
+            }
+            if (!ok) fail = 1;
+            committed = gidx;
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const int e = warp - 2, q = warp & 3, h = e >> 2;
+        const int row = q * 32 + lane, t = t0 + row;
+        const bool valid = t < p.T;
+        const float *xsr = p.xs + (size_t)(valid ? t : 0) * G;
+        float acc[64];
+#pragma unroll
+        for (int j = 0; j < 64; j++) acc[j] = 0.0f;
+        float xn0 = valid ? xsr[0] : 0.0f, xn1 = (valid && G > 1) ? xsr[1] : 0.0f;
+        for (int g = 0; g < G; g++) {
+            const int b = g & 1, k = g >> 1, s = k % kStages;
+            const float xv = xn0;
+            xn0 = xn1;
+            xn1 = (valid && g + 2 < G) ? xsr[g + 2] : 0.0f;   // two groups ahead
+            bool ok = mbar_wait(&tfull[b], (g >> 1) & 1, p.err, G4D_TIMEOUT_FULL | (0xffd << 8));
+            // the scales of this step arrived with its tiles
+            ok = ok && mbar_wait(&full[s], (k / kStages) & 1, p.err, G4D_TIMEOUT_FULL | (0xffc << 8));
+            if (!__all_sync(0xffffffffu, ok)) {
+                if (lane == 0) fail = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * kBN + h * 64);
+            int d0[32], d1[32];
+            tmem_ld32(taddr, d0);
+            tmem_ld32(taddr + 32, d1);
+            tmem_wait_ld();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+            const float *ws = (const float *)(smem + kOffS + s * kScaleBytes + (g & 1) * kBN * 4) + h * 64;
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                const float4 w4 = *(const float4 *)(ws + j);
+                acc[j] = __fmaf_rn(__int2float_rn(d0[j]), __fmul_rn(w4.x, xv), acc[j]);
+                acc[j + 1] = __fmaf_rn(__int2float_rn(d0[j + 1]), __fmul_rn(w4.y, xv), acc[j + 1]);
+                acc[j + 2] = __fmaf_rn(__int2float_rn(d0[j + 2]), __fmul_rn(w4.z, xv), acc[j + 2]);
+                acc[j + 3] = __fmaf_rn(__int2float_rn(d0[j + 3]), __fmul_rn(w4.w, xv), acc[j + 3]);
+            }
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+                const float4 w4 = *(const float4 *)(ws + 32 + j);
+                acc[32 + j] = __fmaf_rn(__int2float_rn(d1[j]), __fmul_rn(w4.x, xv), acc[32 + j]);
+                acc[33 + j] = __fmaf_rn(__int2float_rn(d1[j + 1]), __fmul_rn(w4.y, xv), acc[33 + j]);
+                acc[34 + j] = __fmaf_rn(__int2float_rn(d1[j + 2]), __fmul_rn(w4.z, xv), acc[34 + j]);
+                acc[35 + j] = __fmaf_rn(__int2float_rn(d1[j + 3]), __fmul_rn(w4.w, xv), acc[35 + j]);
+            }
+            if (g & 1) {   // both groups of step k done: release its stage (scales)
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+            }
+        }
+        if (valid && !fail) {
+            const int nb = n0 + h * 64;
+            if (p.epi == EPI_STORE) {
+                float4 *o = (float4 *)(p.out + (size_t)t * p.out_stride + nb);
+#pragma unroll
+                for (int j = 0; j < 16; j++) o[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+            } else if (p.epi == EPI_GEGLU_PAIR) {
+                float *o = p.out + (size_t)t * p.out_stride + (nb >> 1);
+#pragma unroll
+                for (int j = 0; j < 32; j++)
+                    o[j] = geglu_one(acc[2 * j], acc[2 * j + 1], p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+            } else {
+                float *o = p.out + (size_t)t * p.out_stride + nb;
+                const float *u = p.ple_u + (size_t)t * p.u_stride + nb;
+#pragma unroll
+                for (int j = 0; j < 64; j++) o[j] = geglu_one(acc[j], u[j], p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+            }
+        }
+    }
+
+    // ---------------- teardown ----------------
+    __syncwarp();   // the producer and MMA lanes rejoin their warps
+    tc_fence_before();
+    __syncthreads();
+    if (fail && tid == 0) {
+        // let issued copies and committed MMAs finish before the CTA exits
+        const uint64_t t0n = g4_globaltimer();
+        for (int k = 0; k < issued; k++)
+            while (!mbar_try_wait(&full[k % kStages], (k / kStages) & 1) && g4_globaltimer() - t0n < G4_WAIT_NS) {
+            }
+        for (int g = committed > 2 ? committed - 2 : 0; g < committed; g++)
+            while (!mbar_try_wait(&tfull[g & 1], (g >> 1) & 1) && g4_globaltimer() - t0n < G4_WAIT_NS) {
+            }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+    }
+}
+
+// ---- host side ----------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    static bool tried = false;
+    if (!tried) {
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = (EncodeTiledFn)p;
+    }
+    return fn;
+}
+
+// int8 [rows][K] row-major, 128x128-byte boxes, 128-byte swizzle.
+bool make_map(CUtensorMap *m, const void *base, int K, int rows) {
+    EncodeTiledFn fn = encode_fn();
+    if (!fn || ((uintptr_t)base & 15) || K % 128) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)K};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)base, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
 bool g4_gemm_tc_supported(const GemmArgs &a) {
-    (void)a;
-    return false;
+    return a.m.sT != nullptr && a.m.K % kBK == 0 && a.m.N % kBN == 0 && a.T >= 1 && encode_fn() != nullptr &&
+           (a.epi == EPI_STORE || a.epi == EPI_GEGLU_PAIR || a.epi == EPI_PLE) && a.dots_out == nullptr;
 }
 
 cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
-    (void)a;
-    (void)st;
     (void)pdl;
-    return cudaErrorNotSupported;
+    if (!g4_gemm_tc_supported(a)) return cudaErrorNotSupported;
+    CUtensorMap ma, mb;
+    // activation rows beyond T are read but their outputs are not stored
+    if (!make_map(&ma, a.xq, a.m.K, a.T) || !make_map(&mb, a.m.w, a.m.K, a.m.N)) return cudaErrorInvalidValue;
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    TcArgs p{};
+    p.T = a.T;
+    p.N = a.m.N;
+    p.K = a.m.K;
+    p.xs = a.xs;
+    p.wsT = a.m.sT;
+    p.epi = a.epi;
+    p.out = a.out;
+    p.out_stride = a.out_stride;
+    p.ple_u = a.ple_u;
+    p.u_stride = a.u_stride;
+    p.gelu = a.gelu;
+    p.err = a.err;
+    dim3 grid(a.m.N / kBN, (a.T + kBM - 1) / kBM);
+    k_gemm_tc<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, p);
+    return cudaGetLastError();
 }

@@ -30,6 +30,7 @@ enum : int {
 struct DMat {
     const int8_t *w;     // [N][K]
     const uint16_t *s;   // [N][K/64] fp16 bits
+    const float *sT;     // [K/64][N] the same scales as fp32, group-major (tensor-core GEMM), or NULL
     int N, K;
 };
 
@@ -169,6 +170,7 @@ cudaError_t g4_launch_decode(const DecodeParams &p, int grid, cudaStream_t st);
 int g4_decode_max_stages(const DecodeOp *ops, int nops, int grid);
 
 // ---- launchers (g4_*.cu) ---------------------------------------------------
+cudaError_t g4_launch_scales_t(const uint16_t *s, int N, int K, float *sT, cudaStream_t st);
 int g4_gemv_smem_bytes(const GemvArgs &a, int stages);
 // Fills the launch plan (rb = most rows one CTA owns) for a grid of `grid` CTAs.
 void g4_gemv_plan(GemvArgs &a, int grid);

@@ -180,7 +180,21 @@ __global__ void __launch_bounds__(256) k_ple_prep(const float *pli, const float 
     u[base + i] = __fmul_rn(__fadd_rn(y, ple_emb[base + i]), scale);
 }
 
+// sT[g][n] = fp32(s[n][g]): group-major weight scales for the tensor-core GEMM.
+__global__ void k_scales_t(const uint16_t *s, int N, int G, float *sT) {
+    const size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (size_t)N * G) return;
+    const int g = (int)(i / N), n = (int)(i % N);
+    sT[i] = h2f(s[(size_t)n * G + g]);
+}
+
 }  // namespace
+
+cudaError_t g4_launch_scales_t(const uint16_t *s, int N, int K, float *sT, cudaStream_t st) {
+    const size_t n = (size_t)N * (K / 64);
+    k_scales_t<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s, N, K / 64, sT);
+    return cudaGetLastError();
+}
 
 cudaError_t g4_launch_repack(const int8_t *packed_w, const uint16_t *packed_s, int N, int K, int8_t *w, uint16_t *s,
                              int row_offset, int row_mul, cudaStream_t st) {

@@ -224,7 +224,13 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
     TK(cudaMemcpy(dxq.p, xq, (size_t)T * K, cudaMemcpyHostToDevice));
     TK(cudaMemcpy(dxs.p, xs, (size_t)T * G * 4, cudaMemcpyHostToDevice));
     TK(g4_launch_repack((const int8_t *)pw.p, (const uint16_t *)ps.p, N, K, (int8_t *)w.p, (uint16_t *)s.p, 0, 1, 0));
-    DMat m{(const int8_t *)w.p, (const uint16_t *)s.p, N, K};
+    DMat m{(const int8_t *)w.p, (const uint16_t *)s.p, nullptr, N, K};
+    DevBuf sT;
+    if (path == 3) {
+        TK(sT.alloc((size_t)N * G * 4));
+        TK(g4_launch_scales_t(m.s, N, K, (float *)sT.p, 0));
+        m.sT = (const float *)sT.p;
+    }
     if (path == 1) {
         GemvArgs a{};
         a.m = m;
@@ -293,7 +299,7 @@ int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch,
     auto launch = [&](int i) {
         const uint8_t *base = (const uint8_t *)w.p + (size_t)(i % copies) * wbytes;
         GemvArgs a{};
-        a.m = DMat{(const int8_t *)base, (const uint16_t *)(base + (size_t)N * K), N, K};
+        a.m = DMat{(const int8_t *)base, (const uint16_t *)(base + (size_t)N * K), nullptr, N, K};
         a.T = T;
         a.xq_in = (const int8_t *)xq.p;
         a.xs_in = (const float *)xs.p;
@@ -326,6 +332,68 @@ int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch,
     }
     *ms_per_launch = ms / iters;
     if (bytes_per_launch) *bytes_per_launch = (double)wbytes;
+    return G4_OK;
+}
+
+// Time the prefill GEMM (path 2 SIMT dp4a, 3 tcgen05) on a T x N x K problem
+// with device-resident weights cycled over enough copies to exceed L2, and
+// report the average launch duration and the int8 operations per launch
+// (2 T N K).
+int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch, double *ops_per_launch) {
+    if (N < 128 || N % 128 || K % 256 || T < 1 || T > G4_BATCH || iters < 1 || !ms_per_launch ||
+        (path != 2 && path != 3))
+        return G4_ERR_INVALID;
+    const int G = K / 64;
+    const size_t wbytes = (size_t)N * K + (size_t)N * G * 2;
+    const size_t tbytes = (size_t)N * G * 4;
+    int copies = (int)((512ull << 20) / wbytes) + 1;
+    if (copies > 16) copies = 16;
+    DevBuf w, sT, xq, xs, out, err;
+    TK(w.alloc(wbytes * copies));
+    TK(sT.alloc(tbytes));
+    TK(xq.alloc((size_t)T * K));
+    TK(xs.alloc((size_t)T * G * 4));
+    TK(out.alloc((size_t)T * N * 4));
+    TK(err.alloc(64));
+    TK(cudaMemset(w.p, 1, wbytes * copies));
+    TK(cudaMemset(sT.p, 0, tbytes));
+    TK(cudaMemset(xq.p, 1, (size_t)T * K));
+    TK(cudaMemset(xs.p, 0, (size_t)T * G * 4));
+    TK(cudaMemset(err.p, 0, 64));
+    TK(cudaDeviceSynchronize());
+    cudaStream_t st;
+    TK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    auto launch = [&](int i) {
+        const uint8_t *base = (const uint8_t *)w.p + (size_t)(i % copies) * wbytes;
+        GemmArgs a{};
+        a.m = DMat{(const int8_t *)base, (const uint16_t *)(base + (size_t)N * K), (const float *)sT.p, N, K};
+        a.T = T;
+        a.xq = (const int8_t *)xq.p;
+        a.xs = (const float *)xs.p;
+        a.epi = EPI_STORE;
+        a.out = (float *)out.p;
+        a.out_stride = N;
+        a.err = (int *)err.p;
+        return path == 3 ? g4_launch_gemm_tc(a, st, false) : g4_launch_gemm_simt(a, st, false);
+    };
+    for (int i = 0; i < 3; i++) TK(launch(i));
+    cudaEvent_t e0, e1;
+    TK(cudaEventCreate(&e0));
+    TK(cudaEventCreate(&e1));
+    TK(cudaEventRecord(e0, st));
+    for (int i = 0; i < iters; i++) TK(launch(i));
+    TK(cudaEventRecord(e1, st));
+    TK(cudaEventSynchronize(e1));
+    float ms = 0;
+    TK(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaStreamDestroy(st);
+    int derr = 0;
+    TK(cudaMemcpy(&derr, err.p, 4, cudaMemcpyDeviceToHost));
+    if (derr) return G4_ERR_DEVICE;
+    *ms_per_launch = ms / iters;
+    if (ops_per_launch) *ops_per_launch = 2.0 * T * (double)N * K;
     return G4_OK;
 }
 

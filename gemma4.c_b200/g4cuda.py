@@ -76,6 +76,8 @@ def load(path=LIB_PATH):
     L.g4k_quantize.argtypes = [_f32p, C.c_int, C.c_int, _i8p, _f32p]
     L.g4k_linear.argtypes = [_i8p, _u16p, C.c_int, C.c_int, _i8p, _f32p, C.c_int, C.c_int, _f32p, vp]
     L.g4k_rmsnorm_quant.argtypes = [_f32p, C.c_int, _f32p, C.c_float, vp, _i8p, _f32p]
+    L.g4_bench_gemm.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
+                                C.POINTER(C.c_double)]
     L.g4_bench_gemv.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
                                 C.POINTER(C.c_double)]
     L.g4_profiler_range.argtypes = [C.c_int]
@@ -260,6 +262,14 @@ def linear(w_packed, s_packed, N, K, xq, xs, path=0, want_dots=False):
     _check(L.g4k_linear(w_packed, s_packed, N, K, xq, xs, T, path, out,
                         dots.ctypes.data if dots is not None else None))
     return out, dots
+
+
+def bench_gemm(N, K, T, path=3, iters=20):
+    """(ms per launch, int8 ops per launch) of the prefill GEMM."""
+    L = load()
+    ms, ops = C.c_float(), C.c_double()
+    _check(L.g4_bench_gemm(N, K, T, path, iters, C.byref(ms), C.byref(ops)))
+    return ms.value, ops.value
 
 
 def bench_gemv(N, K, T=1, iters=200, pdl=True):

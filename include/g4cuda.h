@@ -164,6 +164,9 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
  * launches (weights cycled through enough copies to exceed L2), and the
  * algorithmic bytes (int8 weights + FP16 scales) one launch streams. */
 int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch, double *bytes_per_launch);
+/* Prefill GEMM timing (path 2 SIMT dp4a, 3 tcgen05) on T x N x K: average
+ * launch duration and int8 operations (2 T N K) per launch. */
+int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch, double *ops_per_launch);
 /* rmsnorm (gemma4.c:360-373) of hidden-width rows followed by quantize */
 int g4k_rmsnorm_quant(const float *x, int rows, const float *w, float eps, float *y, int8_t *q, float *s);
 

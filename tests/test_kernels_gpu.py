@@ -86,6 +86,18 @@ def test_gemm_simt_bitexact(g4, oracle, T, N, K):
     assert np.array_equal(out.view(np.uint32), oracle.linear(xq, xs, wp, sp, N, K).view(np.uint32))
 
 
+@pytest.mark.parametrize("T", [1, 5, 130, 512])
+@pytest.mark.parametrize("N,K", [(2560, 1536), (1536, 4096), (1536, 256), (12288, 1536), (1536, 12288)])
+def test_gemm_tcgen05_bitexact(g4, oracle, T, N, K):
+    """tcgen05 kind::i8 GEMM: exact int32 group dots on the tensor core, the
+    reference's ordered fp32 chain in the epilogue -> bit-identical output."""
+    rng = np.random.default_rng(7 * T + N + K)
+    _, _, wp, sp = packed_case(rng, N, K)
+    xq, xs = oracle.quantize(activations(rng, T, K))
+    out, _ = g4.linear(wp, sp, N, K, xq, xs, path=3)
+    assert np.array_equal(out.view(np.uint32), oracle.linear(xq, xs, wp, sp, N, K).view(np.uint32))
+
+
 def test_rmsnorm_quant(g4, oracle):
     rng = np.random.default_rng(3)
     x = activations(rng, 33, 1536)

@@ -62,6 +62,7 @@ struct g4_ctx {
     float *res[2] = {nullptr, nullptr};
     int cur = 0;
     int8_t *xq = nullptr;
+    float *xsT = nullptr;            // group-major activation scales (tensor-core GEMM)
     float *xs = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *gu = nullptr, *pg = nullptr;
     float *pli = nullptr, *ple_emb = nullptr, *ple_u = nullptr, *logits = nullptr, *part = nullptr;
     float *argmax_part = nullptr, *topk_v = nullptr;
@@ -379,6 +380,7 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
         {(void **)&c->res[1], (size_t)kMaxT * G4_HIDDEN * 4},
         {(void **)&c->xq, (size_t)kMaxT * kMaxFfn},
         {(void **)&c->xs, (size_t)kMaxT * kMaxFfn / 64 * 4},
+        {(void **)&c->xsT, (size_t)G4_XST_STRIDE * kMaxFfn / 64 * 4},
         {(void **)&c->qkv, (size_t)kMaxT * kQkvStride * 4},
         {(void **)&c->attn, (size_t)kMaxT * G4_HEADS * G4_HD_GLOBAL * 4},
         {(void **)&c->h, (size_t)kMaxT * G4_HIDDEN * 4},
@@ -502,6 +504,7 @@ void gemm(Seq &q, const DMat &m, int T, int epi, float *out, int out_stride, con
     a.T = T;
     a.xq = c->xq;
     a.xs = c->xs;
+    a.xsT = c->xsT;
     a.epi = epi;
     a.out = out;
     a.out_stride = out_stride;
@@ -714,7 +717,7 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos) {
     int cur = 0;
     q.ck(g4_launch_rows_embed(c->tokens_d, T, c->embed, c->embed_ple, sqrtf((float)G4_HIDDEN), sqrtf((float)G4_PLE),
                               c->res[0], c->ple_emb, c->err, c->st, q.pdl));
-    q.ck(g4_launch_rows_quant(c->res[0], G4_HIDDEN, T, G4_HIDDEN, c->xq, c->xs, c->st, q.pdl));
+    q.ck(g4_launch_rows_quant(c->res[0], G4_HIDDEN, T, G4_HIDDEN, c->xq, c->xs, c->st, q.pdl, c->xsT));
     gemm(q, c->pmp, T, EPI_STORE, c->pli, G4_NUM_LAYERS * G4_PLE, nullptr, 0);
     q.ck(g4_launch_ple_prep(c->pli, c->ple_emb, c->ple_norm, 1e-6f * G4_HIDDEN, 1.0f / sqrtf(2.0f), T, c->ple_u, c->st,
                             q.pdl, c->strict));
@@ -722,30 +725,30 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos) {
         const Layer &Y = c->L[l];
         if (l == 0) {
             q.ck(g4_launch_rows_norm(0, c->res[cur], T, nullptr, nullptr, nullptr, nullptr, Y.in_norm, G4_RMS_EPS, c->xq,
-                                     c->xs, c->st, q.pdl, nullptr, c->strict));
+                                     c->xs, c->st, q.pdl, nullptr, c->strict, c->xsT));
         } else {
             const Layer &P = c->L[l - 1];
             q.ck(g4_launch_rows_norm(1, c->h, T, P.post_ple, c->res[cur], c->res[cur ^ 1], P.scalar, Y.in_norm,
-                                     G4_RMS_EPS, c->xq, c->xs, c->st, q.pdl, nullptr, c->strict));
+                                     G4_RMS_EPS, c->xq, c->xs, c->st, q.pdl, nullptr, c->strict, c->xsT));
             cur ^= 1;
         }
         gemm(q, Y.qkv, T, EPI_STORE, c->qkv, kQkvStride, nullptr, 0);
         AttnArgs at = attn_base(c, Y, T, start_pos, nullptr);
         q.ck(g4_launch_qkv_post(at, c->st, q.pdl));
         q.ck(c->strict ? g4_launch_attn_strict(at, c->st, q.pdl) : g4_launch_attn_prefill(at, c->st, q.pdl));
-        q.ck(g4_launch_rows_quant(c->attn, Y.qw, T, Y.qw, c->xq, c->xs, c->st, q.pdl));
+        q.ck(g4_launch_rows_quant(c->attn, Y.qw, T, Y.qw, c->xq, c->xs, c->st, q.pdl, c->xsT));
         gemm(q, Y.o, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
         q.ck(g4_launch_rows_norm(1, c->h, T, Y.post_attn, c->res[cur], c->res[cur ^ 1], nullptr, Y.pre_ffn, G4_RMS_EPS,
-                                 c->xq, c->xs, c->st, q.pdl, nullptr, c->strict));
+                                 c->xq, c->xs, c->st, q.pdl, nullptr, c->strict, c->xsT));
         cur ^= 1;
         gemm(q, Y.gu, T, EPI_GEGLU_PAIR, c->gu, Y.ffn, nullptr, 0);
-        q.ck(g4_launch_rows_quant(c->gu, Y.ffn, T, Y.ffn, c->xq, c->xs, c->st, q.pdl));
+        q.ck(g4_launch_rows_quant(c->gu, Y.ffn, T, Y.ffn, c->xq, c->xs, c->st, q.pdl, c->xsT));
         gemm(q, Y.down, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
         q.ck(g4_launch_rows_norm(2, c->h, T, Y.post_ffn, c->res[cur], c->res[cur ^ 1], nullptr, nullptr, G4_RMS_EPS,
-                                 c->xq, c->xs, c->st, q.pdl, nullptr, c->strict));
+                                 c->xq, c->xs, c->st, q.pdl, nullptr, c->strict, c->xsT));
         cur ^= 1;
         gemm(q, Y.pleg, T, EPI_PLE, c->pg, G4_PLE, c->ple_u + l * G4_PLE, G4_NUM_LAYERS * G4_PLE);
-        q.ck(g4_launch_rows_quant(c->pg, G4_PLE, T, G4_PLE, c->xq, c->xs, c->st, q.pdl));
+        q.ck(g4_launch_rows_quant(c->pg, G4_PLE, T, G4_PLE, c->xq, c->xs, c->st, q.pdl, c->xsT));
         gemm(q, Y.plep, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
     }
     const Layer &Z = c->L[c->layers - 1];

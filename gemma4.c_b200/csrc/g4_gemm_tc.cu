@@ -7,18 +7,23 @@
 // chain runs on CUDA cores in the reference's order, so the result is
 // bit-identical to the GEMV and SIMT GEMM paths.
 //
-// One CTA computes a 128 (tokens) x 128 (outputs) tile (10 warps):
+// Persistent CTAs (one per SM) walk 128 (tokens) x 128 (outputs) tiles; the
+// ring, the TMEM buffers and their barrier phases carry over from tile to
+// tile, so one tile's epilogue overlaps the next tile's loads and MMAs.
+// Roles (10 warps):
 //   warp 0      TMA producer: per K step of 128 bytes, a 128x128 int8 tile of
 //               the activations and of the weights (2-D tensor maps, 128-byte
 //               swizzle) plus the step's two groups of weight scales
 //               (transposed fp32 [G][N], 1-D bulk copies) into a 4-stage ring;
-//   warp 1      allocates 256 TMEM columns; one lane issues tcgen05.mma
+//   warp 1      allocates all 512 TMEM columns; one lane issues tcgen05.mma
 //               kind::i8 (M 128, N 128, K 32): two per 64-wide group, into one
-//               of two TMEM accumulators (int32), and commits each group;
-//   warps 2-9   epilogue: thread = token row (TMEM lane), warps 2-5 own
-//               columns 0-63 and warps 6-9 columns 64-127; per group they read
-//               the int32 dots from TMEM and advance their 64 fp32 chains,
-//               then apply the output epilogue (store, GEGLU pair, PLE gate).
+//               of four TMEM accumulators (int32), and commits each group;
+//   warps 2-9   epilogue: thread = token row (TMEM lane), warp w owns the
+//               64 columns (w - 2) / 4 of its lane quadrant; per group it reads
+//               the int32 dots from TMEM (two 32-column loads, the second in
+//               flight during the first half's math) and advances its 64 fp32 chains with the weight and
+//               activation scales staged by the producer, then applies the
+//               output epilogue (store, GEGLU pair, PLE gate).
 // Waits are bounded (mbar_wait); on a timeout every role leaves its loop, the
 // CTA drains the copies and MMAs it issued, and TMEM is freed.
 #include <cuda.h>
@@ -29,18 +34,19 @@
 namespace {
 
 constexpr int kBM = 128, kBN = 128, kBK = 128;   // tile: tokens x outputs x K bytes per stage
-constexpr int kStages = 4;
+constexpr int kStages = 6;
+constexpr int kTmemBufs = 4;                      // int32 group accumulators in flight
+constexpr int kTmemCols = kTmemBufs * kBN;        // 512: all of TMEM (one CTA per SM)
 constexpr int kTileBytes = kBM * kBK;             // 16 KB (A and B alike)
-constexpr int kScaleBytes = 2 * kBN * 4;          // two groups of fp32 weight scales
+constexpr int kScaleBytes = 2 * kBN * 4 + 2 * kBM * 4;   // two groups of fp32 weight and activation scales
 constexpr int kOffA = 0;
 constexpr int kOffB = kOffA + kStages * kTileBytes;
 constexpr int kOffS = kOffB + kStages * kTileBytes;
 constexpr int kOffBar = kOffS + kStages * kScaleBytes;
-// barriers: full[S], empty[S], tfull[2], tempty[2], then the TMEM address word
-constexpr int kSmemBytes = kOffBar + (2 * kStages + 4) * 8 + 16 + 1024;   // + 1 KB for alignment
-constexpr int kThreads = 320;
-constexpr int kEpiWarps = 8;
-constexpr int kTmemCols = 256;
+// barriers: full[S], empty[S], tfull[B], tempty[B], then the TMEM address word
+constexpr int kSmemBytes = kOffBar + (2 * kStages + 2 * kTmemBufs) * 8 + 16 + 1024;   // + 1 KB for alignment
+constexpr int kEpiWarps = 8;                      // 2 per TMEM lane quadrant, 64 columns each
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 G4_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -95,9 +101,43 @@ G4_DEV void tmem_ld32(uint32_t taddr, int (&v)[32]) {
 }
 G4_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
+// Packed pairs of fp32 (two independent IEEE round-to-nearest operations per
+// instruction, so each lane of the pair rounds exactly like fmul/fmaf).
+G4_DEV uint64_t pk(float x, float y) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+G4_DEV float2 upk(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+G4_DEV uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+G4_DEV uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+// One group's step of 32 columns of the chain: acc = fma((float)d, ws * xs, acc).
+G4_DEV void chain32(uint64_t *acc, const int (&d)[32], const float *ws, float xv) {
+    const uint64_t x2 = pk(xv, xv);
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+        const float4 w4 = *(const float4 *)(ws + j);
+        const uint64_t w01 = mul2(pk(w4.x, w4.y), x2), w23 = mul2(pk(w4.z, w4.w), x2);
+        acc[j / 2] = fma2(pk(__int2float_rn(d[j]), __int2float_rn(d[j + 1])), w01, acc[j / 2]);
+        acc[j / 2 + 1] = fma2(pk(__int2float_rn(d[j + 2]), __int2float_rn(d[j + 3])), w23, acc[j / 2 + 1]);
+    }
+}
+
 struct TcArgs {
     int T, N, K;
-    const float *xs;        // [T][K/64] activation scales
+    const float *xsT;       // [K/64][G4_XST_STRIDE] activation scales, group-major
     const float *wsT;       // [K/64][N] weight scales, fp32
     int epi;
     float *out;
@@ -116,11 +156,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *full = (uint64_t *)(smem + kOffBar);
     uint64_t *empty = full + kStages;
     uint64_t *tfull = empty + kStages;
-    uint64_t *tempty = tfull + 2;
-    uint32_t *tmem_slot = (uint32_t *)(tempty + 2);
+    uint64_t *tempty = tfull + kTmemBufs;
+    uint32_t *tmem_slot = (uint32_t *)(tempty + kTmemBufs);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * kBN, t0 = blockIdx.y * kBM;
     const int steps = p.K / kBK, G = p.K >> 6;
+    const int mt = (p.T + kBM - 1) / kBM, tiles = (p.N / kBN) * mt;
+    // persistent: this CTA takes tiles blockIdx.x, + gridDim.x, ...; the m tiles of
+    // one n tile are consecutive, so CTAs sharing weights run together (L2 reuse)
     __shared__ int fail, issued, committed;
 
     if (tid == 0) {
@@ -128,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1 + kEpiWarps);   // the MMA commit and every epilogue warp
         }
-        for (int b = 0; b < 2; b++) {
+        for (int b = 0; b < kTmemBufs; b++) {
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], kEpiWarps);
         }
@@ -151,20 +193,29 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
-            int k = 0;
-            for (; k < steps; k++) {
-                const int s = k % kStages, use = k / kStages;
-                if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | ((k & 0xfff) << 8))) {
-                    fail = 1;
-                    break;
+            int k = 0;   // steps issued so far (all tiles)
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                const int n0 = (tile / mt) * kBN, t0 = (tile % mt) * kBM;
+                for (int ks = 0; ks < steps; ks++, k++) {
+                    const int s = k % kStages, use = k / kStages;
+                    if (use > 0 &&
+                        !mbar_wait(&empty[s], (use - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | ((k & 0xfff) << 8))) {
+                        ok = false;
+                        break;
+                    }
+                    mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + kScaleBytes);
+                    tma_load_2d(smem + kOffA + s * kTileBytes, &map_a, ks * kBK, t0, &full[s]);
+                    tma_load_2d(smem + kOffB + s * kTileBytes, &map_b, ks * kBK, n0, &full[s]);
+                    for (int gi = 0; gi < 2; gi++) {
+                        bulk_g2s_plain(smem + kOffS + s * kScaleBytes + gi * kBN * 4,
+                                       p.wsT + (size_t)(2 * ks + gi) * p.N + n0, kBN * 4, &full[s]);
+                        bulk_g2s_plain(smem + kOffS + s * kScaleBytes + 2 * kBN * 4 + gi * kBM * 4,
+                                       p.xsT + (size_t)(2 * ks + gi) * G4_XST_STRIDE + t0, kBM * 4, &full[s]);
+                    }
                 }
-                mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + kScaleBytes);
-                tma_load_2d(smem + kOffA + s * kTileBytes, &map_a, k * kBK, t0, &full[s]);
-                tma_load_2d(smem + kOffB + s * kTileBytes, &map_b, k * kBK, n0, &full[s]);
-                for (int gi = 0; gi < 2; gi++)
-                    bulk_g2s_plain(smem + kOffS + s * kScaleBytes + gi * kBN * 4,
-                                   p.wsT + (size_t)(2 * k + gi) * p.N + n0, kBN * 4, &full[s]);
             }
+            if (!ok) fail = 1;
             issued = k;
         }
     } else if (warp == 1) {
@@ -172,102 +223,106 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             int k = 0, gidx = 0;
             bool ok = true;
-            for (; k < steps && ok; k++) {
-                const int s = k % kStages;
-                if (!mbar_wait(&full[s], (k / kStages) & 1, p.err, G4D_TIMEOUT_FULL | ((k & 0xfff) << 8))) {
-                    ok = false;
-                    break;
-                }
-                tc_fence_after();
-                for (int gi = 0; gi < 2; gi++, gidx++) {
-                    const int b = gidx & 1, use = gidx >> 1;
-                    if (use > 0 && !mbar_wait(&tempty[b], (use - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | (0xffe << 8))) {
+            for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+                for (int ks = 0; ks < steps && ok; ks++, k++) {
+                    const int s = k % kStages;
+                    if (!mbar_wait(&full[s], (k / kStages) & 1, p.err, G4D_TIMEOUT_FULL | ((k & 0xfff) << 8))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    const uint8_t *ta = smem + kOffA + s * kTileBytes, *tb = smem + kOffB + s * kTileBytes;
-                    for (int kk = 0; kk < 2; kk++) {
-                        const int kb = gi * 64 + kk * 32;
-                        mma_i8(tmem + b * kBN, umma_desc(ta, kb), umma_desc(tb, kb), kk != 0);
+                    for (int gi = 0; gi < 2; gi++, gidx++) {
+                        const int b = gidx % kTmemBufs, use = gidx / kTmemBufs;
+                        if (use > 0 &&
+                            !mbar_wait(&tempty[b], (use - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | (0xffe << 8))) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint8_t *ta = smem + kOffA + s * kTileBytes, *tb = smem + kOffB + s * kTileBytes;
+                        for (int kk = 0; kk < 2; kk++) {
+                            const int kb = gi * 64 + kk * 32;
+                            mma_i8(tmem + b * kBN, umma_desc(ta, kb), umma_desc(tb, kb), kk != 0);
+                        }
+                        mma_commit(&tfull[b]);
                     }
-                    mma_commit(&tfull[b]);
+                    if (ok) mma_commit(&empty[s]);
                 }
-                if (!ok) break;
-                mma_commit(&empty[s]);
             }
             if (!ok) fail = 1;
             committed = gidx;
         }
     } else {
         // ---------------- epilogue ----------------
-        const int e = warp - 2, q = warp & 3, h = e >> 2;
-        const int row = q * 32 + lane, t = t0 + row;
-        const bool valid = t < p.T;
-        const float *xsr = p.xs + (size_t)(valid ? t : 0) * G;
-        float acc[64];
+        // warp w: TMEM lane quadrant w % 4 (token rows), column half (w - 2) / 4.
+        // Each group's 64 columns are two 32-column TMEM loads; the second is in
+        // flight while the first 32 columns advance their chains.
+        const int e = warp - 2, q = warp & 3, ch = e >> 2;
+        const int row = q * 32 + lane;
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ch * 64);
+        int gidx = 0;   // groups consumed so far (all tiles)
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            const int n0 = (tile / mt) * kBN, t = (tile % mt) * kBM + row;
+            uint64_t acc[32];
 #pragma unroll
-        for (int j = 0; j < 64; j++) acc[j] = 0.0f;
-        float xn0 = valid ? xsr[0] : 0.0f, xn1 = (valid && G > 1) ? xsr[1] : 0.0f;
-        for (int g = 0; g < G; g++) {
-            const int b = g & 1, k = g >> 1, s = k % kStages;
-            const float xv = xn0;
-            xn0 = xn1;
-            xn1 = (valid && g + 2 < G) ? xsr[g + 2] : 0.0f;   // two groups ahead
-            bool ok = mbar_wait(&tfull[b], (g >> 1) & 1, p.err, G4D_TIMEOUT_FULL | (0xffd << 8));
-            // the scales of this step arrived with its tiles
-            ok = ok && mbar_wait(&full[s], (k / kStages) & 1, p.err, G4D_TIMEOUT_FULL | (0xffc << 8));
-            if (!__all_sync(0xffffffffu, ok)) {
-                if (lane == 0) fail = 1;
-                break;
-            }
-            tc_fence_after();
-            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * kBN + h * 64);
-            int d0[32], d1[32];
-            tmem_ld32(taddr, d0);
-            tmem_ld32(taddr + 32, d1);
-            tmem_wait_ld();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&tempty[b]);
-            const float *ws = (const float *)(smem + kOffS + s * kScaleBytes + (g & 1) * kBN * 4) + h * 64;
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                const float4 w4 = *(const float4 *)(ws + j);
-                acc[j] = __fmaf_rn(__int2float_rn(d0[j]), __fmul_rn(w4.x, xv), acc[j]);
-                acc[j + 1] = __fmaf_rn(__int2float_rn(d0[j + 1]), __fmul_rn(w4.y, xv), acc[j + 1]);
-                acc[j + 2] = __fmaf_rn(__int2float_rn(d0[j + 2]), __fmul_rn(w4.z, xv), acc[j + 2]);
-                acc[j + 3] = __fmaf_rn(__int2float_rn(d0[j + 3]), __fmul_rn(w4.w, xv), acc[j + 3]);
-            }
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-                const float4 w4 = *(const float4 *)(ws + 32 + j);
-                acc[32 + j] = __fmaf_rn(__int2float_rn(d1[j]), __fmul_rn(w4.x, xv), acc[32 + j]);
-                acc[33 + j] = __fmaf_rn(__int2float_rn(d1[j + 1]), __fmul_rn(w4.y, xv), acc[33 + j]);
-                acc[34 + j] = __fmaf_rn(__int2float_rn(d1[j + 2]), __fmul_rn(w4.z, xv), acc[34 + j]);
-                acc[35 + j] = __fmaf_rn(__int2float_rn(d1[j + 3]), __fmul_rn(w4.w, xv), acc[35 + j]);
-            }
-            if (g & 1) {   // both groups of step k done: release its stage (scales)
+            for (int j = 0; j < 32; j++) acc[j] = 0ull;
+            int dA[32], dB[32];
+            for (int g = 0; g < G; g++, gidx++) {
+                const int b = gidx % kTmemBufs, k = gidx >> 1, s = k % kStages;
+                // wait until group g's dots are in TMEM (and, once per step, its scales in smem)
+                bool got = mbar_wait(&tfull[b], (gidx / kTmemBufs) & 1, p.err, G4D_TIMEOUT_FULL | (0xffd << 8));
+                if ((gidx & 1) == 0)
+                    got = got && mbar_wait(&full[s], (k / kStages) & 1, p.err, G4D_TIMEOUT_FULL | (0xffc << 8));
+                if (!__all_sync(0xffffffffu, got)) {
+                    if (lane == 0) fail = 1;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const float *sc = (const float *)(smem + kOffS + s * kScaleBytes);
+                const float xv = sc[2 * kBN + (gidx & 1) * kBM + row];
+                const float *ws = sc + (gidx & 1) * kBN + ch * 64;
+                // (no load is left pending across the loop's back edge)
+                tmem_ld32(tbase + (uint32_t)(b * kBN), dA);
+                tmem_wait_ld();
+                tmem_ld32(tbase + (uint32_t)(b * kBN + 32), dB);   // in flight during the first half
+                chain32(acc, dA, ws, xv);
+                tmem_wait_ld();
+                tc_fence_before();
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
+                if (lane == 0) mbar_arrive(&tempty[b]);
+                chain32(acc + 16, dB, ws + 32, xv);
+                if (gidx & 1) {   // both groups of step k done: release its stage (scales)
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[s]);
+                }
             }
-        }
-        if (valid && !fail) {
-            const int nb = n0 + h * 64;
+            if (!ok || t >= p.T) continue;
+            const int nb = n0 + ch * 64;
             if (p.epi == EPI_STORE) {
                 float4 *o = (float4 *)(p.out + (size_t)t * p.out_stride + nb);
 #pragma unroll
-                for (int j = 0; j < 16; j++) o[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+                for (int j = 0; j < 16; j++) {
+                    const float2 a = upk(acc[2 * j]), b2 = upk(acc[2 * j + 1]);
+                    o[j] = make_float4(a.x, a.y, b2.x, b2.y);
+                }
             } else if (p.epi == EPI_GEGLU_PAIR) {
                 float *o = p.out + (size_t)t * p.out_stride + (nb >> 1);
 #pragma unroll
-                for (int j = 0; j < 32; j++)
-                    o[j] = geglu_one(acc[2 * j], acc[2 * j + 1], p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                for (int j = 0; j < 32; j++) {
+                    const float2 a = upk(acc[j]);
+                    o[j] = geglu_one(a.x, a.y, p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                }
             } else {
                 float *o = p.out + (size_t)t * p.out_stride + nb;
                 const float *u = p.ple_u + (size_t)t * p.u_stride + nb;
 #pragma unroll
-                for (int j = 0; j < 64; j++) o[j] = geglu_one(acc[j], u[j], p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                for (int j = 0; j < 32; j++) {
+                    const float2 a = upk(acc[j]);
+                    o[2 * j] = geglu_one(a.x, u[2 * j], p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                    o[2 * j + 1] = geglu_one(a.y, u[2 * j + 1], p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                }
             }
         }
     }
@@ -279,11 +334,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (fail && tid == 0) {
         // let issued copies and committed MMAs finish before the CTA exits
         const uint64_t t0n = g4_globaltimer();
-        for (int k = 0; k < issued; k++)
+        for (int k = issued > kStages ? issued - kStages : 0; k < issued; k++)
             while (!mbar_try_wait(&full[k % kStages], (k / kStages) & 1) && g4_globaltimer() - t0n < G4_WAIT_NS) {
             }
-        for (int g = committed > 2 ? committed - 2 : 0; g < committed; g++)
-            while (!mbar_try_wait(&tfull[g & 1], (g >> 1) & 1) && g4_globaltimer() - t0n < G4_WAIT_NS) {
+        for (int g = committed > kTmemBufs ? committed - kTmemBufs : 0; g < committed; g++)
+            while (!mbar_try_wait(&tfull[g % kTmemBufs], (g / kTmemBufs) & 1) &&
+                   g4_globaltimer() - t0n < G4_WAIT_NS) {
             }
     }
     __syncthreads();
@@ -328,7 +384,7 @@ bool make_map(CUtensorMap *m, const void *base, int K, int rows) {
 }  // namespace
 
 bool g4_gemm_tc_supported(const GemmArgs &a) {
-    return a.m.sT != nullptr && a.m.K % kBK == 0 && a.m.N % kBN == 0 && a.T >= 1 && encode_fn() != nullptr &&
+    return a.m.sT != nullptr && a.xsT != nullptr && a.T <= G4_XST_STRIDE && a.m.K % kBK == 0 && a.m.N % kBN == 0 && a.T >= 1 && encode_fn() != nullptr &&
            (a.epi == EPI_STORE || a.epi == EPI_GEGLU_PAIR || a.epi == EPI_PLE) && a.dots_out == nullptr;
 }
 
@@ -348,7 +404,7 @@ cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
     p.T = a.T;
     p.N = a.m.N;
     p.K = a.m.K;
-    p.xs = a.xs;
+    p.xsT = a.xsT;
     p.wsT = a.m.sT;
     p.epi = a.epi;
     p.out = a.out;
@@ -357,7 +413,9 @@ cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
     p.u_stride = a.u_stride;
     p.gelu = a.gelu;
     p.err = a.err;
-    dim3 grid(a.m.N / kBN, (a.T + kBM - 1) / kBM);
-    k_gemm_tc<<<grid, kThreads, kSmemBytes, st>>>(ma, mb, p);
+    static int sms = 0;
+    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int tiles = (a.m.N / kBN) * ((a.T + kBM - 1) / kBM);
+    k_gemm_tc<<<tiles < sms ? tiles : sms, kThreads, kSmemBytes, st>>>(ma, mb, p);
     return cudaGetLastError();
 }

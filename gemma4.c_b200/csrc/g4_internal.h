@@ -87,11 +87,14 @@ struct GemvArgs {
 };
 
 // ---- GEMM (prefill, T > 4) -------------------------------------------------
+constexpr int G4_XST_STRIDE = G4_BATCH;   // row stride of group-major activation scales
+
 struct GemmArgs {
     DMat m;
     int T;
     const int8_t *xq;       // [T][K]
     const float *xs;        // [T][K/64]
+    const float *xsT;       // [K/64][G4_XST_STRIDE] the same scales group-major (tensor-core path), or NULL
     int epi;                // GemvEpi subset: STORE, GEGLU_PAIR, PLE
     float *out;
     int out_stride;
@@ -186,12 +189,14 @@ cudaError_t g4_launch_repack(const int8_t *packed_w, const uint16_t *packed_s, i
                              int row_offset, int row_stride_mul, cudaStream_t st);
 cudaError_t g4_launch_rows_embed(const int *tokens, int T, DMat embed, DMat embed_ple, float mult, float ple_mult,
                                  float *res, float *ple_emb, int *err, cudaStream_t st, bool pdl);
+// xsT (optional): the scales again, group-major [K/64][G4_XST_STRIDE] (tensor-core GEMM)
 cudaError_t g4_launch_rows_quant(const float *src, int src_stride, int T, int K, int8_t *xq, float *xs,
-                                 cudaStream_t st, bool pdl);
+                                 cudaStream_t st, bool pdl, float *xsT = nullptr);
 // mode: 0 = norm+quant, 1 = res+norm+quant, 2 = res+quant, 3 = res finish (no quant)
 cudaError_t g4_launch_rows_norm(int mode, const float *src, int T, const float *w_post, const float *res_in,
                                 float *res_out, const float *scalar, const float *w_pre, float eps, int8_t *xq,
-                                float *xs, cudaStream_t st, bool pdl, float *y_out = nullptr, int strict = 0);
+                                float *xs, cudaStream_t st, bool pdl, float *y_out = nullptr, int strict = 0,
+                                float *xsT = nullptr);
 cudaError_t g4_launch_ple_prep(const float *pli, const float *ple_emb, const float *w, float eps, float scale, int T,
                                float *u, cudaStream_t st, bool pdl, int strict = 0);
 

@@ -72,14 +72,17 @@ __device__ float sumsq_row(const float (&v)[PER], int strict, float *buf, float 
 }
 
 // One warp per 64-group: x -> (q, scale) exactly as gemma4.c:265-279.
-__device__ void quant_group_warp(const float *src, int8_t *q, float *s) {
+__device__ void quant_group_warp(const float *src, int8_t *q, float *s, float *sT = nullptr) {
     const int lane = threadIdx.x & 31;
     const float a = src[lane], b = src[32 + lane];
     const float amax = warp_max(fmaxf(fabsf(a), fabsf(b)));
     const float sc = quant_scale(amax), inv = quant_inv(sc);
     q[lane] = (int8_t)quant_one(a, inv);
     q[32 + lane] = (int8_t)quant_one(b, inv);
-    if (lane == 0) *s = sc;
+    if (lane == 0) {
+        *s = sc;
+        if (sT) *sT = sc;   // group-major copy for the tensor-core GEMM
+    }
 }
 
 // residual <- embed(token) * mult; ple_emb <- embed_per_layer(token) * ple_mult
@@ -103,12 +106,14 @@ __global__ void __launch_bounds__(256) k_rows_embed(const int *tokens, DMat e, D
 }
 
 // grid (T, ceil(G/8)), 8 warps, one 64-group per warp
-__global__ void __launch_bounds__(256) k_rows_quant(const float *src, int src_stride, int K, int8_t *xq, float *xs) {
+__global__ void __launch_bounds__(256) k_rows_quant(const float *src, int src_stride, int K, int8_t *xq, float *xs,
+                                                    float *xsT) {
     griddep_launch();
     griddep_wait();
     const int t = blockIdx.x, g = blockIdx.y * 8 + (threadIdx.x >> 5), G = K / 64;
     if (g >= G) return;
-    quant_group_warp(src + (size_t)t * src_stride + g * 64, xq + (size_t)t * K + g * 64, xs + (size_t)t * G + g);
+    quant_group_warp(src + (size_t)t * src_stride + g * 64, xq + (size_t)t * K + g * 64, xs + (size_t)t * G + g,
+                     xsT ? xsT + (size_t)g * G4_XST_STRIDE + t : nullptr);
 }
 
 // Hidden-width (1536) row ops, one CTA per token row.
@@ -119,7 +124,7 @@ __global__ void __launch_bounds__(256) k_rows_quant(const float *src, int src_st
 __global__ void __launch_bounds__(256) k_rows_norm(int mode, const float *src, const float *w_post,
                                                    const float *res_in, float *res_out, const float *scalar,
                                                    const float *w_pre, float eps, int8_t *xq, float *xs,
-                                                   float *y_out, int strict) {
+                                                   float *y_out, int strict, float *xsT) {
     __shared__ float red[8];
     __shared__ __align__(16) float y[G4_HIDDEN];
     griddep_launch();
@@ -161,7 +166,8 @@ __global__ void __launch_bounds__(256) k_rows_norm(int mode, const float *src, c
     __syncthreads();
     const int warp = tid >> 5;
     for (int g = warp; g < G4_HIDDEN / 64; g += 8)
-        quant_group_warp(y + g * 64, xq + (size_t)t * G4_HIDDEN + g * 64, xs + (size_t)t * (G4_HIDDEN / 64) + g);
+        quant_group_warp(y + g * 64, xq + (size_t)t * G4_HIDDEN + g * 64, xs + (size_t)t * (G4_HIDDEN / 64) + g,
+                         xsT ? xsT + (size_t)g * G4_XST_STRIDE + t : nullptr);
 }
 
 // u[t][l][:] = (rmsnorm(pli[t][l][:], w, eps) + ple_emb[t][l][:]) * scale   (gemma4.c:474-477)
@@ -211,16 +217,16 @@ cudaError_t g4_launch_rows_embed(const int *tokens, int T, DMat embed, DMat embe
 }
 
 cudaError_t g4_launch_rows_quant(const float *src, int src_stride, int T, int K, int8_t *xq, float *xs,
-                                 cudaStream_t st, bool pdl) {
+                                 cudaStream_t st, bool pdl, float *xsT) {
     const int G = K / 64;
-    return g4_launch(k_rows_quant, dim3(T, (G + 7) / 8), dim3(256), 0, st, pdl, src, src_stride, K, xq, xs);
+    return g4_launch(k_rows_quant, dim3(T, (G + 7) / 8), dim3(256), 0, st, pdl, src, src_stride, K, xq, xs, xsT);
 }
 
 cudaError_t g4_launch_rows_norm(int mode, const float *src, int T, const float *w_post, const float *res_in,
                                 float *res_out, const float *scalar, const float *w_pre, float eps, int8_t *xq,
-                                float *xs, cudaStream_t st, bool pdl, float *y_out, int strict) {
+                                float *xs, cudaStream_t st, bool pdl, float *y_out, int strict, float *xsT) {
     return g4_launch(k_rows_norm, dim3(T), dim3(256), 0, st, pdl, mode, src, w_post, res_in, res_out, scalar, w_pre,
-                     eps, xq, xs, y_out, strict);
+                     eps, xq, xs, y_out, strict, xsT);
 }
 
 cudaError_t g4_launch_ple_prep(const float *pli, const float *ple_emb, const float *w, float eps, float scale, int T,

@@ -225,11 +225,17 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
     TK(cudaMemcpy(dxs.p, xs, (size_t)T * G * 4, cudaMemcpyHostToDevice));
     TK(g4_launch_repack((const int8_t *)pw.p, (const uint16_t *)ps.p, N, K, (int8_t *)w.p, (uint16_t *)s.p, 0, 1, 0));
     DMat m{(const int8_t *)w.p, (const uint16_t *)s.p, nullptr, N, K};
-    DevBuf sT;
+    DevBuf sT, xsT;
     if (path == 3) {
+        if (T > G4_XST_STRIDE) return G4_ERR_INVALID;
         TK(sT.alloc((size_t)N * G * 4));
         TK(g4_launch_scales_t(m.s, N, K, (float *)sT.p, 0));
         m.sT = (const float *)sT.p;
+        std::vector<float> h((size_t)G * G4_XST_STRIDE, 0.0f);   // group-major activation scales
+        for (int t = 0; t < T; t++)
+            for (int g = 0; g < G; g++) h[(size_t)g * G4_XST_STRIDE + t] = xs[(size_t)t * G + g];
+        TK(xsT.alloc(h.size() * 4));
+        TK(cudaMemcpy(xsT.p, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
     }
     if (path == 1) {
         GemvArgs a{};
@@ -251,6 +257,7 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
         a.T = T;
         a.xq = (const int8_t *)dxq.p;
         a.xs = (const float *)dxs.p;
+        a.xsT = (const float *)xsT.p;
         a.epi = EPI_STORE;
         a.out = (float *)dout.p;
         a.out_stride = N;
@@ -348,9 +355,11 @@ int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch
     const size_t tbytes = (size_t)N * G * 4;
     int copies = (int)((512ull << 20) / wbytes) + 1;
     if (copies > 16) copies = 16;
-    DevBuf w, sT, xq, xs, out, err;
+    DevBuf w, sT, xq, xs, xsT, out, err;
     TK(w.alloc(wbytes * copies));
     TK(sT.alloc(tbytes));
+    TK(xsT.alloc((size_t)G * G4_XST_STRIDE * 4));
+    TK(cudaMemset(xsT.p, 0, (size_t)G * G4_XST_STRIDE * 4));
     TK(xq.alloc((size_t)T * K));
     TK(xs.alloc((size_t)T * G * 4));
     TK(out.alloc((size_t)T * N * 4));
@@ -370,6 +379,7 @@ int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch
         a.T = T;
         a.xq = (const int8_t *)xq.p;
         a.xs = (const float *)xs.p;
+        a.xsT = (const float *)xsT.p;
         a.epi = EPI_STORE;
         a.out = (float *)out.p;
         a.out_stride = N;

@@ -6,8 +6,9 @@ reference's `./run --bench 512 128` decode figure (README.md:76) — one step is
 one token: forward(1 token) + logits, on the synthetic Gemma 4 E2B model of
 BASELINE config 1 (random-init weights in gemma4.c's .bin layout, seed 0; the
 real checkpoint is not available). Alongside: prefill tok/s at 512 and 16384,
-decode tok/s at 16384, the int8-GEMV roofline, and the reference CPU path timed
-on this host.
+decode tok/s at 16384, the HBM roofline of the decode step kernel, the int8
+tensor-core roofline of the prefill GEMM, and the reference CPU path timed on
+this host.
 
   python bench.py [--gpus N] [--steps K] [--warmup W]        # our CUDA path
   python bench.py --impl reference [...]                     # the reference's CPU path
@@ -35,6 +36,12 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "gemma4.c_b200"))
 
 PUBLISHED_DECODE_512 = 25.16   # README.md:76, tg128 @ d512, Ryzen 7 7700, 8 threads
+INT8_DENSE_TOPS = 4500.0       # B200 datasheet dense int8 (no measured int8 figure on this pool)
+# prefill GEMM shapes of one token through the model: (N, K, count) over the 35 layers
+# + per_layer_model_projection; lm_head is not part of a prefill chunk
+PREFILL_SHAPES = ((2560, 1536, 12), (5120, 1536, 3), (2048, 1536, 16), (4096, 1536, 4),
+                  (1536, 2048, 28), (1536, 4096, 7), (12288, 1536, 15), (24576, 1536, 20),
+                  (1536, 6144, 15), (1536, 12288, 20), (256, 1536, 35), (1536, 256, 35), (8960, 1536, 1))
 PREFILL = 512
 CTX_LONG = 16384
 
@@ -291,18 +298,29 @@ def run_ours(args, dist):
     e2e_ms = dist.max(max(m.elapsed(4, 5), wall * 1e3))
     e2e = dist.world * args.steps / (e2e_ms / 1e3)
 
-    # live kernel profile of one eager decode step: int8 GEMV class roofline
+    # device timeline of one decode step (per op class) and its algorithmic bytes:
+    # int8 weights + fp16 scales of every GEMV incl. lm_head, plus the KV read
     prof_ms, prof_bytes, prof_n = m.profile_decode(2, pos)
     pos += 1
-    gemv_gbs = prof_bytes[0] / (prof_ms[0] / 1e3) / 1e9
+    step_bytes = prof_bytes[0] + prof_bytes[1]
+    # the decode step is ONE kernel (k_decode): its roofline is the step's bytes
+    # over the step time measured above with CUDA events
+    dec_gbs = step_bytes / (per_step / 1e3) / 1e9
     traffic = None
     try:
-        with open(os.path.join(ROOT, "profiles", "decode_gemv_traffic.json")) as f:
-            ratio = json.load(f)["dram_bytes_per_algorithmic_byte"]
-        traffic = prof_bytes[0] / prof_n[0] * ratio
-    except (OSError, KeyError, ValueError, ZeroDivisionError):
+        with open(os.path.join(ROOT, "profiles", "decode_step_traffic.json")) as f:
+            traffic = float(json.load(f)["dram_bytes_per_launch"])
+    except (OSError, KeyError, ValueError):
         traffic = None
-    step_bytes = prof_bytes[0] + prof_bytes[1]
+
+    # prefill GEMM on the tensor cores at T = 512 over the model's shapes
+    gemm_ops = gemm_ms = 0.0
+    for N, K, cnt in PREFILL_SHAPES:
+        if cnt:
+            ms_g, ops_g = g4.bench_gemm(N, K, PREFILL, 3, iters=10)
+            gemm_ms += cnt * ms_g
+            gemm_ops += cnt * ops_g
+    gemm_tops = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms else 0.0
 
     # long context: prefill 16384 then decode
     long = {}
@@ -324,13 +342,17 @@ def run_ours(args, dist):
                    "l2": "weights streamed per step (2.35 GB) exceed L2 (126 MB)"},
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
         "gpu_launches": args.steps * m.launches_per_token(),
-        "roofline": {"bound": "hbm", "achieved": gemv_gbs, "peak": hbm_peak, "unit": "GB/s",
-                     "frac": gemv_gbs / hbm_peak, "traffic": traffic,
-                     "kernel": "int8 decode GEMV (all projections of one token)", "peak_kind": peak_kind},
-        "step_roofline": {"bytes_per_token": step_bytes, "achieved_gbs": step_bytes / (per_step / 1e3) / 1e9,
-                          "frac": step_bytes / (per_step / 1e3) / 1e9 / hbm_peak},
+        "roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": hbm_peak, "unit": "GB/s",
+                     "frac": dec_gbs / hbm_peak, "traffic": traffic, "algorithmic_bytes": step_bytes,
+                     "kernel": "k_decode: persistent single-token step (all int8 GEMVs incl. lm_head, "
+                               "attention, norms) = the only launch per step", "peak_kind": peak_kind},
         "profile_ms": {"gemv": prof_ms[0], "attention": prof_ms[1], "other": prof_ms[2],
-                       "launches": prof_n},
+                       "ops": prof_n, "source": "device timeline of one k_decode launch"},
+        "prefill_roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": INT8_DENSE_TOPS,
+                             "unit": "TOP/s", "frac": gemm_tops / INT8_DENSE_TOPS,
+                             "kernel": "k_gemm_tc (tcgen05 kind::i8, exact per-group fp32 chain) at T=512 over "
+                                       "the model's projection shapes",
+                             "peak_kind": "nominal dense int8 (datasheet); MEASURED_PEAKS.json has none"},
         "prefill_tok_s_512": dist.world * pre512,
     }
     line.update(long)

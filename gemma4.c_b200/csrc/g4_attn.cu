@@ -29,7 +29,8 @@ __global__ void __launch_bounds__(32) k_qkv_post(const AttnArgs a) {
     griddep_launch();
     griddep_wait();
     const int t = blockIdx.x, which = blockIdx.y;   // 0..7 q heads, 8 = k, 9 = v
-    const int p = a.start_pos + t;
+    const int p = a.row_pos ? a.row_pos[t] : a.start_pos + t;
+    const size_t so = a.row_seq ? (size_t)a.row_seq[t] * a.seq_stride : 0;
     float *src = a.qkv + (size_t)t * a.qkv_stride + which * HD;
     const int lane = threadIdx.x;
     for (int i = lane; i < HD; i += 32) x[i] = src[i];
@@ -38,9 +39,32 @@ __global__ void __launch_bounds__(32) k_qkv_post(const AttnArgs a) {
     const float *w = which < kHeads ? a.q_norm : (which == kHeads ? a.k_norm : nullptr);
     norm_rope_warp<HD>(x, w, cosr, sinr, a.pairs, which <= kHeads, a.strict != 0);
     float *dst = which < kHeads ? src
-                 : which == kHeads ? a.kcache + (size_t)(p & a.mask) * HD
-                                   : a.vcache + (size_t)(p & a.mask) * HD;
+                 : which == kHeads ? a.kcache + so + (size_t)(p & a.mask) * HD
+                                   : a.vcache + so + (size_t)(p & a.mask) * HD;
     for (int i = lane; i < HD; i += 32) dst[i] = x[i];
+}
+
+// ---------------------------------------------------------------------------
+// Row-batched decode attention (g4_forward_batch): grid (splits, rows) then
+// (8*HD/256, rows); the same split and combine arithmetic as single-sequence
+// decode, so a batch row gives the same bits as decoding that sequence alone.
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_rows(const AttnArgs a, int splits) {
+    extern __shared__ __align__(16) float sm[];
+    griddep_launch();
+    griddep_wait();
+    attn_rows_split<HD, DecodeKT<HD>::value>(a, blockIdx.y, blockIdx.x, splits, sm);
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_rows_combine(const AttnArgs a, int splits) {
+    __shared__ float wsm[256 + 16];
+    griddep_launch();
+    griddep_wait();
+    const int row = blockIdx.y;
+    attn_combine_part<HD>(a, a.row_pos[row], blockIdx.x, splits, wsm,
+                          a.part + (size_t)row * splits * kHeads * (HD + 4), a.out + (size_t)row * kHeads * HD,
+                          nullptr, nullptr);
 }
 
 // ---------------------------------------------------------------------------
@@ -64,7 +88,7 @@ __global__ void __launch_bounds__(256) k_attn_combine(const AttnArgs a, int spli
     __shared__ float wsm[256 + 16];
     griddep_launch();
     griddep_wait();
-    attn_combine_part<HD>(a, a.pos_dev ? *a.pos_dev : a.start_pos, blockIdx.x, splits, wsm);
+    attn_combine_part<HD>(a, a.pos_dev ? *a.pos_dev : a.start_pos, blockIdx.x, splits, wsm, a.part, a.out, a.xq, a.xs);
 }
 
 // ---------------------------------------------------------------------------
@@ -322,6 +346,26 @@ cudaError_t g4_launch_attn_decode(const AttnArgs &a, int splits, cudaStream_t st
         static bool once = false;
         if (!once) { cudaError_t e = set_smem(k_attn_decode<512>, smem); if (e) return e; once = true; }
         return g4_launch(k_attn_decode<512>, dim3(splits), dim3(256), smem, st, pdl, a, splits);
+    }
+    return cudaErrorInvalidValue;
+}
+
+cudaError_t g4_launch_attn_rows(const AttnArgs &a, int splits, cudaStream_t st, bool pdl) {
+    if (splits < 1 || splits > 256 || a.T < 1 || !a.row_seq || !a.row_pos) return cudaErrorInvalidValue;
+    const dim3 gs(splits, a.T), gc(kHeads * a.hd / 256, a.T);
+    if (a.hd == 256) {
+        const size_t smem = DecodeCfg<256>::smem;
+        static bool once = false;
+        if (!once) { cudaError_t e = set_smem(k_attn_rows<256>, smem); if (e) return e; once = true; }
+        cudaError_t e = g4_launch(k_attn_rows<256>, gs, dim3(256), smem, st, pdl, a, splits);
+        return e ? e : g4_launch(k_attn_rows_combine<256>, gc, dim3(256), 0, st, pdl, a, splits);
+    }
+    if (a.hd == 512) {
+        const size_t smem = DecodeCfg<512>::smem;
+        static bool once = false;
+        if (!once) { cudaError_t e = set_smem(k_attn_rows<512>, smem); if (e) return e; once = true; }
+        cudaError_t e = g4_launch(k_attn_rows<512>, gs, dim3(256), smem, st, pdl, a, splits);
+        return e ? e : g4_launch(k_attn_rows_combine<512>, gc, dim3(256), 0, st, pdl, a, splits);
     }
     return cudaErrorInvalidValue;
 }

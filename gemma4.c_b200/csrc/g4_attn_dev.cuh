@@ -131,56 +131,31 @@ __host__ __device__ constexpr int decode_smem_floats(int hd, int kt) {
 // K/V tiles of KT keys stream through a double-buffered cp.async pipeline.
 // Writes (max, sum, unnormalised output) per head to a.part.
 template <int HD, int KT>
-__device__ __noinline__ void attn_decode_split(const AttnArgs &a, int p, int split, int splits, float *sm) {
-    constexpr int LPK = 32 / KT, KS = HD + 4;
-    float *qn = sm;                       // [8][HD]
-    float *kn = qn + kHeads * HD;         // [HD]
-    float *vn = kn + HD;                  // [HD]
-    float *Ks = vn + HD;                  // [2][KT][KS]
-    float *Vs = Ks + 2 * KT * KS;         // [2][KT][HD]
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    int k0, k1;
-    const int active = split_range(p, a.window, splits, split, &k0, &k1);
-    if (split >= active) return;
+__device__ __noinline__ void attn_decode_split(const AttnArgs &a, int p, int split, int splits, float *sm);
 
+// The tile loop of one split: keys [k0, k1) of the ring (kc, vc) against the 8
+// query heads in qn[8][HD] (shared), one warp per head. When `kn` is given,
+// key `p` is taken from kn/vn (this CTA's own copy of the new key and value)
+// instead of the ring. Writes (max, sum, unnormalised output) per head to part.
+// first_issued: the caller already issued (and committed) tile 0 into buffer 0.
+template <int HD, int KT>
+G4_DEV void attn_split_core(const AttnArgs &a, const float *kc, const float *vc, int p, int k0, int k1,
+                            const float *qn, const float *kn, const float *vn, float *Ks, float *Vs, float *part_base,
+                            bool first_issued) {
+    constexpr int LPK = 32 / KT, KS = HD + 4;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     auto issue = [&](int tile, int buf) {
         const int kt = k0 + tile * KT, nt = min(KT, k1 - kt);
         for (int idx = tid; idx < nt * (HD / 4); idx += kAttnThreads) {
             const int r = idx / (HD / 4), c4 = idx - r * (HD / 4);
             const size_t slot = (size_t)((kt + r) & a.mask) * HD;
-            cp_async16(&Ks[(buf * KT + r) * KS + c4 * 4], a.kcache + slot + c4 * 4);
-            cp_async16(&Vs[(buf * KT + r) * HD + c4 * 4], a.vcache + slot + c4 * 4);
+            cp_async16(&Ks[(buf * KT + r) * KS + c4 * 4], kc + slot + c4 * 4);
+            cp_async16(&Vs[(buf * KT + r) * HD + c4 * 4], vc + slot + c4 * 4);
         }
         cp_async_commit();
     };
     const int ntiles = k1 > k0 ? (k1 - k0 + KT - 1) / KT : 0;
-    if (ntiles > 0) issue(0, 0);
-
-    // q of head `warp`; k and v (warps 0, 1) when the layer owns its cache. All
-    // loads first, then the per-warp norm + rope in registers.
-    constexpr int NI = HD / 32;
-    const float *cosr = a.rope_cos + (size_t)p * a.pairs, *sinr = a.rope_sin + (size_t)p * a.pairs;
-    const bool kv = a.has_kv && warp < 2;
-    float qv[NI], kvv[NI];
-#pragma unroll
-    for (int i = 0; i < NI; i++) {
-        qv[i] = a.qkv[warp * HD + lane + 32 * i];
-        kvv[i] = kv ? a.qkv[(kHeads + warp) * HD + lane + 32 * i] : 0.0f;
-    }
-    norm_rope_regs<HD>(qv, a.q_norm, cosr, sinr, a.pairs, true);
-#pragma unroll
-    for (int i = 0; i < NI; i++) qn[warp * HD + lane + 32 * i] = qv[i];
-    if (kv) {
-        norm_rope_regs<HD>(kvv, warp == 0 ? a.k_norm : nullptr, cosr, sinr, a.pairs, warp == 0);
-        float *x = warp == 0 ? kn : vn;
-        float *dst = (warp == 0 ? a.kcache : a.vcache) + (size_t)(p & a.mask) * HD;
-#pragma unroll
-        for (int i = 0; i < NI; i++) {
-            x[lane + 32 * i] = kvv[i];
-            if (split == 0) dst[lane + 32 * i] = kvv[i];
-        }
-    }
-    attn_sync();
+    if (ntiles > 0 && !first_issued) issue(0, 0);
 
     constexpr int NV = HD / 128;   // float4 output slices per lane
     float4 o[NV];
@@ -200,7 +175,7 @@ __device__ __noinline__ void attn_decode_split(const AttnArgs &a, int p, int spl
         }
         attn_sync();
         float *Kb = Ks + buf * KT * KS, *Vb = Vs + buf * KT * HD;
-        if (a.has_kv && p >= kt && p < kt + nt) {
+        if (kn && p >= kt && p < kt + nt) {
             // the new key/value: this CTA's copy (CTA 0 may still be writing the ring slot)
             const int r = p - kt;
             for (int i = tid; i < HD; i += kAttnThreads) {
@@ -250,7 +225,7 @@ __device__ __noinline__ void attn_decode_split(const AttnArgs &a, int p, int spl
         }
         attn_sync();
     }
-    float *part = a.part + ((size_t)split * kHeads + warp) * (HD + 4);
+    float *part = part_base + (size_t)warp * (HD + 4);
     if (lane == 0) {
         part[0] = m;
         part[1] = l;
@@ -259,11 +234,92 @@ __device__ __noinline__ void attn_decode_split(const AttnArgs &a, int p, int spl
     for (int i = 0; i < NV; i++) *(float4 *)&part[4 + 4 * lane + 128 * i] = o[i];
 }
 
-// Combine the active split partials into the attention output for 256 output
-// dimensions (combine block `blk` of 8*HD/256) and quantise them for o_proj
-// (gemma4.c:459). 256 threads, thread = one dimension. smem: 256 + 16 floats.
+// Decode (T = 1) split-KV attention at position p for split `split` of `splits`, run by 256
+// threads (8 warps; warp h = query head h). The CTA post-processes q (all
+// heads) and, on layers that own the cache, the new k/v; CTA 0 of the grid
+// writes k/v to the ring, and every CTA uses its own copy for key == pos.
+// K/V tiles of KT keys stream through a double-buffered cp.async pipeline.
+// Writes (max, sum, unnormalised output) per head to a.part.
+template <int HD, int KT>
+__device__ __noinline__ void attn_decode_split(const AttnArgs &a, int p, int split, int splits, float *sm) {
+    float *qn = sm;                       // [8][HD]
+    float *kn = qn + kHeads * HD;         // [HD]
+    float *vn = kn + HD;                  // [HD]
+    float *Ks = vn + HD;                  // [2][KT][HD + 4]
+    float *Vs = Ks + 2 * KT * (HD + 4);   // [2][KT][HD]
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int k0, k1;
+    const int active = split_range(p, a.window, splits, split, &k0, &k1);
+    if (split >= active) return;
+    // first K/V tile in flight while q, k and v are prepared
+    {
+        const int nt = min(KT, k1 - k0);
+        for (int idx = tid; idx < nt * (HD / 4); idx += kAttnThreads) {
+            const int r = idx / (HD / 4), c4 = idx - r * (HD / 4);
+            const size_t slot = (size_t)((k0 + r) & a.mask) * HD;
+            cp_async16(&Ks[r * (HD + 4) + c4 * 4], a.kcache + slot + c4 * 4);
+            cp_async16(&Vs[r * HD + c4 * 4], a.vcache + slot + c4 * 4);
+        }
+        cp_async_commit();
+    }
+
+    // q of head `warp`; k and v (warps 0, 1) when the layer owns its cache. All
+    // loads first, then the per-warp norm + rope in registers.
+    constexpr int NI = HD / 32;
+    const float *cosr = a.rope_cos + (size_t)p * a.pairs, *sinr = a.rope_sin + (size_t)p * a.pairs;
+    const bool kv = a.has_kv && warp < 2;
+    float qv[NI], kvv[NI];
+#pragma unroll
+    for (int i = 0; i < NI; i++) {
+        qv[i] = a.qkv[warp * HD + lane + 32 * i];
+        kvv[i] = kv ? a.qkv[(kHeads + warp) * HD + lane + 32 * i] : 0.0f;
+    }
+    norm_rope_regs<HD>(qv, a.q_norm, cosr, sinr, a.pairs, true);
+#pragma unroll
+    for (int i = 0; i < NI; i++) qn[warp * HD + lane + 32 * i] = qv[i];
+    if (kv) {
+        norm_rope_regs<HD>(kvv, warp == 0 ? a.k_norm : nullptr, cosr, sinr, a.pairs, warp == 0);
+        float *x = warp == 0 ? kn : vn;
+        float *dst = (warp == 0 ? a.kcache : a.vcache) + (size_t)(p & a.mask) * HD;
+#pragma unroll
+        for (int i = 0; i < NI; i++) {
+            x[lane + 32 * i] = kvv[i];
+            if (split == 0) dst[lane + 32 * i] = kvv[i];
+        }
+    }
+    attn_sync();
+    attn_split_core<HD, KT>(a, a.kcache, a.vcache, p, k0, k1, qn, a.has_kv ? kn : nullptr, vn, Ks, Vs,
+                            a.part + (size_t)split * kHeads * (HD + 4), true);
+}
+
+// Row-batched decode attention (g4_forward_batch): row `row` of a batch, its
+// sequence's ring and position from a.row_seq / a.row_pos; q already normalised
+// and rotated in a.qkv and the new k/v already in the ring (k_qkv_post).
+template <int HD, int KT>
+G4_DEV void attn_rows_split(const AttnArgs &a, int row, int split, int splits, float *sm) {
+    float *qn = sm;                       // [8][HD]
+    float *Ks = qn + kHeads * HD + 2 * HD;
+    float *Vs = Ks + 2 * KT * (HD + 4);
+    const int tid = threadIdx.x;
+    const int p = a.row_pos[row];
+    const size_t so = (size_t)a.row_seq[row] * a.seq_stride;
+    int k0, k1;
+    const int active = split_range(p, a.window, splits, split, &k0, &k1);
+    if (split >= active) return;
+    const float *q = a.qkv + (size_t)row * a.qkv_stride;
+    for (int i = tid; i < kHeads * HD / 4; i += kAttnThreads) ((float4 *)qn)[i] = ((const float4 *)q)[i];
+    attn_sync();
+    attn_split_core<HD, KT>(a, a.kcache + so, a.vcache + so, p, k0, k1, qn, nullptr, nullptr, Ks, Vs,
+                            a.part + ((size_t)row * splits + split) * kHeads * (HD + 4), false);
+}
+
+// Combine the active split partials (part_base: [splits][8][HD + 4]) into the
+// attention output out[8*HD] for 256 output dimensions (combine block `blk` of
+// 8*HD/256) and, when xq is given, quantise them for o_proj (gemma4.c:459).
+// 256 threads, thread = one dimension. smem: 256 + 16 floats.
 template <int HD>
-__device__ __noinline__ void attn_combine_part(const AttnArgs &a, int p, int blk, int splits, float *wsm) {
+__device__ __noinline__ void attn_combine_part(const AttnArgs &a, int p, int blk, int splits, float *wsm,
+                                               const float *part_base, float *out, int8_t *xq, float *xs) {
     float *red = wsm + 256;
     const int tid = threadIdx.x;
     int k0, k1;
@@ -272,7 +328,7 @@ __device__ __noinline__ void attn_combine_part(const AttnArgs &a, int p, int blk
     const int h = blk / per_head, d = (blk % per_head) * 256 + tid;
     const int warp = tid >> 5, lane = tid & 31;
     const size_t stride = (size_t)kHeads * (HD + 4);
-    const float *ph = a.part + (size_t)h * (HD + 4);
+    const float *ph = part_base + (size_t)h * (HD + 4);
     // this thread's values of the first splits are loaded before the weights
     // exist, so that both loads share one memory round trip
     constexpr int U = 16;
@@ -307,14 +363,18 @@ __device__ __noinline__ void attn_combine_part(const AttnArgs &a, int p, int blk
     }
     o = o / red[8];
     const int col = h * HD + d;
-    a.out[col] = o;
+    out[col] = o;
+    if (!xq) {
+        attn_sync();   // wsm / red are reused by the caller's next combine
+        return;
+    }
     float amax = warp_max(fabsf(o));
     if (lane == 0) red[warp] = amax;
     attn_sync();
     amax = fmaxf(red[warp & ~1], red[warp | 1]);
     const float sc = quant_scale(amax), inv = quant_inv(sc);
-    a.xq[col] = (int8_t)quant_one(o, inv);
-    if ((tid & 63) == 0) a.xs[col >> 6] = sc;
+    xq[col] = (int8_t)quant_one(o, inv);
+    if ((tid & 63) == 0) xs[col >> 6] = sc;
     attn_sync();
 }
 

@@ -543,8 +543,12 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(const DecodeParams P) {
             break;
         case OP_COMBINE:
             if ((int)blockIdx.x < kHeads * op.at.hd / 256) {
-                if (op.at.hd == 256) attn_combine_part<256>(op.at, pos, blockIdx.x, P.splits, scratch);
-                else attn_combine_part<512>(op.at, pos, blockIdx.x, P.splits, scratch);
+                if (op.at.hd == 256)
+                    attn_combine_part<256>(op.at, pos, blockIdx.x, P.splits, scratch, op.at.part, op.at.out, op.at.xq,
+                                           op.at.xs);
+                else
+                    attn_combine_part<512>(op.at, pos, blockIdx.x, P.splits, scratch, op.at.part, op.at.out, op.at.xq,
+                                           op.at.xs);
             }
             break;
         case OP_PLE_PREP: ple_prep_op(op, red); break;

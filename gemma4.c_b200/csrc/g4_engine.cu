@@ -88,6 +88,15 @@ struct g4_ctx {
     bool persistent = true;          // G4_OPT_PERSISTENT
     void *scales_t = nullptr;        // group-major fp32 weight scales (tensor-core GEMM)
     size_t scales_t_bytes = 0;
+    // multi-sequence serving (g4_seq_alloc / g4_forward_batch / g4_logits_batch)
+    int max_seqs = 0;
+    void *bkv = nullptr, *bbuf = nullptr;
+    size_t bkv_bytes = 0;
+    float *bk[G4_NUM_LAYERS] = {}, *bv[G4_NUM_LAYERS] = {};   // sequence 0's K and V of the ring a layer reads
+    int bring[G4_NUM_LAYERS] = {};
+    int *row_seq_d = nullptr, *row_pos_d = nullptr, *bargmax = nullptr;
+    float *bpart = nullptr, *blogits = nullptr, *bres = nullptr, *embed_st = nullptr;
+    std::vector<int> blast;          // last row of each sequence of the last batch
     bool pending = false;            // a single-token forward waiting to be launched
     DecodeOp *dec_fwd = nullptr, *dec_fwdlog = nullptr;
     int n_fwd = 0, n_fwdlog = 0, dec_cur = 0, dec_layers = 0;
@@ -712,7 +721,14 @@ cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev, P
     return q.e;
 }
 
-cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos) {
+// Multi-sequence batch: rows carry their own (sequence, position) (single-token
+// rows of several sequences), or all rows are one sequence `seq` from start_pos.
+struct BatchPlan {
+    bool rows;
+    int seq;
+};
+
+cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp = nullptr) {
     Seq q{c, c->use_pdl};
     int cur = 0;
     q.ck(g4_launch_rows_embed(c->tokens_d, T, c->embed, c->embed_ple, sqrtf((float)G4_HIDDEN), sqrtf((float)G4_PLE),
@@ -734,8 +750,26 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos) {
         }
         gemm(q, Y.qkv, T, EPI_STORE, c->qkv, kQkvStride, nullptr, 0);
         AttnArgs at = attn_base(c, Y, T, start_pos, nullptr);
+        if (bp) {   // the batch rings: [sequence][K ring | V ring]
+            const size_t stride = (size_t)2 * c->bring[l] * Y.hd;
+            at.mask = c->bring[l] - 1;
+            at.kcache = c->bk[l];
+            at.vcache = c->bv[l];
+            if (bp->rows) {
+                at.row_seq = c->row_seq_d;
+                at.row_pos = c->row_pos_d;
+                at.seq_stride = stride;
+                at.part = c->bpart;
+            } else {
+                at.kcache += (size_t)bp->seq * stride;
+                at.vcache += (size_t)bp->seq * stride;
+            }
+        }
         q.ck(g4_launch_qkv_post(at, c->st, q.pdl));
-        q.ck(c->strict ? g4_launch_attn_strict(at, c->st, q.pdl) : g4_launch_attn_prefill(at, c->st, q.pdl));
+        if (bp && bp->rows)
+            q.ck(g4_launch_attn_rows(at, kSplits, c->st, q.pdl));
+        else
+            q.ck(c->strict ? g4_launch_attn_strict(at, c->st, q.pdl) : g4_launch_attn_prefill(at, c->st, q.pdl));
         q.ck(g4_launch_rows_quant(c->attn, Y.qw, T, Y.qw, c->xq, c->xs, c->st, q.pdl, c->xsT));
         gemm(q, Y.o, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
         q.ck(g4_launch_rows_norm(1, c->h, T, Y.post_attn, c->res[cur], c->res[cur ^ 1], nullptr, Y.pre_ffn, G4_RMS_EPS,
@@ -928,6 +962,8 @@ int g4_close(g4_ctx *c) {
         if (c->events[i]) cudaEventDestroy(c->events[i]);
     if (c->arena) cudaFree(c->arena);
     if (c->scales_t) cudaFree(c->scales_t);
+    if (c->bkv) cudaFree(c->bkv);
+    if (c->bbuf) cudaFree(c->bbuf);
     if (c->state) cudaFree(c->state);
     if (c->kv) cudaFree(c->kv);
     if (c->scores) cudaFree(c->scores);
@@ -1261,8 +1297,141 @@ int g4_profiler_range(int on) {
 int g4_device_bytes(g4_ctx *c, uint64_t *weights, uint64_t *total) {
     if (!c) return G4_ERR_INVALID;
     if (weights) *weights = c->arena_used;
-    if (total) *total = c->arena_bytes + c->kv_bytes;
+    if (total) *total = c->arena_bytes + c->kv_bytes + c->bkv_bytes;
     return G4_OK;
+}
+
+// ---- multi-sequence serving ------------------------------------------------
+
+int g4_seq_alloc(g4_ctx *c, int max_seqs, int max_context) {
+    if (!c || max_seqs < 1 || max_seqs > G4_MAX_SEQS || max_context < 1 || max_context > G4_MAX_CONTEXT)
+        return G4_ERR_INVALID;
+    cudaSetDevice(c->device);
+    if (int rc = flush_pending(c)) return rc;
+    CK(cudaStreamSynchronize(c->st));
+    if (c->bkv) cudaFree(c->bkv);
+    if (c->bbuf) cudaFree(c->bbuf);
+    c->bkv = c->bbuf = nullptr;
+    c->max_seqs = 0;
+    c->blast.clear();
+    int gring = 1024;
+    while (gring < max_context) gring <<= 1;
+    // per sequence: the 12 sliding owner rings (1024 slots) and the 3 global owner rings (gring slots)
+    const size_t sl = (size_t)2 * G4_SLIDING_RING * G4_HD_SLIDING * 4, gl = (size_t)2 * gring * G4_HD_GLOBAL * 4;
+    c->bkv_bytes = (size_t)max_seqs * (12 * sl + 3 * gl);
+    if (cudaMalloc(&c->bkv, c->bkv_bytes) != cudaSuccess) {
+        c->bkv = nullptr;
+        c->bkv_bytes = 0;
+        return fail(c, G4_ERR_NOMEM, "sequence KV: %zu bytes", (size_t)max_seqs * (12 * sl + 3 * gl));
+    }
+    for (int l = 0; l < G4_NUM_LAYERS; l++) {
+        const Layer &Y = c->L[l];
+        const int o = Y.owner;
+        uint8_t *base = (uint8_t *)c->bkv;
+        if (Y.global) {
+            c->bring[l] = gring;
+            c->bk[l] = (float *)(base + (size_t)max_seqs * 12 * sl + (size_t)(o / 5) * max_seqs * gl);
+        } else {
+            c->bring[l] = G4_SLIDING_RING;
+            c->bk[l] = (float *)(base + (size_t)((o / 5) * 4 + o % 5) * max_seqs * sl);
+        }
+        c->bv[l] = c->bk[l] + (size_t)c->bring[l] * Y.hd;
+    }
+    // rows, split partials (one row per sequence), logits, gathered residual rows, lm_head scales
+    const size_t part = (size_t)max_seqs * kSplits * G4_HEADS * (G4_HD_GLOBAL + 4) * 4;
+    const size_t logits = (size_t)max_seqs * G4_VOCAB * 4;
+    const size_t est = (size_t)G4_VOCAB * (G4_HIDDEN / 64) * 4;
+    size_t off[8], tot = 0;
+    const size_t sz[8] = {(size_t)G4_BATCH * 4, (size_t)G4_BATCH * 4, (size_t)max_seqs * 4, part, logits,
+                          (size_t)max_seqs * G4_HIDDEN * 4, est, 0};
+    for (int i = 0; i < 7; i++) {
+        off[i] = tot;
+        tot += (sz[i] + 255) & ~(size_t)255;
+    }
+    if (cudaMalloc(&c->bbuf, tot) != cudaSuccess) {
+        c->bbuf = nullptr;
+        return fail(c, G4_ERR_NOMEM, "sequence buffers: %zu bytes", tot);
+    }
+    uint8_t *b = (uint8_t *)c->bbuf;
+    c->row_seq_d = (int *)(b + off[0]);
+    c->row_pos_d = (int *)(b + off[1]);
+    c->bargmax = (int *)(b + off[2]);
+    c->bpart = (float *)(b + off[3]);
+    c->blogits = (float *)(b + off[4]);
+    c->bres = (float *)(b + off[5]);
+    c->embed_st = (float *)(b + off[6]);
+    CK(g4_launch_scales_t(c->embed.s, G4_VOCAB, G4_HIDDEN, c->embed_st, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    c->max_seqs = max_seqs;
+    return G4_OK;
+}
+
+int g4_forward_batch(g4_ctx *c, int n, const int *seq_ids, const int *tokens, const int *offsets,
+                     const int *start_pos) {
+    if (!c) return G4_ERR_INVALID;
+    if (!c->max_seqs) return fail(c, G4_ERR_STATE, "forward_batch: call g4_seq_alloc first");
+    if (c->strict) return fail(c, G4_ERR_STATE, "forward_batch: not available in strict mode");
+    if (n < 1 || n > c->max_seqs || !seq_ids || !tokens || !offsets || !start_pos || offsets[0] != 0)
+        return fail(c, G4_ERR_INVALID, "forward_batch: bad arguments (n %d)", n);
+    const int T = offsets[n];
+    if (T < 1 || T > G4_BATCH) return fail(c, G4_ERR_INVALID, "forward_batch: %d rows (1..%d)", T, G4_BATCH);
+    std::vector<int> rs(T), rp(T);
+    for (int i = 0; i < n; i++) {
+        const int cnt = offsets[i + 1] - offsets[i];
+        if (cnt < 1 || (n > 1 && cnt != 1))
+            return fail(c, G4_ERR_INVALID, "forward_batch: sequence %d has %d tokens (several sequences: 1 each)", i,
+                        cnt);
+        if (seq_ids[i] < 0 || seq_ids[i] >= c->max_seqs)
+            return fail(c, G4_ERR_INVALID, "forward_batch: sequence id %d out of range", seq_ids[i]);
+        for (int j = 0; j < i; j++)
+            if (seq_ids[j] == seq_ids[i]) return fail(c, G4_ERR_INVALID, "forward_batch: sequence %d twice", seq_ids[i]);
+        const long long last = (long long)start_pos[i] + cnt - 1;
+        if (start_pos[i] < 0 || last >= c->bring[4] || last >= G4_MAX_CONTEXT)
+            return fail(c, G4_ERR_INVALID, "forward_batch: positions %d..%lld beyond the sequence capacity %d",
+                        start_pos[i], last, c->bring[4]);
+        for (int k = 0; k < cnt; k++) {
+            const int tk = tokens[offsets[i] + k];
+            if (tk < 0 || tk >= G4_VOCAB) return fail(c, G4_ERR_INVALID, "forward_batch: token %d out of range", tk);
+            rs[offsets[i] + k] = seq_ids[i];
+            rp[offsets[i] + k] = start_pos[i] + k;
+        }
+    }
+    cudaSetDevice(c->device);
+    if (int rc = flush_pending(c)) return rc;
+    CK(cudaMemcpyAsync(c->tokens_d, tokens, (size_t)T * 4, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemcpyAsync(c->row_seq_d, rs.data(), (size_t)T * 4, cudaMemcpyHostToDevice, c->st));
+    CK(cudaMemcpyAsync(c->row_pos_d, rp.data(), (size_t)T * 4, cudaMemcpyHostToDevice, c->st));
+    // one sequence with several tokens: the prefill attention over its ring; else one row per sequence
+    // (single-token rows use the same split attention as single-sequence decode)
+    BatchPlan bp{T == n, seq_ids[0]};
+    cudaError_t e = enqueue_prefill(c, T, start_pos[0], &bp);
+    if (e) return fail(c, G4_ERR_CUDA, "forward_batch launch: %s", cudaGetErrorString(e));
+    c->last_T = 0;   // the single-sequence rows are gone
+    c->blast.resize(n);
+    for (int i = 0; i < n; i++) c->blast[i] = offsets[i + 1] - 1;
+    // the host vectors above are pageable: the copies completed before the calls returned
+    return G4_OK;
+}
+
+int g4_logits_batch(g4_ctx *c, int *argmax, float *logits) {
+    if (!c) return G4_ERR_INVALID;
+    if (c->blast.empty()) return fail(c, G4_ERR_STATE, "logits_batch: no batch forward to read");
+    cudaSetDevice(c->device);
+    const int n = (int)c->blast.size();
+    for (int i = 0; i < n; i++)
+        CK(cudaMemcpyAsync(c->bres + (size_t)i * G4_HIDDEN, c->res[c->cur] + (size_t)c->blast[i] * G4_HIDDEN,
+                           G4_HIDDEN * 4, cudaMemcpyDeviceToDevice, c->st));
+    Seq q{c, c->use_pdl};
+    q.ck(g4_launch_rows_norm(0, c->bres, n, nullptr, nullptr, nullptr, nullptr, c->final_norm, G4_RMS_EPS, c->xq,
+                             c->xs, c->st, q.pdl, nullptr, 0, c->xsT));
+    DMat em = c->embed;
+    em.sT = c->embed_st;
+    gemm(q, em, n, EPI_STORE, c->blogits, G4_VOCAB, nullptr, 0);
+    q.ck(g4_launch_softcap_argmax(c->blogits, n, G4_VOCAB, c->bargmax, c->st));
+    if (q.e) return fail(c, G4_ERR_CUDA, "logits_batch launch: %s", cudaGetErrorString(q.e));
+    if (argmax) CK(cudaMemcpyAsync(argmax, c->bargmax, (size_t)n * 4, cudaMemcpyDeviceToHost, c->st));
+    if (logits) CK(cudaMemcpyAsync(logits, c->blogits, (size_t)n * G4_VOCAB * 4, cudaMemcpyDeviceToHost, c->st));
+    return check_device_error(c);
 }
 
 }  // extern "C"

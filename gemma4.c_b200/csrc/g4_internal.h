@@ -128,6 +128,11 @@ struct AttnArgs {
     int strict;             // reference-order norms / softmax / value sums
     float *scores;          // strict: [T][8][score_stride] scratch
     int score_stride;
+    // multi-sequence batches (g4_forward_batch): row t belongs to sequence
+    // row_seq[t] at position row_pos[t]; sequence s's ring starts seq_stride
+    // floats after sequence 0's. NULL row_seq: one sequence, positions start_pos + t.
+    const int *row_seq, *row_pos;
+    size_t seq_stride;
 };
 
 // ---- persistent decode step (g4_decode.cu) ---------------------------------
@@ -174,12 +179,16 @@ int g4_decode_max_stages(const DecodeOp *ops, int nops, int grid);
 
 // ---- launchers (g4_*.cu) ---------------------------------------------------
 cudaError_t g4_launch_scales_t(const uint16_t *s, int N, int K, float *sT, cudaStream_t st);
+cudaError_t g4_launch_softcap_argmax(float *logits, int rows, int n, int *argmax, cudaStream_t st);
 int g4_gemv_smem_bytes(const GemvArgs &a, int stages);
 // Fills the launch plan (rb = most rows one CTA owns) for a grid of `grid` CTAs.
 void g4_gemv_plan(GemvArgs &a, int grid);
 cudaError_t g4_launch_gemv(const GemvArgs &a, int pro, int epi, int grid, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_gemm(const GemmArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_decode(const AttnArgs &a, int splits, cudaStream_t st, bool pdl);
+// one token per row, each row its own sequence and position (q/k/v already
+// post-processed by g4_launch_qkv_post): split-KV partials then combine into a.out
+cudaError_t g4_launch_attn_rows(const AttnArgs &a, int splits, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_combine(const AttnArgs &a, int splits, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_qkv_post(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_prefill(const AttnArgs &a, cudaStream_t st, bool pdl);

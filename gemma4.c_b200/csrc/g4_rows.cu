@@ -194,7 +194,42 @@ __global__ void k_scales_t(const uint16_t *s, int N, int G, float *sT) {
     sT[i] = h2f(s[(size_t)n * G + g]);
 }
 
+// Logit soft-cap in place and the first maximum of each row (gemma4.c:519,
+// :537-541): one CTA per row.
+__global__ void __launch_bounds__(1024) k_softcap_argmax(float *logits, int n, int *argmax) {
+    __shared__ float bvs[32];
+    __shared__ int bis[32];
+    float *x = logits + (size_t)blockIdx.x * n;
+    float bv = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+        const float v = __fmul_rn(30.0f, tanhf(__fdiv_rn(x[i], 30.0f)));
+        x[i] = v;
+        if (v > bv) { bv = v; bi = i; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+    }
+    const int w = threadIdx.x >> 5;
+    if ((threadIdx.x & 31) == 0) { bvs[w] = bv; bis[w] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int k = 1; k < (int)(blockDim.x >> 5); k++)
+            if (bvs[k] > bv || (bvs[k] == bv && bis[k] < bi)) { bv = bvs[k]; bi = bis[k]; }
+        argmax[blockIdx.x] = bi;
+    }
+}
+
 }  // namespace
+
+cudaError_t g4_launch_softcap_argmax(float *logits, int rows, int n, int *argmax, cudaStream_t st) {
+    if (rows < 1) return cudaErrorInvalidValue;
+    k_softcap_argmax<<<rows, 1024, 0, st>>>(logits, n, argmax);
+    return cudaGetLastError();
+}
 
 cudaError_t g4_launch_scales_t(const uint16_t *s, int N, int K, float *sT, cudaStream_t st) {
     const size_t n = (size_t)N * (K / 64);

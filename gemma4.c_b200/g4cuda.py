@@ -89,6 +89,9 @@ def load(path=LIB_PATH):
     L.g4_trace_decode.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_double),
                                   C.POINTER(C.c_int)]
     L.g4_topk_noalloc.argtypes = [vp, C.c_int, C.c_int, vp, vp, vp]
+    L.g4_seq_alloc.argtypes = [vp, C.c_int, C.c_int]
+    L.g4_forward_batch.argtypes = [vp, C.c_int, _i32p, _i32p, _i32p, _i32p]
+    L.g4_logits_batch.argtypes = [vp, vp, vp]
     _lib = L
     return L
 
@@ -206,6 +209,29 @@ class Model:
         _check(self.L.g4_trace_decode(self.h, token, pos, cap, types, t, C.byref(n)), self.h)
         k = min(n.value, cap)
         return np.array(types[:k], np.int32), np.array(t[:6 * k], np.float64).reshape(k, 6)
+
+    # ---- multi-sequence serving ----
+    def seq_alloc(self, max_seqs, max_context):
+        _check(self.L.g4_seq_alloc(self.h, max_seqs, max_context), self.h)
+
+    def forward_batch(self, seq_ids, token_lists, start_pos):
+        """token_lists[i] (list/array of ids) for sequence seq_ids[i] from start_pos[i]."""
+        seq_ids = np.ascontiguousarray(seq_ids, np.int32)
+        lens = [len(t) for t in token_lists]
+        offsets = np.zeros(len(lens) + 1, np.int32)
+        offsets[1:] = np.cumsum(lens)
+        toks = np.ascontiguousarray(np.concatenate([np.asarray(t, np.int32) for t in token_lists]), np.int32)
+        _check(self.L.g4_forward_batch(self.h, len(lens), seq_ids, toks, offsets,
+                                       np.ascontiguousarray(start_pos, np.int32)), self.h)
+        self._batch_n = len(lens)
+
+    def logits_batch(self, want_logits=False):
+        """(logits [n][vocab] or None, argmax [n]) of the last forward_batch."""
+        n = self._batch_n
+        am = np.zeros(n, np.int32)
+        lg = np.zeros((n, VOCAB), np.float32) if want_logits else None
+        _check(self.L.g4_logits_batch(self.h, am.ctypes.data, lg.ctypes.data if lg is not None else None), self.h)
+        return lg, am
 
     def launches_per_token(self):
         n = C.c_int()

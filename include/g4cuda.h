@@ -112,6 +112,31 @@ const char *g4_strerror(int code);
 #define G4_OPT_PERSISTENT 6
 int g4_set_option(g4_ctx *ctx, int option, int value);
 
+/* ---- multi-sequence serving (ragged batches of independent sequences) ----
+ * No reference counterpart in gemma4.c (one sequence per process); the
+ * single-sequence calls above are unaffected and keep their own KV cache.
+ *
+ * g4_seq_alloc: device KV rings for `max_seqs` sequences (<= G4_MAX_SEQS)
+ * holding positions 0 .. max_context - 1 each (global rings rounded up to a
+ * power of two >= 1024; sliding rings 1024). Re-allocating drops all sequences.
+ *
+ * g4_forward_batch: `n` sequences; sequence seq_ids[i] (distinct, < max_seqs)
+ * consumes tokens[offsets[i] .. offsets[i+1]) at positions start_pos[i] ...,
+ * offsets[0] == 0 and offsets[n] <= 512 rows in total. Either one sequence
+ * with up to 512 tokens (a prefill chunk, in order as for g4_forward) or
+ * several sequences with exactly one token each (a decode step). A batch row
+ * computes the same bits as the same token through g4_forward on a context
+ * holding only that sequence. Not available in strict mode.
+ *
+ * g4_logits_batch: for each sequence of the last g4_forward_batch, the
+ * soft-capped logits of its last token (logits: [n][262144] or NULL) and the
+ * greedy argmax (argmax: [n] or NULL). */
+#define G4_MAX_SEQS 256
+int g4_seq_alloc(g4_ctx *ctx, int max_seqs, int max_context);
+int g4_forward_batch(g4_ctx *ctx, int n, const int *seq_ids, const int *tokens, const int *offsets,
+                     const int *start_pos);
+int g4_logits_batch(g4_ctx *ctx, int *argmax, float *logits);
+
 /* ---- introspection (tests, benchmarks) ---- */
 int g4_read_residual(g4_ctx *ctx, size_t rows, float *out);          /* [rows][1536] */
 /* `nslots` ring slots of the K (which=0) or V (which=1) cache `layer` reads. */

@@ -269,6 +269,65 @@ def prefill_timed(m, n, reps, dist):
     return n / (np.mean(times) / 1e3), float(np.mean(times))
 
 
+def batched_serving(m, dist, seqs=64):
+    """BASELINE config 5 on this GPU: 64 independent sequences, prompts
+    log-uniform in [128, 8192], decode lengths uniform in [32, 512], ids
+    uniform (seed 2 + rank). Each prompt is prefilled (512-token chunks) and its
+    first token sampled; then all unfinished sequences decode together, one
+    token per sequence per step, greedy, through g4_forward_batch /
+    g4_logits_batch (argmax read back every step). Times: CUDA events on the
+    library stream, max over ranks."""
+    import g4cuda as g4
+    rng = np.random.default_rng(2 + dist.rank)
+    plen = np.exp(rng.uniform(np.log(128), np.log(8192), seqs)).astype(np.int64)
+    dlen = rng.integers(32, 513, seqs)
+    prompts = [rng.integers(0, g4.VOCAB, size=int(n)).astype(np.int32) for n in plen]
+    m.seq_alloc(seqs, int(plen.max() + dlen.max()))
+    m.sync()
+    dist.barrier()
+    m.mark(6)
+    nxt = np.zeros(seqs, np.int32)
+    for i, p in enumerate(prompts):
+        for s0 in range(0, len(p), 512):
+            m.forward_batch([i], [p[s0:s0 + 512]], [s0])
+        _, am = m.logits_batch()
+        nxt[i] = am[0]
+    m.mark(7)
+    pos = plen.copy()
+    left = dlen - 1                      # the first token came with the prefill
+    steps = generated = 0
+    kv_bytes = 0.0
+    while True:
+        act = np.nonzero(left > 0)[0]
+        if act.size == 0:
+            break
+        m.forward_batch(act.astype(np.int32), [[int(nxt[i])] for i in act], pos[act].astype(np.int32))
+        _, am = m.logits_batch()
+        nxt[act] = am
+        # KV read this step: sliding layers min(ctx, 512) keys, global layers all keys, fp32 K + V
+        ctx = pos[act] + 1
+        kv_bytes += float((28 * np.minimum(ctx, 512) * 256 * 8 + 7 * ctx * 512 * 8).sum())
+        pos[act] += 1
+        left[act] -= 1
+        steps += 1
+        generated += act.size
+    m.mark(8)
+    pre_ms = dist.max(m.elapsed(6, 7))
+    dec_ms = dist.max(m.elapsed(7, 8))
+    weights = 2350706688.0
+    total_prompt = int(plen.sum())
+    return {
+        "workload": f"{seqs} sequences per GPU, prompts log-uniform [128, 8192] (sum {total_prompt}), "
+                    f"decode lengths U[32, 512] (sum {int(dlen.sum())}), greedy, seed 2+rank",
+        "prefill_tok_s": dist.world * total_prompt / (pre_ms / 1e3),
+        "decode_tok_s": dist.world * generated / (dec_ms / 1e3),
+        "total_tok_s": dist.world * (total_prompt + int(dlen.sum())) / ((pre_ms + dec_ms) / 1e3),
+        "decode_steps": steps,
+        "decode_hbm_gbs_per_gpu": (steps * weights + kv_bytes) / (dec_ms / 1e3) / 1e9,
+        "prefill_s": pre_ms / 1e3, "decode_s": dec_ms / 1e3,
+    }
+
+
 def run_ours(args, dist):
     import g4cuda as g4
     hbm_peak, peak_kind = peaks()
@@ -322,6 +381,8 @@ def run_ours(args, dist):
             gemm_ops += cnt * ops_g
     gemm_tops = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms else 0.0
 
+    batched = batched_serving(m, dist) if not args.no_batched else None
+
     # long context: prefill 16384 then decode
     long = {}
     if not args.short:
@@ -356,6 +417,8 @@ def run_ours(args, dist):
         "prefill_tok_s_512": dist.world * pre512,
     }
     line.update(long)
+    if batched:
+        line["batched"] = batched
     if clk:
         line["clocks"] = clk
     m.close()
@@ -378,6 +441,7 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--short", action="store_true", help="skip the 16384-context runs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-batched", action="store_true", help="skip the 64-sequence serving run (config 5)")
     ap.add_argument("--profile-range", action="store_true",
                     help="open the profiler capture range around the timed decode steps only "
                          "(for ncu --profile-from-start off)")

@@ -90,6 +90,7 @@ struct g4_ctx {
     size_t scales_t_bytes = 0;
     // multi-sequence serving (g4_seq_alloc / g4_forward_batch / g4_logits_batch)
     int max_seqs = 0;
+    int batch_splits = 0;            // G4_OPT_BATCH_SPLITS: 0 = auto
     void *bkv = nullptr, *bbuf = nullptr;
     size_t bkv_bytes = 0;
     float *bk[G4_NUM_LAYERS] = {}, *bv[G4_NUM_LAYERS] = {};   // sequence 0's K and V of the ring a layer reads
@@ -766,8 +767,13 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp
             }
         }
         q.ck(g4_launch_qkv_post(at, c->st, q.pdl));
-        if (bp && bp->rows)
-            q.ck(g4_launch_attn_rows(at, kSplits, c->st, q.pdl));
+        if (bp && bp->rows) {
+            // key splits per row: about four CTAs per SM over the batch but at least 16
+            // (each split's tile loop is latency-bound), or a fixed count
+            int sp = c->batch_splits ? c->batch_splits : (4 * c->num_sms + T - 1) / T;
+            sp = sp < 16 ? 16 : sp > kSplits ? kSplits : sp;
+            q.ck(g4_launch_attn_rows(at, sp, c->st, q.pdl));
+        }
         else
             q.ck(c->strict ? g4_launch_attn_strict(at, c->st, q.pdl) : g4_launch_attn_prefill(at, c->st, q.pdl));
         q.ck(g4_launch_rows_quant(c->attn, Y.qw, T, Y.qw, c->xq, c->xs, c->st, q.pdl, c->xsT));
@@ -978,6 +984,10 @@ int g4_set_option(g4_ctx *c, int option, int value) {
     if (rc) return rc;
     switch (option) {
     case G4_OPT_PERSISTENT: c->persistent = value != 0; break;
+    case G4_OPT_BATCH_SPLITS:
+        if (value < 0 || value > kSplits) return fail(c, G4_ERR_INVALID, "batch splits %d out of range", value);
+        c->batch_splits = value;
+        break;
     case G4_OPT_GRAPHS: c->use_graph = value != 0; break;
     case G4_OPT_PDL:
         c->use_pdl = value != 0;

@@ -26,7 +26,7 @@ MAX_CONTEXT = 131072
 G4_OK = 0
 ERRORS = {-1: "G4_ERR_INVALID", -2: "G4_ERR_FORMAT", -3: "G4_ERR_CUDA", -4: "G4_ERR_NOMEM",
           -5: "G4_ERR_DEVICE", -6: "G4_ERR_STATE"}
-OPT_GRAPHS, OPT_PDL, OPT_GEMM_PATH, OPT_LAYERS, OPT_STRICT, OPT_PERSISTENT = 1, 2, 3, 4, 5, 6
+OPT_GRAPHS, OPT_PDL, OPT_GEMM_PATH, OPT_LAYERS, OPT_STRICT, OPT_PERSISTENT, OPT_BATCH_SPLITS = 1, 2, 3, 4, 5, 6, 7
 SYN_GROUP_SCALES, SYN_RANDOM_NORMS = 1, 2
 
 _f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")

@@ -110,6 +110,13 @@ const char *g4_strerror(int code);
  * forward and the lm_head together, any other call launches the forward alone
  * first. Same bits as the multi-kernel path. Not used in strict mode. */
 #define G4_OPT_PERSISTENT 6
+/* Key splits per row of a multi-sequence decode step (g4_forward_batch):
+ * 0 (default) = about four CTAs per SM over the batch, at least 16 per row;
+ * 148 = the partition
+ * single-sequence decode uses, which makes every batch row bit-identical to
+ * decoding that sequence alone (other values change only the attention's
+ * floating-point summation order). */
+#define G4_OPT_BATCH_SPLITS 7
 int g4_set_option(g4_ctx *ctx, int option, int value);
 
 /* ---- multi-sequence serving (ragged batches of independent sequences) ----
@@ -124,9 +131,10 @@ int g4_set_option(g4_ctx *ctx, int option, int value);
  * consumes tokens[offsets[i] .. offsets[i+1]) at positions start_pos[i] ...,
  * offsets[0] == 0 and offsets[n] <= 512 rows in total. Either one sequence
  * with up to 512 tokens (a prefill chunk, in order as for g4_forward) or
- * several sequences with exactly one token each (a decode step). A batch row
- * computes the same bits as the same token through g4_forward on a context
- * holding only that sequence. Not available in strict mode.
+ * several sequences with exactly one token each (a decode step). With
+ * G4_OPT_BATCH_SPLITS 148 a batch row computes the same bits as the same token
+ * through g4_forward on a context holding only that sequence. Not available in
+ * strict mode.
  *
  * g4_logits_batch: for each sequence of the last g4_forward_batch, the
  * soft-capped logits of its last token (logits: [n][262144] or NULL) and the

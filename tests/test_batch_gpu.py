@@ -5,7 +5,10 @@ prefill kernels over that sequence's rings, and a decode step of several
 sequences (one token each) runs the GEMMs over all rows and the same split
 attention per row as single-sequence decode. So every batch row must give
 exactly the bits of the same token decoded on a context that holds only that
-sequence: logits (soft-capped) and argmax, at every step of a greedy loop.
+sequence: logits (soft-capped) and argmax, at every step of a greedy loop,
+when the batch uses the same key partition (G4_OPT_BATCH_SPLITS 148). The
+default partition (fewer splits per row for large batches) changes only the
+attention's summation order; its rows are checked for self-consistency.
 """
 import numpy as np
 import pytest
@@ -34,6 +37,7 @@ def test_batch_rows_equal_single_sequences(g4, image):
     steps = 3
     with g4.Model(image) as m:
         ref = [_single(m, p, steps) for p in prompts]
+        m.set_option(g4.OPT_BATCH_SPLITS, 148)       # single-sequence decode's key partition
         m.seq_alloc(6, 2048)
         got = [[] for _ in prompts]
         for i, p in enumerate(prompts):           # prefill, one sequence per call, 512-token chunks
@@ -54,6 +58,19 @@ def test_batch_rows_equal_single_sequences(g4, image):
         for (lr, ar), (lb, ab) in zip(ref[i], got[i]):
             assert ar == ab
             assert np.array_equal(lr.view(np.uint32), lb.view(np.uint32))
+
+
+def test_batch_default_splits_consistent(g4, image):
+    rng = np.random.default_rng(42)
+    with g4.Model(image) as m:
+        m.seq_alloc(8, 1024)
+        for i in range(8):
+            m.forward_batch([i], [rng.integers(0, g4.VOCAB, size=20 + 7 * i).astype(np.int32)], [0])
+        pos = [20 + 7 * i for i in range(8)]
+        m.forward_batch(list(range(8)), [[3 + i] for i in range(8)], pos)
+        lg, am = m.logits_batch(want_logits=True)
+        assert np.isfinite(lg).all() and np.abs(lg).max() <= 30.0
+        assert np.array_equal(am, lg.argmax(axis=1).astype(np.int32))
 
 
 def test_batch_api_errors(g4, image):

@@ -77,7 +77,8 @@ class Dist:
             backend = "nccl" if torch.cuda.is_available() else "gloo"
             if backend == "nccl":
                 torch.cuda.set_device(self.local)
-            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120))
+            kw = {"device_id": torch.device("cuda", self.local)} if backend == "nccl" else {}
+            dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120), **kw)
             self.backend = backend
             self.pg = True
 

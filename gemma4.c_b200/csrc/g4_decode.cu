@@ -104,22 +104,30 @@ __host__ __device__ constexpr int dstage_rows(int K) {
                                                        : ((int)(kStageMaxW / (unsigned)K) & ~1);
 }
 
-// This CTA's rows of a GEMV: whole row pairs, split evenly over the grid.
+// This CTA's rows of a GEMV: whole row pairs, split evenly over the grid with
+// the op's precomputed partition (no integer division in the kernel).
 struct CtaRows {
     int n0, rows, R, nst;
 };
-__host__ __device__ inline CtaRows cta_rows_of(const DMat &m, int b, int grid) {
+__host__ __device__ inline CtaRows cta_rows_of(const DecodeOp &op, int b) {
     CtaRows c;
-    const unsigned npairs = (unsigned)m.N >> 1;   // (b + 1) * npairs < 2^32 for N <= 2^24, grid <= 256
-    const int c0 = (int)((unsigned)b * npairs / (unsigned)grid);
-    const int c1 = (int)((unsigned)(b + 1) * npairs / (unsigned)grid);
-    c.n0 = 2 * c0;
-    c.rows = 2 * (c1 - c0);
-    c.R = dstage_rows(m.K);
-    c.nst = (c.rows + c.R - 1) / c.R;
+    const int more = b < op.part_r;
+    c.n0 = 2 * (b * op.part_q + (more ? b : op.part_r));
+    c.rows = 2 * (op.part_q + more);
+    c.R = op.srows;
+    c.nst = op.nst[more];
     return c;
 }
-G4_DEV CtaRows cta_rows(const DMat &m) { return cta_rows_of(m, blockIdx.x, gridDim.x); }
+G4_DEV CtaRows cta_rows(const DecodeOp &op) { return cta_rows_of(op, blockIdx.x); }
+// Fill the partition fields of a GEMV op for a grid of `grid` CTAs.
+void set_partition(DecodeOp &op, int grid) {
+    const int npairs = op.g.m.N / 2, R = dstage_rows(op.g.m.K);
+    op.part_q = npairs / grid;
+    op.part_r = npairs % grid;
+    op.srows = R;
+    op.nst[0] = (2 * op.part_q + R - 1) / R;
+    op.nst[1] = (2 * op.part_q + 2 + R - 1) / R;
+}
 // Row-parallel schedule (a warp per stage) for CTAs with more than 32 rows,
 // else group-parallel (all warps on each stage, one chain pass at the end).
 __host__ __device__ inline bool row_parallel(const CtaRows &cr) { return cr.rows > 32; }
@@ -215,8 +223,8 @@ G4_DEV void row_epilogue(const GemvArgs &a, int epi, int n, float acc, bool acti
 //    shared memory, then warp 0 runs the rows' chains.
 // A warp whose stage wait runs out leaves as a whole warp and sets *fail; it
 // still takes every consumer barrier below, so the CTA never deadlocks.
-G4_DEV __noinline__ void gemv_op(const GemvArgs &a, int pro, int epi, int cs, unsigned &head, uint8_t *smem,
-                                 volatile int *fail, unsigned long long *tr) {
+G4_DEV __noinline__ void gemv_op(const GemvArgs &a, const CtaRows cr, int pro, int epi, int cs, unsigned &head,
+                                 uint8_t *smem, volatile int *fail, unsigned long long *tr) {
     const int K = a.m.K, G = K >> 6;
     uint8_t *ring = smem + kOffRing;
     uint64_t *full = (uint64_t *)(smem + kOffFull);
@@ -230,7 +238,6 @@ G4_DEV __noinline__ void gemv_op(const GemvArgs &a, int pro, int epi, int cs, un
     decode_prologue(a, pro, xq, xs, vec, red);
     csync();
     if (tr && tid == 0) atomicMax(tr, (unsigned long long)g4_globaltimer());
-    const CtaRows cr = cta_rows(a.m);
     float best_v = -INFINITY;
     int best_i = 0x7fffffff;
     unsigned h = head, st = 0;
@@ -377,7 +384,7 @@ G4_DEV void run_gemv(const DecodeOp &op, int cs, unsigned &head, uint8_t *smem, 
     const bool pro_ok = op.pro == PRO_EMBED_QUANT || op.pro == PRO_NORM_QUANT || op.pro == PRO_RES_NORM_QUANT ||
                         op.pro == PRO_LOADQ || op.pro == PRO_QUANT || op.pro == PRO_RES_QUANT;
     const bool epi_ok = op.epi == EPI_STORE || op.epi == EPI_GEGLU_PAIR || op.epi == EPI_PLE || op.epi == EPI_LOGITS;
-    if (pro_ok && epi_ok) return gemv_op(a, op.pro, op.epi, cs, head, smem, fail, tr);
+    if (pro_ok && epi_ok) return gemv_op(a, cta_rows(op), op.pro, op.epi, cs, head, smem, fail, tr);
     g4_set_error(a.err, G4D_BAD_SHAPE);
     if (threadIdx.x == 0) *fail = 1;
 }
@@ -432,7 +439,7 @@ G4_DEV void produce(const DecodeParams &P, uint8_t *smem, volatile int *fail, in
         if (op.type != OP_GEMV) continue;
         const DMat &m = op.g.m;
         const int K = m.K, G = K >> 6;
-        const CtaRows cr = cta_rows(m);
+        const CtaRows cr = cta_rows(op);
         for (int j = 0; j < cr.nst; j++, cs++) {
             if (cs >= kMaxStages) {
                 g4_set_error(P.err, G4D_BAD_SHAPE);
@@ -520,20 +527,22 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(const DecodeParams P) {
         cp_async_commit();
     };
     fetch_op(0);
+    cp_async_wait<0>();
+    csync();
     bool ok = true;
     int cs = 0;
     unsigned head = 0;
     if (P.trace && tid == 0) atomicMax(P.trace, (unsigned long long)g4_globaltimer());
     for (int o = 0; o < P.nops && ok; o++) {
-        cp_async_wait<0>();
-        csync();   // op o's descriptor is in place; op o - 1's buffer is free
+        // op o's descriptor is in place (waited for before the barrier that ended
+        // op o - 1); op o - 1's buffer is free for op o + 1's
         if (o + 1 < P.nops) fetch_op(o + 1);
         const DecodeOp &op = opbuf[o & 1];
         unsigned long long *tr = P.trace ? P.trace + 1 + 6 * o : nullptr;
         switch (op.type) {
         case OP_GEMV:
             run_gemv(op, cs, head, smem, &fail, tr);
-            cs += cta_rows(op.g.m).nst;
+            cs += cta_rows(op).nst;
             break;
         case OP_ATTN:
             if ((int)blockIdx.x < P.splits) {
@@ -556,12 +565,13 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(const DecodeParams P) {
         default:
             if (tid == 0) fail = 1;   // unknown op type (uniform: every thread reads the same op)
         }
+        cp_async_wait<0>();   // this thread's share of op o + 1's descriptor landed
         if (op.barrier) {
             target += gridDim.x;
             ok = grid_barrier(P, target, &fail, tr);
-        } else if (tr) {
+        } else {
             csync();
-            if (tid == 0) {
+            if (tr && tid == 0) {
                 const unsigned long long t = g4_globaltimer();
                 atomicMax(tr + 1, t);
                 atomicMax(tr + 2, t);
@@ -579,6 +589,8 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(const DecodeParams P) {
 
 size_t g4_decode_smem_bytes() { return (size_t)kSmemBytes; }
 
+void g4_decode_set_partition(DecodeOp &op, int grid) { set_partition(op, grid); }
+
 int g4_decode_max_stages(const DecodeOp *ops, int nops, int grid) {
     int worst = 0;
     for (int b = 0; b < grid; b++) {
@@ -586,7 +598,9 @@ int g4_decode_max_stages(const DecodeOp *ops, int nops, int grid) {
         for (int o = 0; o < nops; o++) {
             if (ops[o].type != OP_GEMV) continue;
             const DMat &m = ops[o].g.m;
-            const CtaRows cr = cta_rows_of(m, b, grid);
+            DecodeOp pop = ops[o];
+            set_partition(pop, grid);
+            const CtaRows cr = cta_rows_of(pop, b);
             // group-parallel CTAs keep all their rows' scales ([rows][G] fp16) in 6 KB
             if ((size_t)cr.R * m.K + (size_t)cr.R * (m.K / 64) * 2 > kRingBytes / 2 || m.K > kMaxK ||
                 (!row_parallel(cr) && (size_t)cr.rows * (m.K / 64) * 2 > (size_t)G4_HIDDEN * 4))

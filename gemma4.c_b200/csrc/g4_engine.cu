@@ -822,6 +822,8 @@ int build_decode(g4_ctx *c) {
     c->cur = cur_save;
     if (e) return fail(c, G4_ERR_CUDA, "decode op list: %s", cudaGetErrorString(e));
     ops.back().barrier = 0;
+    for (DecodeOp &op : ops)
+        if (op.type == OP_GEMV) g4_decode_set_partition(op, c->num_sms);
     std::vector<DecodeOp> withlog(ops);
     // replace the last residual update by the lm_head GEMV whose prologue performs it
     const DecodeOp fin = withlog.back();
@@ -842,6 +844,7 @@ int build_decode(g4_ctx *c) {
     lm.g.argmax_part = c->argmax_part;
     lm.g.argmax_out = c->argmax_out;
     lm.g.ticket = c->ticket;
+    g4_decode_set_partition(lm, c->num_sms);
     withlog.back() = lm;
     if (g4_decode_max_stages(ops.data(), (int)ops.size(), c->num_sms) > (1 << 20) ||
         g4_decode_max_stages(withlog.data(), (int)withlog.size(), c->num_sms) > (1 << 20) || c->num_sms < kSplits) {

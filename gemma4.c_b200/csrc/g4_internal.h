@@ -146,6 +146,10 @@ enum DecodeOpType : int {
 
 struct alignas(16) DecodeOp {
     int type, pro, epi, barrier;   // barrier: grid-wide barrier after the op
+    // GEMV row partition over the grid (host-computed): CTA b owns row pairs
+    // [b q + min(b, r), +q + (b < r)); stages of srows rows, nst[0] / nst[1]
+    // stages for q / q + 1 pairs
+    int part_q, part_r, srows, nst[2];
     GemvArgs g;
     AttnArgs at;
     // OP_PLE_PREP
@@ -176,6 +180,8 @@ size_t g4_decode_smem_bytes();
 cudaError_t g4_launch_decode(const DecodeParams &p, int grid, cudaStream_t st);
 // stages of every GEMV op this CTA streams (for sizing checks)
 int g4_decode_max_stages(const DecodeOp *ops, int nops, int grid);
+// the GEMV row partition fields of a decode op for a persistent grid of `grid` CTAs
+void g4_decode_set_partition(DecodeOp &op, int grid);
 
 // ---- launchers (g4_*.cu) ---------------------------------------------------
 cudaError_t g4_launch_scales_t(const uint16_t *s, int N, int K, float *sT, cudaStream_t st);

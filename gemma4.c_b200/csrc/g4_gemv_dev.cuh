@@ -35,17 +35,32 @@ __device__ float block_sum(float v, float *red) {
     return r;
 }
 
+// block_sum without the trailing barrier: `red` (8 floats) must not be
+// written again before the caller's next consumer barrier.
+__device__ float block_sum_once(float v, float *red) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    v = warp_sum(v);
+    if (lane == 0) red[warp] = v;
+    csync();
+    float r = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kWarps; i++) r += red[i];
+    return r;
+}
+
 // Sum of squares of the hidden row whose values this thread holds at
 // e = tid + i * kConsumers: in parallel, or (strict) sequentially in index
-// order through shared memory exactly as gemma4.c:367-368 does.
+// order through shared memory exactly as gemma4.c:367-368 does. `slot` picks
+// one of two reduction buffers so that two sums in a row need no barrier in
+// between (the caller's next barrier frees both).
 template <int PER>
-__device__ float row_sumsq(const float (&v)[PER], bool strict, float *vec, float *red) {
+__device__ float row_sumsq(const float (&v)[PER], bool strict, float *vec, float *red, int slot) {
     const int tid = threadIdx.x;
     if (!strict) {
         float ss = 0.0f;
 #pragma unroll
         for (int i = 0; i < PER; i++) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
-        return block_sum(ss, red);
+        return block_sum_once(ss, red + 16 + 8 * slot);
     }
 #pragma unroll
     for (int i = 0; i < PER; i++) vec[tid + i * kConsumers] = v[i];
@@ -152,7 +167,7 @@ __device__ void prologue(const GemvArgs &a, int8_t *xq, float *xs, float *vec, f
                 hv[i] = h[tid + i * kConsumers];
                 rv[i] = kRes ? a.res_in[t * G4_HIDDEN + tid + i * kConsumers] : 0.0f;
             }
-            const float ss = row_sumsq<PER>(hv, a.strict, vec, red);
+            const float ss = row_sumsq<PER>(hv, a.strict, vec, red, 0);
             const float inv = rms_inv(ss, (float)G4_HIDDEN, a.eps);
             if (PRO == PRO_NORM_QUANT) {
 #pragma unroll
@@ -168,7 +183,7 @@ __device__ void prologue(const GemvArgs &a, int8_t *xq, float *xs, float *vec, f
                     if (blockIdx.x == 0) a.res_out[t * G4_HIDDEN + e] = r;
                 }
                 if (PRO == PRO_RES_NORM_QUANT) {
-                    const float ss2 = row_sumsq<PER>(y, a.strict, vec, red);
+                    const float ss2 = row_sumsq<PER>(y, a.strict, vec, red, 1);
                     const float inv2 = rms_inv(ss2, (float)G4_HIDDEN, a.eps);
 #pragma unroll
                     for (int i = 0; i < PER; i++) y[i] = rms_apply(y[i], inv2, wpre[i]);

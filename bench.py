@@ -44,6 +44,9 @@ PREFILL_SHAPES = ((2560, 1536, 12), (5120, 1536, 3), (2048, 1536, 16), (4096, 15
                   (1536, 6144, 15), (1536, 12288, 20), (256, 1536, 35), (1536, 256, 35), (8960, 1536, 1))
 PREFILL = 512
 CTX_LONG = 16384
+# nominal FP32 FMA peak: 148 SMs x 128 lanes x 2 FLOP x 1.965 GHz (no measured figure on this pool)
+FP32_TFLOPS = 148 * 128 * 2 * 1.965e9 / 1e12
+ATTN_CTX = (512, 2048, 8192, 16384)
 
 
 def env_int(name, default):
@@ -329,6 +332,53 @@ def batched_serving(m, dist, seqs=64):
     }
 
 
+def attention_bench(g4, hbm_peak, prefill_iters=10, decode_iters=50):
+    """Attention over the FP32 KV ring at contexts 512..16384:
+    per layer kind, the last 512-token prefill chunk of a context (causal over
+    the chunk, start = ctx - 512) and one decode token at position ctx - 1, each
+    timed with CUDA events over repeated launches (post-processed q, filled
+    ring). Q/K/V are N(0, 1) from seed 1, q/k RMS-normalised (weight 1) and
+    rotated; the ring's earlier keys are normalised random vectors (a rotation
+    of a Gaussian vector is Gaussian). The model mix is 28 sliding + 7 global
+    layers."""
+    res = {}
+    for ctx in ATTN_CTX:
+        row = {}
+        for hd, kind, n_layers in ((256, "sliding", 28), (512, "global", 7)):
+            window = 512 if hd == 256 else 0
+            ring = 1024 if hd == 256 else max(1024, 1 << (ctx - 1).bit_length())
+            rng = np.random.default_rng(1)
+            qkv = rng.standard_normal((PREFILL, 10 * hd)).astype(np.float32)
+            k = rng.standard_normal((ring, hd)).astype(np.float32)
+            v = rng.standard_normal((ring, hd)).astype(np.float32)
+            k /= np.sqrt((k * k).mean(axis=1, keepdims=True))
+            v /= np.sqrt((v * v).mean(axis=1, keepdims=True))
+            pairs, theta = (128, 1e4) if hd == 256 else (64, 1e6)
+            ang = np.arange(ctx, dtype=np.float64)[:, None] * theta ** (-np.arange(pairs) * 2.0 / hd)[None, :]
+            cos_t, sin_t = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+            start = ctx - PREFILL
+            keys = np.array([min(p + 1, window) if window else p + 1 for p in range(start, ctx)], np.float64)
+            flops = float(keys.sum()) * 8 * hd * 4            # q.k and p.v, 2 FLOP per multiply-add
+            _, ms_p = g4.attention(qkv, hd, k.copy(), v.copy(), start, cos_t, sin_t, mode=g4.ATTN_PREFILL,
+                                   iters=prefill_iters)
+            _, ms_d = g4.attention(qkv[:1], hd, k, v, ctx - 1, cos_t, sin_t, mode=g4.ATTN_DECODE, splits=148,
+                                   iters=decode_iters)
+            dbytes = float(keys[-1]) * hd * 8                 # fp32 K and V rows read by one decode token
+            tfl = flops / (ms_p / 1e3) / 1e12
+            gbs = dbytes / (ms_d / 1e3) / 1e9
+            row[kind] = {"prefill_chunk_us": ms_p * 1e3, "prefill_tflops": tfl,
+                         "prefill_frac_fp32_peak": tfl / FP32_TFLOPS, "decode_us": ms_d * 1e3,
+                         "decode_kv_gbs": gbs, "decode_frac_hbm": gbs / hbm_peak, "layers": n_layers}
+        row["model_prefill_chunk_ms"] = sum(row[k]["prefill_chunk_us"] * row[k]["layers"]
+                                            for k in ("sliding", "global")) / 1e3
+        row["model_decode_us"] = sum(row[k]["decode_us"] * row[k]["layers"] for k in ("sliding", "global"))
+        res[f"ctx{ctx}"] = row
+    res["note"] = ("prefill: FP32 CUDA-core kernel (k_attn_prefill + merge), frac of the nominal FP32 FMA peak "
+                   f"{FP32_TFLOPS:.1f} TFLOP/s; decode: split-KV kernel + combine standalone (inside k_decode "
+                   "the same code runs as one phase), frac of the measured HBM copy bandwidth")
+    return res
+
+
 def run_ours(args, dist):
     import g4cuda as g4
     hbm_peak, peak_kind = peaks()
@@ -383,6 +433,7 @@ def run_ours(args, dist):
     gemm_tops = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms else 0.0
 
     batched = batched_serving(m, dist) if not args.no_batched else None
+    attention = attention_bench(g4, hbm_peak) if not args.no_attention else None
 
     # long context: prefill 16384 then decode
     long = {}
@@ -420,6 +471,8 @@ def run_ours(args, dist):
     line.update(long)
     if batched:
         line["batched"] = batched
+    if attention:
+        line["attention"] = attention
     if clk:
         line["clocks"] = clk
     m.close()
@@ -443,6 +496,7 @@ def main():
     ap.add_argument("--short", action="store_true", help="skip the 16384-context runs")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-batched", action="store_true", help="skip the 64-sequence serving run (config 5)")
+    ap.add_argument("--no-attention", action="store_true", help="skip the attention sweep (config 4)")
     ap.add_argument("--profile-range", action="store_true",
                     help="open the profiler capture range around the timed decode steps only "
                          "(for ncu --profile-from-start off)")

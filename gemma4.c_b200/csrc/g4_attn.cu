@@ -157,163 +157,375 @@ __global__ void __launch_bounds__(256) k_attn_strict(const AttnArgs a) {
 }
 
 // ---------------------------------------------------------------------------
-// Prefill attention: CTA = 4 query tokens x 8 heads (32 rows) against key
-// tiles of 32, FP32 SIMT with online softmax. q must already be normalised and
-// rotated (k_qkv_post) and the chunk's keys already in the ring.
-constexpr int kTile = 32;             // keys per tile
-constexpr int kQT = 4;               // tokens per CTA
-constexpr int kRows = kQT * kHeads;  // 32 query rows
+// Prefill attention (fast path): FP32 on the CUDA cores, register-tiled, with
+// the chunk's work split evenly over a fixed grid.
+//
+// A q tile is QT consecutive tokens x 8 heads = R query rows; all R rows share
+// the single KV head, so one staged key/value tile serves all of them. The
+// keys a q tile needs ([first_key(first token), last token]) are cut into
+// units of BK keys; units are numbered q-tile-major and CTA b of G takes units
+// [U b / G, U (b+1) / G). A CTA that covers a whole q tile writes its output;
+// one that covers part of it writes the partial (row max, row sum, unnormalised
+// output) to a slot, and k_attn_prefill_merge combines the slots of such tiles
+// in CTA order (deterministic for a given T, start_pos and G).
+//
+// Per key tile: S = Q K^T with each thread owning 4 rows x 4 keys over a slice
+// of the head dimension (packed f32x2 FMAs over even/odd dimensions), the
+// online-softmax update in registers (row max / sum by warp shuffles), P
+// written to shared memory duplicated as (p, p) pairs, then O += P V with each
+// thread owning 8 rows (one token's 8 heads) x 8 dimensions. K of the next
+// tile loads (cp.async) during P V, V of this tile during Q K^T.
+template <int HD> struct PreCfg;
+template <> struct PreCfg<256> { static constexpr int QT = 8, BK = 64, DS = 1, KPAD = 4; };
+template <> struct PreCfg<512> { static constexpr int QT = 4, BK = 32, DS = 4, KPAD = 16; };
+
+constexpr int kPreMaxTiles = G4_BATCH / 4;   // q tiles of a chunk at QT >= 4
 
 template <int HD>
-__global__ void __launch_bounds__(256) k_attn_prefill(const AttnArgs a) {
+struct Pre {
+    static constexpr int QT = PreCfg<HD>::QT, BK = PreCfg<HD>::BK, DS = PreCfg<HD>::DS;
+    static constexpr int R = QT * kHeads;              // query rows per q tile
+    static constexpr int KS = HD + PreCfg<HD>::KPAD;   // K row stride (bank spread)
+    static constexpr int KG = BK / 4;                  // key groups of the S phase
+    static constexpr int DG = HD / 8;                  // dimension groups of the P V phase
+    static constexpr int PS = 2 * R;                   // P row stride: R (p, p) pairs
+    static_assert((R / 4) * KG * DS == 256, "S phase covers 256 threads");
+    static_assert((R / 8) * DG == 256, "PV phase covers 256 threads");
+    static constexpr int kFloats = R * HD + BK * KS + BK * HD + BK * PS + 3 * R;
+    static constexpr size_t kSmem = (size_t)kFloats * 4 + (kPreMaxTiles + 4) * 4;
+    // key-tile units of q tile j of a chunk of T tokens starting at sp
+    static G4_DEV int units(int j, int T, int sp, int window) {
+        const int t0 = j * QT, t1 = min(T, t0 + QT) - 1;
+        const int klo = first_key(sp + t0, window), khi = sp + t1;
+        return (khi - klo + BK) / BK;
+    }
+    // pre[0..nq] = prefix sums of units, by warp 0
+    static G4_DEV void prefix(int *pre, int nq, int T, int sp, int window) {
+        const int lane = threadIdx.x & 31;
+        int carry = 0;
+        if (lane == 0) pre[0] = 0;
+        for (int base = 0; base < nq; base += 32) {
+            const int j = base + lane;
+            int v = j < nq ? units(j, T, sp, window) : 0;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, v, o);
+                if (lane >= o) v += n;
+            }
+            if (j < nq) pre[j + 1] = carry + v;
+            carry += __shfl_sync(0xffffffffu, v, 31);
+        }
+    }
+    // the CTA whose unit range holds unit u
+    static G4_DEV int cta_of(long long u, long long U, int G) { return (int)(((u + 1) * G + U - 1) / U) - 1; }
+    // CTA b has no units (more CTAs than units)
+    static G4_DEV bool empty(int b, long long U, int G) { return U * b / G == U * (b + 1) / G; }
+    // partial slot of q tile j written by CTA b (first tile of b: 2b, else 2b + 1)
+    static G4_DEV int slot_of(int b, int j, const int *pre, long long U, int G) {
+        const long long s = U * b / G;
+        return s >= pre[j] ? 2 * b : 2 * b + 1;
+    }
+};
+
+// Stage BK key rows [kt, kt + nt) of a ring into shared memory (row stride
+// dstride); rows past nt are zero.
+template <int HD>
+G4_DEV void pre_load_rows(float *dst, int dstride, const float *cache, int mask, int kt, int nt) {
+    constexpr int C4 = HD / 4, BK = Pre<HD>::BK;
+    for (int idx = threadIdx.x; idx < BK * C4; idx += 256) {
+        const int r = idx / C4, c4 = idx - r * C4;
+        float *d = dst + r * dstride + c4 * 4;
+        if (r < nt) cp_async16(d, cache + (size_t)((kt + r) & mask) * HD + c4 * 4);
+        else *(float4 *)d = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    cp_async_commit();
+}
+
+template <int HD>
+__global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
+    using P = Pre<HD>;
+    constexpr int QT = P::QT, BK = P::BK, DS = P::DS, R = P::R, KS = P::KS, KG = P::KG, DG = P::DG, PS = P::PS;
     extern __shared__ __align__(16) float sm[];
-    float *Qs = sm;                        // [32][HD]
-    float *Ks = Qs + kRows * HD;           // [32][HD + 4]
-    float *Vs = Ks + kTile * (HD + 4);     // [32][HD]
-    float *Ps = Vs + kTile * HD;           // [32][33]
-    float *rm = Ps + kRows * 33;           // [32] running max
-    float *rl = rm + kRows;                // [32] running sum
-    float *rc = rl + kRows;                // [32] correction of this tile
-    const int tid = threadIdx.x;
-    const int t_base = blockIdx.x * kQT;
+    float *Qs = sm;                  // [R][HD]
+    float *Ks = Qs + R * HD;         // [BK][KS]
+    float *Vs = Ks + BK * KS;        // [BK][HD]
+    float *Pt = Vs + BK * HD;        // [BK][R] (p, p) pairs, 16-byte columns swizzled by key
+    float *rc = Pt + BK * PS;        // [R] correction of the current tile
+    float *rl = rc + R;              // [R] running sum
+    float *rm = rl + R;              // [R] running max
+    int *pre = (int *)(rm + R);      // [nq + 1]
 
     griddep_launch();
     griddep_wait();
-
-    // load q rows: row r = token_local * 8 + head
-    for (int idx = tid; idx < kRows * (HD / 4); idx += 256) {
-        const int r = idx / (HD / 4), c4 = idx - r * (HD / 4);
-        const int t = t_base + r / kHeads, h = r % kHeads;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (t < a.T) v = *(const float4 *)(a.qkv + (size_t)t * a.qkv_stride + h * HD + c4 * 4);
-        *(float4 *)&Qs[r * HD + c4 * 4] = v;
+    const int tid = threadIdx.x, T = a.T, sp = a.start_pos;
+    const int nq = (T + QT - 1) / QT;
+    if (tid < 32) P::prefix(pre, nq, T, sp, a.window);
+    __syncthreads();
+    const long long U = pre[nq];
+    const int G = gridDim.x, b = blockIdx.x;
+    const long long u0 = U * b / G, u1 = U * (b + 1) / G;
+    if (u0 >= u1) return;
+    int j = 0;
+    {
+        int lo = 0, hi = nq - 1;   // largest j with pre[j] <= u0
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (pre[mid] <= u0) lo = mid; else hi = mid - 1;
+        }
+        j = lo;
     }
-    if (tid < kRows) {
-        rm[tid] = -INFINITY;
-        rl[tid] = 0.0f;
-    }
-    const int t_last = min(a.T, t_base + kQT) - 1;
-    const int p_first = a.start_pos + t_base, p_last = a.start_pos + t_last;
-    const int k_lo = first_key(p_first, a.window), k_hi = p_last;   // inclusive
+    const int j0 = j;
 
-    // S-phase mapping: rows (2qr, 2qr+1), keys (kr, kr+16)
-    const int qr = tid >> 4, kr = tid & 15;
-    int prow[2], pfirst[2];
-#pragma unroll
-    for (int i = 0; i < 2; i++) {
-        const int r = 2 * qr + i, t = t_base + r / kHeads;
-        prow[i] = t < a.T ? a.start_pos + t : -1;
-        pfirst[i] = prow[i] >= 0 ? first_key(prow[i], a.window) : 0;
-    }
-    // PV mapping: rows 4*(tid/32) .. +3, dims 4*lane + 128*i
-    const int rg = tid >> 5, lane = tid & 31;
-    constexpr int NV = HD / 128;
-    float4 o[4][NV];
-#pragma unroll
-    for (int r = 0; r < 4; r++)
-#pragma unroll
-        for (int i = 0; i < NV; i++) o[r][i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // S-phase coordinates: rows 4 ty + i, keys tx + KG jj, dimension slice sl
+    const int sl = tid % DS, tx = (tid / DS) % KG, ty = tid / (DS * KG);
+    // P V coordinates: rows 8 rg + r (token rg of the tile, head r), dims 4 dg + {0, HD/2}
+    const int rg = tid / DG, dg = tid % DG;
 
-    for (int kt = k_lo; kt <= k_hi; kt += kTile) {
-        const int nt = min(kTile, k_hi + 1 - kt);
-        __syncthreads();
-        for (int idx = tid; idx < nt * (HD / 4); idx += 256) {
+    long long u = u0;
+    while (u < u1) {
+        const int t0 = j * QT;
+        const int seg_end = (int)min(u1, (long long)pre[j + 1]);
+        const int n = seg_end - (int)u;
+        const int klo = first_key(sp + t0, a.window), kend = sp + min(T, t0 + QT);
+        const int kt0 = klo + ((int)u - pre[j]) * BK;
+        // Q tile and the first K tile
+        for (int idx = tid; idx < R * (HD / 4); idx += 256) {
             const int r = idx / (HD / 4), c4 = idx - r * (HD / 4);
-            const size_t slot = (size_t)((kt + r) & a.mask) * HD;
-            cp_async16(&Ks[r * (HD + 4) + c4 * 4], a.kcache + slot + c4 * 4);
-            cp_async16(&Vs[r * HD + c4 * 4], a.vcache + slot + c4 * 4);
+            const int t = t0 + (r >> 3), h = r & 7;
+            float *d = Qs + r * HD + c4 * 4;
+            if (t < T) cp_async16(d, a.qkv + (size_t)t * a.qkv_stride + h * HD + c4 * 4);
+            else *(float4 *)d = make_float4(0.f, 0.f, 0.f, 0.f);
         }
-        cp_async_commit();
-        cp_async_wait<0>();
-        __syncthreads();
-        // scores
-        float s[2][2];
+        pre_load_rows<HD>(Ks, KS, a.kcache, a.mask, kt0, min(BK, kend - kt0));
+
+        // this thread's S rows all belong to token t0 + (4 ty) / 8
+        const int ts = t0 + ((4 * ty) >> 3);
+        const int prow = ts < T ? sp + ts : -1;
+        const int pfk = prow >= 0 ? first_key(prow, a.window) : 0;
+        float mrow[4], lrow[4];
 #pragma unroll
-        for (int i = 0; i < 2; i++)
+        for (int i = 0; i < 4; i++) { mrow[i] = -INFINITY; lrow[i] = 0.0f; }
+        uint64_t o[8][4];
 #pragma unroll
-            for (int jj = 0; jj < 2; jj++) s[i][jj] = 0.0f;
-        const float *q0 = Qs + (2 * qr) * HD, *q1 = q0 + HD;
-        const float *k0 = Ks + kr * (HD + 4), *k1 = Ks + (kr + 16) * (HD + 4);
+        for (int r = 0; r < 8; r++)
+#pragma unroll
+            for (int c = 0; c < 4; c++) o[r][c] = 0ull;
+
+        for (int it = 0; it < n; it++) {
+            const int kt = kt0 + it * BK;
+            const int nt = min(BK, kend - kt);
+            cp_async_wait<0>();
+            __syncthreads();                       // Q, K(kt) visible; V, P free
+            pre_load_rows<HD>(Vs, HD, a.vcache, a.mask, kt, nt);
+            // ---- S = Q K^T over this thread's dimension slice
+            uint64_t acc[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) acc[i][jj] = 0ull;
+            const float *qb = Qs + (4 * ty) * HD, *kb = Ks + tx * KS;
 #pragma unroll 4
-        for (int d = 0; d < HD; d += 4) {
-            const float4 a0 = *(const float4 *)&q0[d], a1 = *(const float4 *)&q1[d];
-            const float4 b0 = *(const float4 *)&k0[d], b1 = *(const float4 *)&k1[d];
-            s[0][0] = fmaf(a0.x, b0.x, fmaf(a0.y, b0.y, fmaf(a0.z, b0.z, fmaf(a0.w, b0.w, s[0][0]))));
-            s[0][1] = fmaf(a0.x, b1.x, fmaf(a0.y, b1.y, fmaf(a0.z, b1.z, fmaf(a0.w, b1.w, s[0][1]))));
-            s[1][0] = fmaf(a1.x, b0.x, fmaf(a1.y, b0.y, fmaf(a1.z, b0.z, fmaf(a1.w, b0.w, s[1][0]))));
-            s[1][1] = fmaf(a1.x, b1.x, fmaf(a1.y, b1.y, fmaf(a1.z, b1.z, fmaf(a1.w, b1.w, s[1][1]))));
-        }
-        // mask + online softmax per row (16 lanes share a row pair)
+            for (int c = sl; c < HD / 4; c += DS) {
+                ulonglong2 qv[4], kv[4];
 #pragma unroll
-        for (int i = 0; i < 2; i++) {
-            const int r = 2 * qr + i;
-            float mloc = -INFINITY;
+                for (int i = 0; i < 4; i++) qv[i] = *(const ulonglong2 *)(qb + i * HD + 4 * c);
 #pragma unroll
-            for (int jj = 0; jj < 2; jj++) {
-                const int key = kt + kr + 16 * jj;
-                const bool ok = prow[i] >= 0 && (kr + 16 * jj) < nt && key <= prow[i] && key >= pfirst[i];
-                if (!ok) s[i][jj] = -INFINITY;
-                mloc = fmaxf(mloc, s[i][jj]);
+                for (int jj = 0; jj < 4; jj++) kv[jj] = *(const ulonglong2 *)(kb + jj * KG * KS + 4 * c);
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int jj = 0; jj < 4; jj++) acc[i][jj] = fma2(qv[i].x, kv[jj].x, acc[i][jj]);
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int jj = 0; jj < 4; jj++) acc[i][jj] = fma2(qv[i].y, kv[jj].y, acc[i][jj]);
+            }
+            float s[4][4];
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) {
+                    const float2 v = upk(acc[i][jj]);
+                    float x = v.x + v.y;
+#pragma unroll
+                    for (int off = 1; off < DS; off <<= 1) x += __shfl_xor_sync(0xffffffffu, x, off);
+                    const int key = kt + tx + KG * jj;
+                    const bool ok = prow >= 0 && key < kend && key <= prow && key >= pfk;
+                    s[i][jj] = ok ? x : -INFINITY;
+                }
+            // ---- online softmax (row state replicated over the row's key lanes)
+            float corr[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                float mx = fmaxf(fmaxf(s[i][0], s[i][1]), fmaxf(s[i][2], s[i][3]));
+#pragma unroll
+                for (int off = DS; off < DS * KG; off <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+                const float mn = fmaxf(mrow[i], mx);
+                corr[i] = mrow[i] == -INFINITY ? 0.0f : expf(mrow[i] - mn);
+                float ps = 0.0f;
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) {
+                    s[i][jj] = s[i][jj] == -INFINITY ? 0.0f : expf(s[i][jj] - mn);
+                    ps += s[i][jj];
+                }
+#pragma unroll
+                for (int off = DS; off < DS * KG; off <<= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+                lrow[i] = lrow[i] * corr[i] + ps;
+                mrow[i] = mn;
+            }
+            if (tx == 0 && sl == 0) {
+                *(float4 *)&rc[4 * ty] = make_float4(corr[0], corr[1], corr[2], corr[3]);
+                *(float4 *)&rl[4 * ty] = make_float4(lrow[0], lrow[1], lrow[2], lrow[3]);
+                *(float4 *)&rm[4 * ty] = make_float4(mrow[0], mrow[1], mrow[2], mrow[3]);
             }
 #pragma unroll
-            for (int off = 8; off > 0; off >>= 1) mloc = fmaxf(mloc, __shfl_xor_sync(0xffffffffu, mloc, off));
-            const float mold = rm[r];
-            const float mn = fmaxf(mold, mloc);
-            float psum = 0.0f;
-#pragma unroll
-            for (int jj = 0; jj < 2; jj++) {
-                const float pv = (s[i][jj] == -INFINITY) ? 0.0f : expf(s[i][jj] - mn);
-                Ps[r * 33 + kr + 16 * jj] = pv;
-                psum += pv;
+            for (int jj = 0; jj < 4; jj++) {
+                if (DS > 1 && jj != sl) continue;
+                const int kl = tx + KG * jj;
+                const int f = (tx * DS + jj) & 7;
+                float *pr = Pt + kl * PS;
+                *(float4 *)&pr[4 * ((2 * ty) ^ f)] = make_float4(s[0][jj], s[0][jj], s[1][jj], s[1][jj]);
+                *(float4 *)&pr[4 * ((2 * ty + 1) ^ f)] = make_float4(s[2][jj], s[2][jj], s[3][jj], s[3][jj]);
             }
+            cp_async_wait<0>();
+            __syncthreads();                       // V, P, rc visible; K free
+            if (it + 1 < n) pre_load_rows<HD>(Ks, KS, a.kcache, a.mask, kt + BK, min(BK, kend - kt - BK));
+            // ---- O = O * corr + P V
+            {
+                const float4 c0 = *(const float4 *)&rc[8 * rg], c1 = *(const float4 *)&rc[8 * rg + 4];
+                const float cr[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
 #pragma unroll
-            for (int off = 8; off > 0; off >>= 1) psum += __shfl_xor_sync(0xffffffffu, psum, off);
-            __syncwarp();
-            if (kr == 0) {
-                const float corr = (mold == -INFINITY) ? 0.0f : expf(mold - mn);
-                rc[r] = corr;
-                rl[r] = rl[r] * corr + psum;
-                rm[r] = mn;
+                for (int r = 0; r < 8; r++) {
+                    const uint64_t c2 = pk(cr[r], cr[r]);
+#pragma unroll
+                    for (int c = 0; c < 4; c++) o[r][c] = mul2(o[r][c], c2);
+                }
             }
-        }
-        __syncthreads();
-        // PV
+            const float *vb = Vs + 4 * dg;
+#pragma unroll 4
+            for (int k = 0; k < BK; k++) {
+                const int f = ((k % KG) * DS + k / KG) & 7;
+                const float *pr = Pt + k * PS;
+                const ulonglong2 va = *(const ulonglong2 *)(vb + k * HD);
+                const ulonglong2 vv = *(const ulonglong2 *)(vb + k * HD + HD / 2);
 #pragma unroll
-        for (int r = 0; r < 4; r++) {
-            const float corr = rc[rg * 4 + r];
-#pragma unroll
-            for (int i = 0; i < NV; i++) {
-                o[r][i].x *= corr; o[r][i].y *= corr; o[r][i].z *= corr; o[r][i].w *= corr;
-            }
-        }
-        for (int jk = 0; jk < nt; jk++) {
-            const float *vr = Vs + jk * HD + 4 * lane;
-            float4 vv[NV];
-#pragma unroll
-            for (int i = 0; i < NV; i++) vv[i] = *(const float4 *)&vr[128 * i];
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-                const float pk = Ps[(rg * 4 + r) * 33 + jk];
-#pragma unroll
-                for (int i = 0; i < NV; i++) {
-                    o[r][i].x = fmaf(pk, vv[i].x, o[r][i].x);
-                    o[r][i].y = fmaf(pk, vv[i].y, o[r][i].y);
-                    o[r][i].z = fmaf(pk, vv[i].z, o[r][i].z);
-                    o[r][i].w = fmaf(pk, vv[i].w, o[r][i].w);
+                for (int m = 0; m < 4; m++) {
+                    const ulonglong2 pp = *(const ulonglong2 *)&pr[4 * ((4 * rg + m) ^ f)];
+                    o[2 * m][0] = fma2(pp.x, va.x, o[2 * m][0]);
+                    o[2 * m][1] = fma2(pp.x, va.y, o[2 * m][1]);
+                    o[2 * m][2] = fma2(pp.x, vv.x, o[2 * m][2]);
+                    o[2 * m][3] = fma2(pp.x, vv.y, o[2 * m][3]);
+                    o[2 * m + 1][0] = fma2(pp.y, va.x, o[2 * m + 1][0]);
+                    o[2 * m + 1][1] = fma2(pp.y, va.y, o[2 * m + 1][1]);
+                    o[2 * m + 1][2] = fma2(pp.y, vv.x, o[2 * m + 1][2]);
+                    o[2 * m + 1][3] = fma2(pp.y, vv.y, o[2 * m + 1][3]);
                 }
             }
         }
+        // ---- emit: whole q tile -> output rows; part of it -> partial slot
+        const int t = t0 + rg;
+        const bool whole = (int)u == pre[j] && seg_end == pre[j + 1];
+        if (whole) {
+            if (t < T) {
+                float *dst = a.out + (size_t)t * (kHeads * HD) + 4 * dg;
+#pragma unroll
+                for (int r = 0; r < 8; r++) {
+                    const float inv = 1.0f / rl[8 * rg + r];
+                    const uint64_t i2 = pk(inv, inv);
+                    const float2 x0 = upk(mul2(o[r][0], i2)), x1 = upk(mul2(o[r][1], i2));
+                    const float2 y0 = upk(mul2(o[r][2], i2)), y1 = upk(mul2(o[r][3], i2));
+                    *(float4 *)&dst[r * HD] = make_float4(x0.x, x0.y, x1.x, x1.y);
+                    *(float4 *)&dst[r * HD + HD / 2] = make_float4(y0.x, y0.y, y1.x, y1.y);
+                }
+            }
+        } else {
+            const int slot = j == j0 ? 2 * b : 2 * b + 1;
+            float *ps = a.pre_part + (size_t)slot * G4_PRE_PART_SLOT;
+#pragma unroll
+            for (int r = 0; r < 8; r++) {
+                float *dst = ps + (size_t)(8 * rg + r) * HD + 4 * dg;
+                const float2 x0 = upk(o[r][0]), x1 = upk(o[r][1]), y0 = upk(o[r][2]), y1 = upk(o[r][3]);
+                *(float4 *)&dst[0] = make_float4(x0.x, x0.y, x1.x, x1.y);
+                *(float4 *)&dst[HD / 2] = make_float4(y0.x, y0.y, y1.x, y1.y);
+            }
+            if (dg == 0)
+#pragma unroll
+                for (int r = 0; r < 8; r++) {
+                    ps[R * HD + 8 * rg + r] = rm[8 * rg + r];
+                    ps[R * HD + R + 8 * rg + r] = rl[8 * rg + r];
+                }
+        }
+        u = seg_end;
+        j++;
+    }
+}
+
+// Combine the partial slots of q tiles that k_attn_prefill split over CTAs
+// (max-rescaled sums, slots in CTA order). grid (q tiles, tokens per tile):
+// CTA (j, y) merges the 8 head rows of token y of q tile j.
+constexpr int kMergeMaxSlots = 256;
+
+template <int HD>
+__global__ void __launch_bounds__(256) k_attn_prefill_merge(const AttnArgs a) {
+    using P = Pre<HD>;
+    constexpr int QT = P::QT, R = P::R;
+    __shared__ int pre[kPreMaxTiles + 4];
+    __shared__ int slots[kMergeMaxSlots];
+    __shared__ float wgt[kHeads][kMergeMaxSlots];
+    __shared__ int nslots;
+    griddep_launch();
+    griddep_wait();
+    const int T = a.T, nq = (T + QT - 1) / QT, j = blockIdx.x, tok = j * QT + blockIdx.y;
+    if (tok >= T) return;
+    const int tid = threadIdx.x;
+    if (tid < 32) P::prefix(pre, nq, T, a.start_pos, a.window);
+    __syncthreads();
+    const long long U = pre[nq];
+    const int G = a.pre_ctas;
+    const int bf = P::cta_of(pre[j], U, G), bl = P::cta_of(pre[j + 1] - 1, U, G);
+    if (bf == bl) return;
+    if (tid == 0) {
+        int n = 0;
+        for (int bb = bf; bb <= bl && n < kMergeMaxSlots; bb++)
+            if (!P::empty(bb, U, G)) slots[n++] = P::slot_of(bb, j, pre, U, G);
+        nslots = n;
     }
     __syncthreads();
-#pragma unroll
-    for (int r = 0; r < 4; r++) {
-        const int row = rg * 4 + r, t = t_base + row / kHeads, h = row % kHeads;
-        if (t >= a.T) continue;
-        const float inv = 1.0f / rl[row];
-        float *dst = a.out + (size_t)t * (kHeads * HD) + h * HD + 4 * lane;
-#pragma unroll
-        for (int i = 0; i < NV; i++)
-            *(float4 *)&dst[128 * i] = make_float4(o[r][i].x * inv, o[r][i].y * inv, o[r][i].z * inv, o[r][i].w * inv);
+    const int ns = nslots, row0 = 8 * blockIdx.y;   // tile rows of this token
+    // per head: weights exp(m_s - max) / sum_s l_s exp(m_s - max); warp h = head h
+    {
+        const int h = tid >> 5, lane = tid & 31;
+        float mx = -INFINITY;
+        for (int si = lane; si < ns; si += 32)
+            mx = fmaxf(mx, a.pre_part[(size_t)slots[si] * G4_PRE_PART_SLOT + R * HD + row0 + h]);
+        mx = warp_max(mx);
+        float l = 0.0f;
+        for (int si = lane; si < ns; si += 32) {
+            const float *ps = a.pre_part + (size_t)slots[si] * G4_PRE_PART_SLOT;
+            const float m = ps[R * HD + row0 + h];
+            const float w = m == -INFINITY ? 0.0f : expf(m - mx);
+            wgt[h][si] = w;
+            l = fmaf(ps[R * HD + R + row0 + h], w, l);
+        }
+        l = warp_sum(l);
+        const float inv = 1.0f / l;
+        __syncwarp();
+        for (int si = lane; si < ns; si += 32) wgt[h][si] *= inv;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < kHeads * HD / 4; idx += 256) {
+        const int h = idx / (HD / 4), c4 = idx - h * (HD / 4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int si = 0; si < ns; si++) {
+            const float w = wgt[h][si];
+            const float4 v = *(const float4 *)&a.pre_part[(size_t)slots[si] * G4_PRE_PART_SLOT +
+                                                         (size_t)(row0 + h) * HD + c4 * 4];
+            acc.x = fmaf(v.x, w, acc.x);
+            acc.y = fmaf(v.y, w, acc.y);
+            acc.z = fmaf(v.z, w, acc.z);
+            acc.w = fmaf(v.w, w, acc.w);
+        }
+        *(float4 *)&a.out[(size_t)tok * (kHeads * HD) + h * HD + c4 * 4] = acc;
     }
 }
 
@@ -322,7 +534,40 @@ cudaError_t set_smem(K kern, size_t bytes) {
     return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
 }
 
-size_t prefill_smem(int hd) { return (size_t)(kRows * hd + kTile * (hd + 4) + kTile * hd + kRows * 33 + 3 * kRows) * 4; }
+// Host copy of the unit schedule: does any q tile span more than one CTA?
+template <int HD>
+bool prefill_needs_merge(const AttnArgs &a) {
+    using P = Pre<HD>;
+    const int nq = (a.T + P::QT - 1) / P::QT;
+    int pre[kPreMaxTiles + 1];
+    pre[0] = 0;
+    for (int j = 0; j < nq; j++) {
+        const int t0 = j * P::QT, t1 = (a.T < t0 + P::QT ? a.T : t0 + P::QT) - 1;
+        const int pf = a.start_pos + t0;
+        const int klo = (a.window && pf + 1 > a.window) ? pf + 1 - a.window : 0;
+        pre[j + 1] = pre[j] + (a.start_pos + t1 - klo + P::BK) / P::BK;
+    }
+    const long long U = pre[nq];
+    const int G = a.pre_ctas;
+    auto cta_of = [&](long long u) { return (int)(((u + 1) * G + U - 1) / U) - 1; };
+    for (int j = 0; j < nq; j++)
+        if (cta_of(pre[j]) != cta_of(pre[j + 1] - 1)) return true;
+    return false;
+}
+
+template <int HD>
+cudaError_t launch_prefill(const AttnArgs &a, cudaStream_t st, bool pdl) {
+    static bool once = false;
+    if (!once) {
+        cudaError_t e = set_smem(k_attn_prefill<HD>, Pre<HD>::kSmem);
+        if (e) return e;
+        once = true;
+    }
+    cudaError_t e = g4_launch(k_attn_prefill<HD>, dim3(a.pre_ctas), dim3(256), Pre<HD>::kSmem, st, pdl, a);
+    if (e || !prefill_needs_merge<HD>(a)) return e;
+    const int nq = (a.T + Pre<HD>::QT - 1) / Pre<HD>::QT;
+    return g4_launch(k_attn_prefill_merge<HD>, dim3(nq, Pre<HD>::QT), dim3(256), 0, st, pdl, a);
+}
 
 }  // namespace
 
@@ -387,17 +632,9 @@ cudaError_t g4_launch_attn_strict(const AttnArgs &a, cudaStream_t st, bool pdl) 
 }
 
 cudaError_t g4_launch_attn_prefill(const AttnArgs &a, cudaStream_t st, bool pdl) {
-    const size_t smem = prefill_smem(a.hd);
-    dim3 grid((a.T + kQT - 1) / kQT);
-    if (a.hd == 256) {
-        static bool once = false;
-        if (!once) { cudaError_t e = set_smem(k_attn_prefill<256>, smem); if (e) return e; once = true; }
-        return g4_launch(k_attn_prefill<256>, grid, dim3(256), smem, st, pdl, a);
-    }
-    if (a.hd == 512) {
-        static bool once = false;
-        if (!once) { cudaError_t e = set_smem(k_attn_prefill<512>, smem); if (e) return e; once = true; }
-        return g4_launch(k_attn_prefill<512>, grid, dim3(256), smem, st, pdl, a);
-    }
+    if (a.T < 1 || a.T > G4_BATCH || !a.pre_part || a.pre_ctas < 1 || a.pre_ctas > kMergeMaxSlots)
+        return cudaErrorInvalidValue;
+    if (a.hd == 256) return launch_prefill<256>(a, st, pdl);
+    if (a.hd == 512) return launch_prefill<512>(a, st, pdl);
     return cudaErrorInvalidValue;
 }

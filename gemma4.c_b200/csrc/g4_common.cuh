@@ -200,6 +200,28 @@ G4_DEV float expf_host(float x) {
     return __double2float_rn(y);
 }
 
+// Packed pairs of fp32 (two independent IEEE round-to-nearest operations per
+// instruction, so each lane of the pair rounds exactly like fmul/fmaf).
+G4_DEV uint64_t pk(float x, float y) {
+    uint64_t r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+    return r;
+}
+G4_DEV float2 upk(uint64_t v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+G4_DEV uint64_t mul2(uint64_t a, uint64_t b) {
+    uint64_t r;
+    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
+    return r;
+}
+G4_DEV uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+    uint64_t r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
 // ---- reductions -----------------------------------------------------------
 G4_DEV float warp_sum(float v) {
 #pragma unroll

@@ -65,6 +65,7 @@ struct g4_ctx {
     float *xsT = nullptr;            // group-major activation scales (tensor-core GEMM)
     float *xs = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *gu = nullptr, *pg = nullptr;
     float *pli = nullptr, *ple_emb = nullptr, *ple_u = nullptr, *logits = nullptr, *part = nullptr;
+    float *pre_part = nullptr;       // prefill attention partial slots
     float *argmax_part = nullptr, *topk_v = nullptr;
     int *argmax_out = nullptr, *topk_i = nullptr;
     unsigned *ticket = nullptr;
@@ -401,6 +402,7 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
         {(void **)&c->ple_u, (size_t)kMaxT * G4_NUM_LAYERS * G4_PLE * 4},
         {(void **)&c->logits, (size_t)G4_VOCAB * 4},
         {(void **)&c->part, (size_t)kSplits * G4_HEADS * (G4_HD_GLOBAL + 4) * 4},
+        {(void **)&c->pre_part, (size_t)2 * c->num_sms * G4_PRE_PART_SLOT * 4},
         {(void **)&c->argmax_part, (size_t)1024 * 4 * 2 * 4},
         {(void **)&c->topk_v, (size_t)1024 * 64 * 4},
         {(void **)&c->topk_i, (size_t)1024 * 64 * 4},
@@ -547,6 +549,8 @@ AttnArgs attn_base(g4_ctx *c, const Layer &Y, int T, int start_pos, const int *p
     a.kcache = Y.kcache;
     a.vcache = Y.vcache;
     a.part = c->part;
+    a.pre_part = c->pre_part;
+    a.pre_ctas = c->num_sms;
     a.out = c->attn;
     a.xq = c->xq;
     a.xs = c->xs;

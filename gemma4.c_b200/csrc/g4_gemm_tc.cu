@@ -101,28 +101,6 @@ G4_DEV void tmem_ld32(uint32_t taddr, int (&v)[32]) {
 }
 G4_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// Packed pairs of fp32 (two independent IEEE round-to-nearest operations per
-// instruction, so each lane of the pair rounds exactly like fmul/fmaf).
-G4_DEV uint64_t pk(float x, float y) {
-    uint64_t r;
-    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
-    return r;
-}
-G4_DEV float2 upk(uint64_t v) {
-    float2 r;
-    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-    return r;
-}
-G4_DEV uint64_t mul2(uint64_t a, uint64_t b) {
-    uint64_t r;
-    asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-    return r;
-}
-G4_DEV uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
-    uint64_t r;
-    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-    return r;
-}
 // One group's step of 32 columns of the chain: acc = fma((float)d, ws * xs, acc).
 G4_DEV void chain32(uint64_t *acc, const int (&d)[32], const float *ws, float xv) {
     const uint64_t x2 = pk(xv, xv);

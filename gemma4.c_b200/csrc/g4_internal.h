@@ -87,7 +87,10 @@ struct GemvArgs {
 };
 
 // ---- GEMM (prefill, T > 4) -------------------------------------------------
-constexpr int G4_XST_STRIDE = G4_BATCH;   // row stride of group-major activation scales
+constexpr int G4_XST_STRIDE = G4_BATCH;
+// one prefill-attention partial: rows x (hd outputs) + row max + row sum, for
+// 64 rows at hd 256 (32 rows at hd 512 need less)
+constexpr int G4_PRE_PART_SLOT = 64 * (256 + 2);   // row stride of group-major activation scales
 
 struct GemmArgs {
     DMat m;
@@ -133,6 +136,10 @@ struct AttnArgs {
     // floats after sequence 0's. NULL row_seq: one sequence, positions start_pos + t.
     const int *row_seq, *row_pos;
     size_t seq_stride;
+    // fast prefill: CTAs of the balanced key-tile schedule and their partial
+    // slots (2 per CTA, G4_PRE_PART_SLOT floats each)
+    float *pre_part;
+    int pre_ctas;
 };
 
 // ---- persistent decode step (g4_decode.cu) ---------------------------------

@@ -279,6 +279,123 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
     return G4_OK;
 }
 
+// One attention sub-layer over an FP32 KV ring (gemma4.c:411-461), through the
+// same launchers the model uses; optionally timed. See g4cuda.h.
+int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, const float *qkv,
+                  const float *q_norm, const float *k_norm, const float *rope_cos, const float *rope_sin,
+                  float *kring, float *vring, float *out, int iters, float *ms_per_call) {
+    if ((hd != 256 && hd != 512) || ring < 1024 || (ring & (ring - 1)) || T < 1 || T > G4_BATCH ||
+        start_pos < 0 || mode < 0 || mode > 3 || !qkv || !rope_cos || !rope_sin || !kring || !vring || !out ||
+        iters < 0 || (iters > 0 && !ms_per_call))
+        return G4_ERR_INVALID;
+    if ((mode == 2 || mode == 3) && (splits < 1 || splits > 256)) return G4_ERR_INVALID;
+    if (mode == 2 && T != 1) return G4_ERR_INVALID;
+    const int window = hd == 256 ? G4_SLIDING_WINDOW : 0;
+    const int pairs = hd == 256 ? 128 : 64;
+    const int npos = start_pos + T;
+    // every key a query sees must still be in the ring
+    if ((window ? (T - 1 + window) : npos) > ring) return G4_ERR_INVALID;
+    const int stride = 10 * hd;
+    const int sms = num_sms();
+    DevBuf dqkv, dqn, dkn, dcos, dsin, dk, dv, dout, dpart, dpre, dscores, derr, drs, drp;
+    TK(dqkv.alloc((size_t)T * stride * 4));
+    TK(dqn.alloc((size_t)hd * 4));
+    TK(dkn.alloc((size_t)hd * 4));
+    TK(dcos.alloc((size_t)npos * pairs * 4));
+    TK(dsin.alloc((size_t)npos * pairs * 4));
+    TK(dk.alloc((size_t)ring * hd * 4));
+    TK(dv.alloc((size_t)ring * hd * 4));
+    TK(dout.alloc((size_t)T * 8 * hd * 4));
+    TK(dpart.alloc((size_t)(mode == 3 ? T : 1) * (splits > 0 ? splits : 1) * 8 * (hd + 4) * 4));
+    TK(dpre.alloc((size_t)2 * sms * G4_PRE_PART_SLOT * 4));
+    if (mode == 1) TK(dscores.alloc((size_t)T * 8 * npos * 4));
+    TK(derr.alloc(64));
+    TK(cudaMemset(derr.p, 0, 64));
+    std::vector<float> ones(hd, 1.0f);
+    TK(cudaMemcpy(dqkv.p, qkv, (size_t)T * stride * 4, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(dqn.p, q_norm ? q_norm : ones.data(), (size_t)hd * 4, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(dkn.p, k_norm ? k_norm : ones.data(), (size_t)hd * 4, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(dcos.p, rope_cos, (size_t)npos * pairs * 4, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(dsin.p, rope_sin, (size_t)npos * pairs * 4, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(dk.p, kring, (size_t)ring * hd * 4, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(dv.p, vring, (size_t)ring * hd * 4, cudaMemcpyHostToDevice));
+    AttnArgs a{};
+    a.hd = hd;
+    a.pairs = pairs;
+    a.window = window;
+    a.mask = ring - 1;
+    a.T = T;
+    a.start_pos = start_pos;
+    a.qkv = (float *)dqkv.p;
+    a.qkv_stride = stride;
+    a.has_kv = 1;
+    a.q_norm = (const float *)dqn.p;
+    a.k_norm = (const float *)dkn.p;
+    a.rope_cos = (const float *)dcos.p;
+    a.rope_sin = (const float *)dsin.p;
+    a.kcache = (float *)dk.p;
+    a.vcache = (float *)dv.p;
+    a.part = (float *)dpart.p;
+    a.out = (float *)dout.p;
+    a.err = (int *)derr.p;
+    a.strict = mode == 1;
+    a.scores = (float *)dscores.p;
+    a.score_stride = npos;
+    a.pre_part = (float *)dpre.p;
+    a.pre_ctas = sms;
+    if (mode == 3) {
+        std::vector<int> rs(T, 0), rp(T);
+        for (int t = 0; t < T; t++) rp[t] = start_pos + t;
+        TK(drs.alloc((size_t)T * 4));
+        TK(drp.alloc((size_t)T * 4));
+        TK(cudaMemcpy(drs.p, rs.data(), (size_t)T * 4, cudaMemcpyHostToDevice));
+        TK(cudaMemcpy(drp.p, rp.data(), (size_t)T * 4, cudaMemcpyHostToDevice));
+        a.row_seq = (const int *)drs.p;
+        a.row_pos = (const int *)drp.p;
+    }
+    // q/k/v post-processing (decode does its own inside the split kernel)
+    if (mode != 2) TK(g4_launch_qkv_post(a, 0, false));
+    auto attend = [&]() -> cudaError_t {
+        switch (mode) {
+        case 0: return g4_launch_attn_prefill(a, 0, false);
+        case 1: return g4_launch_attn_strict(a, 0, false);
+        case 2: {
+            cudaError_t e = g4_launch_attn_decode(a, splits, 0, false);
+            return e ? e : g4_launch_attn_combine(a, splits, 0, false);
+        }
+        default: return g4_launch_attn_rows(a, splits, 0, false);
+        }
+    };
+    TK(attend());
+    TK(cudaDeviceSynchronize());
+    int err = 0;
+    TK(cudaMemcpy(&err, derr.p, 4, cudaMemcpyDeviceToHost));
+    if (err) return G4_ERR_DEVICE;
+    TK(cudaMemcpy(out, dout.p, (size_t)T * 8 * hd * 4, cudaMemcpyDeviceToHost));
+    TK(cudaMemcpy(kring, dk.p, (size_t)ring * hd * 4, cudaMemcpyDeviceToHost));
+    TK(cudaMemcpy(vring, dv.p, (size_t)ring * hd * 4, cudaMemcpyDeviceToHost));
+    if (iters > 0) {
+        // the attention kernels are pure functions of the post-processed q and
+        // the rings, so repeating them re-does the same work
+        for (int i = 0; i < 3; i++) TK(attend());
+        cudaEvent_t e0, e1;
+        TK(cudaEventCreate(&e0));
+        TK(cudaEventCreate(&e1));
+        cudaEventRecord(e0, 0);
+        for (int i = 0; i < iters; i++) attend();
+        cudaEventRecord(e1, 0);
+        cudaError_t e = cudaEventSynchronize(e1);
+        float ms = 0.0f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+        TK(e);
+        TK(cudaGetLastError());
+        *ms_per_call = ms / iters;
+    }
+    return G4_OK;
+}
+
 // Time the decode GEMV on an N x K matrix (random device-resident weights):
 // `copies` distinct weight sets are cycled so the working set exceeds L2, and
 // `iters` back-to-back launches are timed with CUDA events on one stream.

@@ -80,6 +80,8 @@ def load(path=LIB_PATH):
                                 C.POINTER(C.c_double)]
     L.g4_bench_gemv.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
                                 C.POINTER(C.c_double)]
+    L.g4k_attention.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, vp, vp, _f32p,
+                                _f32p, _f32p, _f32p, _f32p, C.c_int, C.POINTER(C.c_float)]
     L.g4_profiler_range.argtypes = [C.c_int]
     L.g4_mark.argtypes = [vp, C.c_int]
     L.g4_elapsed.argtypes = [vp, C.c_int, C.c_int, C.POINTER(C.c_float)]
@@ -304,6 +306,28 @@ def bench_gemv(N, K, T=1, iters=200, pdl=True):
     ms, by = C.c_float(), C.c_double()
     _check(L.g4_bench_gemv(N, K, T, iters, int(pdl), C.byref(ms), C.byref(by)))
     return ms.value, by.value
+
+
+ATTN_PREFILL, ATTN_STRICT, ATTN_DECODE, ATTN_ROWS = 0, 1, 2, 3
+
+
+def attention(qkv, hd, kring, vring, start_pos, cos_t, sin_t, mode=ATTN_PREFILL, splits=148, q_norm=None,
+              k_norm=None, iters=0):
+    """One attention sub-layer on the GPU (g4k_attention). qkv[T][10*hd] raw
+    q | k | v; kring / vring [ring][hd] are updated in place with the chunk's
+    keys and values. Returns (out[T][8*hd], ms per call or None)."""
+    L = load()
+    qkv = np.ascontiguousarray(qkv, np.float32)
+    T = qkv.shape[0]
+    out = np.empty((T, 8 * hd), np.float32)
+    qn = None if q_norm is None else np.ascontiguousarray(q_norm, np.float32)
+    kn = None if k_norm is None else np.ascontiguousarray(k_norm, np.float32)
+    ms = C.c_float(0.0)
+    _check(L.g4k_attention(hd, kring.shape[0], T, start_pos, mode, splits, qkv,
+                           None if qn is None else qn.ctypes.data, None if kn is None else kn.ctypes.data,
+                           np.ascontiguousarray(cos_t, np.float32), np.ascontiguousarray(sin_t, np.float32),
+                           kring, vring, out, iters, C.byref(ms)))
+    return out, (ms.value if iters else None)
 
 
 def rmsnorm_quant(x, w, eps=1e-6):

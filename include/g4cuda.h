@@ -200,6 +200,21 @@ int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch,
 /* Prefill GEMM timing (path 2 SIMT dp4a, 3 tcgen05) on T x N x K: average
  * launch duration and int8 operations (2 T N K) per launch. */
 int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch, double *ops_per_launch);
+/* One attention sub-layer (attention, gemma4.c:411-461) over an FP32 KV ring:
+ * hd 256 = sliding layer (window 512, 128 rope pairs), hd 512 = global layer
+ * (no window, 64 pairs). qkv[T][10*hd] holds each token's raw q (8 heads) | k | v;
+ * q_norm / k_norm [hd] (NULL = weight 1); rope_cos / rope_sin
+ * [start_pos + T][pairs]; kring / vring [ring][hd] (ring a power of two >= 1024)
+ * are read and receive the chunk's keys and values; out[T][8*hd].
+ * mode 0: prefill fast path (q/k/v post-processing + tiled kernel); 1: strict
+ * (the reference's floating-point order); 2: single-token decode (split-KV
+ * over `splits` CTAs + combine, T == 1); 3: batched-row decode path (one row
+ * per token at start_pos + t, `splits` key splits). iters > 0: the attention
+ * kernels (without post-processing) are then repeated `iters` times and the
+ * average duration per call is written to ms_per_call. */
+int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, const float *qkv,
+                  const float *q_norm, const float *k_norm, const float *rope_cos, const float *rope_sin,
+                  float *kring, float *vring, float *out, int iters, float *ms_per_call);
 /* rmsnorm (gemma4.c:360-373) of hidden-width rows followed by quantize */
 int g4k_rmsnorm_quant(const float *x, int rows, const float *w, float eps, float *y, int8_t *q, float *s);
 

@@ -1,0 +1,105 @@
+"""Attention sub-layer (gemma4.c:411-461) on the GPU against the oracle.
+
+Inputs follow the attention benchmark: raw q (8 heads), k and v drawn N(0, 1),
+q/k RMS-normalised with weight 1 and rotated, v normalised without a weight,
+then unscaled q.k scores over the ring (sliding: hd 256, window 512, ring
+1024; global: hd 512, no window). Earlier positions' keys are random
+normalised vectors already in the ring.
+
+  - strict mode: bit-exact with the oracle (reference floating-point order);
+  - fast prefill (tiled kernel + CTA-split merge), decode (split-KV + combine)
+    and batched-row paths: outputs within 2e-4 absolute of the oracle (values
+    are O(1); the fast paths differ only in summation order and in the device
+    expf; the oracle itself is within ~2e-5 of a float64 evaluation), ring
+    contents within 1e-5;
+  - the fast prefill is deterministic (same bits on a second call).
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+OUT_ATOL = 2e-4
+RING_ATOL = 1e-5
+
+
+def rope_tables(n, pairs, hd, theta):
+    inv = theta ** (-np.arange(pairs, dtype=np.float64) * 2.0 / hd)
+    ang = np.arange(n, dtype=np.float64)[:, None] * inv[None, :]
+    return np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+
+def inputs(hd, T, start_pos, ring, seed):
+    rng = np.random.default_rng(seed)
+    qkv = rng.standard_normal((T, 10 * hd)).astype(np.float32)
+    k = rng.standard_normal((ring, hd)).astype(np.float32)
+    v = rng.standard_normal((ring, hd)).astype(np.float32)
+    k /= np.sqrt((k * k).mean(axis=1, keepdims=True))
+    v /= np.sqrt((v * v).mean(axis=1, keepdims=True))
+    pairs, theta = (128, 1e4) if hd == 256 else (64, 1e6)
+    cos_t, sin_t = rope_tables(start_pos + T, pairs, hd, theta)
+    return qkv, k, v, cos_t, sin_t
+
+
+CASES = [
+    (256, 1, 0, 1024), (256, 37, 0, 1024), (256, 512, 0, 1024), (256, 512, 700, 1024), (256, 9, 2000, 1024),
+    (512, 1, 0, 4096), (512, 37, 0, 4096), (512, 512, 0, 4096), (512, 300, 1500, 4096), (512, 512, 3000, 4096),
+]
+
+
+def _oracle(oracle, hd, T, start_pos, ring, seed):
+    qkv, k, v, cos_t, sin_t = inputs(hd, T, start_pos, ring, seed)
+    ko, vo = k.copy(), v.copy()
+    out = oracle.attention(qkv, hd, ko, vo, start_pos, cos_t, sin_t)
+    return (qkv, k, v, cos_t, sin_t), (out, ko, vo)
+
+
+@pytest.mark.parametrize("hd,T,start_pos,ring", CASES)
+def test_prefill_fast_tracks_oracle(g4, oracle, hd, T, start_pos, ring):
+    (qkv, k, v, cos_t, sin_t), (eo, ek, ev) = _oracle(oracle, hd, T, start_pos, ring, 100 + T + start_pos)
+    k1, v1 = k.copy(), v.copy()
+    out, _ = g4.attention(qkv, hd, k1, v1, start_pos, cos_t, sin_t, mode=g4.ATTN_PREFILL)
+    assert np.abs(k1 - ek).max() <= RING_ATOL and np.abs(v1 - ev).max() <= RING_ATOL
+    err = np.abs(out - eo).max()
+    assert err <= OUT_ATOL, f"max abs error {err}"
+    k2, v2 = k.copy(), v.copy()
+    out2, _ = g4.attention(qkv, hd, k2, v2, start_pos, cos_t, sin_t, mode=g4.ATTN_PREFILL)
+    assert np.array_equal(out.view(np.uint32), out2.view(np.uint32))
+
+
+@pytest.mark.parametrize("hd,T,start_pos,ring", [c for c in CASES if c[1] <= 37])
+def test_strict_bitexact(g4, oracle, hd, T, start_pos, ring):
+    (qkv, k, v, cos_t, sin_t), (eo, ek, ev) = _oracle(oracle, hd, T, start_pos, ring, 200 + T + start_pos)
+    out, _ = g4.attention(qkv, hd, k, v, start_pos, cos_t, sin_t, mode=g4.ATTN_STRICT)
+    assert np.array_equal(k.view(np.uint32), ek.view(np.uint32))
+    assert np.array_equal(v.view(np.uint32), ev.view(np.uint32))
+    assert np.array_equal(out.view(np.uint32), eo.view(np.uint32))
+
+
+@pytest.mark.parametrize("hd,pos,ring", [(256, 0, 1024), (256, 600, 1024), (256, 3000, 1024),
+                                         (512, 0, 4096), (512, 2047, 4096), (512, 4000, 4096)])
+def test_decode_tracks_oracle(g4, oracle, hd, pos, ring):
+    (qkv, k, v, cos_t, sin_t), (eo, ek, ev) = _oracle(oracle, hd, 1, pos, ring, 300 + pos)
+    out, _ = g4.attention(qkv, hd, k, v, pos, cos_t, sin_t, mode=g4.ATTN_DECODE, splits=148)
+    assert np.abs(k - ek).max() <= RING_ATOL and np.abs(v - ev).max() <= RING_ATOL
+    err = np.abs(out - eo).max()
+    assert err <= OUT_ATOL, f"max abs error {err}"
+
+
+@pytest.mark.parametrize("hd,T,start_pos,ring,splits", [(256, 7, 900, 1024, 16), (512, 5, 2500, 4096, 37)])
+def test_rows_tracks_oracle(g4, oracle, hd, T, start_pos, ring, splits):
+    (qkv, k, v, cos_t, sin_t), (eo, ek, ev) = _oracle(oracle, hd, T, start_pos, ring, 400 + T)
+    out, _ = g4.attention(qkv, hd, k, v, start_pos, cos_t, sin_t, mode=g4.ATTN_ROWS, splits=splits)
+    err = np.abs(out - eo).max()
+    assert err <= OUT_ATOL, f"max abs error {err}"
+
+
+def test_attention_api_errors(g4):
+    qkv, k, v, cos_t, sin_t = inputs(256, 4, 0, 1024, 1)
+    with pytest.raises(g4.G4Error):
+        g4.attention(qkv, 384, k, v, 0, cos_t, sin_t)                      # head_dim
+    with pytest.raises(g4.G4Error):
+        g4.attention(qkv, 256, k, v, 0, cos_t, sin_t, mode=g4.ATTN_DECODE)  # decode needs T == 1
+    small = np.zeros((512, 256), np.float32)
+    with pytest.raises(g4.G4Error):
+        g4.attention(qkv, 256, small, small.copy(), 0, cos_t, sin_t)       # ring < 1024

@@ -18,12 +18,14 @@
 //   warp 1      allocates all 512 TMEM columns; one lane issues tcgen05.mma
 //               kind::i8 (M 128, N 128, K 32): two per 64-wide group, into one
 //               of four TMEM accumulators (int32), and commits each group;
-//   warps 2-9   epilogue: thread = token row (TMEM lane), warp w owns the
-//               64 columns (w - 2) / 4 of its lane quadrant; per group it reads
-//               the int32 dots from TMEM (two 32-column loads, the second in
-//               flight during the first half's math) and advances its 64 fp32 chains with the weight and
-//               activation scales staged by the producer, then applies the
-//               output epilogue (store, GEGLU pair, PLE gate).
+//   warps 2-17  epilogue: thread = token row (TMEM lane), warp w owns the
+//               32 columns (w - 2) / 4 of its lane quadrant (four warps per
+//               quadrant, so each scheduler has four to hide the TMEM-load and
+//               conversion latencies); per group it reads the int32 dots from
+//               TMEM (one 32-column load), frees the accumulator and advances
+//               its 32 fp32 chains with the weight and activation scales
+//               staged by the producer, then applies the output epilogue
+//               (store, GEGLU pair, PLE gate).
 // Waits are bounded (mbar_wait); on a timeout every role leaves its loop, the
 // CTA drains the copies and MMAs it issued, and TMEM is freed.
 #include <cuda.h>
@@ -44,8 +46,10 @@ constexpr int kOffB = kOffA + kStages * kTileBytes;
 constexpr int kOffS = kOffB + kStages * kTileBytes;
 constexpr int kOffBar = kOffS + kStages * kScaleBytes;
 // barriers: full[S], empty[S], tfull[B], tempty[B], then the TMEM address word
-constexpr int kSmemBytes = kOffBar + (2 * kStages + 2 * kTmemBufs) * 8 + 16 + 1024;   // + 1 KB for alignment
-constexpr int kEpiWarps = 8;                      // 2 per TMEM lane quadrant, 64 columns each
+constexpr int kOffGelu = (kOffBar + (2 * kStages + 2 * kTmemBufs) * 8 + 16 + 127) & ~127;
+constexpr int kGeluSize = 4096;                   // GELU table (GEGLU / PLE epilogues), staged once
+constexpr int kSmemBytes = kOffGelu + kGeluSize * 4 + 1024;   // + 1 KB for alignment
+constexpr int kEpiWarps = 16;                     // 4 per TMEM lane quadrant, 32 columns each
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 
 G4_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
@@ -157,6 +161,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = 0;
         committed = 0;
     }
+    float *gelu_s = (float *)(smem + kOffGelu);
+    if (p.epi != EPI_STORE)
+        for (int i = tid; i < kGeluSize; i += kThreads) gelu_s[i] = p.gelu[i];
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
                      "r"(kTmemCols)
@@ -232,20 +239,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------- epilogue ----------------
-        // warp w: TMEM lane quadrant w % 4 (token rows), column half (w - 2) / 4.
-        // Each group's 64 columns are two 32-column TMEM loads; the second is in
-        // flight while the first 32 columns advance their chains.
-        const int e = warp - 2, q = warp & 3, ch = e >> 2;
+        // warp w: TMEM lane quadrant w % 4 (token rows), 32-column block (w - 2) / 4.
+        const int e = warp - 2, q = warp & 3, cb = e >> 2;
         const int row = q * 32 + lane;
-        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(ch * 64);
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32);
         int gidx = 0;   // groups consumed so far (all tiles)
         bool ok = true;
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
             const int n0 = (tile / mt) * kBN, t = (tile % mt) * kBM + row;
-            uint64_t acc[32];
+            uint64_t acc[16];
 #pragma unroll
-            for (int j = 0; j < 32; j++) acc[j] = 0ull;
-            int dA[32], dB[32];
+            for (int j = 0; j < 16; j++) acc[j] = 0ull;
+            int d[32];
             for (int g = 0; g < G; g++, gidx++) {
                 const int b = gidx % kTmemBufs, k = gidx >> 1, s = k % kStages;
                 // wait until group g's dots are in TMEM (and, once per step, its scales in smem)
@@ -258,48 +263,51 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const float *sc = (const float *)(smem + kOffS + s * kScaleBytes);
-                const float xv = sc[2 * kBN + (gidx & 1) * kBM + row];
-                const float *ws = sc + (gidx & 1) * kBN + ch * 64;
-                // (no load is left pending across the loop's back edge)
-                tmem_ld32(tbase + (uint32_t)(b * kBN), dA);
-                tmem_wait_ld();
-                tmem_ld32(tbase + (uint32_t)(b * kBN + 32), dB);   // in flight during the first half
-                chain32(acc, dA, ws, xv);
+                tmem_ld32(tbase + (uint32_t)(b * kBN), d);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[b]);
-                chain32(acc + 16, dB, ws + 32, xv);
+                const float *sc = (const float *)(smem + kOffS + s * kScaleBytes);
+                const float xv = sc[2 * kBN + (gidx & 1) * kBM + row];
+                chain32(acc, d, sc + (gidx & 1) * kBN + cb * 32, xv);
                 if (gidx & 1) {   // both groups of step k done: release its stage (scales)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[s]);
                 }
             }
             if (!ok || t >= p.T) continue;
-            const int nb = n0 + ch * 64;
+            const int nb = n0 + cb * 32;
             if (p.epi == EPI_STORE) {
                 float4 *o = (float4 *)(p.out + (size_t)t * p.out_stride + nb);
 #pragma unroll
-                for (int j = 0; j < 16; j++) {
+                for (int j = 0; j < 8; j++) {
                     const float2 a = upk(acc[2 * j]), b2 = upk(acc[2 * j + 1]);
                     o[j] = make_float4(a.x, a.y, b2.x, b2.y);
                 }
             } else if (p.epi == EPI_GEGLU_PAIR) {
-                float *o = p.out + (size_t)t * p.out_stride + (nb >> 1);
+                float4 *o = (float4 *)(p.out + (size_t)t * p.out_stride + (nb >> 1));
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const float2 a = upk(acc[j]);
-                    o[j] = geglu_one(a.x, a.y, p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                for (int j = 0; j < 4; j++) {
+                    float r[4];
+#pragma unroll
+                    for (int i = 0; i < 4; i++) {
+                        const float2 a = upk(acc[4 * j + i]);
+                        r[i] = geglu_one(a.x, a.y, gelu_s, kGeluSize, -8.0f, 8.0f, 4095.0f / 16.0f);
+                    }
+                    o[j] = make_float4(r[0], r[1], r[2], r[3]);
                 }
             } else {
-                float *o = p.out + (size_t)t * p.out_stride + nb;
-                const float *u = p.ple_u + (size_t)t * p.u_stride + nb;
+                float4 *o = (float4 *)(p.out + (size_t)t * p.out_stride + nb);
+                const float4 *u = (const float4 *)(p.ple_u + (size_t)t * p.u_stride + nb);
 #pragma unroll
-                for (int j = 0; j < 32; j++) {
-                    const float2 a = upk(acc[j]);
-                    o[2 * j] = geglu_one(a.x, u[2 * j], p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
-                    o[2 * j + 1] = geglu_one(a.y, u[2 * j + 1], p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                for (int j = 0; j < 8; j++) {
+                    const float4 u4 = u[j];
+                    const float2 a = upk(acc[2 * j]), b2 = upk(acc[2 * j + 1]);
+                    o[j] = make_float4(geglu_one(a.x, u4.x, gelu_s, kGeluSize, -8.0f, 8.0f, 4095.0f / 16.0f),
+                                       geglu_one(a.y, u4.y, gelu_s, kGeluSize, -8.0f, 8.0f, 4095.0f / 16.0f),
+                                       geglu_one(b2.x, u4.z, gelu_s, kGeluSize, -8.0f, 8.0f, 4095.0f / 16.0f),
+                                       geglu_one(b2.y, u4.w, gelu_s, kGeluSize, -8.0f, 8.0f, 4095.0f / 16.0f));
                 }
             }
         }

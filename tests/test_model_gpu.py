@@ -93,6 +93,23 @@ def test_graph_replay_equals_eager(g4, image):
     assert np.array_equal(outs[0], outs[1])
 
 
+def test_prefill_gemm_paths_bitidentical(g4, image):
+    """The tensor-core GEMM (store, GEGLU-pair and PLE-gate epilogues) and the
+    SIMT dp4a GEMM run the same per-group fp32 chain, so a whole prefill gives
+    the same bits on either path."""
+    rng = np.random.default_rng(10)
+    toks = rng.integers(0, 262144, size=300).astype(np.int32)
+    res, lgs = [], []
+    for path in (2, 1):
+        with g4.Model(image) as m:
+            m.set_option(g4.OPT_GEMM_PATH, path)
+            m.forward(toks, 0)
+            res.append(m.residual(300))
+            lgs.append(m.logits(299)[0])
+    assert np.array_equal(res[0].view(np.uint32), res[1].view(np.uint32))
+    assert np.array_equal(lgs[0].view(np.uint32), lgs[1].view(np.uint32))
+
+
 def test_api_errors(g4, gpu):
     with pytest.raises(g4.G4Error) as e:
         gpu.forward(np.array([262144], np.int32), 0)

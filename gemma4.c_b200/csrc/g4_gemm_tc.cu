@@ -35,22 +35,34 @@
 
 namespace {
 
-constexpr int kBM = 128, kBN = 128, kBK = 128;   // tile: tokens x outputs x K bytes per stage
+constexpr int kBM = 128, kBK = 128;   // tile: tokens x K bytes per stage (outputs: BN below)
 constexpr int kStages = 6;
-constexpr int kTmemBufs = 4;                      // int32 group accumulators in flight
-constexpr int kTmemCols = kTmemBufs * kBN;        // 512: all of TMEM (one CTA per SM)
-constexpr int kTileBytes = kBM * kBK;             // 16 KB (A and B alike)
-constexpr int kScaleBytes = 2 * kBN * 4 + 2 * kBM * 4;   // two groups of fp32 weight and activation scales
-constexpr int kOffA = 0;
-constexpr int kOffB = kOffA + kStages * kTileBytes;
-constexpr int kOffS = kOffB + kStages * kTileBytes;
-constexpr int kOffBar = kOffS + kStages * kScaleBytes;
-// barriers: full[S], empty[S], tfull[B], tempty[B], then the TMEM address word
-constexpr int kOffGelu = (kOffBar + (2 * kStages + 2 * kTmemBufs) * 8 + 16 + 127) & ~127;
+constexpr int kTileBytesA = kBM * kBK;            // 16 KB
 constexpr int kGeluSize = 4096;                   // GELU table (GEGLU / PLE epilogues), staged once
-constexpr int kSmemBytes = kOffGelu + kGeluSize * 4 + 1024;   // + 1 KB for alignment
-constexpr int kEpiWarps = 16;                     // 4 per TMEM lane quadrant, 32 columns each
+constexpr int kEpiWarps = 16;                     // 4 per TMEM lane quadrant, BN / 4 columns each
 constexpr int kThreads = 64 + 32 * kEpiWarps;
+
+// Output-tile width BN (128, 64 or 32): narrower tiles give GEMMs with few
+// output columns (N = 1536, 256) enough tiles for every SM.
+template <int BN>
+struct TcCfg {
+    static constexpr int kTmemBufs = 512 / BN > 8 ? 8 : 512 / BN;   // int32 group accumulators in flight
+    static constexpr int kTmemCols = kTmemBufs * BN;                 // 512 / 512 / 256
+    static constexpr int kTileBytesB = BN * kBK;
+    static constexpr int kScaleBytes = 2 * BN * 4 + 2 * kBM * 4;     // two groups of weight and activation scales
+    static constexpr int kOffA = 0;
+    static constexpr int kOffB = kOffA + kStages * kTileBytesA;
+    static constexpr int kOffS = kOffB + kStages * kTileBytesB;
+    static constexpr int kOffBar = kOffS + kStages * kScaleBytes;
+    // barriers: full[S], empty[S], tfull[B], tempty[B], then the TMEM address word
+    static constexpr int kOffGelu = (kOffBar + (2 * kStages + 2 * kTmemBufs) * 8 + 16 + 127) & ~127;
+    static constexpr int kSmemBytes = kOffGelu + kGeluSize * 4 + 1024;   // + 1 KB for alignment
+    static constexpr int CW = BN / 4;                                    // columns per epilogue warp
+    // Instruction descriptor: S32 accumulate, signed int8 A and B, both K-major,
+    // N = BN (>> 3), M = 128 (>> 4).
+    static constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(BN >> 3) << 17) |
+                                       ((uint32_t)(kBM >> 4) << 24);
+};
 
 G4_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -72,16 +84,11 @@ G4_DEV uint64_t umma_desc(const void *tile, int kbyte) {
     const uint32_t a = smem_u32(tile) + (uint32_t)kbyte;
     return (uint64_t)((a >> 4) & 0x3FFF) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
-// Instruction descriptor: S32 accumulate, signed int8 A and B, both K-major,
-// N = 128 (>> 3), M = 128 (>> 4).
-constexpr uint32_t kIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kBN >> 3) << 17) |
-                            ((uint32_t)(kBM >> 4) << 24);
-
-G4_DEV void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, bool accumulate) {
+G4_DEV void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, bool accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
-        "l"(da), "l"(db), "r"(kIdesc), "r"((uint32_t)accumulate)
+        "l"(da), "l"(db), "r"(idesc), "r"((uint32_t)accumulate)
         : "memory");
 }
 G4_DEV void mma_commit(uint64_t *bar) {
@@ -103,13 +110,35 @@ G4_DEV void tmem_ld32(uint32_t taddr, int (&v)[32]) {
         : "r"(taddr)
         : "memory");
 }
+G4_DEV void tmem_ld16(uint32_t taddr, int (&v)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]),
+          "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr)
+        : "memory");
+}
+G4_DEV void tmem_ld8(uint32_t taddr, int (&v)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+                 : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7])
+                 : "r"(taddr)
+                 : "memory");
+}
+template <int CW>
+G4_DEV void tmem_ld(uint32_t taddr, int (&v)[CW]) {
+    if constexpr (CW == 32) tmem_ld32(taddr, v);
+    else if constexpr (CW == 16) tmem_ld16(taddr, v);
+    else tmem_ld8(taddr, v);
+}
 G4_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// One group's step of 32 columns of the chain: acc = fma((float)d, ws * xs, acc).
-G4_DEV void chain32(uint64_t *acc, const int (&d)[32], const float *ws, float xv) {
+// One group's step of CW columns of the chain: acc = fma((float)d, ws * xs, acc).
+template <int CW>
+G4_DEV void chain(uint64_t *acc, const int (&d)[CW], const float *ws, float xv) {
     const uint64_t x2 = pk(xv, xv);
 #pragma unroll
-    for (int j = 0; j < 32; j += 4) {
+    for (int j = 0; j < CW; j += 4) {
         const float4 w4 = *(const float4 *)(ws + j);
         const uint64_t w01 = mul2(pk(w4.x, w4.y), x2), w23 = mul2(pk(w4.z, w4.w), x2);
         acc[j / 2] = fma2(pk(__int2float_rn(d[j]), __int2float_rn(d[j + 1])), w01, acc[j / 2]);
@@ -130,19 +159,22 @@ struct TcArgs {
     int *err;
 };
 
+template <int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const TcArgs p) {
+    using C = TcCfg<BN>;
+    constexpr int kTmemBufs = C::kTmemBufs, CW = C::CW;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
-    uint64_t *full = (uint64_t *)(smem + kOffBar);
+    uint64_t *full = (uint64_t *)(smem + C::kOffBar);
     uint64_t *empty = full + kStages;
     uint64_t *tfull = empty + kStages;
     uint64_t *tempty = tfull + kTmemBufs;
     uint32_t *tmem_slot = (uint32_t *)(tempty + kTmemBufs);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int steps = p.K / kBK, G = p.K >> 6;
-    const int mt = (p.T + kBM - 1) / kBM, tiles = (p.N / kBN) * mt;
+    const int mt = (p.T + kBM - 1) / kBM, tiles = (p.N / BN) * mt;
     // persistent: this CTA takes tiles blockIdx.x, + gridDim.x, ...; the m tiles of
     // one n tile are consecutive, so CTAs sharing weights run together (L2 reuse)
     __shared__ int fail, issued, committed;
@@ -161,12 +193,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         issued = 0;
         committed = 0;
     }
-    float *gelu_s = (float *)(smem + kOffGelu);
+    float *gelu_s = (float *)(smem + C::kOffGelu);
     if (p.epi != EPI_STORE)
         for (int i = tid; i < kGeluSize; i += kThreads) gelu_s[i] = p.gelu[i];
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
-                     "r"(kTmemCols)
+                     "r"(C::kTmemCols)
                      : "memory");
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
@@ -181,7 +213,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             int k = 0;   // steps issued so far (all tiles)
             bool ok = true;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                const int n0 = (tile / mt) * kBN, t0 = (tile % mt) * kBM;
+                const int n0 = (tile / mt) * BN, t0 = (tile % mt) * kBM;
                 for (int ks = 0; ks < steps; ks++, k++) {
                     const int s = k % kStages, use = k / kStages;
                     if (use > 0 &&
@@ -189,13 +221,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         ok = false;
                         break;
                     }
-                    mbar_arrive_expect_tx(&full[s], 2 * kTileBytes + kScaleBytes);
-                    tma_load_2d(smem + kOffA + s * kTileBytes, &map_a, ks * kBK, t0, &full[s]);
-                    tma_load_2d(smem + kOffB + s * kTileBytes, &map_b, ks * kBK, n0, &full[s]);
+                    mbar_arrive_expect_tx(&full[s], kTileBytesA + C::kTileBytesB + C::kScaleBytes);
+                    tma_load_2d(smem + C::kOffA + s * kTileBytesA, &map_a, ks * kBK, t0, &full[s]);
+                    tma_load_2d(smem + C::kOffB + s * C::kTileBytesB, &map_b, ks * kBK, n0, &full[s]);
                     for (int gi = 0; gi < 2; gi++) {
-                        bulk_g2s_plain(smem + kOffS + s * kScaleBytes + gi * kBN * 4,
-                                       p.wsT + (size_t)(2 * ks + gi) * p.N + n0, kBN * 4, &full[s]);
-                        bulk_g2s_plain(smem + kOffS + s * kScaleBytes + 2 * kBN * 4 + gi * kBM * 4,
+                        bulk_g2s_plain(smem + C::kOffS + s * C::kScaleBytes + gi * BN * 4,
+                                       p.wsT + (size_t)(2 * ks + gi) * p.N + n0, BN * 4, &full[s]);
+                        bulk_g2s_plain(smem + C::kOffS + s * C::kScaleBytes + 2 * BN * 4 + gi * kBM * 4,
                                        p.xsT + (size_t)(2 * ks + gi) * G4_XST_STRIDE + t0, kBM * 4, &full[s]);
                     }
                 }
@@ -224,10 +256,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                             break;
                         }
                         tc_fence_after();
-                        const uint8_t *ta = smem + kOffA + s * kTileBytes, *tb = smem + kOffB + s * kTileBytes;
+                        const uint8_t *ta = smem + C::kOffA + s * kTileBytesA, *tb = smem + C::kOffB + s * C::kTileBytesB;
                         for (int kk = 0; kk < 2; kk++) {
                             const int kb = gi * 64 + kk * 32;
-                            mma_i8(tmem + b * kBN, umma_desc(ta, kb), umma_desc(tb, kb), kk != 0);
+                            mma_i8(tmem + b * BN, umma_desc(ta, kb), umma_desc(tb, kb), C::kIdesc, kk != 0);
                         }
                         mma_commit(&tfull[b]);
                     }
@@ -239,18 +271,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
     } else {
         // ---------------- epilogue ----------------
-        // warp w: TMEM lane quadrant w % 4 (token rows), 32-column block (w - 2) / 4.
+        // warp w: TMEM lane quadrant w % 4 (token rows), CW-column block (w - 2) / 4.
         const int e = warp - 2, q = warp & 3, cb = e >> 2;
         const int row = q * 32 + lane;
-        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * 32);
+        const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * CW);
         int gidx = 0;   // groups consumed so far (all tiles)
         bool ok = true;
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-            const int n0 = (tile / mt) * kBN, t = (tile % mt) * kBM + row;
-            uint64_t acc[16];
+            const int n0 = (tile / mt) * BN, t = (tile % mt) * kBM + row;
+            uint64_t acc[CW / 2];
 #pragma unroll
-            for (int j = 0; j < 16; j++) acc[j] = 0ull;
-            int d[32];
+            for (int j = 0; j < CW / 2; j++) acc[j] = 0ull;
+            int d[CW];
             for (int g = 0; g < G; g++, gidx++) {
                 const int b = gidx % kTmemBufs, k = gidx >> 1, s = k % kStages;
                 // wait until group g's dots are in TMEM (and, once per step, its scales in smem)
@@ -263,32 +295,32 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                tmem_ld32(tbase + (uint32_t)(b * kBN), d);
+                tmem_ld<CW>(tbase + (uint32_t)(b * BN), d);
                 tmem_wait_ld();
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[b]);
-                const float *sc = (const float *)(smem + kOffS + s * kScaleBytes);
-                const float xv = sc[2 * kBN + (gidx & 1) * kBM + row];
-                chain32(acc, d, sc + (gidx & 1) * kBN + cb * 32, xv);
+                const float *sc = (const float *)(smem + C::kOffS + s * C::kScaleBytes);
+                const float xv = sc[2 * BN + (gidx & 1) * kBM + row];
+                chain<CW>(acc, d, sc + (gidx & 1) * BN + cb * CW, xv);
                 if (gidx & 1) {   // both groups of step k done: release its stage (scales)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&empty[s]);
                 }
             }
             if (!ok || t >= p.T) continue;
-            const int nb = n0 + cb * 32;
+            const int nb = n0 + cb * CW;
             if (p.epi == EPI_STORE) {
                 float4 *o = (float4 *)(p.out + (size_t)t * p.out_stride + nb);
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
+                for (int j = 0; j < CW / 4; j++) {
                     const float2 a = upk(acc[2 * j]), b2 = upk(acc[2 * j + 1]);
                     o[j] = make_float4(a.x, a.y, b2.x, b2.y);
                 }
             } else if (p.epi == EPI_GEGLU_PAIR) {
                 float4 *o = (float4 *)(p.out + (size_t)t * p.out_stride + (nb >> 1));
 #pragma unroll
-                for (int j = 0; j < 4; j++) {
+                for (int j = 0; j < CW / 8; j++) {
                     float r[4];
 #pragma unroll
                     for (int i = 0; i < 4; i++) {
@@ -301,7 +333,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 float4 *o = (float4 *)(p.out + (size_t)t * p.out_stride + nb);
                 const float4 *u = (const float4 *)(p.ple_u + (size_t)t * p.u_stride + nb);
 #pragma unroll
-                for (int j = 0; j < 8; j++) {
+                for (int j = 0; j < CW / 4; j++) {
                     const float4 u4 = u[j];
                     const float2 a = upk(acc[2 * j]), b2 = upk(acc[2 * j + 1]);
                     o[j] = make_float4(geglu_one(a.x, u4.x, gelu_s, kGeluSize, -8.0f, 8.0f, 4095.0f / 16.0f),
@@ -331,7 +363,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     if (warp == 1) {
         tc_fence_after();
-        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(C::kTmemCols) : "memory");
     }
 }
 
@@ -354,38 +386,65 @@ EncodeTiledFn encode_fn() {
     return fn;
 }
 
-// int8 [rows][K] row-major, 128x128-byte boxes, 128-byte swizzle.
-bool make_map(CUtensorMap *m, const void *base, int K, int rows) {
+// int8 [rows][K] row-major, boxes of box_rows x 128 bytes, 128-byte swizzle.
+bool make_map(CUtensorMap *m, const void *base, int K, int rows, int box_rows) {
     EncodeTiledFn fn = encode_fn();
     if (!fn || ((uintptr_t)base & 15) || K % 128) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)K};
-    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, (void *)base, dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// Output-tile width for an N-column GEMM over mt token tiles: the widest whose
+// waves of tiles over the SMs cost least, counting each tile as its width plus
+// a fixed per-tile overhead of about 64 columns.
+int pick_bn(int N, int mt, int sms) {
+    int best = 128;
+    long best_cost = -1;
+    for (int bn = 128; bn >= 32; bn >>= 1) {
+        if (N % bn) continue;
+        const long tiles = (long)(N / bn) * mt, waves = (tiles + sms - 1) / sms;
+        const long cost = waves * (bn + 64);
+        if (best_cost < 0 || cost < best_cost) { best = bn; best_cost = cost; }
+    }
+    return best;
+}
+
+template <int BN>
+cudaError_t launch_bn(const CUtensorMap &ma, const CUtensorMap &mb, const TcArgs &p, int sms, cudaStream_t st) {
+    static bool configured = false;
+    if (!configured) {
+        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             TcCfg<BN>::kSmemBytes);
+        if (e != cudaSuccess) return e;
+        configured = true;
+    }
+    const int tiles = (p.N / BN) * ((p.T + kBM - 1) / kBM);
+    k_gemm_tc<BN><<<tiles < sms ? tiles : sms, kThreads, TcCfg<BN>::kSmemBytes, st>>>(ma, mb, p);
+    return cudaGetLastError();
+}
+
 }  // namespace
 
 bool g4_gemm_tc_supported(const GemmArgs &a) {
-    return a.m.sT != nullptr && a.xsT != nullptr && a.T <= G4_XST_STRIDE && a.m.K % kBK == 0 && a.m.N % kBN == 0 && a.T >= 1 && encode_fn() != nullptr &&
-           (a.epi == EPI_STORE || a.epi == EPI_GEGLU_PAIR || a.epi == EPI_PLE) && a.dots_out == nullptr;
+    return a.m.sT != nullptr && a.xsT != nullptr && a.T <= G4_XST_STRIDE && a.m.K % kBK == 0 && a.m.N % 32 == 0 &&
+           a.T >= 1 && encode_fn() != nullptr && (a.epi == EPI_STORE || a.epi == EPI_GEGLU_PAIR || a.epi == EPI_PLE) &&
+           a.dots_out == nullptr;
 }
 
 cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
     (void)pdl;
     if (!g4_gemm_tc_supported(a)) return cudaErrorNotSupported;
+    static int sms = 0;
+    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int bn = pick_bn(a.m.N, (a.T + kBM - 1) / kBM, sms);
     CUtensorMap ma, mb;
     // activation rows beyond T are read but their outputs are not stored
-    if (!make_map(&ma, a.xq, a.m.K, a.T) || !make_map(&mb, a.m.w, a.m.K, a.m.N)) return cudaErrorInvalidValue;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
-        if (e != cudaSuccess) return e;
-        configured = true;
-    }
+    if (!make_map(&ma, a.xq, a.m.K, a.T, kBM) || !make_map(&mb, a.m.w, a.m.K, a.m.N, bn)) return cudaErrorInvalidValue;
     TcArgs p{};
     p.T = a.T;
     p.N = a.m.N;
@@ -399,9 +458,7 @@ cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
     p.u_stride = a.u_stride;
     p.gelu = a.gelu;
     p.err = a.err;
-    static int sms = 0;
-    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    const int tiles = (a.m.N / kBN) * ((a.T + kBM - 1) / kBM);
-    k_gemm_tc<<<tiles < sms ? tiles : sms, kThreads, kSmemBytes, st>>>(ma, mb, p);
-    return cudaGetLastError();
+    if (bn == 128) return launch_bn<128>(ma, mb, p, sms, st);
+    if (bn == 64) return launch_bn<64>(ma, mb, p, sms, st);
+    return launch_bn<32>(ma, mb, p, sms, st);
 }

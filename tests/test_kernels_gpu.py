@@ -87,7 +87,8 @@ def test_gemm_simt_bitexact(g4, oracle, T, N, K):
 
 
 @pytest.mark.parametrize("T", [1, 5, 130, 512])
-@pytest.mark.parametrize("N,K", [(2560, 1536), (1536, 4096), (1536, 256), (12288, 1536), (1536, 12288)])
+@pytest.mark.parametrize("N,K", [(2560, 1536), (1536, 4096), (1536, 256), (12288, 1536), (1536, 12288),
+                                 (256, 1536), (2048, 1536)])
 def test_gemm_tcgen05_bitexact(g4, oracle, T, N, K):
     """tcgen05 kind::i8 GEMM: exact int32 group dots on the tensor core, the
     reference's ordered fp32 chain in the epilogue -> bit-identical output."""

@@ -160,10 +160,14 @@ struct TcArgs {
 };
 
 template <int BN>
+// 18 warps, one CTA per SM: at most 96 registers a thread (five warps share one
+// scheduler's quarter of the register file)
 __global__ void __launch_bounds__(kThreads, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, const TcArgs p) {
     using C = TcCfg<BN>;
-    constexpr int kTmemBufs = C::kTmemBufs, CW = C::CW;
+    // TMEM holds kPairs pairs of group accumulators: a K step's two groups
+    // are committed, waited for and released together
+    constexpr int kTmemBufs = C::kTmemBufs, kPairs = kTmemBufs / 2, CW = C::CW;
     extern __shared__ uint8_t smem_raw[];
     // 1024-byte alignment for the swizzled tiles
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
@@ -173,7 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *tempty = tfull + kTmemBufs;
     uint32_t *tmem_slot = (uint32_t *)(tempty + kTmemBufs);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int steps = p.K / kBK, G = p.K >> 6;
+    const int steps = p.K / kBK;
     const int mt = (p.T + kBM - 1) / kBM, tiles = (p.N / BN) * mt;
     // persistent: this CTA takes tiles blockIdx.x, + gridDim.x, ...; the m tiles of
     // one n tile are consecutive, so CTAs sharing weights run together (L2 reuse)
@@ -184,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1 + kEpiWarps);   // the MMA commit and every epilogue warp
         }
-        for (int b = 0; b < kTmemBufs; b++) {
+        for (int b = 0; b < kPairs; b++) {
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], kEpiWarps);
         }
@@ -238,36 +242,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            int k = 0, gidx = 0;
+            int k = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                for (int ks = 0; ks < steps && ok; ks++, k++) {
-                    const int s = k % kStages;
-                    if (!mbar_wait(&full[s], (k / kStages) & 1, p.err, G4D_TIMEOUT_FULL | ((k & 0xfff) << 8))) {
+                for (int ks = 0; ks < steps; ks++, k++) {
+                    const int s = k % kStages, pb = k % kPairs, use = k / kPairs;
+                    if (!mbar_wait(&full[s], (k / kStages) & 1, p.err, G4D_TIMEOUT_FULL | ((k & 0xfff) << 8)) ||
+                        (use > 0 &&
+                         !mbar_wait(&tempty[pb], (use - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | (0xffe << 8)))) {
                         ok = false;
                         break;
                     }
                     tc_fence_after();
-                    for (int gi = 0; gi < 2; gi++, gidx++) {
-                        const int b = gidx % kTmemBufs, use = gidx / kTmemBufs;
-                        if (use > 0 &&
-                            !mbar_wait(&tempty[b], (use - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | (0xffe << 8))) {
-                            ok = false;
-                            break;
-                        }
-                        tc_fence_after();
-                        const uint8_t *ta = smem + C::kOffA + s * kTileBytesA, *tb = smem + C::kOffB + s * C::kTileBytesB;
+                    const uint8_t *ta = smem + C::kOffA + s * kTileBytesA, *tb = smem + C::kOffB + s * C::kTileBytesB;
+                    for (int gi = 0; gi < 2; gi++)
                         for (int kk = 0; kk < 2; kk++) {
                             const int kb = gi * 64 + kk * 32;
-                            mma_i8(tmem + b * BN, umma_desc(ta, kb), umma_desc(tb, kb), C::kIdesc, kk != 0);
+                            mma_i8(tmem + (pb * 2 + gi) * BN, umma_desc(ta, kb), umma_desc(tb, kb), C::kIdesc, kk != 0);
                         }
-                        mma_commit(&tfull[b]);
-                    }
-                    if (ok) mma_commit(&empty[s]);
+                    mma_commit(&tfull[pb]);
+                    mma_commit(&empty[s]);
                 }
             }
             if (!ok) fail = 1;
-            committed = gidx;
+            committed = k;
         }
     } else {
         // ---------------- epilogue ----------------
@@ -275,7 +273,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int e = warp - 2, q = warp & 3, cb = e >> 2;
         const int row = q * 32 + lane;
         const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * CW);
-        int gidx = 0;   // groups consumed so far (all tiles)
+        int kidx = 0;   // K steps consumed so far (all tiles)
         bool ok = true;
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
             const int n0 = (tile / mt) * BN, t = (tile % mt) * kBM + row;
@@ -283,30 +281,32 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int j = 0; j < CW / 2; j++) acc[j] = 0ull;
             int d[CW];
-            for (int g = 0; g < G; g++, gidx++) {
-                const int b = gidx % kTmemBufs, k = gidx >> 1, s = k % kStages;
-                // wait until group g's dots are in TMEM (and, once per step, its scales in smem)
-                bool got = mbar_wait(&tfull[b], (gidx / kTmemBufs) & 1, p.err, G4D_TIMEOUT_FULL | (0xffd << 8));
-                if ((gidx & 1) == 0)
-                    got = got && mbar_wait(&full[s], (k / kStages) & 1, p.err, G4D_TIMEOUT_FULL | (0xffc << 8));
+            for (int ks = 0; ks < steps; ks++, kidx++) {
+                const int pb = kidx % kPairs, s = kidx % kStages;
+                // wait until the step's two groups of dots are in TMEM and its scales in smem
+                const bool got =
+                    mbar_wait(&tfull[pb], (kidx / kPairs) & 1, p.err, G4D_TIMEOUT_FULL | (0xffd << 8)) &&
+                    mbar_wait(&full[s], (kidx / kStages) & 1, p.err, G4D_TIMEOUT_FULL | (0xffc << 8));
                 if (!__all_sync(0xffffffffu, got)) {
                     if (lane == 0) fail = 1;
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                tmem_ld<CW>(tbase + (uint32_t)(b * BN), d);
-                tmem_wait_ld();
-                tc_fence_before();
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&tempty[b]);
                 const float *sc = (const float *)(smem + C::kOffS + s * C::kScaleBytes);
-                const float xv = sc[2 * BN + (gidx & 1) * kBM + row];
-                chain<CW>(acc, d, sc + (gidx & 1) * BN + cb * CW, xv);
-                if (gidx & 1) {   // both groups of step k done: release its stage (scales)
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll 1
+                for (int gi = 0; gi < 2; gi++) {
+                    tmem_ld<CW>(tbase + (uint32_t)((pb * 2 + gi) * BN), d);
+                    tmem_wait_ld();
+                    if (gi == 1) {   // both groups read: the pair of accumulators is free
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[pb]);
+                    }
+                    chain<CW>(acc, d, sc + gi * BN + cb * CW, sc[2 * BN + gi * kBM + row]);
                 }
+                __syncwarp();   // the step's scales are consumed: release its stage
+                if (lane == 0) mbar_arrive(&empty[s]);
             }
             if (!ok || t >= p.T) continue;
             const int nb = n0 + cb * CW;
@@ -355,8 +355,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int k = issued > kStages ? issued - kStages : 0; k < issued; k++)
             while (!mbar_try_wait(&full[k % kStages], (k / kStages) & 1) && g4_globaltimer() - t0n < G4_WAIT_NS) {
             }
-        for (int g = committed > kTmemBufs ? committed - kTmemBufs : 0; g < committed; g++)
-            while (!mbar_try_wait(&tfull[g % kTmemBufs], (g / kTmemBufs) & 1) &&
+        for (int g = committed > kPairs ? committed - kPairs : 0; g < committed; g++)
+            while (!mbar_try_wait(&tfull[g % kPairs], (g / kPairs) & 1) &&
                    g4_globaltimer() - t0n < G4_WAIT_NS) {
             }
     }

@@ -67,6 +67,8 @@ struct g4_ctx {
     float *pli = nullptr, *ple_emb = nullptr, *ple_u = nullptr, *logits = nullptr, *part = nullptr;
     float *pre_part = nullptr;       // prefill attention partial slots
     float *argmax_part = nullptr, *topk_v = nullptr;
+    unsigned long long *rng_d = nullptr;   // sampling xorshift state (gemma4.c:527: starts at 42)
+    int *sample_tok = nullptr;
     int *argmax_out = nullptr, *topk_i = nullptr;
     unsigned *ticket = nullptr;
     int *err = nullptr, *tokens_d = nullptr, *pos_d = nullptr;
@@ -404,6 +406,8 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
         {(void **)&c->part, (size_t)kSplits * G4_HEADS * (G4_HD_GLOBAL + 4) * 4},
         {(void **)&c->pre_part, (size_t)2 * c->num_sms * G4_PRE_PART_SLOT * 4},
         {(void **)&c->argmax_part, (size_t)1024 * 4 * 2 * 4},
+        {(void **)&c->rng_d, 8},
+        {(void **)&c->sample_tok, 4},
         {(void **)&c->topk_v, (size_t)1024 * 64 * 4},
         {(void **)&c->topk_i, (size_t)1024 * 64 * 4},
         {(void **)&c->argmax_out, 64},
@@ -421,6 +425,10 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
     for (auto &b : bufs) {
         *b.p = c->state + off;
         off += (b.bytes + 255) & ~(size_t)255;
+    }
+    {
+        const unsigned long long seed = 42;
+        CK(cudaMemcpy(c->rng_d, &seed, 8, cudaMemcpyHostToDevice));
     }
     // KV rings: 12 sliding (owners 0-3, 5-8, 10-13) + 3 global (owners 4, 9, 14)
     const size_t sl = (size_t)2 * G4_SLIDING_RING * G4_HD_SLIDING * 4, gl = (size_t)2 * G4_MAX_CONTEXT * G4_HD_GLOBAL * 4;
@@ -1147,6 +1155,30 @@ int g4_topk(g4_ctx *c, size_t row, int k, float *values, int *ids) {
                       c->st));
     CK(cudaMemcpyAsync(values, c->topk_v + 1024 * 32, (size_t)k * 4, cudaMemcpyDeviceToHost, c->st));
     CK(cudaMemcpyAsync(ids, c->topk_i + 1024 * 32, (size_t)k * 4, cudaMemcpyDeviceToHost, c->st));
+    return check_device_error(c);
+}
+
+int g4_set_seed(g4_ctx *c, uint64_t seed) {
+    if (!c) return G4_ERR_INVALID;
+    cudaSetDevice(c->device);
+    int rc = flush_pending(c);
+    if (rc) return rc;
+    const unsigned long long v = seed;
+    CK(cudaMemcpyAsync(c->rng_d, &v, 8, cudaMemcpyHostToDevice, c->st));
+    CK(cudaStreamSynchronize(c->st));
+    return G4_OK;
+}
+
+int g4_sample(g4_ctx *c, size_t row, float temperature, int *token) {
+    if (!c || !token) return G4_ERR_INVALID;
+    if (!(temperature > 0.0f)) return g4_logits(c, row, nullptr, token);   // greedy: the first maximum
+    int rc = g4_logits(c, row, nullptr, nullptr);
+    if (rc) return rc;
+    CK(g4_launch_topk(c->logits, G4_VOCAB, 64, c->topk_v, c->topk_i, c->topk_v + 1024 * 32, c->topk_i + 1024 * 32,
+                      c->st));
+    CK(g4_launch_sample64(c->topk_v + 1024 * 32, c->topk_i + 1024 * 32, temperature, c->rng_d, c->sample_tok,
+                          c->st));
+    CK(cudaMemcpyAsync(token, c->sample_tok, 4, cudaMemcpyDeviceToHost, c->st));
     return check_device_error(c);
 }
 

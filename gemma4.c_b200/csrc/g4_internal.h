@@ -203,6 +203,9 @@ cudaError_t g4_launch_attn_decode(const AttnArgs &a, int splits, cudaStream_t st
 // post-processed by g4_launch_qkv_post): split-KV partials then combine into a.out
 cudaError_t g4_launch_attn_rows(const AttnArgs &a, int splits, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_combine(const AttnArgs &a, int splits, cudaStream_t st, bool pdl);
+// top-64 temperature sampling (gemma4.c:536-561) from a top-64 list; state: xorshift state
+cudaError_t g4_launch_sample64(const float *vals, const int *ids, float temperature, unsigned long long *state,
+                               int *token, cudaStream_t st);
 cudaError_t g4_launch_qkv_post(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_prefill(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_strict(const AttnArgs &a, cudaStream_t st, bool pdl);

@@ -150,6 +150,53 @@ cudaError_t g4_launch_topk(const float *x, int n, int k, float *part_v, int *par
     return cudaGetLastError();
 }
 
+// Temperature sampling over the top 64 (gemma4.c:527-561), one warp: the
+// candidates are the top-64 list (value descending, id ascending on ties, as
+// the reference's insertion keeps them); expf terms in parallel with the host
+// library's expf, then the reference's sequential sum, 95 % prefix, xorshift
+// draw and walk in one lane. temperature <= 0: the first maximum (argmax).
+__global__ void k_sample64(const float *vals, const int *ids, float temperature, unsigned long long *state,
+                           int *token) {
+    __shared__ float e[64];
+    const int lane = threadIdx.x;
+    if (!(temperature > 0.0f)) {
+        if (lane == 0) *token = ids[0];
+        return;
+    }
+    const float mx = __fdiv_rn(vals[0], temperature);
+    for (int i = lane; i < 64; i += 32) e[i] = expf_host(__fsub_rn(__fdiv_rn(vals[i], temperature), mx));
+    __syncwarp();
+    if (lane != 0) return;
+    float sum = 0.0f;
+    for (int i = 0; i < 64; i++) sum = __fadd_rn(sum, e[i]);
+    const float lim = __fmul_rn(0.95f, sum);
+    float mass = 0.0f;
+    int count = 0;
+    while (count < 64 && mass < lim) mass = __fadd_rn(mass, e[count++]);
+    unsigned long long x = *state;   // random_uniform (gemma4.c:529-534)
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    *state = x;
+    const float u = __fdiv_rn((float)((x * 0x2545F4914F6CDD1DULL) >> 40), 16777216.0f);
+    float th = __fmul_rn(u, mass);
+    int tok = ids[count > 0 ? count - 1 : 0];
+    for (int i = 0; i < count; i++) {
+        th = __fsub_rn(th, e[i]);
+        if (th <= 0.0f) {
+            tok = ids[i];
+            break;
+        }
+    }
+    *token = tok;
+}
+
+cudaError_t g4_launch_sample64(const float *vals, const int *ids, float temperature, unsigned long long *state,
+                               int *token, cudaStream_t st) {
+    k_sample64<<<1, 32, 0, st>>>(vals, ids, temperature, state, token);
+    return cudaGetLastError();
+}
+
 extern "C" {
 
 int g4_topk_noalloc(const float *logits, int n, int k, float *values, int *ids, void *stream) {
@@ -393,6 +440,28 @@ int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, 
         TK(cudaGetLastError());
         *ms_per_call = ms / iters;
     }
+    return G4_OK;
+}
+
+// sample() (gemma4.c:536-561) on one logits row: top-64 + temperature draw on
+// the device; *state is the xorshift state before the call and receives it after.
+int g4k_sample(const float *logits, int n, float temperature, unsigned long long *state, int *token) {
+    if (!logits || !state || !token || n < 64 || n > 64 * 4096) return G4_ERR_INVALID;
+    DevBuf dl, pv, pi, tv, ti, dst, dtok;
+    TK(dl.alloc((size_t)n * 4));
+    TK(pv.alloc(4096 * 4));
+    TK(pi.alloc(4096 * 4));
+    TK(tv.alloc(64 * 4));
+    TK(ti.alloc(64 * 4));
+    TK(dst.alloc(8));
+    TK(dtok.alloc(4));
+    TK(cudaMemcpy(dl.p, logits, (size_t)n * 4, cudaMemcpyHostToDevice));
+    TK(cudaMemcpy(dst.p, state, 8, cudaMemcpyHostToDevice));
+    TK(g4_launch_topk((const float *)dl.p, n, 64, (float *)pv.p, (int *)pi.p, (float *)tv.p, (int *)ti.p, 0));
+    TK(g4_launch_sample64((const float *)tv.p, (const int *)ti.p, temperature, (unsigned long long *)dst.p,
+                          (int *)dtok.p, 0));
+    TK(cudaMemcpy(token, dtok.p, 4, cudaMemcpyDeviceToHost));
+    TK(cudaMemcpy(state, dst.p, 8, cudaMemcpyDeviceToHost));
     return G4_OK;
 }
 

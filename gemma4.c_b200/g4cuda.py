@@ -82,6 +82,9 @@ def load(path=LIB_PATH):
                                 C.POINTER(C.c_double)]
     L.g4k_attention.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, vp, vp, _f32p,
                                 _f32p, _f32p, _f32p, _f32p, C.c_int, C.POINTER(C.c_float)]
+    L.g4k_sample.argtypes = [_f32p, C.c_int, C.c_float, C.POINTER(C.c_ulonglong), C.POINTER(C.c_int)]
+    L.g4_sample.argtypes = [vp, C.c_size_t, C.c_float, C.POINTER(C.c_int)]
+    L.g4_set_seed.argtypes = [vp, C.c_uint64]
     L.g4_profiler_range.argtypes = [C.c_int]
     L.g4_mark.argtypes = [vp, C.c_int]
     L.g4_elapsed.argtypes = [vp, C.c_int, C.c_int, C.POINTER(C.c_float)]
@@ -161,6 +164,15 @@ class Model:
         am = C.c_int(-1)
         _check(self.L.g4_logits(self.h, row, out.ctypes.data if out is not None else None, C.byref(am)), self.h)
         return out, am.value
+
+    def sample(self, row, temperature):
+        """Next token drawn on the device (g4_sample) from logits row `row`."""
+        tok = C.c_int(0)
+        _check(self.L.g4_sample(self.h, row, temperature, C.byref(tok)), self.h)
+        return tok.value
+
+    def set_seed(self, seed):
+        _check(self.L.g4_set_seed(self.h, seed), self.h)
 
     def topk(self, row, k):
         v = np.empty(k, np.float32)
@@ -328,6 +340,15 @@ def attention(qkv, hd, kring, vring, start_pos, cos_t, sin_t, mode=ATTN_PREFILL,
                            np.ascontiguousarray(cos_t, np.float32), np.ascontiguousarray(sin_t, np.float32),
                            kring, vring, out, iters, C.byref(ms)))
     return out, (ms.value if iters else None)
+
+
+def sample(logits, temperature, state):
+    """Device sample() (g4k_sample) of one logits row; returns (token, state after)."""
+    L = load()
+    st, tok = C.c_ulonglong(state), C.c_int(0)
+    _check(L.g4k_sample(np.ascontiguousarray(logits, np.float32), logits.size, temperature, C.byref(st),
+                        C.byref(tok)))
+    return tok.value, st.value
 
 
 def rmsnorm_quant(x, w, eps=1e-6):

@@ -69,6 +69,15 @@ int g4_logits(g4_ctx *ctx, size_t row, float *out, int *argmax);
  * the candidate list of gemma4.c:544-551. Synchronises. */
 int g4_topk(g4_ctx *ctx, size_t row, int k, float *values, int *ids);
 
+/* sample (gemma4.c:536-561) on the device: temperature > 0 draws from the
+ * smallest prefix of the top 64 holding 95 % of their probability mass with the
+ * reference's xorshift generator (random_uniform, gemma4.c:527-534), whose state
+ * lives in the context (42 after g4_open, like the reference); temperature <= 0
+ * is the greedy argmax. Only the token (4 bytes) is read back. */
+int g4_sample(g4_ctx *ctx, size_t row, float temperature, int *token);
+/* Set the sampling generator's state (the reference's rng_state). */
+int g4_set_seed(g4_ctx *ctx, uint64_t seed);
+
 /* Top-k (k <= 64) of n <= 262144 floats already in device memory, written to
  * caller-provided device buffers `values`/`ids` on `stream` (a cudaStream_t;
  * NULL = the default stream): the same selection as g4_topk (descending,
@@ -215,6 +224,9 @@ int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch
 int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, const float *qkv,
                   const float *q_norm, const float *k_norm, const float *rope_cos, const float *rope_sin,
                   float *kring, float *vring, float *out, int iters, float *ms_per_call);
+/* sample (gemma4.c:536-561) of one logits row[n] on the device (top-64 and the
+ * draw); *state: the xorshift state before the call, the state after it on return */
+int g4k_sample(const float *logits, int n, float temperature, unsigned long long *state, int *token);
 /* rmsnorm (gemma4.c:360-373) of hidden-width rows followed by quantize */
 int g4k_rmsnorm_quant(const float *x, int rows, const float *w, float eps, float *y, int8_t *q, float *s);
 

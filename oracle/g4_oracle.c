@@ -278,6 +278,40 @@ void or_topk(const float *x, int n, int k, float *vals, int *ids) {
     }
 }
 
+/* gemma4.c:529-534 random_uniform: xorshift64 step, top 24 bits of the
+ * multiplied state over 2^24. */
+float or_random_uniform(unsigned long long *state) {
+    unsigned long long x = *state;
+    x ^= x >> 12;
+    x ^= x << 25;
+    x ^= x >> 27;
+    *state = x;
+    return (float)((x * 0x2545F4914F6CDD1DULL) >> 40) / 16777216.0f;
+}
+
+/* gemma4.c:536-561 sample: greedy argmax at temperature <= 0; otherwise the
+ * top-64 list (or_topk order), exp(score / T - top / T) with a running sum, the
+ * smallest prefix holding 95 % of the sum, one uniform draw scaled by that
+ * prefix mass and a walk down the prefix. */
+int or_sample(const float *logits, int n, float temperature, unsigned long long *state) {
+    if (temperature <= 0.0f) return or_argmax(logits, n);
+    float vals[64];
+    int ids[64];
+    or_topk(logits, n, 64, vals, ids);
+    float sum = 0.0f, mx = vals[0] / temperature;
+    for (int i = 0; i < 64; i++) {
+        vals[i] = expf(vals[i] / temperature - mx);
+        sum += vals[i];
+    }
+    float mass = 0.0f;
+    int count = 0;
+    while (mass < 0.95f * sum) mass += vals[count++];
+    float th = or_random_uniform(state) * mass;
+    for (int i = 0; i < count; i++)
+        if ((th -= vals[i]) <= 0.0f) return ids[i];
+    return ids[count - 1];
+}
+
 /* ------------------------------------------------------------------------ */
 /* Whole model                                                               */
 

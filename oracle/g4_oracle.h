@@ -58,4 +58,7 @@ int or_num_threads(void);
 #ifdef __cplusplus
 }
 #endif
+float or_random_uniform(unsigned long long *state);
+int or_sample(const float *logits, int n, float temperature, unsigned long long *state);
+
 #endif

@@ -64,6 +64,8 @@ class Oracle:
         L.or_argmax.argtypes = [_f32p, C.c_int]
         L.or_argmax.restype = C.c_int
         L.or_topk.argtypes = [_f32p, C.c_int, C.c_int, _f32p, _i32p]
+        L.or_sample.argtypes = [_f32p, C.c_int, C.c_float, C.POINTER(C.c_ulonglong)]
+        L.or_sample.restype = C.c_int
         L.or_attend.argtypes = [_f32p, _f32p, C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
         L.or_model_open.argtypes = [C.c_void_p, C.c_uint64]
         L.or_model_open.restype = C.c_void_p
@@ -115,6 +117,12 @@ class Oracle:
         self.lib.or_rope(v, np.ascontiguousarray(cos_t), np.ascontiguousarray(sin_t), cos_t.shape[1],
                          heads, head_dim, start_pos, T)
         return v
+
+    def sample(self, logits, temperature, state):
+        """gemma4.c:536-561 on one row; returns (token, state after the draw)."""
+        st = C.c_ulonglong(state)
+        tok = self.lib.or_sample(np.ascontiguousarray(logits, np.float32), logits.size, temperature, C.byref(st))
+        return tok, st.value
 
     def attention(self, qkv, hd, kring, vring, start_pos, cos_t, sin_t, q_norm=None, k_norm=None):
         """One attention sub-layer as attention_layer restates gemma4.c:411-461,
@@ -244,9 +252,19 @@ class Reference:
         L.g4ref_rope.argtypes = [_f32p, _f32p, C.c_int, _f32p, C.c_int, C.c_int, C.c_int, C.c_size_t]
         L.g4ref_embedding.argtypes = [_f32p, C.c_void_p, C.c_void_p, C.c_int, _i32p, C.c_size_t, C.c_float]
         L.softmax.argtypes = [_f32p, C.c_int]
+        L.sample.argtypes = [_f32p, C.c_int, C.c_float]
+        L.sample.restype = C.c_int
 
     def threads(self):
         return self.lib.g4ref_threads()
+
+    def sample(self, logits, temperature, state):
+        """The reference's own sample() with its global rng_state set to `state`;
+        returns (token, rng_state after the call)."""
+        rs = C.c_ulonglong.in_dll(self.lib, "rng_state")
+        rs.value = state
+        tok = self.lib.sample(np.array(logits, np.float32, copy=True), logits.size, temperature)
+        return tok, rs.value
 
     def quantize(self, x):
         x = np.ascontiguousarray(x, np.float32)
@@ -277,41 +295,6 @@ class Reference:
         self.lib.g4ref_rope(np.ascontiguousarray(cos_t), np.ascontiguousarray(sin_t), cos_t.shape[1], v,
                             heads, head_dim, start_pos, v.shape[0])
         return v
-
-    def attention(self, qkv, hd, kring, vring, start_pos, cos_t, sin_t, q_norm=None, k_norm=None):
-        """One attention sub-layer as attention_layer restates gemma4.c:411-461,
-        from raw per-token q (8 heads) | k | v rows: q/k RMSNorm (k, q with
-        weights), v RMSNorm without weight, RoPE, ring write at (start_pos + t)
-        & (ring - 1), then or_attend per (token, head). hd 256 is a sliding
-        layer (window 512), hd 512 a global one. kring / vring are updated in
-        place; returns out[T][8*hd]."""
-        qkv = np.ascontiguousarray(qkv, np.float32)
-        T = qkv.shape[0]
-        ring = kring.shape[0]
-        mask, window = ring - 1, (512 if hd == 256 else 0)
-        q = qkv[:, :8 * hd].reshape(T * 8, hd)
-        k = qkv[:, 8 * hd:9 * hd]
-        v = qkv[:, 9 * hd:10 * hd]
-        q = self.rope(self.rmsnorm(q, q_norm if q_norm is not None else np.ones(hd, np.float32)).reshape(T, 8 * hd),
-                      cos_t, sin_t, 8, hd, start_pos)
-        k = self.rope(self.rmsnorm(k, k_norm if k_norm is not None else np.ones(hd, np.float32)),
-                      cos_t, sin_t, 1, hd, start_pos)
-        v = self.rmsnorm(v, None)
-        for t in range(T):
-            kring[(start_pos + t) & mask] = k[t]
-            vring[(start_pos + t) & mask] = v[t]
-        out = np.empty((T, 8 * hd), np.float32)
-        scores = np.empty(start_pos + T, np.float32)
-        kp, vp = _ptr(kring), _ptr(vring)
-        row = np.empty(hd, np.float32)
-        for t in range(T):
-            p = start_pos + t
-            first = p + 1 - window if window and p + 1 > window else 0
-            for h in range(8):
-                qh = np.ascontiguousarray(q[t, h * hd:(h + 1) * hd])
-                self.lib.or_attend(row, qh, kp, vp, first, p + 1 - first, mask, hd, scores)
-                out[t, h * hd:(h + 1) * hd] = row
-        return out
 
     def geglu(self, gate, up, width, up_stride, table):
         gate = np.array(gate, np.float32, copy=True, order="C")

@@ -7,6 +7,9 @@ outputs as small .npz fixtures:
   kernels.npz — quantize, matmul_int8 (two shapes), rmsnorm (with and without
                 weight), apply_rope (sliding and partial global), geglu
                 (including the table edges), embedding, softmax;
+  sample.npz  — sample() (top-64, temperature, 95 % prefix, xorshift draw) on
+                48 seeded logits rows of 1024 values at several temperatures,
+                with the generator state chained from 42 through the rows;
   model.npz   — whole-model forward/logits on the seed-0 synthetic E2B image
                 (per-group scales, random norms): a 6-token prefill and one
                 decode step; stores the top-32 of the logits, float64 checksums
@@ -124,8 +127,27 @@ def model(ref):
     return out
 
 
+def samples(ref):
+    rng = np.random.default_rng(11)
+    rows, temps, toks, states = [], [], [], []
+    state = 42
+    for i in range(48):
+        lg = (rng.standard_normal(1024) * rng.uniform(0.5, 6.0)).astype(np.float32)
+        if i % 6 == 0:                      # ties at the top
+            lg[rng.integers(0, 1024, 20)] = lg.max()
+        t = (0.0, 0.25, 0.7, 1.0, 1.6, 3.0)[i % 6]
+        tok, state = ref.sample(lg, t, state)
+        rows.append(lg)
+        temps.append(t)
+        toks.append(tok)
+        states.append(state)
+    return {"logits": np.stack(rows), "temperature": np.array(temps, np.float32),
+            "token": np.array(toks, np.int32), "state": np.array(states, np.uint64)}
+
+
 def main():
     ref = Reference()
+    np.savez_compressed(os.path.join(HERE, "sample.npz"), **samples(ref))
     np.savez_compressed(os.path.join(HERE, "kernels.npz"), **kernels(ref))
     np.savez_compressed(os.path.join(HERE, "model.npz"), **model(ref))
     print("wrote", os.listdir(HERE))

@@ -87,3 +87,12 @@ def test_whole_model(oracle, image):
         assert (lg.astype(np.float64) ** 2).sum() == g["decode_sum"][1]
     finally:
         m.close()
+
+
+def test_sample(oracle):
+    """sample() (gemma4.c:536-561) with the generator state chained through the rows."""
+    g = np.load(os.path.join(GOLD, "sample.npz"))
+    state = 42
+    for lg, t, tok, st in zip(g["logits"], g["temperature"], g["token"], g["state"]):
+        got, state = oracle.sample(lg, float(t), state)
+        assert got == int(tok) and state == int(st)

@@ -227,6 +227,22 @@ struct Pre {
     }
 };
 
+// Quantise (gemma4.c:265-279) one 64-wide group held as 4 values in each of 16
+// consecutive lanes: the group's max |x| over the 16 lanes, then scale and
+// rounded int8 values exactly as quantize(). All 32 lanes must call it.
+G4_DEV void quant_lanes16(float4 v, int8_t *q, float *xs, float *xsT, bool leader) {
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+    for (int off = 1; off < 16; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const float sc = quant_scale(m), inv = quant_inv(sc);
+    *(char4 *)q = make_char4((signed char)quant_one(v.x, inv), (signed char)quant_one(v.y, inv),
+                             (signed char)quant_one(v.z, inv), (signed char)quant_one(v.w, inv));
+    if (leader) {
+        *xs = sc;
+        if (xsT) *xsT = sc;
+    }
+}
+
 // Stage BK key rows [kt, kt + nt) of a ring into shared memory (row stride
 // dstride); rows past nt are zero.
 template <int HD>
@@ -426,16 +442,26 @@ __global__ void __launch_bounds__(256, 1) k_attn_prefill(const AttnArgs a) {
         const int t = t0 + rg;
         const bool whole = (int)u == pre[j] && seg_end == pre[j + 1];
         if (whole) {
-            if (t < T) {
-                float *dst = a.out + (size_t)t * (kHeads * HD) + 4 * dg;
+            if (t < T) {   // warp-uniform: the warp's lanes share rg
+                constexpr int K = kHeads * HD;
+                float *dst = a.out + (size_t)t * K + 4 * dg;
 #pragma unroll
                 for (int r = 0; r < 8; r++) {
                     const float inv = 1.0f / rl[8 * rg + r];
                     const uint64_t i2 = pk(inv, inv);
                     const float2 x0 = upk(mul2(o[r][0], i2)), x1 = upk(mul2(o[r][1], i2));
                     const float2 y0 = upk(mul2(o[r][2], i2)), y1 = upk(mul2(o[r][3], i2));
-                    *(float4 *)&dst[r * HD] = make_float4(x0.x, x0.y, x1.x, x1.y);
-                    *(float4 *)&dst[r * HD + HD / 2] = make_float4(y0.x, y0.y, y1.x, y1.y);
+                    const float4 va = make_float4(x0.x, x0.y, x1.x, x1.y), vb = make_float4(y0.x, y0.y, y1.x, y1.y);
+                    *(float4 *)&dst[r * HD] = va;
+                    *(float4 *)&dst[r * HD + HD / 2] = vb;
+                    if (a.quant_out) {
+                        const int ca = r * HD + 4 * dg, cb2 = ca + HD / 2;   // row columns of va, vb
+                        quant_lanes16(va, a.xq + (size_t)t * K + ca, a.xs + (size_t)t * (K / 64) + ca / 64,
+                                      a.xsT ? a.xsT + (size_t)(ca / 64) * G4_XST_STRIDE + t : nullptr, (dg & 15) == 0);
+                        quant_lanes16(vb, a.xq + (size_t)t * K + cb2, a.xs + (size_t)t * (K / 64) + cb2 / 64,
+                                      a.xsT ? a.xsT + (size_t)(cb2 / 64) * G4_XST_STRIDE + t : nullptr,
+                                      (dg & 15) == 0);
+                    }
                 }
             }
         } else {
@@ -526,6 +552,12 @@ __global__ void __launch_bounds__(256) k_attn_prefill_merge(const AttnArgs a) {
             acc.w = fmaf(v.w, w, acc.w);
         }
         *(float4 *)&a.out[(size_t)tok * (kHeads * HD) + h * HD + c4 * 4] = acc;
+        if (a.quant_out) {   // idx runs in whole warps: 16 consecutive lanes hold one 64-wide group
+            constexpr int K = kHeads * HD;
+            const int col = h * HD + c4 * 4;
+            quant_lanes16(acc, a.xq + (size_t)tok * K + col, a.xs + (size_t)tok * (K / 64) + col / 64,
+                          a.xsT ? a.xsT + (size_t)(col / 64) * G4_XST_STRIDE + tok : nullptr, (c4 & 15) == 0);
+        }
     }
 }
 

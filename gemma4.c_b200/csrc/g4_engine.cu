@@ -19,6 +19,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <utility>
 #include <vector>
 
 #include "../../include/g4cuda.h"
@@ -63,6 +64,10 @@ struct g4_ctx {
     int cur = 0;
     int8_t *xq = nullptr;
     float *xsT = nullptr;            // group-major activation scales (tensor-core GEMM)
+    // second activation set: the gate/up GEMM quantises its GEGLU rows into it
+    // while its own input (xq, xs, xsT) is still being read
+    int8_t *xq2 = nullptr;
+    float *xs2 = nullptr, *xsT2 = nullptr;
     float *xs = nullptr, *qkv = nullptr, *attn = nullptr, *h = nullptr, *gu = nullptr, *pg = nullptr;
     float *pli = nullptr, *ple_emb = nullptr, *ple_u = nullptr, *logits = nullptr, *part = nullptr;
     float *pre_part = nullptr;       // prefill attention partial slots
@@ -394,6 +399,9 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
         {(void **)&c->xq, (size_t)kMaxT * kMaxFfn},
         {(void **)&c->xs, (size_t)kMaxT * kMaxFfn / 64 * 4},
         {(void **)&c->xsT, (size_t)G4_XST_STRIDE * kMaxFfn / 64 * 4},
+        {(void **)&c->xq2, (size_t)kMaxT * kMaxFfn},
+        {(void **)&c->xs2, (size_t)kMaxT * kMaxFfn / 64 * 4},
+        {(void **)&c->xsT2, (size_t)G4_XST_STRIDE * kMaxFfn / 64 * 4},
         {(void **)&c->qkv, (size_t)kMaxT * kQkvStride * 4},
         {(void **)&c->attn, (size_t)kMaxT * G4_HEADS * G4_HD_GLOBAL * 4},
         {(void **)&c->h, (size_t)kMaxT * G4_HIDDEN * 4},
@@ -517,7 +525,10 @@ void gemv(Seq &q, GemvArgs &a, int pro, int epi) {
     q.ck(g4_launch_gemv(a, pro, epi, grid, q.c->st, q.pdl));
 }
 
-void gemm(Seq &q, const DMat &m, int T, int epi, float *out, int out_stride, const float *u, int u_stride) {
+// Returns true when the tensor-core path also quantised its GEGLU rows into
+// xq / xs / xsT (fuse_quant and EPI_GEGLU_PAIR); then `out` is not written.
+bool gemm(Seq &q, const DMat &m, int T, int epi, float *out, int out_stride, const float *u, int u_stride,
+          bool fuse_quant = false) {
     g4_ctx *c = q.c;
     GemmArgs a{};
     a.m = m;
@@ -532,10 +543,18 @@ void gemm(Seq &q, const DMat &m, int T, int epi, float *out, int out_stride, con
     a.u_stride = u_stride;
     a.gelu = c->gelu;
     a.err = c->err;
-    if (c->gemm_path == 1 || !g4_gemm_tc_supported(a) || c->gemm_path == -1)
+    if (c->gemm_path == 1 || !g4_gemm_tc_supported(a) || c->gemm_path == -1) {
         q.ck(g4_launch_gemm_simt(a, c->st, q.pdl));
-    else
-        q.ck(g4_launch_gemm_tc(a, c->st, q.pdl));
+        return false;
+    }
+    const bool fuse = fuse_quant && epi == EPI_GEGLU_PAIR && m.N % 128 == 0;
+    if (fuse) {   // into the second set: this GEMM still reads xq / xs / xsT
+        a.qout = c->xq2;
+        a.qs = c->xs2;
+        a.qsT = c->xsT2;
+    }
+    q.ck(g4_launch_gemm_tc(a, c->st, q.pdl));
+    return fuse;
 }
 
 AttnArgs attn_base(g4_ctx *c, const Layer &Y, int T, int start_pos, const int *pos_dev) {
@@ -786,16 +805,31 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp
             sp = sp < 16 ? 16 : sp > kSplits ? kSplits : sp;
             q.ck(g4_launch_attn_rows(at, sp, c->st, q.pdl));
         }
-        else
-            q.ck(c->strict ? g4_launch_attn_strict(at, c->st, q.pdl) : g4_launch_attn_prefill(at, c->st, q.pdl));
-        q.ck(g4_launch_rows_quant(c->attn, Y.qw, T, Y.qw, c->xq, c->xs, c->st, q.pdl, c->xsT));
+        else if (!c->strict) {
+            // the tiled kernel also quantises its output rows for o_proj
+            at.quant_out = 1;
+            at.xsT = c->xsT;
+            q.ck(g4_launch_attn_prefill(at, c->st, q.pdl));
+        } else
+            q.ck(g4_launch_attn_strict(at, c->st, q.pdl));
+        if (!at.quant_out) q.ck(g4_launch_rows_quant(c->attn, Y.qw, T, Y.qw, c->xq, c->xs, c->st, q.pdl, c->xsT));
         gemm(q, Y.o, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
         q.ck(g4_launch_rows_norm(1, c->h, T, Y.post_attn, c->res[cur], c->res[cur ^ 1], nullptr, Y.pre_ffn, G4_RMS_EPS,
                                  c->xq, c->xs, c->st, q.pdl, nullptr, c->strict, c->xsT));
         cur ^= 1;
-        gemm(q, Y.gu, T, EPI_GEGLU_PAIR, c->gu, Y.ffn, nullptr, 0);
-        q.ck(g4_launch_rows_quant(c->gu, Y.ffn, T, Y.ffn, c->xq, c->xs, c->st, q.pdl, c->xsT));
-        gemm(q, Y.down, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
+        if (gemm(q, Y.gu, T, EPI_GEGLU_PAIR, c->gu, Y.ffn, nullptr, 0, true)) {
+            // down_proj reads the second set the fused epilogue wrote
+            std::swap(c->xq, c->xq2);
+            std::swap(c->xs, c->xs2);
+            std::swap(c->xsT, c->xsT2);
+            gemm(q, Y.down, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
+            std::swap(c->xq, c->xq2);
+            std::swap(c->xs, c->xs2);
+            std::swap(c->xsT, c->xsT2);
+        } else {
+            q.ck(g4_launch_rows_quant(c->gu, Y.ffn, T, Y.ffn, c->xq, c->xs, c->st, q.pdl, c->xsT));
+            gemm(q, Y.down, T, EPI_STORE, c->h, G4_HIDDEN, nullptr, 0);
+        }
         q.ck(g4_launch_rows_norm(2, c->h, T, Y.post_ffn, c->res[cur], c->res[cur ^ 1], nullptr, nullptr, G4_RMS_EPS,
                                  c->xq, c->xs, c->st, q.pdl, nullptr, c->strict, c->xsT));
         cur ^= 1;

@@ -56,7 +56,11 @@ struct TcCfg {
     static constexpr int kOffBar = kOffS + kStages * kScaleBytes;
     // barriers: full[S], empty[S], tfull[B], tempty[B], then the TMEM address word
     static constexpr int kOffGelu = (kOffBar + (2 * kStages + 2 * kTmemBufs) * 8 + 16 + 127) & ~127;
-    static constexpr int kSmemBytes = kOffGelu + kGeluSize * 4 + 1024;   // + 1 KB for alignment
+    // GEGLU quantisation: per lane quadrant an mbarrier (its four warps) and
+    // per tile parity x column block x row the row's max |x| over 16 outputs
+    static constexpr int kOffQbar = kOffGelu + kGeluSize * 4;
+    static constexpr int kOffAmax = kOffQbar + 64;
+    static constexpr int kSmemBytes = kOffAmax + 2 * 4 * kBM * 4 + 1024;   // + 1 KB for alignment
     static constexpr int CW = BN / 4;                                    // columns per epilogue warp
     // Instruction descriptor: S32 accumulate, signed int8 A and B, both K-major,
     // N = BN (>> 3), M = 128 (>> 4).
@@ -157,6 +161,8 @@ struct TcArgs {
     int u_stride;
     const float *gelu;
     int *err;
+    int8_t *qout;           // GEGLU rows quantised (BN 128 only), or NULL
+    float *qs, *qsT;
 };
 
 template <int BN>
@@ -192,6 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&tfull[b], 1);
             mbar_init(&tempty[b], kEpiWarps);
         }
+        for (int qd = 0; qd < 4; qd++) mbar_init((uint64_t *)(smem + C::kOffQbar) + qd, 4);
         mbar_fence_init();
         fail = 0;
         issued = 0;
@@ -275,7 +282,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t tbase = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(cb * CW);
         int kidx = 0;   // K steps consumed so far (all tiles)
         bool ok = true;
+        int tcount = -1;   // tiles of this CTA so far (parity of the quantisation exchange)
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
+            tcount++;
             const int n0 = (tile / mt) * BN, t = (tile % mt) * kBM + row;
             uint64_t acc[CW / 2];
 #pragma unroll
@@ -308,8 +317,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncwarp();   // the step's scales are consumed: release its stage
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
-            if (!ok || t >= p.T) continue;
+            if (!ok) continue;
             const int nb = n0 + cb * CW;
+            const bool qexch = p.epi == EPI_GEGLU_PAIR && BN == 128 && p.qout;   // every lane takes part
+            if (t >= p.T && !qexch) continue;
             if (p.epi == EPI_STORE) {
                 float4 *o = (float4 *)(p.out + (size_t)t * p.out_stride + nb);
 #pragma unroll
@@ -317,6 +328,48 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float2 a = upk(acc[2 * j]), b2 = upk(acc[2 * j + 1]);
                     o[j] = make_float4(a.x, a.y, b2.x, b2.y);
                 }
+            } else if (qexch) {
+              if constexpr (BN == 128) {
+                // this tile's 64 GEGLU outputs of a row form one quantisation group,
+                // spread over the quadrant's four warps (16 each): exchange the
+                // row maxima through shared memory under the quadrant's mbarrier
+                float r[CW / 2];
+                float m = 0.0f;
+#pragma unroll
+                for (int j = 0; j < CW / 2; j++) {
+                    const float2 a = upk(acc[j]);
+                    r[j] = geglu_one(a.x, a.y, gelu_s, kGeluSize, -8.0f, 8.0f, 4095.0f / 16.0f);
+                    m = fmaxf(m, fabsf(r[j]));
+                }
+                float *amax = (float *)(smem + C::kOffAmax) + (tcount & 1) * 4 * kBM;
+                uint64_t *qbar = (uint64_t *)(smem + C::kOffQbar) + q;
+                amax[cb * kBM + row] = m;
+                __syncwarp();
+                if (lane == 0) mbar_arrive(qbar);
+                const bool got = mbar_wait(qbar, tcount & 1, p.err, G4D_TIMEOUT_FULL | (0xffb << 8));
+                if (!__all_sync(0xffffffffu, got)) {
+                    if (lane == 0) fail = 1;
+                    ok = false;
+                    continue;
+                }
+                const float gm = fmaxf(fmaxf(amax[row], amax[kBM + row]), fmaxf(amax[2 * kBM + row], amax[3 * kBM + row]));
+                const float sc = quant_scale(gm), inv = quant_inv(sc);
+                if (t < p.T) {
+                    const int K2 = p.N >> 1, g = n0 >> 7;   // 64 outputs per 128-column tile
+                    uint32_t w4[CW / 8];
+#pragma unroll
+                    for (int j = 0; j < CW / 8; j++)
+                        w4[j] = (uint32_t)(uint8_t)quant_one(r[4 * j], inv) |
+                                ((uint32_t)(uint8_t)quant_one(r[4 * j + 1], inv) << 8) |
+                                ((uint32_t)(uint8_t)quant_one(r[4 * j + 2], inv) << 16) |
+                                ((uint32_t)(uint8_t)quant_one(r[4 * j + 3], inv) << 24);
+                    *(uint4 *)(p.qout + (size_t)t * K2 + (nb >> 1)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
+                    if (cb == 0) {
+                        p.qs[(size_t)t * (K2 / 64) + g] = sc;
+                        if (p.qsT) p.qsT[(size_t)g * G4_XST_STRIDE + t] = sc;
+                    }
+                }
+              }
             } else if (p.epi == EPI_GEGLU_PAIR) {
                 float4 *o = (float4 *)(p.out + (size_t)t * p.out_stride + (nb >> 1));
 #pragma unroll
@@ -441,7 +494,8 @@ cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
     if (!g4_gemm_tc_supported(a)) return cudaErrorNotSupported;
     static int sms = 0;
     if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
-    const int bn = pick_bn(a.m.N, (a.T + kBM - 1) / kBM, sms);
+    const bool fuse_q = a.epi == EPI_GEGLU_PAIR && a.qout && a.qs && a.m.N % 128 == 0;
+    const int bn = fuse_q ? 128 : pick_bn(a.m.N, (a.T + kBM - 1) / kBM, sms);
     CUtensorMap ma, mb;
     // activation rows beyond T are read but their outputs are not stored
     if (!make_map(&ma, a.xq, a.m.K, a.T, kBM) || !make_map(&mb, a.m.w, a.m.K, a.m.N, bn)) return cudaErrorInvalidValue;
@@ -458,6 +512,11 @@ cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
     p.u_stride = a.u_stride;
     p.gelu = a.gelu;
     p.err = a.err;
+    if (fuse_q) {
+        p.qout = a.qout;
+        p.qs = a.qs;
+        p.qsT = a.qsT;
+    }
     if (bn == 128) return launch_bn<128>(ma, mb, p, sms, st);
     if (bn == 64) return launch_bn<64>(ma, mb, p, sms, st);
     return launch_bn<32>(ma, mb, p, sms, st);

@@ -106,6 +106,11 @@ struct GemmArgs {
     const float *gelu;
     int32_t *dots_out;      // optional debug
     int *err;
+    // EPI_GEGLU_PAIR on the tensor-core path: quantise the GEGLU rows for the
+    // next GEMM (quantize, gemma4.c:265-279) into qout [T][N/2], qs [T][N/128]
+    // and qsT (group-major) instead of storing them as fp32; NULL = store
+    int8_t *qout;
+    float *qs, *qsT;
 };
 
 // ---- attention ---------------------------------------------------------------
@@ -140,6 +145,10 @@ struct AttnArgs {
     // slots (2 per CTA, G4_PRE_PART_SLOT floats each)
     float *pre_part;
     int pre_ctas;
+    // fast prefill: also quantise the output rows for o_proj (gemma4.c:459)
+    // into xq [T][8*hd], xs [T][8*hd/64] and, when set, xsT (group-major)
+    int quant_out;
+    float *xsT;
 };
 
 // ---- persistent decode step (g4_decode.cu) ---------------------------------

@@ -330,13 +330,14 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
 // same launchers the model uses; optionally timed. See g4cuda.h.
 int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, const float *qkv,
                   const float *q_norm, const float *k_norm, const float *rope_cos, const float *rope_sin,
-                  float *kring, float *vring, float *out, int iters, float *ms_per_call) {
+                  float *kring, float *vring, float *out, int8_t *xq, float *xs, int iters, float *ms_per_call) {
     if ((hd != 256 && hd != 512) || ring < 1024 || (ring & (ring - 1)) || T < 1 || T > G4_BATCH ||
         start_pos < 0 || mode < 0 || mode > 3 || !qkv || !rope_cos || !rope_sin || !kring || !vring || !out ||
         iters < 0 || (iters > 0 && !ms_per_call))
         return G4_ERR_INVALID;
     if ((mode == 2 || mode == 3) && (splits < 1 || splits > 256)) return G4_ERR_INVALID;
     if (mode == 2 && T != 1) return G4_ERR_INVALID;
+    if ((xq || xs) && (mode != 0 || !xq || !xs)) return G4_ERR_INVALID;
     const int window = hd == 256 ? G4_SLIDING_WINDOW : 0;
     const int pairs = hd == 256 ? 128 : 64;
     const int npos = start_pos + T;
@@ -344,7 +345,7 @@ int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, 
     if ((window ? (T - 1 + window) : npos) > ring) return G4_ERR_INVALID;
     const int stride = 10 * hd;
     const int sms = num_sms();
-    DevBuf dqkv, dqn, dkn, dcos, dsin, dk, dv, dout, dpart, dpre, dscores, derr, drs, drp;
+    DevBuf dqkv, dqn, dkn, dcos, dsin, dk, dv, dout, dpart, dpre, dscores, derr, drs, drp, dxq, dxs;
     TK(dqkv.alloc((size_t)T * stride * 4));
     TK(dqn.alloc((size_t)hd * 4));
     TK(dkn.alloc((size_t)hd * 4));
@@ -390,6 +391,13 @@ int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, 
     a.score_stride = npos;
     a.pre_part = (float *)dpre.p;
     a.pre_ctas = sms;
+    if (xq) {   // the tiled kernel's fused quantisation of its output rows
+        TK(dxq.alloc((size_t)T * 8 * hd));
+        TK(dxs.alloc((size_t)T * 8 * hd / 64 * 4));
+        a.quant_out = 1;
+        a.xq = (int8_t *)dxq.p;
+        a.xs = (float *)dxs.p;
+    }
     if (mode == 3) {
         std::vector<int> rs(T, 0), rp(T);
         for (int t = 0; t < T; t++) rp[t] = start_pos + t;
@@ -419,6 +427,10 @@ int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, 
     TK(cudaMemcpy(&err, derr.p, 4, cudaMemcpyDeviceToHost));
     if (err) return G4_ERR_DEVICE;
     TK(cudaMemcpy(out, dout.p, (size_t)T * 8 * hd * 4, cudaMemcpyDeviceToHost));
+    if (xq) {
+        TK(cudaMemcpy(xq, dxq.p, (size_t)T * 8 * hd, cudaMemcpyDeviceToHost));
+        TK(cudaMemcpy(xs, dxs.p, (size_t)T * 8 * hd / 64 * 4, cudaMemcpyDeviceToHost));
+    }
     TK(cudaMemcpy(kring, dk.p, (size_t)ring * hd * 4, cudaMemcpyDeviceToHost));
     TK(cudaMemcpy(vring, dv.p, (size_t)ring * hd * 4, cudaMemcpyDeviceToHost));
     if (iters > 0) {

@@ -81,7 +81,7 @@ def load(path=LIB_PATH):
     L.g4_bench_gemv.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
                                 C.POINTER(C.c_double)]
     L.g4k_attention.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, vp, vp, _f32p,
-                                _f32p, _f32p, _f32p, _f32p, C.c_int, C.POINTER(C.c_float)]
+                                _f32p, _f32p, _f32p, _f32p, vp, vp, C.c_int, C.POINTER(C.c_float)]
     L.g4k_sample.argtypes = [_f32p, C.c_int, C.c_float, C.POINTER(C.c_ulonglong), C.POINTER(C.c_int)]
     L.g4_sample.argtypes = [vp, C.c_size_t, C.c_float, C.POINTER(C.c_int)]
     L.g4_set_seed.argtypes = [vp, C.c_uint64]
@@ -324,10 +324,11 @@ ATTN_PREFILL, ATTN_STRICT, ATTN_DECODE, ATTN_ROWS = 0, 1, 2, 3
 
 
 def attention(qkv, hd, kring, vring, start_pos, cos_t, sin_t, mode=ATTN_PREFILL, splits=148, q_norm=None,
-              k_norm=None, iters=0):
+              k_norm=None, iters=0, quant=False):
     """One attention sub-layer on the GPU (g4k_attention). qkv[T][10*hd] raw
     q | k | v; kring / vring [ring][hd] are updated in place with the chunk's
-    keys and values. Returns (out[T][8*hd], ms per call or None)."""
+    keys and values. Returns (out[T][8*hd], ms per call or None), and with
+    quant=True (prefill mode) also the kernel's quantised rows (xq, xs)."""
     L = load()
     qkv = np.ascontiguousarray(qkv, np.float32)
     T = qkv.shape[0]
@@ -335,10 +336,15 @@ def attention(qkv, hd, kring, vring, start_pos, cos_t, sin_t, mode=ATTN_PREFILL,
     qn = None if q_norm is None else np.ascontiguousarray(q_norm, np.float32)
     kn = None if k_norm is None else np.ascontiguousarray(k_norm, np.float32)
     ms = C.c_float(0.0)
+    xq = np.empty((T, 8 * hd), np.int8) if quant else None
+    xs = np.empty((T, 8 * hd // 64), np.float32) if quant else None
     _check(L.g4k_attention(hd, kring.shape[0], T, start_pos, mode, splits, qkv,
                            None if qn is None else qn.ctypes.data, None if kn is None else kn.ctypes.data,
                            np.ascontiguousarray(cos_t, np.float32), np.ascontiguousarray(sin_t, np.float32),
-                           kring, vring, out, iters, C.byref(ms)))
+                           kring, vring, out, None if xq is None else xq.ctypes.data,
+                           None if xs is None else xs.ctypes.data, iters, C.byref(ms)))
+    if quant:
+        return out, (ms.value if iters else None), xq, xs
     return out, (ms.value if iters else None)
 
 

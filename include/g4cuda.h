@@ -220,10 +220,12 @@ int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch
  * over `splits` CTAs + combine, T == 1); 3: batched-row decode path (one row
  * per token at start_pos + t, `splits` key splits). iters > 0: the attention
  * kernels (without post-processing) are then repeated `iters` times and the
- * average duration per call is written to ms_per_call. */
+ * average duration per call is written to ms_per_call. xq / xs (mode 0, both
+ * or neither): the output rows as the kernel quantises them for o_proj
+ * (quantize, gemma4.c:265-279): xq[T][8*hd], xs[T][8*hd/64]. */
 int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, const float *qkv,
                   const float *q_norm, const float *k_norm, const float *rope_cos, const float *rope_sin,
-                  float *kring, float *vring, float *out, int iters, float *ms_per_call);
+                  float *kring, float *vring, float *out, int8_t *xq, float *xs, int iters, float *ms_per_call);
 /* sample (gemma4.c:536-561) of one logits row[n] on the device (top-64 and the
  * draw); *state: the xorshift state before the call, the state after it on return */
 int g4k_sample(const float *logits, int n, float temperature, unsigned long long *state, int *token);

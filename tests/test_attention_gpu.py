@@ -12,7 +12,8 @@ normalised vectors already in the ring.
     are O(1); the fast paths differ only in summation order and in the device
     expf; the oracle itself is within ~2e-5 of a float64 evaluation), ring
     contents within 1e-5;
-  - the fast prefill is deterministic (same bits on a second call).
+  - the fast prefill is deterministic (same bits on a second call), and its
+    fused quantisation of the output rows equals quantize() of them.
 """
 import numpy as np
 import pytest
@@ -63,8 +64,11 @@ def test_prefill_fast_tracks_oracle(g4, oracle, hd, T, start_pos, ring):
     err = np.abs(out - eo).max()
     assert err <= OUT_ATOL, f"max abs error {err}"
     k2, v2 = k.copy(), v.copy()
-    out2, _ = g4.attention(qkv, hd, k2, v2, start_pos, cos_t, sin_t, mode=g4.ATTN_PREFILL)
+    out2, _, xq, xs = g4.attention(qkv, hd, k2, v2, start_pos, cos_t, sin_t, mode=g4.ATTN_PREFILL, quant=True)
     assert np.array_equal(out.view(np.uint32), out2.view(np.uint32))
+    # the fused quantisation for o_proj is quantize() of those rows
+    eq, es = oracle.quantize(out2)
+    assert np.array_equal(xq, eq) and np.array_equal(xs.view(np.uint32), es.view(np.uint32))
 
 
 @pytest.mark.parametrize("hd,T,start_pos,ring", [c for c in CASES if c[1] <= 37])

@@ -58,7 +58,7 @@ __global__ void __launch_bounds__(256) k_attn_rows(const AttnArgs a, int splits)
 
 template <int HD>
 __global__ void __launch_bounds__(256) k_attn_rows_combine(const AttnArgs a, int splits) {
-    __shared__ float wsm[256 + 16];
+    __shared__ float wsm[512 + 16];
     griddep_launch();
     griddep_wait();
     const int row = blockIdx.y;
@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a, int split
 
 template <int HD>
 __global__ void __launch_bounds__(256) k_attn_combine(const AttnArgs a, int splits) {
-    __shared__ float wsm[256 + 16];
+    __shared__ float wsm[512 + 16];
     griddep_launch();
     griddep_wait();
     attn_combine_part<HD>(a, a.pos_dev ? *a.pos_dev : a.start_pos, blockIdx.x, splits, wsm, a.part, a.out, a.xq, a.xs);
@@ -629,7 +629,7 @@ cudaError_t g4_launch_attn_decode(const AttnArgs &a, int splits, cudaStream_t st
 
 cudaError_t g4_launch_attn_rows(const AttnArgs &a, int splits, cudaStream_t st, bool pdl) {
     if (splits < 1 || splits > 256 || a.T < 1 || !a.row_seq || !a.row_pos) return cudaErrorInvalidValue;
-    const dim3 gs(splits, a.T), gc(kHeads * a.hd / 256, a.T);
+    const dim3 gs(splits, a.T), gc(kHeads * a.hd / kCombineDims, a.T);
     if (a.hd == 256) {
         const size_t smem = DecodeCfg<256>::smem;
         static bool once = false;
@@ -649,7 +649,7 @@ cudaError_t g4_launch_attn_rows(const AttnArgs &a, int splits, cudaStream_t st, 
 
 cudaError_t g4_launch_attn_combine(const AttnArgs &a, int splits, cudaStream_t st, bool pdl) {
     if (splits < 1 || splits > 256) return cudaErrorInvalidValue;
-    const int grid = kHeads * a.hd / 256;
+    const int grid = kHeads * a.hd / kCombineDims;
     if (a.hd == 256) return g4_launch(k_attn_combine<256>, dim3(grid), dim3(256), 0, st, pdl, a, splits);
     if (a.hd == 512) return g4_launch(k_attn_combine<512>, dim3(grid), dim3(256), 0, st, pdl, a, splits);
     return cudaErrorInvalidValue;

@@ -314,27 +314,32 @@ G4_DEV void attn_rows_split(const AttnArgs &a, int row, int split, int splits, f
 }
 
 // Combine the active split partials (part_base: [splits][8][HD + 4]) into the
-// attention output out[8*HD] for 256 output dimensions (combine block `blk` of
-// 8*HD/256) and, when xq is given, quantise them for o_proj (gemma4.c:459).
-// 256 threads, thread = one dimension. smem: 256 + 16 floats.
+// attention output out[8*HD] for 64 output dimensions (combine block `blk` of
+// 8*HD/64) and, when xq is given, quantise them for o_proj (gemma4.c:459): the
+// block is exactly one 64-wide quantisation group. 256 threads = 64 dimensions
+// x 4 slices of the splits (slice q takes splits q, q + 4, ...); each slice's
+// weighted sum runs over its splits in ascending order and the four are added
+// in slice order, so the result does not depend on timing.
+// smem: 256 (split weights) + 256 (slice sums) + 16 floats.
+constexpr int kCombineDims = 64;
 template <int HD>
 __device__ __noinline__ void attn_combine_part(const AttnArgs &a, int p, int blk, int splits, float *wsm,
                                                const float *part_base, float *out, int8_t *xq, float *xs) {
-    float *red = wsm + 256;
+    float *psum = wsm + 256, *red = wsm + 512;
     const int tid = threadIdx.x;
     int k0, k1;
     const int active = split_range(p, a.window, splits, 0, &k0, &k1);
-    const int per_head = HD / 256;
-    const int h = blk / per_head, d = (blk % per_head) * 256 + tid;
+    const int col0 = blk * kCombineDims, h = col0 / HD;
+    const int dl = tid & (kCombineDims - 1), sl = tid >> 6, d = col0 % HD + dl;
     const int warp = tid >> 5, lane = tid & 31;
     const size_t stride = (size_t)kHeads * (HD + 4);
     const float *ph = part_base + (size_t)h * (HD + 4);
-    // this thread's values of the first splits are loaded before the weights
+    // this thread's values of its first splits are loaded before the weights
     // exist, so that both loads share one memory round trip
     constexpr int U = 16;
     float pv[U];
 #pragma unroll
-    for (int u = 0; u < U; u++) pv[u] = u < active ? ph[u * stride + 4 + d] : 0.0f;
+    for (int u = 0; u < U; u++) pv[u] = sl + 4 * u < active ? ph[(sl + 4 * u) * stride + 4 + d] : 0.0f;
     if (warp == 0) {
         // split weights exp(m_s - max) and the total sum, lanes over splits (active <= 256)
         float mx = -INFINITY;
@@ -351,30 +356,43 @@ __device__ __noinline__ void attn_combine_part(const AttnArgs &a, int p, int blk
         if (lane == 0) red[8] = lsum;
     }
     attn_sync();
-    float o = 0.0f;   // sum over splits in ascending order
-    for (int s0 = 0; s0 < active; s0 += U) {
-        if (s0 > 0) {
+    float o = 0.0f;   // this slice's splits in ascending order
+    for (int u0 = 0; sl + 4 * u0 < active; u0 += U) {
+        if (u0 > 0) {
 #pragma unroll
-            for (int u = 0; u < U; u++) pv[u] = s0 + u < active ? ph[(s0 + u) * stride + 4 + d] : 0.0f;
+            for (int u = 0; u < U; u++) {
+                const int s = sl + 4 * (u0 + u);
+                pv[u] = s < active ? ph[s * stride + 4 + d] : 0.0f;
+            }
         }
 #pragma unroll
-        for (int u = 0; u < U; u++)
-            if (s0 + u < active) o = fmaf(wsm[s0 + u], pv[u], o);
+        for (int u = 0; u < U; u++) {
+            const int s = sl + 4 * (u0 + u);
+            if (s < active) o = fmaf(wsm[s], pv[u], o);
+        }
     }
-    o = o / red[8];
-    const int col = h * HD + d;
-    out[col] = o;
+    psum[sl * kCombineDims + dl] = o;
+    attn_sync();
+    if (tid < kCombineDims) {
+        o = __fadd_rn(__fadd_rn(__fadd_rn(psum[dl], psum[kCombineDims + dl]), psum[2 * kCombineDims + dl]),
+                      psum[3 * kCombineDims + dl]) /
+            red[8];
+        out[col0 + dl] = o;
+        if (xq) {
+            const float amax = warp_max(fabsf(o));
+            if (lane == 0) red[warp] = amax;
+        }
+    }
     if (!xq) {
         attn_sync();   // wsm / red are reused by the caller's next combine
         return;
     }
-    float amax = warp_max(fabsf(o));
-    if (lane == 0) red[warp] = amax;
     attn_sync();
-    amax = fmaxf(red[warp & ~1], red[warp | 1]);
-    const float sc = quant_scale(amax), inv = quant_inv(sc);
-    xq[col] = (int8_t)quant_one(o, inv);
-    if ((tid & 63) == 0) xs[col >> 6] = sc;
+    if (tid < kCombineDims) {
+        const float sc = quant_scale(fmaxf(red[0], red[1])), inv = quant_inv(sc);
+        xq[col0 + dl] = (int8_t)quant_one(o, inv);
+        if (tid == 0) xs[col0 >> 6] = sc;
+    }
     attn_sync();
 }
 

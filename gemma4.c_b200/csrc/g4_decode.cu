@@ -41,7 +41,7 @@ __host__ __device__ constexpr int cmax(int a, int b) { return a > b ? a : b; }
 constexpr int kAttnBytes = cmax(decode_smem_floats(256, kKT256), decode_smem_floats(512, kKT512)) * 4;
 constexpr int kGemvScratch = kMaxK + (kMaxK / 64) * 4 + G4_HIDDEN * 4;   // xq + xs + vec bytes
 constexpr int kDotsBytes = 32 * (kMaxK / 64) * 4;   // group-parallel dots: [G][32 rows] int32
-constexpr int kScratchBytes = cmax(cmax(kAttnBytes, kGemvScratch + kDotsBytes), (256 + 16) * 4);
+constexpr int kScratchBytes = cmax(cmax(kAttnBytes, kGemvScratch + kDotsBytes), (512 + 16) * 4);
 
 constexpr int kOffRing = 0;
 constexpr int kOffFull = kOffRing + (int)kRingBytes;
@@ -551,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1) k_decode(const DecodeParams P) {
             }
             break;
         case OP_COMBINE:
-            if ((int)blockIdx.x < kHeads * op.at.hd / 256) {
+            if ((int)blockIdx.x < kHeads * op.at.hd / kCombineDims) {
                 if (op.at.hd == 256)
                     attn_combine_part<256>(op.at, pos, blockIdx.x, P.splits, scratch, op.at.part, op.at.out, op.at.xq,
                                            op.at.xs);

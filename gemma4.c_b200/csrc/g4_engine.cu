@@ -105,6 +105,14 @@ struct g4_ctx {
     int bring[G4_NUM_LAYERS] = {};
     int *row_seq_d = nullptr, *row_pos_d = nullptr, *bargmax = nullptr;
     float *bpart = nullptr, *blogits = nullptr, *bres = nullptr, *embed_st = nullptr;
+    // logits of many rows (g4_logits_rows): two chunks of kDumpRows rows, their
+    // copy stream and events; own group-major lm_head scales when no batch state
+    void *dump_buf = nullptr;
+    float *dump_log[2] = {nullptr, nullptr};
+    int *dump_arg = nullptr;
+    float *dump_st_scales = nullptr;
+    cudaStream_t dump_st = nullptr;
+    cudaEvent_t dump_done[2] = {nullptr, nullptr}, dump_copied[2] = {nullptr, nullptr};
     std::vector<int> blast;          // last row of each sequence of the last batch
     bool pending = false;            // a single-token forward waiting to be launched
     DecodeOp *dec_fwd = nullptr, *dec_fwdlog = nullptr;
@@ -1017,6 +1025,13 @@ int g4_close(g4_ctx *c) {
         if (c->events[i]) cudaEventDestroy(c->events[i]);
     if (c->arena) cudaFree(c->arena);
     if (c->scales_t) cudaFree(c->scales_t);
+    if (c->dump_st) cudaStreamSynchronize(c->dump_st);
+    for (int i = 0; i < 2; i++) {
+        if (c->dump_done[i]) cudaEventDestroy(c->dump_done[i]);
+        if (c->dump_copied[i]) cudaEventDestroy(c->dump_copied[i]);
+    }
+    if (c->dump_st) cudaStreamDestroy(c->dump_st);
+    if (c->dump_buf) cudaFree(c->dump_buf);
     if (c->bkv) cudaFree(c->bkv);
     if (c->bbuf) cudaFree(c->bbuf);
     if (c->state) cudaFree(c->state);
@@ -1494,6 +1509,57 @@ int g4_forward_batch(g4_ctx *c, int n, const int *seq_ids, const int *tokens, co
     for (int i = 0; i < n; i++) c->blast[i] = offsets[i + 1] - 1;
     // the host vectors above are pageable: the copies completed before the calls returned
     return G4_OK;
+}
+
+// Logits of rows [row0, row0 + n) of the last forward into out[n][262144]
+// (the reference's --dump-logits loop, gemma4.c:567-570): chunks of kDumpRows
+// rows, each the final norm + one tensor-core lm_head GEMM + soft-cap on the
+// library stream, copied to the host on a second stream while the next chunk
+// computes. Bit-identical to g4_logits row by row.
+constexpr int kDumpRows = 64;
+int g4_logits_rows(g4_ctx *c, size_t row0, size_t n, float *out) {
+    if (!c || !out || n == 0) return G4_ERR_INVALID;
+    if (c->last_T == 0 || row0 + n > (size_t)c->last_T)
+        return fail(c, G4_ERR_STATE, "logits_rows: rows %zu..%zu not computed by the last forward (%d rows)", row0,
+                    row0 + n, c->last_T);
+    cudaSetDevice(c->device);
+    int rc = flush_pending(c);
+    if (rc) return rc;
+    if (!c->dump_buf) {
+        const size_t lb = (size_t)kDumpRows * G4_VOCAB * 4, sb = (size_t)G4_VOCAB * (G4_HIDDEN / 64) * 4;
+        CK(cudaMalloc(&c->dump_buf, 2 * lb + sb + kDumpRows * 4));
+        uint8_t *b = (uint8_t *)c->dump_buf;
+        c->dump_log[0] = (float *)b;
+        c->dump_log[1] = (float *)(b + lb);
+        c->dump_st_scales = (float *)(b + 2 * lb);
+        c->dump_arg = (int *)(b + 2 * lb + sb);
+        CK(g4_launch_scales_t(c->embed.s, G4_VOCAB, G4_HIDDEN, c->dump_st_scales, c->st));
+        CK(cudaStreamCreateWithFlags(&c->dump_st, cudaStreamNonBlocking));
+        for (int i = 0; i < 2; i++) {
+            CK(cudaEventCreateWithFlags(&c->dump_done[i], cudaEventDisableTiming));
+            CK(cudaEventCreateWithFlags(&c->dump_copied[i], cudaEventDisableTiming));
+            CK(cudaEventRecord(c->dump_copied[i], c->dump_st));
+        }
+    }
+    DMat em = c->embed;
+    em.sT = c->dump_st_scales;
+    for (size_t r = 0, ch = 0; r < n; r += kDumpRows, ch++) {
+        const int m = (int)(n - r < (size_t)kDumpRows ? n - r : kDumpRows), b = (int)(ch & 1);
+        Seq q{c, c->use_pdl};
+        CK(cudaStreamWaitEvent(c->st, c->dump_copied[b], 0));   // this buffer's previous copy is done
+        q.ck(g4_launch_rows_norm(0, c->res[c->cur] + (row0 + r) * G4_HIDDEN, m, nullptr, nullptr, nullptr, nullptr,
+                                 c->final_norm, G4_RMS_EPS, c->xq, c->xs, c->st, q.pdl, nullptr, 0, c->xsT));
+        gemm(q, em, m, EPI_STORE, c->dump_log[b], G4_VOCAB, nullptr, 0);
+        q.ck(g4_launch_softcap_argmax(c->dump_log[b], m, G4_VOCAB, c->dump_arg, c->st));
+        if (q.e) return fail(c, G4_ERR_CUDA, "logits_rows launch: %s", cudaGetErrorString(q.e));
+        CK(cudaEventRecord(c->dump_done[b], c->st));
+        CK(cudaStreamWaitEvent(c->dump_st, c->dump_done[b], 0));
+        CK(cudaMemcpyAsync(out + r * G4_VOCAB, c->dump_log[b], (size_t)m * G4_VOCAB * 4,
+                           cudaMemcpyDeviceToHost, c->dump_st));
+        CK(cudaEventRecord(c->dump_copied[b], c->dump_st));
+    }
+    CK(cudaStreamSynchronize(c->dump_st));
+    return check_device_error(c);
 }
 
 int g4_logits_batch(g4_ctx *c, int *argmax, float *logits) {

@@ -85,6 +85,7 @@ def load(path=LIB_PATH):
     L.g4k_sample.argtypes = [_f32p, C.c_int, C.c_float, C.POINTER(C.c_ulonglong), C.POINTER(C.c_int)]
     L.g4_sample.argtypes = [vp, C.c_size_t, C.c_float, C.POINTER(C.c_int)]
     L.g4_set_seed.argtypes = [vp, C.c_uint64]
+    L.g4_logits_rows.argtypes = [vp, C.c_size_t, C.c_size_t, vp]
     L.g4_profiler_range.argtypes = [C.c_int]
     L.g4_mark.argtypes = [vp, C.c_int]
     L.g4_elapsed.argtypes = [vp, C.c_int, C.c_int, C.POINTER(C.c_float)]
@@ -164,6 +165,13 @@ class Model:
         am = C.c_int(-1)
         _check(self.L.g4_logits(self.h, row, out.ctypes.data if out is not None else None, C.byref(am)), self.h)
         return out, am.value
+
+    def logits_rows(self, row0, n, out=None):
+        """Logits of n rows of the last forward (g4_logits_rows), [n][VOCAB]."""
+        if out is None:
+            out = np.empty((n, VOCAB), np.float32)
+        _check(self.L.g4_logits_rows(self.h, row0, n, out.ctypes.data), self.h)
+        return out
 
     def sample(self, row, temperature):
         """Next token drawn on the device (g4_sample) from logits row `row`."""

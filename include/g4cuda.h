@@ -65,6 +65,13 @@ int g4_forward(g4_ctx *ctx, const int *tokens, size_t count, int start_pos);
  * benchmark computes logits it never reads, gemma4.c:641). */
 int g4_logits(g4_ctx *ctx, size_t row, float *out, int *argmax);
 
+/* The logits of rows [row0, row0 + n) of the last forward into out[n][262144]
+ * (the reference's --dump-logits loop over logits(), gemma4.c:567-570): the
+ * lm_head of 64 rows at a time on the tensor cores, each chunk copied to the
+ * host while the next computes (page-locked `out` copies fastest). Identical
+ * bits to g4_logits row by row. Synchronises. */
+int g4_logits_rows(g4_ctx *ctx, size_t row0, size_t n, float *out);
+
 /* Top-k (k <= 64) of the logits of `row`, descending, ties to the lower id:
  * the candidate list of gemma4.c:544-551. Synchronises. */
 int g4_topk(g4_ctx *ctx, size_t row, int k, float *values, int *ids);

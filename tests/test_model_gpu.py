@@ -110,6 +110,23 @@ def test_prefill_gemm_paths_bitidentical(g4, image):
     assert np.array_equal(lgs[0].view(np.uint32), lgs[1].view(np.uint32))
 
 
+def test_logits_rows_equal_logits(g4, image):
+    """g4_logits_rows (the --dump-logits loop: lm_head GEMM over 64-row chunks,
+    copies overlapped) gives every row the same bits as g4_logits."""
+    rng = np.random.default_rng(12)
+    toks = rng.integers(0, 262144, size=300).astype(np.int32)
+    with g4.Model(image) as m:
+        m.forward(toks, 0)
+        allrows = m.logits_rows(0, 300)
+        part = m.logits_rows(100, 37)
+        for r in (0, 63, 64, 150, 299):
+            lg, _ = m.logits(r)
+            assert np.array_equal(allrows[r].view(np.uint32), lg.view(np.uint32))
+        assert np.array_equal(part.view(np.uint32), allrows[100:137].view(np.uint32))
+        with pytest.raises(g4.G4Error):
+            m.logits_rows(290, 20)
+
+
 def test_api_errors(g4, gpu):
     with pytest.raises(g4.G4Error) as e:
         gpu.forward(np.array([262144], np.int32), 0)

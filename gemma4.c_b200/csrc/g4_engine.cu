@@ -206,8 +206,8 @@ int upload_mat(g4_ctx *c, const HostMat &hm, DMat dst, int row_offset, int row_m
     uint16_t *ss = (uint16_t *)(stage + (((size_t)rows * K + 255) & ~(size_t)255));
     for (int r0 = 0; r0 < hm.N; r0 += rows) {
         int nr = hm.N - r0 < rows ? hm.N - r0 : rows;
-        CK(cudaMemcpyAsync(sw, hm.w + (size_t)r0 * K, (size_t)nr * K, cudaMemcpyHostToDevice, c->st));
-        CK(cudaMemcpyAsync(ss, hm.s + (size_t)r0 * G, (size_t)nr * G * 2, cudaMemcpyHostToDevice, c->st));
+        CK(cudaMemcpyAsync(sw, hm.w + (size_t)r0 * K, (size_t)nr * K, cudaMemcpyDefault, c->st));
+        CK(cudaMemcpyAsync(ss, hm.s + (size_t)r0 * G, (size_t)nr * G * 2, cudaMemcpyDefault, c->st));
         CK(g4_launch_repack((const int8_t *)sw, ss, nr, K, (int8_t *)dst.w, (uint16_t *)dst.s, row_offset + r0 * row_mul,
                             row_mul, c->st));
         CK(cudaStreamSynchronize(c->st));
@@ -227,17 +227,21 @@ DMat alloc_mat(g4_ctx *c, int N, int K) {
 const float *upload_vec(g4_ctx *c, const float *h, size_t n, int *rc) {
     float *d = (float *)arena_take(c, n * 4);
     if (!d) { *rc = G4_ERR_NOMEM; return nullptr; }
-    cudaError_t e = cudaMemcpyAsync(d, h, n * 4, cudaMemcpyHostToDevice, c->st);
+    cudaError_t e = cudaMemcpyAsync(d, h, n * 4, cudaMemcpyDefault, c->st);   // host or device image
     if (e != cudaSuccess) *rc = G4_ERR_CUDA;
     return d;
 }
 
 size_t mat_bytes(int N, int K) { return (((size_t)N * K + 255) & ~(size_t)255) + (((size_t)N * (K / 64) * 2 + 255) & ~(size_t)255); }
 
-int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes) {
-    if (bytes < G4_WEIGHTS_OFFSET + (uint64_t)G4_NUM_RECORDS * G4_RECORD_BYTES || memcmp(img, "MOG", 4) != 0)
+// img: the model image (host memory, or device memory when hdr is given);
+// hdr: a host copy of the image's first G4_WEIGHTS_OFFSET + record-table bytes
+// (magic and records are parsed on the host), or NULL when img is host memory.
+int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes, const uint8_t *hdr = nullptr) {
+    const uint8_t *h = hdr ? hdr : img;
+    if (bytes < G4_WEIGHTS_OFFSET + (uint64_t)G4_NUM_RECORDS * G4_RECORD_BYTES || memcmp(h, "MOG", 4) != 0)
         return fail(c, G4_ERR_FORMAT, "not a gemma4.c model image (magic \"MOG\")");
-    const Rec *r = (const Rec *)(img + G4_WEIGHTS_OFFSET);
+    const Rec *r = (const Rec *)(h + G4_WEIGHTS_OFFSET);
 
     CK(cudaSetDevice(c->device));
     CK(cudaDeviceGetAttribute(&c->num_sms, cudaDevAttrMultiProcessorCount, c->device));
@@ -999,19 +1003,66 @@ int g4_open(const void *image, uint64_t bytes, int device, g4_ctx **out) {
 
 const char *g4_open_error(void) { return g_open_msg; }
 
+// The .bin straight to the device: the file is read in 64 MB pieces into two
+// page-locked buffers, each piece copied to a device-resident image while the
+// next one is read; the repacking then reads that image (device to device).
+// Only the header and record table are parsed from a host copy.
 int g4_open_file(const char *path, int device, g4_ctx **out) {
-    if (!path || !out) return G4_ERR_INVALID;
+    if (!path || !out || device < 0) return G4_ERR_INVALID;
+    *out = nullptr;
     FILE *f = fopen(path, "rb");
     if (!f) return G4_ERR_INVALID;
     fseek(f, 0, SEEK_END);
-    long long n = ftell(f);
+    const long long n = ftell(f);
     fseek(f, 0, SEEK_SET);
-    uint8_t *buf = (uint8_t *)malloc((size_t)n);
-    if (!buf) { fclose(f); return G4_ERR_NOMEM; }
-    size_t got = fread(buf, 1, (size_t)n, f);
+    const size_t hdr_bytes = (size_t)G4_WEIGHTS_OFFSET + (size_t)G4_NUM_RECORDS * G4_RECORD_BYTES;
+    if (n < (long long)hdr_bytes) {
+        fclose(f);
+        return G4_ERR_FORMAT;
+    }
+    constexpr size_t kPiece = 64ull << 20;
+    int rc = G4_OK;
+    uint8_t *hdr = (uint8_t *)malloc(hdr_bytes);
+    uint8_t *pin[2] = {nullptr, nullptr};
+    uint8_t *dimg = nullptr;
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev[2] = {nullptr, nullptr};
+    if (!hdr || cudaSetDevice(device) != cudaSuccess || cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking) ||
+        cudaMalloc(&dimg, (size_t)n) != cudaSuccess || cudaHostAlloc(&pin[0], kPiece, 0) != cudaSuccess ||
+        cudaHostAlloc(&pin[1], kPiece, 0) != cudaSuccess || cudaEventCreate(&ev[0]) || cudaEventCreate(&ev[1])) {
+        rc = G4_ERR_NOMEM;
+    }
+    for (size_t off = 0, i = 0; rc == G4_OK && off < (size_t)n; off += kPiece, i++) {
+        const size_t len = (size_t)n - off < kPiece ? (size_t)n - off : kPiece;
+        uint8_t *b = pin[i & 1];
+        if (i >= 2 && cudaEventSynchronize(ev[i & 1]) != cudaSuccess) rc = G4_ERR_CUDA;   // its last copy is done
+        if (rc == G4_OK && fread(b, 1, len, f) != len) rc = G4_ERR_FORMAT;
+        if (rc == G4_OK && off < hdr_bytes)
+            memcpy(hdr + off, b, hdr_bytes - off < len ? hdr_bytes - off : len);
+        if (rc == G4_OK && (cudaMemcpyAsync(dimg + off, b, len, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+                            cudaEventRecord(ev[i & 1], st) != cudaSuccess))
+            rc = G4_ERR_CUDA;
+    }
     fclose(f);
-    int rc = got == (size_t)n ? g4_open(buf, (uint64_t)n, device, out) : G4_ERR_FORMAT;
-    free(buf);
+    if (st && cudaStreamSynchronize(st) != cudaSuccess && rc == G4_OK) rc = G4_ERR_CUDA;
+    if (rc == G4_OK) {
+        g4_ctx *c = new g4_ctx();
+        c->device = device;
+        rc = open_impl(c, dimg, (uint64_t)n, hdr);
+        if (rc != G4_OK) {
+            snprintf(g_open_msg, sizeof(g_open_msg), "%s", c->msg);
+            g4_close(c);
+        } else {
+            *out = c;
+        }
+    }
+    for (int i = 0; i < 2; i++) {
+        if (pin[i]) cudaFreeHost(pin[i]);
+        if (ev[i]) cudaEventDestroy(ev[i]);
+    }
+    if (st) cudaStreamDestroy(st);
+    if (dimg) cudaFree(dimg);
+    free(hdr);
     return rc;
 }
 

@@ -45,7 +45,10 @@ typedef struct g4_ctx g4_ctx;
  * Replaces main's mmap + pointer fix-up + calloc(InferenceState)
  * (gemma4.c:673-686). The image is only read during the call. */
 int g4_open(const void *image, uint64_t bytes, int device, g4_ctx **out);
-/* Same, reading the file at `path`. */
+/* Same, reading the .bin at `path` straight to the device: 64 MB pieces through
+ * two page-locked buffers, each copied while the next is read, then the
+ * one-time repacking from that device image (it needs the file's size in free
+ * device memory during the call). */
 int g4_open_file(const char *path, int device, g4_ctx **out);
 int g4_close(g4_ctx *ctx);
 /* Message for the last failed g4_open / g4_open_file in this process. */

@@ -98,6 +98,19 @@ def test_rows_tracks_oracle(g4, oracle, hd, T, start_pos, ring, splits):
     assert err <= OUT_ATOL, f"max abs error {err}"
 
 
+def test_global_layer_at_max_context(g4, oracle):
+    """The last positions of the 131072-slot global ring (gemma4.c MAX_CONTEXT):
+    a 5-token prefill chunk ending at position 131071 and one decode token at
+    131071, all earlier keys in the ring."""
+    hd, ring, T, start = 512, 131072, 5, 131067
+    (qkv, k, v, cos_t, sin_t), (eo, ek, ev) = _oracle(oracle, hd, T, start, ring, 500)
+    out, _ = g4.attention(qkv, hd, k.copy(), v.copy(), start, cos_t, sin_t, mode=g4.ATTN_PREFILL)
+    assert np.abs(out - eo).max() <= OUT_ATOL
+    (qkv1, k1, v1, cos1, sin1), (eo1, _, _) = _oracle(oracle, hd, 1, ring - 1, ring, 501)
+    out1, _ = g4.attention(qkv1, hd, k1, v1, ring - 1, cos1, sin1, mode=g4.ATTN_DECODE, splits=148)
+    assert np.abs(out1 - eo1).max() <= OUT_ATOL
+
+
 def test_attention_api_errors(g4):
     qkv, k, v, cos_t, sin_t = inputs(256, 4, 0, 1024, 1)
     with pytest.raises(g4.G4Error):

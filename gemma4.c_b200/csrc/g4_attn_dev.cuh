@@ -120,8 +120,13 @@ G4_DEV void norm_rope_regs(float (&v)[HD / 32], const float *w, const float *cos
 }
 
 // Shared-memory floats of one decode split with KT-key tiles (double buffered).
+// K tile row stride of the decode split: key rows land 4 (hd 256, 8 lanes per
+// key phase) or 8 (hd 512, lanes of 4 keys x 2 dimension parts) banks apart, so
+// the score phase's 16-byte loads are free of bank conflicts.
+__host__ __device__ constexpr int dec_ks(int hd) { return hd == 512 ? hd + 8 : hd + 4; }
+
 __host__ __device__ constexpr int decode_smem_floats(int hd, int kt) {
-    return kHeads * hd + 2 * hd + 2 * kt * (hd + 4) + 2 * kt * hd;
+    return kHeads * hd + 2 * hd + 2 * kt * dec_ks(hd) + 2 * kt * hd;
 }
 
 // Decode (T = 1) split-KV attention at position p for split `split` of `splits`, run by 256
@@ -142,7 +147,7 @@ template <int HD, int KT>
 G4_DEV void attn_split_core(const AttnArgs &a, const float *kc, const float *vc, int p, int k0, int k1,
                             const float *qn, const float *kn, const float *vn, float *Ks, float *Vs, float *part_base,
                             bool first_issued) {
-    constexpr int LPK = 32 / KT, KS = HD + 4;
+    constexpr int LPK = 32 / KT, KS = dec_ks(HD), QC = HD / (4 * LPK);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     auto issue = [&](int tile, int buf) {
         const int kt = k0 + tile * KT, nt = min(KT, k1 - kt);
@@ -162,8 +167,12 @@ G4_DEV void attn_split_core(const AttnArgs &a, const float *kc, const float *vc,
 #pragma unroll
     for (int i = 0; i < NV; i++) o[i] = make_float4(0.f, 0.f, 0.f, 0.f);
     float m = -INFINITY, l = 0.0f;
-    const float *q = qn + warp * HD;
     const int key_lane = lane % KT, dpart = lane / KT;   // score phase: key and dimension part
+    // this lane's query slice (16-byte chunks dpart, dpart + LPK, ...) stays in
+    // registers for the whole split
+    float4 qr[QC];
+#pragma unroll
+    for (int j = 0; j < QC; j++) qr[j] = *(const float4 *)&qn[warp * HD + 4 * (dpart + LPK * j)];
 
     for (int t = 0; t < ntiles; t++) {
         const int buf = t & 1, kt = k0 + t * KT, nt = min(KT, k1 - kt);
@@ -186,12 +195,11 @@ G4_DEV void attn_split_core(const AttnArgs &a, const float *kc, const float *vc,
         }
         float s = -INFINITY;
         {
-            const float *kr = Kb + key_lane * KS + dpart * (HD / LPK);
-            const float *qq = q + dpart * (HD / LPK);
+            const float *kr = Kb + key_lane * KS + 4 * dpart;
             float acc = 0.0f;
-#pragma unroll 8
-            for (int d = 0; d < HD / LPK; d += 4) {
-                const float4 a4 = *(const float4 *)&qq[d], k4 = *(const float4 *)&kr[d];
+#pragma unroll
+            for (int j = 0; j < QC; j++) {
+                const float4 a4 = qr[j], k4 = *(const float4 *)&kr[4 * LPK * j];
                 acc = fmaf(a4.x, k4.x, acc);
                 acc = fmaf(a4.y, k4.y, acc);
                 acc = fmaf(a4.z, k4.z, acc);
@@ -245,8 +253,8 @@ __device__ __noinline__ void attn_decode_split(const AttnArgs &a, int p, int spl
     float *qn = sm;                       // [8][HD]
     float *kn = qn + kHeads * HD;         // [HD]
     float *vn = kn + HD;                  // [HD]
-    float *Ks = vn + HD;                  // [2][KT][HD + 4]
-    float *Vs = Ks + 2 * KT * (HD + 4);   // [2][KT][HD]
+    float *Ks = vn + HD;                  // [2][KT][dec_ks(HD)]
+    float *Vs = Ks + 2 * KT * dec_ks(HD); // [2][KT][HD]
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     int k0, k1;
     const int active = split_range(p, a.window, splits, split, &k0, &k1);
@@ -257,7 +265,7 @@ __device__ __noinline__ void attn_decode_split(const AttnArgs &a, int p, int spl
         for (int idx = tid; idx < nt * (HD / 4); idx += kAttnThreads) {
             const int r = idx / (HD / 4), c4 = idx - r * (HD / 4);
             const size_t slot = (size_t)((k0 + r) & a.mask) * HD;
-            cp_async16(&Ks[r * (HD + 4) + c4 * 4], a.kcache + slot + c4 * 4);
+            cp_async16(&Ks[r * dec_ks(HD) + c4 * 4], a.kcache + slot + c4 * 4);
             cp_async16(&Vs[r * HD + c4 * 4], a.vcache + slot + c4 * 4);
         }
         cp_async_commit();
@@ -299,7 +307,7 @@ template <int HD, int KT>
 G4_DEV void attn_rows_split(const AttnArgs &a, int row, int split, int splits, float *sm) {
     float *qn = sm;                       // [8][HD]
     float *Ks = qn + kHeads * HD + 2 * HD;
-    float *Vs = Ks + 2 * KT * (HD + 4);
+    float *Vs = Ks + 2 * KT * dec_ks(HD);
     const int tid = threadIdx.x;
     const int p = a.row_pos[row];
     const size_t so = (size_t)a.row_seq[row] * a.seq_stride;

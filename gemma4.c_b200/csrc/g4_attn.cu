@@ -561,11 +561,6 @@ __global__ void __launch_bounds__(256) k_attn_prefill_merge(const AttnArgs a) {
     }
 }
 
-template <typename K>
-cudaError_t set_smem(K kern, size_t bytes) {
-    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
-}
-
 // Host copy of the unit schedule: does any q tile span more than one CTA?
 template <int HD>
 bool prefill_needs_merge(const AttnArgs &a) {
@@ -589,11 +584,9 @@ bool prefill_needs_merge(const AttnArgs &a) {
 
 template <int HD>
 cudaError_t launch_prefill(const AttnArgs &a, cudaStream_t st, bool pdl) {
-    static bool once = false;
-    if (!once) {
-        cudaError_t e = set_smem(k_attn_prefill<HD>, Pre<HD>::kSmem);
+    {
+        cudaError_t e = g4_smem_optin((const void *)k_attn_prefill<HD>, (int)Pre<HD>::kSmem);
         if (e) return e;
-        once = true;
     }
     cudaError_t e = g4_launch(k_attn_prefill<HD>, dim3(a.pre_ctas), dim3(256), Pre<HD>::kSmem, st, pdl, a);
     if (e || !prefill_needs_merge<HD>(a)) return e;
@@ -614,14 +607,12 @@ cudaError_t g4_launch_attn_decode(const AttnArgs &a, int splits, cudaStream_t st
     if (splits < 1 || splits > 256) return cudaErrorInvalidValue;
     if (a.hd == 256) {
         const size_t smem = DecodeCfg<256>::smem;
-        static bool once = false;
-        if (!once) { cudaError_t e = set_smem(k_attn_decode<256>, smem); if (e) return e; once = true; }
+        { cudaError_t e = g4_smem_optin((const void *)k_attn_decode<256>, (int)smem); if (e) return e; }
         return g4_launch(k_attn_decode<256>, dim3(splits), dim3(256), smem, st, pdl, a, splits);
     }
     if (a.hd == 512) {
         const size_t smem = DecodeCfg<512>::smem;
-        static bool once = false;
-        if (!once) { cudaError_t e = set_smem(k_attn_decode<512>, smem); if (e) return e; once = true; }
+        { cudaError_t e = g4_smem_optin((const void *)k_attn_decode<512>, (int)smem); if (e) return e; }
         return g4_launch(k_attn_decode<512>, dim3(splits), dim3(256), smem, st, pdl, a, splits);
     }
     return cudaErrorInvalidValue;
@@ -632,15 +623,13 @@ cudaError_t g4_launch_attn_rows(const AttnArgs &a, int splits, cudaStream_t st, 
     const dim3 gs(splits, a.T), gc(kHeads * a.hd / kCombineDims, a.T);
     if (a.hd == 256) {
         const size_t smem = DecodeCfg<256>::smem;
-        static bool once = false;
-        if (!once) { cudaError_t e = set_smem(k_attn_rows<256>, smem); if (e) return e; once = true; }
+        { cudaError_t e = g4_smem_optin((const void *)k_attn_rows<256>, (int)smem); if (e) return e; }
         cudaError_t e = g4_launch(k_attn_rows<256>, gs, dim3(256), smem, st, pdl, a, splits);
         return e ? e : g4_launch(k_attn_rows_combine<256>, gc, dim3(256), 0, st, pdl, a, splits);
     }
     if (a.hd == 512) {
         const size_t smem = DecodeCfg<512>::smem;
-        static bool once = false;
-        if (!once) { cudaError_t e = set_smem(k_attn_rows<512>, smem); if (e) return e; once = true; }
+        { cudaError_t e = g4_smem_optin((const void *)k_attn_rows<512>, (int)smem); if (e) return e; }
         cudaError_t e = g4_launch(k_attn_rows<512>, gs, dim3(256), smem, st, pdl, a, splits);
         return e ? e : g4_launch(k_attn_rows_combine<512>, gc, dim3(256), 0, st, pdl, a, splits);
     }

@@ -613,11 +613,9 @@ int g4_decode_max_stages(const DecodeOp *ops, int nops, int grid) {
 }
 
 cudaError_t g4_launch_decode(const DecodeParams &p, int grid, cudaStream_t st) {
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(k_decode, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    {
+        cudaError_t e = g4_smem_optin((const void *)k_decode, kSmemBytes);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);

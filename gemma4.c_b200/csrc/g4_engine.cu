@@ -19,6 +19,7 @@
 #include <stdlib.h>
 #include <string.h>
 
+#include <mutex>
 #include <utility>
 #include <vector>
 
@@ -965,6 +966,27 @@ int check_device_error(g4_ctx *c) {
 
 // ---------------------------------------------------------------------------
 // C ABI
+
+cudaError_t g4_smem_optin(const void *kernel, int bytes) {
+    static std::mutex mu;
+    static std::vector<std::pair<int, const void *>> done;
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(mu);
+    for (const auto &d : done)
+        if (d.first == dev && d.second == kernel) return cudaSuccess;
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+    if (e == cudaSuccess) done.emplace_back(dev, kernel);
+    return e;
+}
+
+int g4_device_sms() {
+    int dev = 0, n = 148;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    return n;
+}
 
 extern "C" {
 

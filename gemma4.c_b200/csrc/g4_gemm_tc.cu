@@ -469,12 +469,9 @@ int pick_bn(int N, int mt, int sms) {
 
 template <int BN>
 cudaError_t launch_bn(const CUtensorMap &ma, const CUtensorMap &mb, const TcArgs &p, int sms, cudaStream_t st) {
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(k_gemm_tc<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             TcCfg<BN>::kSmemBytes);
+    {
+        cudaError_t e = g4_smem_optin((const void *)k_gemm_tc<BN>, TcCfg<BN>::kSmemBytes);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     const int tiles = (p.N / BN) * ((p.T + kBM - 1) / kBM);
     k_gemm_tc<BN><<<tiles < sms ? tiles : sms, kThreads, TcCfg<BN>::kSmemBytes, st>>>(ma, mb, p);
@@ -492,8 +489,7 @@ bool g4_gemm_tc_supported(const GemmArgs &a) {
 cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
     (void)pdl;
     if (!g4_gemm_tc_supported(a)) return cudaErrorNotSupported;
-    static int sms = 0;
-    if (!sms) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, 0);
+    const int sms = g4_device_sms();
     const bool fuse_q = a.epi == EPI_GEGLU_PAIR && a.qout && a.qs && a.m.N % 128 == 0;
     const int bn = fuse_q ? 128 : pick_bn(a.m.N, (a.T + kBM - 1) / kBM, sms);
     CUtensorMap ma, mb;

@@ -216,11 +216,9 @@ template <int T, int PRO, int EPI>
 cudaError_t launch_t(const GemvArgs &a, int grid, cudaStream_t st, bool pdl) {
     const Layout L = make_layout(a.m.K, T, PRO);
     auto kern = k_gemv<T, PRO, EPI>;
-    static bool configured = false;
-    if (!configured) {
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, 200 * 1024);
+    {
+        cudaError_t e = g4_smem_optin((const void *)kern, 200 * 1024);
         if (e != cudaSuccess) return e;
-        configured = true;
     }
     if (L.total > 200 * 1024) return cudaErrorInvalidValue;
     return g4_launch(kern, dim3(grid), dim3(kThreads), (size_t)L.total, st, pdl, a);

@@ -215,6 +215,11 @@ cudaError_t g4_launch_attn_combine(const AttnArgs &a, int splits, cudaStream_t s
 // top-64 temperature sampling (gemma4.c:536-561) from a top-64 list; state: xorshift state
 cudaError_t g4_launch_sample64(const float *vals, const int *ids, float temperature, unsigned long long *state,
                                int *token, cudaStream_t st);
+// Raise a kernel's dynamic shared-memory limit to `bytes` once per device
+// (the attribute lives in each device's context); thread-safe.
+cudaError_t g4_smem_optin(const void *kernel, int bytes);
+// Multiprocessor count of the current device.
+int g4_device_sms();
 cudaError_t g4_launch_qkv_post(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_prefill(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_strict(const AttnArgs &a, cudaStream_t st, bool pdl);

@@ -249,6 +249,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
+            const uint64_t dA0 = umma_desc(smem + C::kOffA, 0), dB0 = umma_desc(smem + C::kOffB, 0);
             int k = 0;
             bool ok = true;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
@@ -261,11 +262,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint8_t *ta = smem + C::kOffA + s * kTileBytesA, *tb = smem + C::kOffB + s * C::kTileBytesB;
+                    // descriptors: the stage's tile base plus the K offset, in 16-byte units
+                    // of the start-address field (addresses stay below 2^18, so no carry)
+                    const uint64_t da = dA0 + (uint64_t)((s * kTileBytesA) >> 4);
+                    const uint64_t db = dB0 + (uint64_t)((s * C::kTileBytesB) >> 4);
+#pragma unroll
                     for (int gi = 0; gi < 2; gi++)
+#pragma unroll
                         for (int kk = 0; kk < 2; kk++) {
-                            const int kb = gi * 64 + kk * 32;
-                            mma_i8(tmem + (pb * 2 + gi) * BN, umma_desc(ta, kb), umma_desc(tb, kb), C::kIdesc, kk != 0);
+                            const int kb = (gi * 64 + kk * 32) >> 4;
+                            mma_i8(tmem + (pb * 2 + gi) * BN, da + kb, db + kb, C::kIdesc, kk != 0);
                         }
                     mma_commit(&tfull[pb]);
                     mma_commit(&empty[s]);

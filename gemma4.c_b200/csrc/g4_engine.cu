@@ -92,6 +92,11 @@ struct g4_ctx {
     cudaGraphExec_t g_decode = nullptr;
     int graph_cur = 0;
     bool decode_warm = false;
+    // multi-sequence steps (one row per sequence): one graph per row count;
+    // the first step of a row count runs eagerly, the next one is captured
+    std::vector<cudaGraphExec_t> g_rows;
+    std::vector<char> rows_warm;
+    int rows_cur = 0;
     cudaEvent_t events[16] = {};
     // persistent single-token decode (g4_decode.cu)
     bool persistent = true;          // G4_OPT_PERSISTENT
@@ -560,6 +565,11 @@ bool gemm(Seq &q, const DMat &m, int T, int epi, float *out, int out_stride, con
         q.ck(g4_launch_gemm_simt(a, c->st, q.pdl));
         return false;
     }
+    // a few token rows (multi-sequence decode): the weight-streaming mma GEMM
+    if ((c->gemm_path == 3 || (c->gemm_path == 0 && T <= G4_SKINNY_MAX_T)) && g4_gemm_skinny_supported(a)) {
+        q.ck(g4_launch_gemm_skinny(a, c->st, q.pdl));
+        return false;
+    }
     const bool fuse = fuse_quant && epi == EPI_GEGLU_PAIR && m.N % 128 == 0;
     if (fuse) {   // into the second set: this GEMM still reads xq / xs / xsT
         a.qout = c->xq2;
@@ -860,6 +870,13 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp
 
 // Record the single-token step as persistent-decode op lists (forward only, and
 // forward + logits of row 0) and upload them; called once the context exists.
+void drop_row_graphs(g4_ctx *c) {
+    for (cudaGraphExec_t &g : c->g_rows)
+        if (g) cudaGraphExecDestroy(g);
+    c->g_rows.clear();
+    c->rows_warm.clear();
+}
+
 void free_decode(g4_ctx *c) {
     if (c->dec_fwd) cudaFree(c->dec_fwd);
     if (c->dec_fwdlog) cudaFree(c->dec_fwdlog);
@@ -1093,6 +1110,7 @@ int g4_close(g4_ctx *c) {
     flush_pending(c);
     if (c->st) cudaStreamSynchronize(c->st);
     free_decode(c);
+    drop_row_graphs(c);
     if (c->g_decode) cudaGraphExecDestroy(c->g_decode);
     for (int i = 0; i < 16; i++)
         if (c->events[i]) cudaEventDestroy(c->events[i]);
@@ -1119,6 +1137,7 @@ int g4_set_option(g4_ctx *c, int option, int value) {
     if (!c) return G4_ERR_INVALID;
     int rc = flush_pending(c);
     if (rc) return rc;
+    drop_row_graphs(c);   // every option can change what a multi-sequence step launches
     switch (option) {
     case G4_OPT_PERSISTENT: c->persistent = value != 0; break;
     case G4_OPT_BATCH_SPLITS:
@@ -1480,6 +1499,7 @@ int g4_seq_alloc(g4_ctx *c, int max_seqs, int max_context) {
     cudaSetDevice(c->device);
     if (int rc = flush_pending(c)) return rc;
     CK(cudaStreamSynchronize(c->st));
+    drop_row_graphs(c);   // the graphs hold the old rings' addresses
     if (c->bkv) cudaFree(c->bkv);
     if (c->bbuf) cudaFree(c->bbuf);
     c->bkv = c->bbuf = nullptr;
@@ -1575,8 +1595,42 @@ int g4_forward_batch(g4_ctx *c, int n, const int *seq_ids, const int *tokens, co
     // one sequence with several tokens: the prefill attention over its ring; else one row per sequence
     // (single-token rows use the same split attention as single-sequence decode)
     BatchPlan bp{T == n, seq_ids[0]};
-    cudaError_t e = enqueue_prefill(c, T, start_pos[0], &bp);
-    if (e) return fail(c, G4_ERR_CUDA, "forward_batch launch: %s", cudaGetErrorString(e));
+    if (bp.rows && c->use_graph) {
+        // rows read their sequence and position from the device arrays above, so
+        // one graph per row count replays any step of that many sequences
+        if ((int)c->g_rows.size() <= T) {
+            c->g_rows.resize(T + 1, nullptr);
+            c->rows_warm.resize(T + 1, 0);
+        }
+        if (!c->g_rows[T] && c->rows_warm[T]) {
+            cudaGraph_t g = nullptr;
+            CK(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
+            cudaError_t e = enqueue_prefill(c, T, start_pos[0], &bp);
+            cudaError_t e2 = cudaStreamEndCapture(c->st, &g);
+            if (e || e2) {
+                if (g) cudaGraphDestroy(g);
+                return fail(c, G4_ERR_CUDA, "forward_batch capture: %s", cudaGetErrorString(e ? e : e2));
+            }
+            e = cudaGraphInstantiate(&c->g_rows[T], g, 0);
+            cudaGraphDestroy(g);
+            if (e) {
+                c->g_rows[T] = nullptr;
+                return fail(c, G4_ERR_CUDA, "forward_batch graph: %s", cudaGetErrorString(e));
+            }
+            c->rows_cur = c->cur;
+        }
+        if (c->g_rows[T]) {
+            CK(cudaGraphLaunch(c->g_rows[T], c->st));
+            c->cur = c->rows_cur;
+        } else {
+            cudaError_t e = enqueue_prefill(c, T, start_pos[0], &bp);
+            if (e) return fail(c, G4_ERR_CUDA, "forward_batch launch: %s", cudaGetErrorString(e));
+            c->rows_warm[T] = 1;
+        }
+    } else {
+        cudaError_t e = enqueue_prefill(c, T, start_pos[0], &bp);
+        if (e) return fail(c, G4_ERR_CUDA, "forward_batch launch: %s", cudaGetErrorString(e));
+    }
     c->last_T = 0;   // the single-sequence rows are gone
     c->blast.resize(n);
     for (int i = 0; i < n; i++) c->blast[i] = offsets[i + 1] - 1;

@@ -1,0 +1,315 @@
+// g4_gemm_skinny.cu — int8 GEMM over a few token rows (T <= 64): the
+// multi-sequence decode step (one row per sequence) and short chunks.
+//
+// Reference: matmul_int8 (gemma4.c:192-262) per token row, with the exact
+// arithmetic of every other path: the int32 dot of each 64-wide group, then
+// the fp32 chain acc = fma((float)dot_g, ws[n][g] * xs[t][g], acc) over g
+// ascending, so the outputs are bit-identical to the GEMV, SIMT and tcgen05
+// paths.
+//
+// With T <= 64 rows the GEMM does 2T operations per weight byte and is bound
+// by the weight stream; what limits a 128-row tensor-core tile here is that a
+// CTA walks all K groups in sequence (the chain must run g ascending), so the
+// weight stream only covers the SMs if a CTA owns few output rows. Here a CTA
+// owns a block of 16 x WM consecutive output rows (one contiguous byte run of
+// W) and every token row:
+//   - one producer lane, per stage of four groups: the block's weight tile
+//     (one 64-byte group x 16 WM rows per box, so a row is 64 bytes in shared
+//     memory and the fragment loads below are bank-conflict free), the
+//     activation tile (64 bytes x Tp token rows; rows >= T are zero-filled by
+//     the tensor map), and the groups' weight and activation scales (fp32,
+//     group-major). The weight boxes of the first stages are issued before
+//     waiting for the previous kernel (programmatic dependent launch): they
+//     do not depend on it.
+//   - consumer warp (rb, tg): output rows 16 rb .. 16 rb + 15 of the block x
+//     token rows 8 NT tg ..; per group and 8-token tile two mma.sync
+//     m16n8k32 (s8 x s8 -> s32) give the exact group dots in registers, and
+//     the lane advances its four fp32 chains right away (packed f32x2, each
+//     lane of the pair rounds like fmaf).
+// Fragment order: the int32 dot does not depend on the order of its 64
+// products, so a lane loads 16 contiguous bytes of its weight row (bytes
+// 16 q .. 16 q + 15 of the group, q = lane % 4) and of its token row and
+// feeds words 0-1 to the first MMA and words 2-3 to the second. A and B see
+// the same byte for every k slot (the slot's k depends only on lane % 4 in
+// both fragment layouts), so each MMA pair sums exactly the group's products.
+#include <cuda.h>
+
+#include "g4_common.cuh"
+#include "g4_internal.h"
+
+namespace {
+
+constexpr int kGS = 4;            // groups per stage
+constexpr int kMaxWarps = 15;     // consumer warps per CTA (+ the producer: 4 warps per scheduler)
+constexpr int kStageBudget = 160 * 1024;
+constexpr int kSmemMax = 200 * 1024;   // opt-in size (launches use less; the ring depth varies per shape)
+
+struct SkArgs {
+    int T, N, K;
+    int tp;                 // token rows staged per group (multiple of 8)
+    int wm, wt;             // consumer warps along output rows / token rows
+    int stages;
+    uint32_t stage_bytes, off_x, off_ws, off_xs;
+    int epi;
+    float *out;
+    int out_stride;
+    const float *ple_u;
+    int u_stride;
+    const float *gelu;
+    int *err;
+};
+
+G4_DEV void tma2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+G4_DEV void tma2d_hint(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+        "%3}], [%4], %5;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
+// d += A (16 x 32, s8, row) * B (32 x 8, s8, col), int32 accumulate.
+G4_DEV void mma_s8(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0, uint32_t b1) {
+    asm("mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+        "{%0, %1, %2, %3};"
+        : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+G4_DEV void emit(const SkArgs &p, int t, int n, float v) {
+    if (p.epi == EPI_PLE)
+        v = geglu_one(v, p.ple_u[(size_t)t * p.u_stride + n], p.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+    p.out[(size_t)t * p.out_stride + n] = v;
+}
+
+template <int NT>
+__global__ void __launch_bounds__(32 * (kMaxWarps + 1), 1)
+    k_gemm_skinny(const __grid_constant__ CUtensorMap mw, const __grid_constant__ CUtensorMap mx,
+                  const __grid_constant__ CUtensorMap mws, const __grid_constant__ CUtensorMap mxs, const SkArgs p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int nc = p.wm * p.wt, RB = 16 * p.wm;
+    const int r0 = blockIdx.x * RB;
+    const int nst = p.K / (64 * kGS), S = p.stages;
+    uint64_t *full = (uint64_t *)(smem + (size_t)S * p.stage_bytes);
+    uint64_t *empty = full + S;
+    if (tid == 0) {
+        for (int s = 0; s < S; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], nc);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+    griddep_launch();
+
+    if (warp == nc) {
+        // ---------------- producer ----------------
+        if (lane == 0) {
+            const uint64_t pol = l2_policy_evict_first();
+            const int pre = nst < S ? nst : S;
+            int issued = 0;
+            auto weights = [&](int st, int s) {
+                uint8_t *b = smem + (size_t)s * p.stage_bytes;
+                mbar_arrive_expect_tx(&full[s], p.stage_bytes);
+#pragma unroll
+                for (int gi = 0; gi < kGS; gi++)
+                    tma2d_hint(b + gi * RB * 64, &mw, (st * kGS + gi) * 64, r0, &full[s], pol);
+                tma2d(b + p.off_ws, &mws, r0, st * kGS, &full[s]);
+            };
+            for (int st = 0; st < pre; st++) weights(st, st);
+            griddep_wait();   // activations and their scales come from the previous kernel
+            for (int st = 0; st < nst; st++) {
+                const int s = st % S;
+                if (st >= pre) {
+                    if (!mbar_wait(&empty[s], ((st / S) - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | (st << 8))) break;
+                    weights(st, s);
+                }
+                uint8_t *b = smem + (size_t)s * p.stage_bytes;
+#pragma unroll
+                for (int gi = 0; gi < kGS; gi++) tma2d(b + p.off_x + gi * p.tp * 64, &mx, (st * kGS + gi) * 64, 0, &full[s]);
+                tma2d(b + p.off_xs, &mxs, 0, st * kGS, &full[s]);
+                issued = st + 1;
+            }
+            // Let every copy land before the CTA's shared memory goes away (after a
+            // consumer timeout the consumers may have left early). Stages [0, pre) were
+            // armed before the loop, so they count too; bounded by one deadline.
+            const int armed = issued > pre ? issued : pre;
+            const uint64_t t0 = g4_globaltimer();
+            for (int k = armed > S ? armed - S : 0; k < armed; k++)
+                while (!mbar_try_wait(&full[k % S], (k / S) & 1) && g4_globaltimer() - t0 < G4_WAIT_NS) {
+                }
+        }
+        __syncwarp();
+        return;
+    }
+
+    // ---------------- consumers ----------------
+    const int rb = warp % p.wm, tg = warp / p.wm;
+    const int gid = lane >> 2, q = lane & 3;
+    uint64_t acc_lo[NT], acc_hi[NT];   // rows gid / gid + 8, token rows 2q and 2q + 1 of each tile
+#pragma unroll
+    for (int j = 0; j < NT; j++) acc_lo[j] = acc_hi[j] = pk(0.0f, 0.0f);
+    griddep_wait();   // the previous kernel may still read what the epilogue overwrites
+    bool ok = true;
+    for (int st = 0; st < nst; st++) {
+        const int s = st % S;
+        const bool got = mbar_wait(&full[s], (st / S) & 1, p.err, G4D_TIMEOUT_FULL | (st << 8));
+        if (!__all_sync(0xffffffffu, got)) {
+            ok = false;
+            break;
+        }
+        const uint8_t *b = smem + (size_t)s * p.stage_bytes;
+        const uint8_t *wb = b + (rb * 16 + gid) * 64 + q * 16;
+        const uint8_t *xb = b + p.off_x + (tg * 8 * NT + gid) * 64 + q * 16;
+        const float *wsb = (const float *)(b + p.off_ws) + rb * 16 + gid;
+        const float *xsb = (const float *)(b + p.off_xs) + tg * 8 * NT + 2 * q;
+#pragma unroll
+        for (int gi = 0; gi < kGS; gi++) {
+            const uint4 alo = *(const uint4 *)(wb + gi * RB * 64);
+            const uint4 ahi = *(const uint4 *)(wb + gi * RB * 64 + 8 * 64);
+            const float wlo = wsb[gi * RB], whi = wsb[gi * RB + 8];
+#pragma unroll
+            for (int j = 0; j < NT; j++) {
+                const uint4 bx = *(const uint4 *)(xb + (gi * p.tp + 8 * j) * 64);
+                int d[4] = {0, 0, 0, 0};
+                mma_s8(d, alo.x, ahi.x, alo.y, ahi.y, bx.x, bx.y);
+                mma_s8(d, alo.z, ahi.z, alo.w, ahi.w, bx.z, bx.w);
+                const float2 xv = *(const float2 *)(xsb + gi * p.tp + 8 * j);
+                const uint64_t x2 = pk(xv.x, xv.y);
+                acc_lo[j] = fma2(pk(__int2float_rn(d[0]), __int2float_rn(d[1])), mul2(pk(wlo, wlo), x2), acc_lo[j]);
+                acc_hi[j] = fma2(pk(__int2float_rn(d[2]), __int2float_rn(d[3])), mul2(pk(whi, whi), x2), acc_hi[j]);
+            }
+        }
+        __syncwarp();   // this warp's reads of the stage are done
+        if (lane == 0) mbar_arrive(&empty[s]);
+    }
+    if (!ok) return;
+
+    // ---------------- epilogue ----------------
+    const int n_lo = r0 + rb * 16 + gid;
+#pragma unroll
+    for (int j = 0; j < NT; j++) {
+        const int t0 = tg * 8 * NT + 8 * j + 2 * q;
+        const float2 lo = upk(acc_lo[j]), hi = upk(acc_hi[j]);
+        if (p.epi == EPI_GEGLU_PAIR) {
+            // interleaved rows: gate n (even gid) and up n + 1 live four lanes apart
+            const float ulo0 = __shfl_down_sync(0xffffffffu, lo.x, 4), ulo1 = __shfl_down_sync(0xffffffffu, lo.y, 4);
+            const float uhi0 = __shfl_down_sync(0xffffffffu, hi.x, 4), uhi1 = __shfl_down_sync(0xffffffffu, hi.y, 4);
+            if (gid & 1) continue;
+            const float *tab = p.gelu;
+            const int h_lo = n_lo >> 1, h_hi = (n_lo + 8) >> 1;
+            if (t0 < p.T) {
+                p.out[(size_t)t0 * p.out_stride + h_lo] = geglu_one(lo.x, ulo0, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                p.out[(size_t)t0 * p.out_stride + h_hi] = geglu_one(hi.x, uhi0, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+            }
+            if (t0 + 1 < p.T) {
+                p.out[(size_t)(t0 + 1) * p.out_stride + h_lo] =
+                    geglu_one(lo.y, ulo1, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                p.out[(size_t)(t0 + 1) * p.out_stride + h_hi] =
+                    geglu_one(hi.y, uhi1, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+            }
+        } else {
+            if (t0 < p.T) {
+                emit(p, t0, n_lo, lo.x);
+                emit(p, t0, n_lo + 8, hi.x);
+            }
+            if (t0 + 1 < p.T) {
+                emit(p, t0 + 1, n_lo, lo.y);
+                emit(p, t0 + 1, n_lo + 8, hi.y);
+            }
+        }
+    }
+}
+
+// ---- host side ----------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Row-major [rows][cols] of `esize`-byte elements (row stride `stride` bytes),
+// boxes of box_rows x box_cols, no swizzle; out-of-range rows read as zero.
+bool make_map2d(CUtensorMap *m, CUtensorMapDataType type, const void *base, int cols, int rows, size_t stride,
+                int box_cols, int box_rows) {
+    EncodeTiledFn fn = (EncodeTiledFn)g4_tmap_encoder();
+    if (!fn || ((uintptr_t)base & 15) || (stride & 15)) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)stride};
+    const cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, type, 2, (void *)base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+              CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// Output rows per CTA (16 x wm): the widest block that still gives about two
+// CTAs per SM, so the weight stream covers every SM.
+int pick_wm(int N, int wt, int sms) {
+    for (int wm = 8; wm > 1; wm >>= 1)
+        if (N % (16 * wm) == 0 && wm * wt <= kMaxWarps && N / (16 * wm) >= 2 * sms) return wm;
+    return 1;
+}
+
+template <int NT>
+cudaError_t launch_nt(const CUtensorMap (&maps)[4], const SkArgs &p, int grid, cudaStream_t st, bool pdl) {
+    const int threads = 32 * (p.wm * p.wt + 1);
+    const int smem = p.stages * (int)p.stage_bytes + 2 * p.stages * 8 + 128;
+    if (smem > kSmemMax) return cudaErrorInvalidValue;
+    cudaError_t e = g4_smem_optin((const void *)k_gemm_skinny<NT>, kSmemMax);
+    if (e != cudaSuccess) return e;
+    return g4_launch(k_gemm_skinny<NT>, dim3(grid), dim3(threads), (size_t)smem, st, pdl, maps[0], maps[1], maps[2],
+                     maps[3], p);
+}
+
+}  // namespace
+
+bool g4_gemm_skinny_supported(const GemmArgs &a) {
+    return a.T >= 1 && a.T <= G4_SKINNY_MAX_T && a.m.sT != nullptr && a.xsT != nullptr && a.m.K % (64 * kGS) == 0 &&
+           a.m.N % 16 == 0 && (a.epi == EPI_STORE || a.epi == EPI_GEGLU_PAIR || a.epi == EPI_PLE) &&
+           a.dots_out == nullptr && g4_tmap_encoder() != nullptr;
+}
+
+cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, int wm) {
+    if (!g4_gemm_skinny_supported(a)) return cudaErrorNotSupported;
+    const int nt = a.T > 32 ? 2 : 1;
+    const int wt = (a.T + 8 * nt - 1) / (8 * nt);
+    if (wm <= 0) wm = pick_wm(a.m.N, wt, g4_device_sms());
+    if (wm * wt > kMaxWarps || a.m.N % (16 * wm)) return cudaErrorInvalidValue;
+    SkArgs p{};
+    p.T = a.T;
+    p.N = a.m.N;
+    p.K = a.m.K;
+    p.tp = wt * 8 * nt;
+    p.wm = wm;
+    p.wt = wt;
+    const int RB = 16 * wm, G = a.m.K / 64;
+    p.off_x = (uint32_t)(kGS * RB * 64);
+    p.off_ws = p.off_x + (uint32_t)(kGS * p.tp * 64);
+    p.off_xs = p.off_ws + (uint32_t)(kGS * RB * 4);
+    p.stage_bytes = p.off_xs + (uint32_t)(kGS * p.tp * 4);
+    int stages = kStageBudget / (int)p.stage_bytes;
+    p.stages = stages < 2 ? 2 : stages > 8 ? 8 : stages;
+    p.epi = a.epi;
+    p.out = a.out;
+    p.out_stride = a.out_stride;
+    p.ple_u = a.ple_u;
+    p.u_stride = a.u_stride;
+    p.gelu = a.gelu;
+    p.err = a.err;
+    CUtensorMap maps[4];
+    if (!make_map2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, a.m.w, a.m.K, a.m.N, (size_t)a.m.K, 64, RB) ||
+        !make_map2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, a.xq, a.m.K, a.T, (size_t)a.m.K, 64, p.tp) ||
+        !make_map2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.m.sT, a.m.N, G, (size_t)a.m.N * 4, RB, kGS) ||
+        !make_map2d(&maps[3], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.xsT, G4_XST_STRIDE, G, (size_t)G4_XST_STRIDE * 4,
+                    p.tp, kGS))
+        return cudaErrorInvalidValue;
+    const int grid = a.m.N / RB;
+    return nt == 2 ? launch_nt<2>(maps, p, grid, st, pdl) : launch_nt<1>(maps, p, grid, st, pdl);
+}

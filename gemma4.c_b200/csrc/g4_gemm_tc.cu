@@ -486,6 +486,8 @@ cudaError_t launch_bn(const CUtensorMap &ma, const CUtensorMap &mb, const TcArgs
 
 }  // namespace
 
+void *g4_tmap_encoder() { return (void *)encode_fn(); }
+
 bool g4_gemm_tc_supported(const GemmArgs &a) {
     return a.m.sT != nullptr && a.xsT != nullptr && a.T <= G4_XST_STRIDE && a.m.K % kBK == 0 && a.m.N % 32 == 0 &&
            a.T >= 1 && encode_fn() != nullptr && (a.epi == EPI_STORE || a.epi == EPI_GEGLU_PAIR || a.epi == EPI_PLE) &&

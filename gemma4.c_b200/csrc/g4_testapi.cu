@@ -273,7 +273,7 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
     TK(g4_launch_repack((const int8_t *)pw.p, (const uint16_t *)ps.p, N, K, (int8_t *)w.p, (uint16_t *)s.p, 0, 1, 0));
     DMat m{(const int8_t *)w.p, (const uint16_t *)s.p, nullptr, N, K};
     DevBuf sT, xsT;
-    if (path == 3) {
+    if (path == 3 || path == 4) {
         if (T > G4_XST_STRIDE) return G4_ERR_INVALID;
         TK(sT.alloc((size_t)N * G * 4));
         TK(g4_launch_scales_t(m.s, N, K, (float *)sT.p, 0));
@@ -313,6 +313,9 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
         if (path == 3) {
             if (!g4_gemm_tc_supported(a)) return G4_ERR_INVALID;
             TK(g4_launch_gemm_tc(a, 0, false));
+        } else if (path == 4) {
+            if (!g4_gemm_skinny_supported(a)) return G4_ERR_INVALID;
+            TK(g4_launch_gemm_skinny(a, 0, false));
         } else {
             TK(g4_launch_gemm_simt(a, 0, false));
         }
@@ -540,13 +543,13 @@ int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch,
     return G4_OK;
 }
 
-// Time the prefill GEMM (path 2 SIMT dp4a, 3 tcgen05) on a T x N x K problem
+// Time the prefill GEMM (path 2 SIMT dp4a, 3 tcgen05, 4 small-batch mma) on a T x N x K problem
 // with device-resident weights cycled over enough copies to exceed L2, and
 // report the average launch duration and the int8 operations per launch
 // (2 T N K).
 int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch, double *ops_per_launch) {
-    if (N < 128 || N % 128 || K % 256 || T < 1 || T > G4_BATCH || iters < 1 || !ms_per_launch ||
-        (path != 2 && path != 3))
+    if (N < 128 || N % 128 || K % 256 || T < 1 || T > G4_BATCH || iters < 1 || !ms_per_launch || path < 2 ||
+        path > 4 || (path == 4 && T > G4_SKINNY_MAX_T))
         return G4_ERR_INVALID;
     const int G = K / 64;
     const size_t wbytes = (size_t)N * K + (size_t)N * G * 2;
@@ -582,7 +585,9 @@ int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch
         a.out = (float *)out.p;
         a.out_stride = N;
         a.err = (int *)err.p;
-        return path == 3 ? g4_launch_gemm_tc(a, st, false) : g4_launch_gemm_simt(a, st, false);
+        return path == 4   ? g4_launch_gemm_skinny(a, st, false)
+               : path == 3 ? g4_launch_gemm_tc(a, st, false)
+                           : g4_launch_gemm_simt(a, st, false);
     };
     for (int i = 0; i < 3; i++) TK(launch(i));
     cudaEvent_t e0, e1;

@@ -117,7 +117,9 @@ const char *g4_strerror(int code);
 /* Options (g4_set_option): */
 #define G4_OPT_GRAPHS 1      /* capture single-token decode in a CUDA graph (default 1) */
 #define G4_OPT_PDL 2         /* programmatic dependent launch between kernels (default 1) */
-#define G4_OPT_GEMM_PATH 3   /* prefill GEMM: 0 auto, 1 SIMT dp4a, 2 tcgen05 */
+#define G4_OPT_GEMM_PATH 3   /* prefill GEMM: 0 auto (small-batch mma for T <= 64 rows,
+                                else tcgen05), 1 SIMT dp4a, 2 tcgen05, 3 small-batch mma
+                                where it applies */
 #define G4_OPT_LAYERS 4      /* run only the first N layers (testing aid; default 35) */
 /* Reference-order arithmetic (default 0): RMSNorm sums of squares, attention
  * scores, softmax and value sums are evaluated in gemma4.c's sequential order
@@ -209,14 +211,16 @@ int g4k_quantize(const float *x, int rows, int width, int8_t *q, float *s);
 /* matmul_int8 (gemma4.c:257-262) on a packed matrix (exporter.py:304-316 layout):
  * out[T][N]; `dots` (may be NULL) receives the int32 of every (t, n, 64-group)
  * as [T][N][K/64]. path: 0 auto, 1 decode GEMV (T <= 4), 2 SIMT GEMM,
- * 3 tcgen05 GEMM. */
+ * 3 tcgen05 GEMM, 4 small-batch mma GEMM (T <= 64); paths 3 and 4 do not
+ * return dots. */
 int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, const int8_t *xq, const float *xs,
                int T, int path, float *out, int32_t *dots);
 /* Average duration of the decode GEMV on an N x K int8 matrix over `iters`
  * launches (weights cycled through enough copies to exceed L2), and the
  * algorithmic bytes (int8 weights + FP16 scales) one launch streams. */
 int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch, double *bytes_per_launch);
-/* Prefill GEMM timing (path 2 SIMT dp4a, 3 tcgen05) on T x N x K: average
+/* Prefill GEMM timing (path 2 SIMT dp4a, 3 tcgen05, 4 small-batch mma with
+ * T <= 64) on T x N x K: average
  * launch duration and int8 operations (2 T N K) per launch. */
 int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch, double *ops_per_launch);
 /* One attention sub-layer (attention, gemma4.c:411-461) over an FP32 KV ring:

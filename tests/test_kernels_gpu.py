@@ -99,6 +99,29 @@ def test_gemm_tcgen05_bitexact(g4, oracle, T, N, K):
     assert np.array_equal(out.view(np.uint32), oracle.linear(xq, xs, wp, sp, N, K).view(np.uint32))
 
 
+@pytest.mark.parametrize("T", [1, 5, 8, 31, 33, 64])
+@pytest.mark.parametrize("N,K", [(2560, 1536), (1536, 4096), (1536, 256), (12288, 1536), (1536, 12288),
+                                 (256, 1536), (32768, 256), (65536, 256)])
+def test_gemm_skinny_bitexact(g4, oracle, T, N, K):
+    """Small-batch GEMM (mma.sync m16n8k32 s8 group dots, T <= 64 token rows):
+    the same ordered fp32 chain -> bit-identical output. The shapes cover every
+    row-block width it picks (16, 32, 64 and 128 output rows per CTA) and both
+    token tilings (8 and 16 rows per warp)."""
+    rng = np.random.default_rng(11 * T + N + K)
+    _, _, wp, sp = packed_case(rng, N, K)
+    xq, xs = oracle.quantize(activations(rng, T, K))
+    out, _ = g4.linear(wp, sp, N, K, xq, xs, path=4)
+    assert np.array_equal(out.view(np.uint32), oracle.linear(xq, xs, wp, sp, N, K).view(np.uint32))
+
+
+def test_gemm_skinny_rejects_large_batches(g4, oracle):
+    rng = np.random.default_rng(2)
+    _, _, wp, sp = packed_case(rng, 256, 256)
+    xq, xs = oracle.quantize(activations(rng, 65, 256))
+    with pytest.raises(g4.G4Error):
+        g4.linear(wp, sp, 256, 256, xq, xs, path=4)
+
+
 def test_rmsnorm_quant(g4, oracle):
     rng = np.random.default_rng(3)
     x = activations(rng, 33, 1536)

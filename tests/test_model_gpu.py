@@ -110,6 +110,25 @@ def test_prefill_gemm_paths_bitidentical(g4, image):
     assert np.array_equal(lgs[0].view(np.uint32), lgs[1].view(np.uint32))
 
 
+@pytest.mark.parametrize("T", [20, 64])
+def test_small_batch_gemm_paths_bitidentical(g4, image, T):
+    """A chunk of at most 64 rows takes the small-batch mma GEMM by default;
+    its store, GEGLU-pair and PLE-gate epilogues give the bits of the
+    tensor-core and SIMT paths."""
+    rng = np.random.default_rng(20 + T)
+    toks = rng.integers(0, 262144, size=T).astype(np.int32)
+    res, lgs = [], []
+    for path in (3, 2, 1):
+        with g4.Model(image) as m:
+            m.set_option(g4.OPT_GEMM_PATH, path)
+            m.forward(toks, 0)
+            res.append(m.residual(T))
+            lgs.append(m.logits(T - 1)[0])
+    for i in (1, 2):
+        assert np.array_equal(res[0].view(np.uint32), res[i].view(np.uint32))
+        assert np.array_equal(lgs[0].view(np.uint32), lgs[i].view(np.uint32))
+
+
 def test_logits_rows_equal_logits(g4, image):
     """g4_logits_rows (the --dump-logits loop: lm_head GEMM over 64-row chunks,
     copies overlapped) gives every row the same bits as g4_logits."""

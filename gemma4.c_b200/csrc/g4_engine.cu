@@ -566,7 +566,7 @@ bool gemm(Seq &q, const DMat &m, int T, int epi, float *out, int out_stride, con
         return false;
     }
     // a few token rows (multi-sequence decode): the weight-streaming mma GEMM
-    if ((c->gemm_path == 3 || (c->gemm_path == 0 && T <= G4_SKINNY_MAX_T)) && g4_gemm_skinny_supported(a)) {
+    if ((c->gemm_path == 3 && g4_gemm_skinny_supported(a)) || (c->gemm_path == 0 && g4_gemm_skinny_preferred(a))) {
         q.ck(g4_launch_gemm_skinny(a, c->st, q.pdl));
         return false;
     }

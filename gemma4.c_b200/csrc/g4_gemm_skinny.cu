@@ -10,9 +10,10 @@
 // With T <= 64 rows the GEMM does 2T operations per weight byte and is bound
 // by the weight stream; what limits a 128-row tensor-core tile here is that a
 // CTA walks all K groups in sequence (the chain must run g ascending), so the
-// weight stream only covers the SMs if a CTA owns few output rows. Here a CTA
-// owns a block of 16 x WM consecutive output rows (one contiguous byte run of
-// W) and every token row:
+// weight stream only covers the SMs if a CTA owns few output rows. Here the
+// work unit is a block of 16 x WM consecutive output rows (one contiguous byte
+// run of W) x every token row; persistent CTAs walk blocks blockIdx.x,
+// + gridDim.x, ... with one ring whose phases run on from block to block:
 //   - one producer lane, per stage of four groups: the block's weight tile
 //     (one 64-byte group x 16 WM rows per box, so a row is 64 bytes in shared
 //     memory and the fragment loads below are bank-conflict free), the
@@ -39,7 +40,7 @@
 
 namespace {
 
-constexpr int kGS = 4;            // groups per stage
+constexpr int kMaxGS = 8;         // groups per stage (a box row of up to 512 bytes)
 constexpr int kMaxWarps = 15;     // consumer warps per CTA (+ the producer: 4 warps per scheduler)
 constexpr int kStageBudget = 160 * 1024;
 constexpr int kSmemMax = 200 * 1024;   // opt-in size (launches use less; the ring depth varies per shape)
@@ -49,6 +50,7 @@ struct SkArgs {
     int tp;                 // token rows staged per group (multiple of 8)
     int wm, wt;             // consumer warps along output rows / token rows
     int stages;
+    int gs;                 // groups per stage (8, or 4 when K % 512 != 0)
     uint32_t stage_bytes, off_x, off_ws, off_xs;
     int epi;
     float *out;
@@ -96,8 +98,14 @@ __global__ void __launch_bounds__(32 * (kMaxWarps + 1), 1)
     uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 127) & ~(uintptr_t)127);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nc = p.wm * p.wt, RB = 16 * p.wm;
-    const int r0 = blockIdx.x * RB;
-    const int nst = p.K / (64 * kGS), S = p.stages;
+    const int GS = p.gs, RW = 64 * GS;   // a staged row: GS groups of 64 bytes
+    constexpr int kUnroll = NT == 4 ? 2 : 4;
+    const int nst = p.K / RW, S = p.stages;
+    // persistent: row blocks blockIdx.x, + gridDim.x, ...; the ring and its
+    // barrier phases run on across blocks (global stage counter c)
+    const int nblk = p.N / RB;
+    const int my_blocks = (nblk - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;
+    const int total = my_blocks * nst;
     uint64_t *full = (uint64_t *)(smem + (size_t)S * p.stage_bytes);
     uint64_t *empty = full + S;
     if (tid == 0) {
@@ -114,29 +122,28 @@ __global__ void __launch_bounds__(32 * (kMaxWarps + 1), 1)
         // ---------------- producer ----------------
         if (lane == 0) {
             const uint64_t pol = l2_policy_evict_first();
-            const int pre = nst < S ? nst : S;
+            const int pre = total < S ? total : S;
             int issued = 0;
-            auto weights = [&](int st, int s) {
+            auto weights = [&](int c) {
+                const int s = c % S, st = c % nst, r0 = ((int)blockIdx.x + (c / nst) * (int)gridDim.x) * RB;
                 uint8_t *b = smem + (size_t)s * p.stage_bytes;
                 mbar_arrive_expect_tx(&full[s], p.stage_bytes);
-#pragma unroll
-                for (int gi = 0; gi < kGS; gi++)
-                    tma2d_hint(b + gi * RB * 64, &mw, (st * kGS + gi) * 64, r0, &full[s], pol);
-                tma2d(b + p.off_ws, &mws, r0, st * kGS, &full[s]);
+                // the int8 rows are viewed as 16-bit elements: x counts byte pairs
+                tma2d_hint(b, &mw, st * RW / 2, r0, &full[s], pol);
+                tma2d(b + p.off_ws, &mws, r0, st * GS, &full[s]);
             };
-            for (int st = 0; st < pre; st++) weights(st, st);
+            for (int c = 0; c < pre; c++) weights(c);
             griddep_wait();   // activations and their scales come from the previous kernel
-            for (int st = 0; st < nst; st++) {
-                const int s = st % S;
-                if (st >= pre) {
-                    if (!mbar_wait(&empty[s], ((st / S) - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | (st << 8))) break;
-                    weights(st, s);
+            for (int c = 0; c < total; c++) {
+                const int s = c % S, st = c % nst;
+                if (c >= pre) {
+                    if (!mbar_wait(&empty[s], ((c / S) - 1) & 1, p.err, G4D_TIMEOUT_EMPTY | ((c & 0xfff) << 8))) break;
+                    weights(c);
                 }
                 uint8_t *b = smem + (size_t)s * p.stage_bytes;
-#pragma unroll
-                for (int gi = 0; gi < kGS; gi++) tma2d(b + p.off_x + gi * p.tp * 64, &mx, (st * kGS + gi) * 64, 0, &full[s]);
-                tma2d(b + p.off_xs, &mxs, 0, st * kGS, &full[s]);
-                issued = st + 1;
+                tma2d(b + p.off_x, &mx, st * RW / 2, 0, &full[s]);
+                tma2d(b + p.off_xs, &mxs, 0, st * GS, &full[s]);
+                issued = c + 1;
             }
             // Let every copy land before the CTA's shared memory goes away (after a
             // consumer timeout the consumers may have left early). Stages [0, pre) were
@@ -154,76 +161,79 @@ __global__ void __launch_bounds__(32 * (kMaxWarps + 1), 1)
     // ---------------- consumers ----------------
     const int rb = warp % p.wm, tg = warp / p.wm;
     const int gid = lane >> 2, q = lane & 3;
-    uint64_t acc_lo[NT], acc_hi[NT];   // rows gid / gid + 8, token rows 2q and 2q + 1 of each tile
+    griddep_wait();   // the previous kernel may still read what the epilogues overwrite
+    for (int bi = 0, c = 0; bi < my_blocks; bi++) {
+        uint64_t acc_lo[NT], acc_hi[NT];   // rows gid / gid + 8, token rows 2q and 2q + 1 of each tile
 #pragma unroll
-    for (int j = 0; j < NT; j++) acc_lo[j] = acc_hi[j] = pk(0.0f, 0.0f);
-    griddep_wait();   // the previous kernel may still read what the epilogue overwrites
-    bool ok = true;
-    for (int st = 0; st < nst; st++) {
-        const int s = st % S;
-        const bool got = mbar_wait(&full[s], (st / S) & 1, p.err, G4D_TIMEOUT_FULL | (st << 8));
-        if (!__all_sync(0xffffffffu, got)) {
-            ok = false;
-            break;
-        }
-        const uint8_t *b = smem + (size_t)s * p.stage_bytes;
-        const uint8_t *wb = b + (rb * 16 + gid) * 64 + q * 16;
-        const uint8_t *xb = b + p.off_x + (tg * 8 * NT + gid) * 64 + q * 16;
-        const float *wsb = (const float *)(b + p.off_ws) + rb * 16 + gid;
-        const float *xsb = (const float *)(b + p.off_xs) + tg * 8 * NT + 2 * q;
+        for (int j = 0; j < NT; j++) acc_lo[j] = acc_hi[j] = pk(0.0f, 0.0f);
+        for (int st = 0; st < nst; st++, c++) {
+            const int s = c % S;
+            const bool got = mbar_wait(&full[s], (c / S) & 1, p.err, G4D_TIMEOUT_FULL | ((c & 0xfff) << 8));
+            if (!__all_sync(0xffffffffu, got)) return;
+            const uint8_t *b = smem + (size_t)s * p.stage_bytes;
+            const uint8_t *wb = b + (rb * 16 + gid) * RW + q * 16;
+            const uint8_t *xb = b + p.off_x + (tg * 8 * NT + gid) * RW + q * 16;
+            const float *wsb = (const float *)(b + p.off_ws) + rb * 16 + gid;
+            const float *xsb = (const float *)(b + p.off_xs) + tg * 8 * NT + 2 * q;
+#pragma unroll(kUnroll)
+            for (int gi = 0; gi < GS; gi++) {
+                const uint4 alo = *(const uint4 *)(wb + gi * 64);
+                const uint4 ahi = *(const uint4 *)(wb + gi * 64 + 8 * RW);
+                const float wlo = wsb[gi * RB], whi = wsb[gi * RB + 8];
 #pragma unroll
-        for (int gi = 0; gi < kGS; gi++) {
-            const uint4 alo = *(const uint4 *)(wb + gi * RB * 64);
-            const uint4 ahi = *(const uint4 *)(wb + gi * RB * 64 + 8 * 64);
-            const float wlo = wsb[gi * RB], whi = wsb[gi * RB + 8];
-#pragma unroll
-            for (int j = 0; j < NT; j++) {
-                const uint4 bx = *(const uint4 *)(xb + (gi * p.tp + 8 * j) * 64);
-                int d[4] = {0, 0, 0, 0};
-                mma_s8(d, alo.x, ahi.x, alo.y, ahi.y, bx.x, bx.y);
-                mma_s8(d, alo.z, ahi.z, alo.w, ahi.w, bx.z, bx.w);
-                const float2 xv = *(const float2 *)(xsb + gi * p.tp + 8 * j);
-                const uint64_t x2 = pk(xv.x, xv.y);
-                acc_lo[j] = fma2(pk(__int2float_rn(d[0]), __int2float_rn(d[1])), mul2(pk(wlo, wlo), x2), acc_lo[j]);
-                acc_hi[j] = fma2(pk(__int2float_rn(d[2]), __int2float_rn(d[3])), mul2(pk(whi, whi), x2), acc_hi[j]);
+                for (int j = 0; j < NT; j++) {
+                    const uint4 bx = *(const uint4 *)(xb + gi * 64 + 8 * j * RW);
+                    int d[4] = {0, 0, 0, 0};
+                    mma_s8(d, alo.x, ahi.x, alo.y, ahi.y, bx.x, bx.y);
+                    mma_s8(d, alo.z, ahi.z, alo.w, ahi.w, bx.z, bx.w);
+                    const float2 xv = *(const float2 *)(xsb + gi * p.tp + 8 * j);
+                    const uint64_t x2 = pk(xv.x, xv.y);
+                    acc_lo[j] =
+                        fma2(pk(__int2float_rn(d[0]), __int2float_rn(d[1])), mul2(pk(wlo, wlo), x2), acc_lo[j]);
+                    acc_hi[j] =
+                        fma2(pk(__int2float_rn(d[2]), __int2float_rn(d[3])), mul2(pk(whi, whi), x2), acc_hi[j]);
+                }
             }
+            __syncwarp();   // this warp's reads of the stage are done
+            if (lane == 0) mbar_arrive(&empty[s]);
         }
-        __syncwarp();   // this warp's reads of the stage are done
-        if (lane == 0) mbar_arrive(&empty[s]);
-    }
-    if (!ok) return;
 
-    // ---------------- epilogue ----------------
-    const int n_lo = r0 + rb * 16 + gid;
+        // ---------------- epilogue of the block ----------------
+        const int n_lo = ((int)blockIdx.x + bi * (int)gridDim.x) * RB + rb * 16 + gid;
 #pragma unroll
-    for (int j = 0; j < NT; j++) {
-        const int t0 = tg * 8 * NT + 8 * j + 2 * q;
-        const float2 lo = upk(acc_lo[j]), hi = upk(acc_hi[j]);
-        if (p.epi == EPI_GEGLU_PAIR) {
-            // interleaved rows: gate n (even gid) and up n + 1 live four lanes apart
-            const float ulo0 = __shfl_down_sync(0xffffffffu, lo.x, 4), ulo1 = __shfl_down_sync(0xffffffffu, lo.y, 4);
-            const float uhi0 = __shfl_down_sync(0xffffffffu, hi.x, 4), uhi1 = __shfl_down_sync(0xffffffffu, hi.y, 4);
-            if (gid & 1) continue;
-            const float *tab = p.gelu;
-            const int h_lo = n_lo >> 1, h_hi = (n_lo + 8) >> 1;
-            if (t0 < p.T) {
-                p.out[(size_t)t0 * p.out_stride + h_lo] = geglu_one(lo.x, ulo0, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
-                p.out[(size_t)t0 * p.out_stride + h_hi] = geglu_one(hi.x, uhi0, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
-            }
-            if (t0 + 1 < p.T) {
-                p.out[(size_t)(t0 + 1) * p.out_stride + h_lo] =
-                    geglu_one(lo.y, ulo1, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
-                p.out[(size_t)(t0 + 1) * p.out_stride + h_hi] =
-                    geglu_one(hi.y, uhi1, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
-            }
-        } else {
-            if (t0 < p.T) {
-                emit(p, t0, n_lo, lo.x);
-                emit(p, t0, n_lo + 8, hi.x);
-            }
-            if (t0 + 1 < p.T) {
-                emit(p, t0 + 1, n_lo, lo.y);
-                emit(p, t0 + 1, n_lo + 8, hi.y);
+        for (int j = 0; j < NT; j++) {
+            const int t0 = tg * 8 * NT + 8 * j + 2 * q;
+            const float2 lo = upk(acc_lo[j]), hi = upk(acc_hi[j]);
+            if (p.epi == EPI_GEGLU_PAIR) {
+                // interleaved rows: gate n (even gid) and up n + 1 live four lanes apart
+                const float ulo0 = __shfl_down_sync(0xffffffffu, lo.x, 4);
+                const float ulo1 = __shfl_down_sync(0xffffffffu, lo.y, 4);
+                const float uhi0 = __shfl_down_sync(0xffffffffu, hi.x, 4);
+                const float uhi1 = __shfl_down_sync(0xffffffffu, hi.y, 4);
+                if (gid & 1) continue;
+                const float *tab = p.gelu;
+                const int h_lo = n_lo >> 1, h_hi = (n_lo + 8) >> 1;
+                if (t0 < p.T) {
+                    p.out[(size_t)t0 * p.out_stride + h_lo] =
+                        geglu_one(lo.x, ulo0, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                    p.out[(size_t)t0 * p.out_stride + h_hi] =
+                        geglu_one(hi.x, uhi0, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                }
+                if (t0 + 1 < p.T) {
+                    p.out[(size_t)(t0 + 1) * p.out_stride + h_lo] =
+                        geglu_one(lo.y, ulo1, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                    p.out[(size_t)(t0 + 1) * p.out_stride + h_hi] =
+                        geglu_one(hi.y, uhi1, tab, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+                }
+            } else {
+                if (t0 < p.T) {
+                    emit(p, t0, n_lo, lo.x);
+                    emit(p, t0, n_lo + 8, hi.x);
+                }
+                if (t0 + 1 < p.T) {
+                    emit(p, t0 + 1, n_lo, lo.y);
+                    emit(p, t0 + 1, n_lo + 8, hi.y);
+                }
             }
         }
     }
@@ -249,38 +259,65 @@ bool make_map2d(CUtensorMap *m, CUtensorMapDataType type, const void *base, int 
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// Output rows per CTA (16 x wm): the widest block that still gives about two
-// CTAs per SM, so the weight stream covers every SM.
-int pick_wm(int N, int wt, int sms) {
-    for (int wm = 8; wm > 1; wm >>= 1)
-        if (N % (16 * wm) == 0 && wm * wt <= kMaxWarps && N / (16 * wm) >= 2 * sms) return wm;
-    return 1;
+// Tiling for an N-output GEMM over T token rows (sweeps on the B200): the
+// widest row block (16 wm rows; fewer re-reads of the activation tile per
+// weight byte) that still leaves about half an SM's worth of blocks per SM
+// pair, i.e. >= sms / 2 blocks; then the fewest 8-token tiles per warp (nt)
+// that keep the CTA at 4 consumer warps (one row block wide) or 8.
+void pick_tiling(int N, int T, int sms, int *wm_out, int *nt_out) {
+    int wm = 1;
+    for (int w = 8; w > 1; w >>= 1)
+        if (N % (16 * w) == 0 && N / (16 * w) >= sms / 2) {
+            wm = w;
+            break;
+        }
+    const int cap = wm <= 2 ? 4 : 8;
+    int nt = 1;
+    while (nt < 4 && wm * ((T + 8 * nt - 1) / (8 * nt)) > cap) nt <<= 1;
+    while (wm > 1 && wm * ((T + 8 * nt - 1) / (8 * nt)) > kMaxWarps) wm >>= 1;
+    *wm_out = wm;
+    *nt_out = nt;
 }
 
 template <int NT>
-cudaError_t launch_nt(const CUtensorMap (&maps)[4], const SkArgs &p, int grid, cudaStream_t st, bool pdl) {
+cudaError_t launch_nt(const CUtensorMap (&maps)[4], const SkArgs &p, int blocks, cudaStream_t st, bool pdl) {
     const int threads = 32 * (p.wm * p.wt + 1);
     const int smem = p.stages * (int)p.stage_bytes + 2 * p.stages * 8 + 128;
     if (smem > kSmemMax) return cudaErrorInvalidValue;
     cudaError_t e = g4_smem_optin((const void *)k_gemm_skinny<NT>, kSmemMax);
     if (e != cudaSuccess) return e;
-    return g4_launch(k_gemm_skinny<NT>, dim3(grid), dim3(threads), (size_t)smem, st, pdl, maps[0], maps[1], maps[2],
-                     maps[3], p);
+    // persistent CTAs: as many as fit on the SMs (two when the ring and the
+    // register file allow)
+    const int per_sm = smem <= 110 * 1024 && threads <= 256 ? 2 : 1, cap = per_sm * g4_device_sms();
+    return g4_launch(k_gemm_skinny<NT>, dim3(blocks < cap ? blocks : cap), dim3(threads), (size_t)smem, st, pdl,
+                     maps[0], maps[1], maps[2], maps[3], p);
 }
 
 }  // namespace
 
 bool g4_gemm_skinny_supported(const GemmArgs &a) {
-    return a.T >= 1 && a.T <= G4_SKINNY_MAX_T && a.m.sT != nullptr && a.xsT != nullptr && a.m.K % (64 * kGS) == 0 &&
+    return a.T >= 1 && a.T <= G4_SKINNY_MAX_T && a.m.sT != nullptr && a.xsT != nullptr && a.m.K % 256 == 0 &&
            a.m.N % 16 == 0 && (a.epi == EPI_STORE || a.epi == EPI_GEGLU_PAIR || a.epi == EPI_PLE) &&
            a.dots_out == nullptr && g4_tmap_encoder() != nullptr;
 }
 
-cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, int wm) {
+bool g4_gemm_skinny_preferred(const GemmArgs &a) {
+    // measured: faster than the tcgen05 GEMM on every projection shape up to 32
+    // token rows, and up to 64 rows where N < 8192; the lm_head and the wide
+    // gate/up GEMM at 33-64 rows stay on the tensor-core tiles
+    return g4_gemm_skinny_supported(a) && (a.T <= 32 || a.m.N < 8192);
+}
+
+cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, int wm, int nt) {
     if (!g4_gemm_skinny_supported(a)) return cudaErrorNotSupported;
-    const int nt = a.T > 32 ? 2 : 1;
+    if (wm <= 0 || nt <= 0) {
+        int w, n;
+        pick_tiling(a.m.N, a.T, g4_device_sms(), &w, &n);
+        if (wm <= 0) wm = w;
+        if (nt <= 0) nt = n;
+    }
+    if (nt != 1 && nt != 2 && nt != 4) return cudaErrorInvalidValue;
     const int wt = (a.T + 8 * nt - 1) / (8 * nt);
-    if (wm <= 0) wm = pick_wm(a.m.N, wt, g4_device_sms());
     if (wm * wt > kMaxWarps || a.m.N % (16 * wm)) return cudaErrorInvalidValue;
     SkArgs p{};
     p.T = a.T;
@@ -290,10 +327,12 @@ cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, 
     p.wm = wm;
     p.wt = wt;
     const int RB = 16 * wm, G = a.m.K / 64;
-    p.off_x = (uint32_t)(kGS * RB * 64);
-    p.off_ws = p.off_x + (uint32_t)(kGS * p.tp * 64);
-    p.off_xs = p.off_ws + (uint32_t)(kGS * RB * 4);
-    p.stage_bytes = p.off_xs + (uint32_t)(kGS * p.tp * 4);
+    p.gs = a.m.K % (64 * kMaxGS) == 0 ? kMaxGS : 4;
+    const int RW = 64 * p.gs;
+    p.off_x = (uint32_t)(RB * RW);
+    p.off_ws = p.off_x + (uint32_t)(p.tp * RW);
+    p.off_xs = p.off_ws + (uint32_t)(p.gs * RB * 4);
+    p.stage_bytes = p.off_xs + (uint32_t)(p.gs * p.tp * 4);
     int stages = kStageBudget / (int)p.stage_bytes;
     p.stages = stages < 2 ? 2 : stages > 8 ? 8 : stages;
     p.epi = a.epi;
@@ -304,12 +343,17 @@ cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, 
     p.gelu = a.gelu;
     p.err = a.err;
     CUtensorMap maps[4];
-    if (!make_map2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT8, a.m.w, a.m.K, a.m.N, (size_t)a.m.K, 64, RB) ||
-        !make_map2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT8, a.xq, a.m.K, a.T, (size_t)a.m.K, 64, p.tp) ||
-        !make_map2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.m.sT, a.m.N, G, (size_t)a.m.N * 4, RB, kGS) ||
+    // the int8 matrices as 16-bit elements, so that one box row carries 512 bytes
+    if (!make_map2d(&maps[0], CU_TENSOR_MAP_DATA_TYPE_UINT16, a.m.w, a.m.K / 2, a.m.N, (size_t)a.m.K, RW / 2, RB) ||
+        !make_map2d(&maps[1], CU_TENSOR_MAP_DATA_TYPE_UINT16, a.xq, a.m.K / 2, a.T, (size_t)a.m.K, RW / 2, p.tp) ||
+        !make_map2d(&maps[2], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.m.sT, a.m.N, G, (size_t)a.m.N * 4, RB, p.gs) ||
         !make_map2d(&maps[3], CU_TENSOR_MAP_DATA_TYPE_FLOAT32, a.xsT, G4_XST_STRIDE, G, (size_t)G4_XST_STRIDE * 4,
-                    p.tp, kGS))
+                    p.tp, p.gs))
         return cudaErrorInvalidValue;
-    const int grid = a.m.N / RB;
-    return nt == 2 ? launch_nt<2>(maps, p, grid, st, pdl) : launch_nt<1>(maps, p, grid, st, pdl);
+    const int blocks = a.m.N / RB;
+    switch (nt) {
+    case 4: return launch_nt<4>(maps, p, blocks, st, pdl);
+    case 2: return launch_nt<2>(maps, p, blocks, st, pdl);
+    default: return launch_nt<1>(maps, p, blocks, st, pdl);
+    }
 }

@@ -116,8 +116,9 @@ struct GemmArgs {
 // Small-batch GEMM (g4_gemm_skinny.cu): T <= G4_SKINNY_MAX_T token rows.
 constexpr int G4_SKINNY_MAX_T = 64;
 bool g4_gemm_skinny_supported(const GemmArgs &a);
-// wm: output rows per CTA / 16 (0 = chosen from the shape)
-cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, int wm = 0);
+bool g4_gemm_skinny_preferred(const GemmArgs &a);   // supported and faster than the tcgen05 GEMM
+// wm: output rows per block / 16, nt: 8-token tiles per warp (0 = chosen from the shape)
+cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, int wm = 0, int nt = 0);
 // cuTensorMapEncodeTiled from the driver (NULL if unavailable)
 void *g4_tmap_encoder();
 

@@ -105,8 +105,8 @@ def test_gemm_tcgen05_bitexact(g4, oracle, T, N, K):
 def test_gemm_skinny_bitexact(g4, oracle, T, N, K):
     """Small-batch GEMM (mma.sync m16n8k32 s8 group dots, T <= 64 token rows):
     the same ordered fp32 chain -> bit-identical output. The shapes cover every
-    row-block width it picks (16, 32, 64 and 128 output rows per CTA) and both
-    token tilings (8 and 16 rows per warp)."""
+    row-block width it picks (16, 32, 64 and 128 output rows) and token tiles
+    of 8, 16 and 32 rows per warp, with 4 or 8 groups per stage."""
     rng = np.random.default_rng(11 * T + N + K)
     _, _, wp, sp = packed_case(rng, N, K)
     xq, xs = oracle.quantize(activations(rng, T, K))

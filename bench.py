@@ -273,7 +273,7 @@ def prefill_timed(m, n, reps, dist):
     return n / (np.mean(times) / 1e3), float(np.mean(times))
 
 
-def batched_serving(m, dist, seqs=64):
+def batched_serving(m, dist, seqs=64, profile_step=None):
     """BASELINE config 5 on this GPU: 64 independent sequences, prompts
     log-uniform in [128, 8192], decode lengths uniform in [32, 512], ids
     uniform (seed 2 + rank). Each prompt is prefilled (512-token chunks) and its
@@ -305,9 +305,15 @@ def batched_serving(m, dist, seqs=64):
         act = np.nonzero(left > 0)[0]
         if act.size == 0:
             break
+        if steps == profile_step:
+            m.sync()
+            m.L.g4_profiler_range(1)
         m.forward_batch(act.astype(np.int32), [[int(nxt[i])] for i in act], pos[act].astype(np.int32))
         _, am = m.logits_batch()
         nxt[act] = am
+        if steps == profile_step:
+            m.sync()
+            m.L.g4_profiler_range(0)
         # KV read this step: sliding layers min(ctx, 512) keys, global layers all keys, fp32 K + V
         ctx = pos[act] + 1
         kv_bytes += float((28 * np.minimum(ctx, 512) * 256 * 8 + 7 * ctx * 512 * 8).sum())
@@ -432,7 +438,7 @@ def run_ours(args, dist):
             gemm_ops += cnt * ops_g
     gemm_tops = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms else 0.0
 
-    batched = batched_serving(m, dist) if not args.no_batched else None
+    batched = batched_serving(m, dist, profile_step=20 if args.profile_range else None) if not args.no_batched else None
     attention = attention_bench(g4, hbm_peak) if not args.no_attention else None
 
     # long context: prefill 16384 then decode
@@ -498,8 +504,8 @@ def main():
     ap.add_argument("--no-batched", action="store_true", help="skip the 64-sequence serving run (config 5)")
     ap.add_argument("--no-attention", action="store_true", help="skip the attention sweep (config 4)")
     ap.add_argument("--profile-range", action="store_true",
-                    help="open the profiler capture range around the timed decode steps only "
-                         "(for ncu --profile-from-start off)")
+                    help="open the profiler capture range around the timed decode steps and one "
+                         "64-sequence serving step (step 20) only (for ncu --profile-from-start off)")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)
     if args.impl == "reference":

@@ -92,10 +92,11 @@ struct g4_ctx {
     cudaGraphExec_t g_decode = nullptr;
     int graph_cur = 0;
     bool decode_warm = false;
-    // multi-sequence steps (one row per sequence): one graph per row count;
-    // the first step of a row count runs eagerly, the next one is captured
+    // multi-sequence steps (one row per sequence): one graph per row count,
+    // captured once that count has run kRowGraphAfter steps eagerly (a capture
+    // costs ~10 ms of host time; serving shifts its batch size every few steps)
     std::vector<cudaGraphExec_t> g_rows;
-    std::vector<char> rows_warm;
+    std::vector<int> rows_warm;
     int rows_cur = 0;
     cudaEvent_t events[16] = {};
     // persistent single-token decode (g4_decode.cu)
@@ -778,6 +779,8 @@ cudaError_t enqueue_small(g4_ctx *c, int T, int start_pos, const int *pos_dev, P
 
 // Multi-sequence batch: rows carry their own (sequence, position) (single-token
 // rows of several sequences), or all rows are one sequence `seq` from start_pos.
+constexpr int kRowGraphAfter = 32;   // eager steps of a row count before its graph is captured
+
 struct BatchPlan {
     bool rows;
     int seq;
@@ -1602,7 +1605,7 @@ int g4_forward_batch(g4_ctx *c, int n, const int *seq_ids, const int *tokens, co
             c->g_rows.resize(T + 1, nullptr);
             c->rows_warm.resize(T + 1, 0);
         }
-        if (!c->g_rows[T] && c->rows_warm[T]) {
+        if (!c->g_rows[T] && c->rows_warm[T] >= kRowGraphAfter) {
             cudaGraph_t g = nullptr;
             CK(cudaStreamBeginCapture(c->st, cudaStreamCaptureModeThreadLocal));
             cudaError_t e = enqueue_prefill(c, T, start_pos[0], &bp);
@@ -1625,7 +1628,7 @@ int g4_forward_batch(g4_ctx *c, int n, const int *seq_ids, const int *tokens, co
         } else {
             cudaError_t e = enqueue_prefill(c, T, start_pos[0], &bp);
             if (e) return fail(c, G4_ERR_CUDA, "forward_batch launch: %s", cudaGetErrorString(e));
-            c->rows_warm[T] = 1;
+            c->rows_warm[T]++;
         }
     } else {
         cudaError_t e = enqueue_prefill(c, T, start_pos[0], &bp);

@@ -92,3 +92,31 @@ def test_batch_api_errors(g4, image):
         m.forward_batch([0, 1], [[5], [6]], [0, 0])
         _, am = m.logits_batch()
         assert am.shape == (2,)
+
+
+def test_batch_step_graph_replay_equals_eager(g4, image):
+    """After 32 eager steps of one row count the step is captured as a CUDA
+    graph and replayed; replayed steps give the bits of eager steps
+    (G4_OPT_GRAPHS 0) on the same inputs."""
+    rng = np.random.default_rng(43)
+    prompts = [rng.integers(0, g4.VOCAB, size=n).astype(np.int32) for n in (7, 12)]
+    runs = []
+    for graphs in (1, 0):
+        with g4.Model(image) as m:
+            m.set_option(g4.OPT_GRAPHS, graphs)
+            m.seq_alloc(2, 256)
+            nxt = []
+            for i, p in enumerate(prompts):
+                m.forward_batch([i], [p], [0])
+                nxt.append(int(m.logits_batch()[1][0]))
+            pos = [len(p) for p in prompts]
+            out = []
+            for _ in range(36):
+                m.forward_batch([0, 1], [[t] for t in nxt], pos)
+                lg, am = m.logits_batch(want_logits=True)
+                out.append(lg.copy())
+                nxt = [int(a) for a in am]
+                pos = [p + 1 for p in pos]
+            runs.append(out)
+    for a, b in zip(*runs):
+        assert np.array_equal(a.view(np.uint32), b.view(np.uint32))

@@ -209,11 +209,19 @@ G4_DEV void attn_split_core(const AttnArgs &a, const float *kc, const float *vc,
             for (int off = KT; off < 32; off <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
             if (key_lane < nt) s = acc;
         }
-        const float mt = warp_max(s);
+        // the tile's KT scores sit in lanes differing in their low log2(KT) bits, so
+        // the reductions need only those levels (the dropped levels of the full
+        // butterfly take maxima of equal values and add zeros: same bits)
+        float mt = s;
+#pragma unroll
+        for (int off = KT / 2; off >= 1; off >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, off));
         const float mn = fmaxf(m, mt);
         const float corr = (m == -INFINITY) ? 0.0f : expf(m - mn);
         const float pj = (key_lane < nt && dpart == 0) ? expf(s - mn) : 0.0f;
-        l = l * corr + warp_sum(pj);
+        float ps = pj;   // nonzero in lanes 0 .. KT-1 only; lane 0's sum is the one kept
+#pragma unroll
+        for (int off = KT / 2; off >= 1; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
+        l = l * corr + ps;
         m = mn;
 #pragma unroll
         for (int i = 0; i < NV; i++) {

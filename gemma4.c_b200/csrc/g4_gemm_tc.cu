@@ -426,6 +426,57 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---- peak of the int8 tensor pipe -----------------------------------------------
+// Back-to-back tcgen05.mma kind::i8 (M 128, N 256, K 32) from two zero tiles in
+// shared memory (128-byte swizzle, as the GEMM's) into one TMEM accumulator,
+// committed once at the end; one CTA per SM. Throughput does not depend on the
+// operand values, so this is the measured denominator for the GEMM's int8 rate.
+constexpr int kPeakN = 256;
+constexpr uint32_t kPeakIdesc = (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(kPeakN >> 3) << 17) |
+                                ((uint32_t)(kBM >> 4) << 24);
+constexpr int kPeakSmem = kBM * kBK + kPeakN * kBK + 64 + 1024;
+
+__global__ void __launch_bounds__(128, 1) k_mma_peak(int iters, int *err) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint8_t *A = smem, *B = smem + kBM * kBK;
+    uint64_t *bar = (uint64_t *)(B + kPeakN * kBK);
+    uint32_t *slot = (uint32_t *)(bar + 1);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    for (int i = tid; i < (kBM + kPeakN) * kBK / 16; i += 128) ((int4 *)smem)[i] = make_int4(0, 0, 0, 0);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // the zeros, visible to the tensor core
+    if (tid == 0) {
+        mbar_init(bar, 1);
+        mbar_fence_init();
+    }
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(slot)),
+                     "r"(kPeakN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *slot;
+    if (tid == 0) {
+        const uint64_t da = umma_desc(A, 0), db = umma_desc(B, 0);
+        for (int i = 0; i < iters; i++) {
+            const uint64_t kb = (uint64_t)((i & 3) * 32) >> 4;   // the four 32-byte K chunks of a row
+            mma_i8(tmem, da + kb, db + kb, kPeakIdesc, i != 0);
+        }
+        mma_commit(bar);
+    }
+    __syncwarp();
+    mbar_wait(bar, 0, err, G4D_TIMEOUT_FULL | (0xffa << 8));   // bounded; all MMAs retired
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kPeakN) : "memory");
+    }
+}
+
 // ---- host side ----------------------------------------------------------------
 typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
@@ -492,6 +543,16 @@ bool g4_gemm_tc_supported(const GemmArgs &a) {
     return a.m.sT != nullptr && a.xsT != nullptr && a.T <= G4_XST_STRIDE && a.m.K % kBK == 0 && a.m.N % 32 == 0 &&
            a.T >= 1 && encode_fn() != nullptr && (a.epi == EPI_STORE || a.epi == EPI_GEGLU_PAIR || a.epi == EPI_PLE) &&
            a.dots_out == nullptr;
+}
+
+cudaError_t g4_launch_mma_peak(int iters, int *err, cudaStream_t st, double *ops) {
+    if (iters < 1) return cudaErrorInvalidValue;
+    cudaError_t e = g4_smem_optin((const void *)k_mma_peak, kPeakSmem);
+    if (e != cudaSuccess) return e;
+    const int sms = g4_device_sms();
+    if (ops) *ops = 2.0 * kBM * kPeakN * 32 * (double)iters * sms;
+    k_mma_peak<<<sms, 128, kPeakSmem, st>>>(iters, err);
+    return cudaGetLastError();
 }
 
 cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {

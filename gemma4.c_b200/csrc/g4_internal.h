@@ -119,6 +119,9 @@ bool g4_gemm_skinny_supported(const GemmArgs &a);
 bool g4_gemm_skinny_preferred(const GemmArgs &a);   // supported and faster than the tcgen05 GEMM
 // wm: output rows per block / 16, nt: 8-token tiles per warp (0 = chosen from the shape)
 cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, int wm = 0, int nt = 0);
+// Peak of the int8 tensor pipe (back-to-back tcgen05 kind::i8 MMAs on every SM);
+// *ops receives the int8 operations of the launch
+cudaError_t g4_launch_mma_peak(int iters, int *err, cudaStream_t st, double *ops);
 // cuTensorMapEncodeTiled from the driver (NULL if unavailable)
 void *g4_tmap_encoder();
 

@@ -18,6 +18,7 @@
 cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_gemm_simt(const GemmArgs &a, cudaStream_t st, bool pdl);
 bool g4_gemm_tc_supported(const GemmArgs &a);
+cudaError_t g4_launch_mma_peak(int iters, int *err, cudaStream_t st, double *ops);
 
 namespace {
 
@@ -562,6 +563,35 @@ int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch,
     }
     *ms_per_launch = ms / iters;
     if (bytes_per_launch) *bytes_per_launch = (double)wbytes;
+    return G4_OK;
+}
+
+// Measured int8 tensor peak: k_mma_peak timed with CUDA events after one warm-up
+// launch; TOP/s = ops / time.
+int g4_bench_mma_i8(int iters, float *ms_per_launch, double *ops_per_launch) {
+    if (iters < 1 || iters > (1 << 24) || !ms_per_launch) return G4_ERR_INVALID;
+    DevBuf err;
+    TK(err.alloc(64));
+    TK(cudaMemset(err.p, 0, 64));
+    double ops = 0;
+    TK(g4_launch_mma_peak(iters, (int *)err.p, 0, &ops));
+    TK(cudaDeviceSynchronize());
+    cudaEvent_t e0, e1;
+    TK(cudaEventCreate(&e0));
+    TK(cudaEventCreate(&e1));
+    TK(cudaEventRecord(e0, 0));
+    TK(g4_launch_mma_peak(iters, (int *)err.p, 0, &ops));
+    TK(cudaEventRecord(e1, 0));
+    TK(cudaEventSynchronize(e1));
+    float ms = 0;
+    TK(cudaEventElapsedTime(&ms, e0, e1));
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    int derr = 0;
+    TK(cudaMemcpy(&derr, err.p, 4, cudaMemcpyDeviceToHost));
+    if (derr) return G4_ERR_DEVICE;
+    *ms_per_launch = ms;
+    if (ops_per_launch) *ops_per_launch = ops;
     return G4_OK;
 }
 

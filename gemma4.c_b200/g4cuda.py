@@ -78,6 +78,7 @@ def load(path=LIB_PATH):
     L.g4k_rmsnorm_quant.argtypes = [_f32p, C.c_int, _f32p, C.c_float, vp, _i8p, _f32p]
     L.g4_bench_gemm.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
                                 C.POINTER(C.c_double)]
+    L.g4_bench_mma_i8.argtypes = [C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_double)]
     L.g4_bench_gemv.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
                                 C.POINTER(C.c_double)]
     L.g4k_attention.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, vp, vp, _f32p,
@@ -317,6 +318,14 @@ def bench_gemm(N, K, T, path=3, iters=20):
     L = load()
     ms, ops = C.c_float(), C.c_double()
     _check(L.g4_bench_gemm(N, K, T, path, iters, C.byref(ms), C.byref(ops)))
+    return ms.value, ops.value
+
+
+def bench_mma_i8(iters=20000):
+    """(ms, int8 ops) of one launch of back-to-back tcgen05 kind::i8 MMAs on every SM."""
+    L = load()
+    ms, ops = C.c_float(), C.c_double()
+    _check(L.g4_bench_mma_i8(iters, C.byref(ms), C.byref(ops)))
     return ms.value, ops.value
 
 

@@ -223,6 +223,11 @@ int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch,
  * T <= 64) on T x N x K: average
  * launch duration and int8 operations (2 T N K) per launch. */
 int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch, double *ops_per_launch);
+/* Measured int8 tensor-core peak of this GPU (no reference counterpart: the
+ * denominator of the prefill GEMM's roofline): `iters` back-to-back tcgen05
+ * kind::i8 MMAs (M 128, N 256, K 32) on every SM; duration of one launch and
+ * its int8 operations. */
+int g4_bench_mma_i8(int iters, float *ms_per_launch, double *ops_per_launch);
 /* One attention sub-layer (attention, gemma4.c:411-461) over an FP32 KV ring:
  * hd 256 = sliding layer (window 512, 128 rope pairs), hd 512 = global layer
  * (no window, 64 pairs). qkv[T][10*hd] holds each token's raw q (8 heads) | k | v;

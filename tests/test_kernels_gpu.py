@@ -138,3 +138,13 @@ def test_rmsnorm_quant(g4, oracle):
     # quantising the kernel's own y is exact
     q2, s2 = oracle.quantize(y)
     assert np.array_equal(q, q2) and np.array_equal(s.view(np.uint32), s2.view(np.uint32))
+
+
+def test_mma_i8_peak_runs(g4):
+    """The int8 tensor-pipe microbenchmark (the measured denominator of the
+    prefill GEMM roofline) completes without a device error, and its rate is
+    within a plausible range for a B200 (between 0.5 and 1.2 x the 4.5 POP/s
+    datasheet dense figure)."""
+    ms, ops = g4.bench_mma_i8(4000)
+    tops = ops / (ms * 1e-3) / 1e12
+    assert 0.5 * 4500 < tops < 1.2 * 4500, tops

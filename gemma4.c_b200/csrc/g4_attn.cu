@@ -61,10 +61,13 @@ __global__ void __launch_bounds__(256) k_attn_rows_combine(const AttnArgs a, int
     __shared__ float wsm[512 + 16];
     griddep_launch();
     griddep_wait();
-    const int row = blockIdx.y;
+    const int row = blockIdx.y, W = kHeads * HD;
+    // with quant_out the rows are also quantised for o_proj (one 64-wide group per block)
     attn_combine_part<HD>(a, a.row_pos[row], blockIdx.x, splits, wsm,
-                          a.part + (size_t)row * splits * kHeads * (HD + 4), a.out + (size_t)row * kHeads * HD,
-                          nullptr, nullptr);
+                          a.part + (size_t)row * splits * kHeads * (HD + 4), a.out + (size_t)row * W,
+                          a.quant_out ? a.xq + (size_t)row * W : nullptr,
+                          a.quant_out ? a.xs + (size_t)row * (W / 64) : nullptr,
+                          a.quant_out && a.xsT ? a.xsT + row : nullptr);
 }
 
 // ---------------------------------------------------------------------------

@@ -340,7 +340,8 @@ G4_DEV void attn_rows_split(const AttnArgs &a, int row, int split, int splits, f
 constexpr int kCombineDims = 64;
 template <int HD>
 __device__ __noinline__ void attn_combine_part(const AttnArgs &a, int p, int blk, int splits, float *wsm,
-                                               const float *part_base, float *out, int8_t *xq, float *xs) {
+                                               const float *part_base, float *out, int8_t *xq, float *xs,
+                                               float *xsT = nullptr) {
     float *psum = wsm + 256, *red = wsm + 512;
     const int tid = threadIdx.x;
     int k0, k1;
@@ -407,7 +408,10 @@ __device__ __noinline__ void attn_combine_part(const AttnArgs &a, int p, int blk
     if (tid < kCombineDims) {
         const float sc = quant_scale(fmaxf(red[0], red[1])), inv = quant_inv(sc);
         xq[col0 + dl] = (int8_t)quant_one(o, inv);
-        if (tid == 0) xs[col0 >> 6] = sc;
+        if (tid == 0) {
+            xs[col0 >> 6] = sc;
+            if (xsT) xsT[(size_t)(col0 >> 6) * G4_XST_STRIDE] = sc;   // group-major copy (GEMM operand)
+        }
     }
     attn_sync();
 }

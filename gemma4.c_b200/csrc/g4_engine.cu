@@ -829,6 +829,11 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp
             // (each split's tile loop is latency-bound), or a fixed count
             int sp = c->batch_splits ? c->batch_splits : (4 * c->num_sms + T - 1) / T;
             sp = sp < 16 ? 16 : sp > kSplits ? kSplits : sp;
+            // the combine also quantises the rows for o_proj
+            at.quant_out = 1;
+            at.xq = c->xq;
+            at.xs = c->xs;
+            at.xsT = c->xsT;
             q.ck(g4_launch_attn_rows(at, sp, c->st, q.pdl));
         }
         else if (!c->strict) {

@@ -571,7 +571,8 @@ bool gemm(Seq &q, const DMat &m, int T, int epi, float *out, int out_stride, con
         q.ck(g4_launch_gemm_skinny(a, c->st, q.pdl));
         return false;
     }
-    const bool fuse = fuse_quant && epi == EPI_GEGLU_PAIR && m.N % 128 == 0;
+    // (the transposed-role tiles of a few token rows do not quantise: rows_quant follows)
+    const bool fuse = fuse_quant && epi == EPI_GEGLU_PAIR && m.N % 128 == 0 && !g4_gemm_tc_swapped(a);
     if (fuse) {   // into the second set: this GEMM still reads xq / xs / xsT
         a.qout = c->xq2;
         a.qs = c->xs2;

@@ -302,10 +302,11 @@ bool g4_gemm_skinny_supported(const GemmArgs &a) {
 }
 
 bool g4_gemm_skinny_preferred(const GemmArgs &a) {
-    // measured: faster than the tcgen05 GEMM on every projection shape up to 32
-    // token rows, and up to 64 rows where N < 8192; the lm_head and the wide
-    // gate/up GEMM at 33-64 rows stay on the tensor-core tiles
-    return g4_gemm_skinny_supported(a) && (a.T <= 32 || a.m.N < 8192);
+    // measured against the tcgen05 GEMM with transposed roles (128 weight rows x
+    // the token rows): faster on every shape with N < 8192 and on all shapes up
+    // to 8 token rows; the lm_head, the gate/up and the per-layer model
+    // projection (N >= 8192) at 9-64 rows go to the tensor cores
+    return g4_gemm_skinny_supported(a) && (a.T <= 8 || a.m.N < 8192);
 }
 
 cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, int wm, int nt) {

@@ -163,6 +163,9 @@ struct TcArgs {
     int *err;
     int8_t *qout;           // GEGLU rows quantised (BN 128 only), or NULL
     float *qs, *qsT;
+    // Transposed roles (few token rows): A = 128 weight rows, B = the BN >= T
+    // token rows; a TMEM lane is then an output and a column a token
+    int swap;
 };
 
 template <int BN>
@@ -184,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t *tmem_slot = (uint32_t *)(tempty + kTmemBufs);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int steps = p.K / kBK;
-    const int mt = (p.T + kBM - 1) / kBM, tiles = (p.N / BN) * mt;
+    const int mt = (p.T + kBM - 1) / kBM, tiles = p.swap ? p.N / kBM : (p.N / BN) * mt;
     // persistent: this CTA takes tiles blockIdx.x, + gridDim.x, ...; the m tiles of
     // one n tile are consecutive, so CTAs sharing weights run together (L2 reuse)
     __shared__ int fail, issued, committed;
@@ -224,7 +227,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             int k = 0;   // steps issued so far (all tiles)
             bool ok = true;
             for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
-                const int n0 = (tile / mt) * BN, t0 = (tile % mt) * kBM;
+                // A rows (token rows, or weight rows when swapped) and B rows
+                const int ra = p.swap ? tile * kBM : (tile % mt) * kBM, rb = p.swap ? 0 : (tile / mt) * BN;
+                // per group: BN column scales then 128 row scales (weight / activation,
+                // or activation / weight when swapped)
+                const float *colT = p.swap ? p.xsT + rb : p.wsT + rb, *rowT = p.swap ? p.wsT + ra : p.xsT + ra;
+                const size_t colS = p.swap ? G4_XST_STRIDE : p.N, rowS = p.swap ? p.N : G4_XST_STRIDE;
                 for (int ks = 0; ks < steps; ks++, k++) {
                     const int s = k % kStages, use = k / kStages;
                     if (use > 0 &&
@@ -233,13 +241,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     mbar_arrive_expect_tx(&full[s], kTileBytesA + C::kTileBytesB + C::kScaleBytes);
-                    tma_load_2d(smem + C::kOffA + s * kTileBytesA, &map_a, ks * kBK, t0, &full[s]);
-                    tma_load_2d(smem + C::kOffB + s * C::kTileBytesB, &map_b, ks * kBK, n0, &full[s]);
+                    tma_load_2d(smem + C::kOffA + s * kTileBytesA, &map_a, ks * kBK, ra, &full[s]);
+                    tma_load_2d(smem + C::kOffB + s * C::kTileBytesB, &map_b, ks * kBK, rb, &full[s]);
                     for (int gi = 0; gi < 2; gi++) {
                         bulk_g2s_plain(smem + C::kOffS + s * C::kScaleBytes + gi * BN * 4,
-                                       p.wsT + (size_t)(2 * ks + gi) * p.N + n0, BN * 4, &full[s]);
+                                       colT + (size_t)(2 * ks + gi) * colS, BN * 4, &full[s]);
                         bulk_g2s_plain(smem + C::kOffS + s * C::kScaleBytes + 2 * BN * 4 + gi * kBM * 4,
-                                       p.xsT + (size_t)(2 * ks + gi) * G4_XST_STRIDE + t0, kBM * 4, &full[s]);
+                                       rowT + (size_t)(2 * ks + gi) * rowS, kBM * 4, &full[s]);
                     }
                 }
             }
@@ -291,7 +299,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         int tcount = -1;   // tiles of this CTA so far (parity of the quantisation exchange)
         for (int tile = blockIdx.x; tile < tiles && ok; tile += gridDim.x) {
             tcount++;
-            const int n0 = (tile / mt) * BN, t = (tile % mt) * kBM + row;
+            const int n0 = p.swap ? tile * kBM + row : (tile / mt) * BN;   // swapped: this lane's output
+            const int t = p.swap ? 0 : (tile % mt) * kBM + row;
             uint64_t acc[CW / 2];
 #pragma unroll
             for (int j = 0; j < CW / 2; j++) acc[j] = 0ull;
@@ -324,6 +333,43 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (lane == 0) mbar_arrive(&empty[s]);
             }
             if (!ok) continue;
+            if (p.swap) {
+                // lane = output n0, columns = token rows cb * CW + j (the chain's product
+                // xs * ws equals ws * xs: IEEE multiplication commutes)
+                const int n = n0, tb = cb * CW;
+                if (p.epi == EPI_GEGLU_PAIR) {
+#pragma unroll
+                    for (int j = 0; j < CW / 2; j++) {
+                        const float2 a = upk(acc[j]);
+                        const float u0 = __shfl_down_sync(0xffffffffu, a.x, 1);   // row n + 1 = the up row
+                        const float u1 = __shfl_down_sync(0xffffffffu, a.y, 1);
+                        if (n & 1) continue;
+                        const int t0 = tb + 2 * j;
+                        if (t0 < p.T)
+                            p.out[(size_t)t0 * p.out_stride + (n >> 1)] =
+                                geglu_one(a.x, u0, gelu_s, kGeluSize, -8.0f, 8.0f, 4095.0f / 16.0f);
+                        if (t0 + 1 < p.T)
+                            p.out[(size_t)(t0 + 1) * p.out_stride + (n >> 1)] =
+                                geglu_one(a.y, u1, gelu_s, kGeluSize, -8.0f, 8.0f, 4095.0f / 16.0f);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < CW / 2; j++) {
+                        const float2 a = upk(acc[j]);
+#pragma unroll
+                        for (int h = 0; h < 2; h++) {
+                            const int tt = tb + 2 * j + h;
+                            if (tt >= p.T) continue;
+                            float v = h ? a.y : a.x;
+                            if (p.epi == EPI_PLE)
+                                v = geglu_one(v, p.ple_u[(size_t)tt * p.u_stride + n], gelu_s, kGeluSize, -8.0f,
+                                              8.0f, 4095.0f / 16.0f);
+                            p.out[(size_t)tt * p.out_stride + n] = v;
+                        }
+                    }
+                }
+                continue;
+            }
             const int nb = n0 + cb * CW;
             const bool qexch = p.epi == EPI_GEGLU_PAIR && BN == 128 && p.qout;   // every lane takes part
             if (t >= p.T && !qexch) continue;
@@ -530,7 +576,7 @@ cudaError_t launch_bn(const CUtensorMap &ma, const CUtensorMap &mb, const TcArgs
         cudaError_t e = g4_smem_optin((const void *)k_gemm_tc<BN>, TcCfg<BN>::kSmemBytes);
         if (e != cudaSuccess) return e;
     }
-    const int tiles = (p.N / BN) * ((p.T + kBM - 1) / kBM);
+    const int tiles = p.swap ? p.N / kBM : (p.N / BN) * ((p.T + kBM - 1) / kBM);
     k_gemm_tc<BN><<<tiles < sms ? tiles : sms, kThreads, TcCfg<BN>::kSmemBytes, st>>>(ma, mb, p);
     return cudaGetLastError();
 }
@@ -555,16 +601,25 @@ cudaError_t g4_launch_mma_peak(int iters, int *err, cudaStream_t st, double *ops
     return cudaGetLastError();
 }
 
+bool g4_gemm_tc_swapped(const GemmArgs &a) {
+    // up to 64 token rows: the weights fill the MMA's 128 rows and the tokens its N
+    return g4_gemm_tc_supported(a) && a.T <= 64 && a.m.N % kBM == 0 && !a.qout;
+}
+
 cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
     (void)pdl;
     if (!g4_gemm_tc_supported(a)) return cudaErrorNotSupported;
     const int sms = g4_device_sms();
-    const bool fuse_q = a.epi == EPI_GEGLU_PAIR && a.qout && a.qs && a.m.N % 128 == 0;
-    const int bn = fuse_q ? 128 : pick_bn(a.m.N, (a.T + kBM - 1) / kBM, sms);
+    const bool swap = g4_gemm_tc_swapped(a);
+    const bool fuse_q = !swap && a.epi == EPI_GEGLU_PAIR && a.qout && a.qs && a.m.N % 128 == 0;
+    const int bn = swap ? (a.T <= 32 ? 32 : 64) : fuse_q ? 128 : pick_bn(a.m.N, (a.T + kBM - 1) / kBM, sms);
     CUtensorMap ma, mb;
-    // activation rows beyond T are read but their outputs are not stored
-    if (!make_map(&ma, a.xq, a.m.K, a.T, kBM) || !make_map(&mb, a.m.w, a.m.K, a.m.N, bn)) return cudaErrorInvalidValue;
+    // rows of either operand beyond its extent read as zero and are not stored
+    if (swap ? (!make_map(&ma, a.m.w, a.m.K, a.m.N, kBM) || !make_map(&mb, a.xq, a.m.K, a.T, bn))
+             : (!make_map(&ma, a.xq, a.m.K, a.T, kBM) || !make_map(&mb, a.m.w, a.m.K, a.m.N, bn)))
+        return cudaErrorInvalidValue;
     TcArgs p{};
+    p.swap = swap ? 1 : 0;
     p.T = a.T;
     p.N = a.m.N;
     p.K = a.m.K;

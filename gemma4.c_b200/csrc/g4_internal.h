@@ -115,6 +115,7 @@ struct GemmArgs {
 
 // Small-batch GEMM (g4_gemm_skinny.cu): T <= G4_SKINNY_MAX_T token rows.
 constexpr int G4_SKINNY_MAX_T = 64;
+bool g4_gemm_tc_swapped(const GemmArgs &a);   // the tcgen05 GEMM runs with transposed roles (T <= 64)
 bool g4_gemm_skinny_supported(const GemmArgs &a);
 bool g4_gemm_skinny_preferred(const GemmArgs &a);   // supported and faster than the tcgen05 GEMM
 // wm: output rows per block / 16, nt: 8-token tiles per warp (0 = chosen from the shape)

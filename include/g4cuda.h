@@ -117,9 +117,10 @@ const char *g4_strerror(int code);
 /* Options (g4_set_option): */
 #define G4_OPT_GRAPHS 1      /* capture single-token decode in a CUDA graph (default 1) */
 #define G4_OPT_PDL 2         /* programmatic dependent launch between kernels (default 1) */
-#define G4_OPT_GEMM_PATH 3   /* prefill GEMM: 0 auto (small-batch mma up to 32 token rows,
-                                or 64 when N < 8192; else tcgen05), 1 SIMT dp4a,
-                                2 tcgen05, 3 small-batch mma wherever it applies (T <= 64) */
+#define G4_OPT_GEMM_PATH 3   /* prefill GEMM: 0 auto (small-batch mma for T <= 64 rows when
+                                N < 8192 or T <= 8; else tcgen05, with transposed roles
+                                up to 64 rows), 1 SIMT dp4a, 2 tcgen05, 3 small-batch mma
+                                wherever it applies (T <= 64) */
 #define G4_OPT_LAYERS 4      /* run only the first N layers (testing aid; default 35) */
 /* Reference-order arithmetic (default 0): RMSNorm sums of squares, attention
  * scores, softmax and value sums are evaluated in gemma4.c's sequential order

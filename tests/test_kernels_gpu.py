@@ -86,12 +86,14 @@ def test_gemm_simt_bitexact(g4, oracle, T, N, K):
     assert np.array_equal(out.view(np.uint32), oracle.linear(xq, xs, wp, sp, N, K).view(np.uint32))
 
 
-@pytest.mark.parametrize("T", [1, 5, 130, 512])
+@pytest.mark.parametrize("T", [1, 5, 33, 64, 130, 512])
 @pytest.mark.parametrize("N,K", [(2560, 1536), (1536, 4096), (1536, 256), (12288, 1536), (1536, 12288),
                                  (256, 1536), (2048, 1536)])
 def test_gemm_tcgen05_bitexact(g4, oracle, T, N, K):
     """tcgen05 kind::i8 GEMM: exact int32 group dots on the tensor core, the
-    reference's ordered fp32 chain in the epilogue -> bit-identical output."""
+    reference's ordered fp32 chain in the epilogue -> bit-identical output.
+    Up to 64 token rows it runs with transposed roles (128 weight rows as the
+    MMA's M, the tokens as its N = 32 or 64)."""
     rng = np.random.default_rng(7 * T + N + K)
     _, _, wp, sp = packed_case(rng, N, K)
     xq, xs = oracle.quantize(activations(rng, T, K))

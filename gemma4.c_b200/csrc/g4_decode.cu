@@ -321,6 +321,9 @@ G4_DEV __noinline__ void gemv_op(const GemvArgs &a, const CtaRows cr, int pro, i
             const int r = lane < cr.rows ? lane : cr.rows - 1;
             const uint16_t *sr = S + r * G;
             float acc = 0.0f;
+            // unrolled so that later groups' loads issue while the chain runs
+            // (the chain order itself is unchanged)
+#pragma unroll 4
             for (int g = 0; g < G; g += 4) {
                 const uint2 s4 = *(const uint2 *)(sr + g);
                 const float4 x4 = *(const float4 *)(xs + g);

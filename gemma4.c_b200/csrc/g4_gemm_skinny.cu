@@ -14,19 +14,23 @@
 // work unit is a block of 16 x WM consecutive output rows (one contiguous byte
 // run of W) x every token row; persistent CTAs walk blocks blockIdx.x,
 // + gridDim.x, ... with one ring whose phases run on from block to block:
-//   - one producer lane, per stage of four groups: the block's weight tile
-//     (one 64-byte group x 16 WM rows per box, so a row is 64 bytes in shared
-//     memory and the fragment loads below are bank-conflict free), the
-//     activation tile (64 bytes x Tp token rows; rows >= T are zero-filled by
-//     the tensor map), and the groups' weight and activation scales (fp32,
-//     group-major). The weight boxes of the first stages are issued before
-//     waiting for the previous kernel (programmatic dependent launch): they
-//     do not depend on it.
+//   - one producer lane, per stage of GS = 8 groups (4 when K % 512 != 0):
+//     the block's weight tile (16 WM rows x 64 GS bytes; the int8 matrix is
+//     viewed as 16-bit elements so that one box row, i.e. one TMA row
+//     request, carries 512 bytes: 64-byte rows made the copy engine the
+//     limiter), the activation tile (Tp token rows x 64 GS bytes; rows >= T
+//     are zero-filled by the tensor map), and the groups' weight and
+//     activation scales (fp32, group-major). The weight boxes of the first
+//     stages are issued before waiting for the previous kernel (programmatic
+//     dependent launch): they do not depend on it.
 //   - consumer warp (rb, tg): output rows 16 rb .. 16 rb + 15 of the block x
 //     token rows 8 NT tg ..; per group and 8-token tile two mma.sync
 //     m16n8k32 (s8 x s8 -> s32) give the exact group dots in registers, and
 //     the lane advances its four fp32 chains right away (packed f32x2, each
-//     lane of the pair rounds like fmaf).
+//     lane of the pair rounds like fmaf). The legacy mma.sync path runs at
+//     ~60-80 cycles per m16n8k32 per scheduler on sm_100a, which is what
+//     bounds this kernel (measured per stage); for wide N the tcgen05 GEMM
+//     with transposed roles takes over (g4_gemm_skinny_preferred).
 // Fragment order: the int32 dot does not depend on the order of its 64
 // products, so a lane loads 16 contiguous bytes of its weight row (bytes
 // 16 q .. 16 q + 15 of the group, q = lane % 4) and of its token row and

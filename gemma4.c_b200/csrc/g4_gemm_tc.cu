@@ -26,6 +26,11 @@
 //               its 32 fp32 chains with the weight and activation scales
 //               staged by the producer, then applies the output epilogue
 //               (store, GEGLU pair, PLE gate).
+// Up to 64 token rows the roles are transposed (TcArgs::swap): A is a tile of
+// 128 weight rows and B the token rows padded to BN = 32 or 64, so a TMEM
+// lane is an output and a column a token; the stage's column scales are then
+// the activations' and the row scales the weights' (the chain's product
+// xs * ws equals ws * xs), and the epilogue stores per (token, output).
 // Waits are bounded (mbar_wait); on a timeout every role leaves its loop, the
 // CTA drains the copies and MMAs it issued, and TMEM is freed.
 #include <cuda.h>

@@ -78,7 +78,7 @@ __host__ __device__ inline Layout make_layout(int K, int T, int pro) {
 template <int T, int PRO, int EPI>
 __global__ void __launch_bounds__(kThreads, 2) k_gemv(const GemvArgs a) {
     extern __shared__ __align__(128) uint8_t smem[];
-    const int K = a.m.K, N = a.m.N, G = K >> 6, NC = K >> 8;
+    const int K = a.m.K, N = a.m.N, G = K >> 6;
     const Layout L = make_layout(K, T, PRO);
     const int R = L.R, S = L.S, PPS = L.R / 2;   // pairs per stage
     uint8_t *ring = smem + L.off_ring;

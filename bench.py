@@ -2,7 +2,7 @@
 """Benchmark of the gemma4.c forward path on B200 (libg4cuda.so).
 
 Headline (one JSON line on rank 0): decode tok/s at context 512, the
-reference's `./run --bench 512 128` decode figure (README.md:76) — one step is
+reference's `./run --bench 512 128` decode figure (the reference's README.md:76) — one step is
 one token: forward(1 token) + logits, on the synthetic Gemma 4 E2B model of
 BASELINE config 1 (random-init weights in gemma4.c's .bin layout, seed 0; the
 real checkpoint is not available). Alongside: prefill tok/s at 512 and 16384,
@@ -35,7 +35,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "gemma4.c_b200"))
 
-PUBLISHED_DECODE_512 = 25.16   # README.md:76, tg128 @ d512, Ryzen 7 7700, 8 threads
+PUBLISHED_DECODE_512 = 25.16   # the reference's README.md:76: tg128 @ d512, Ryzen 7 7700, 8 threads
 INT8_DENSE_TOPS = 4500.0       # B200 datasheet dense int8 (reported beside the measured peak)
 # prefill GEMM shapes of one token through the model: (N, K, count) over the 35 layers
 # + per_layer_model_projection; lm_head is not part of a prefill chunk

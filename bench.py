@@ -4,7 +4,7 @@
 Headline (one JSON line on rank 0): decode tok/s at context 512, the
 reference's `./run --bench 512 128` decode figure (the reference's README.md:76) — one step is
 one token: forward(1 token) + logits, on the synthetic Gemma 4 E2B model of
-BASELINE config 1 (random-init weights in gemma4.c's .bin layout, seed 0; the
+benchmark config 1 (random-init weights in gemma4.c's .bin layout, seed 0; the
 real checkpoint is not available). Alongside: prefill tok/s at 512 and 16384,
 decode tok/s at 16384, the HBM roofline of the decode step kernel, the int8
 tensor-core roofline of the prefill GEMM, and the reference CPU path timed on
@@ -274,7 +274,7 @@ def prefill_timed(m, n, reps, dist):
 
 
 def batched_serving(m, dist, seqs=64, profile_step=None):
-    """BASELINE config 5 on this GPU: 64 independent sequences, prompts
+    """Benchmark config 5 (multi-sequence serving) on this GPU: 64 independent sequences, prompts
     log-uniform in [128, 8192], decode lengths uniform in [32, 512], ids
     uniform (seed 2 + rank). Each prompt is prefilled (512-token chunks) and its
     first token sampled; then all unfinished sequences decode together, one
@@ -339,7 +339,7 @@ def batched_serving(m, dist, seqs=64, profile_step=None):
 
 
 def attention_bench(g4, hbm_peak, prefill_iters=10, decode_iters=50):
-    """Attention over the FP32 KV ring at contexts 512..16384:
+    """Attention over the FP32 KV ring at contexts 512..16384 (benchmark config 4):
     per layer kind, the last 512-token prefill chunk of a context (causal over
     the chunk, start = ctx - 512) and one decode token at position ctx - 1, each
     timed with CUDA events over repeated launches (post-processed q, filled

@@ -1,6 +1,6 @@
 """Kernel-level parity on the GPU, through the C ABI, against the oracle.
 
-Bar (BASELINE north_star): the int8 dot products (int32 per token, row and
+Bar: the int8 dot products (int32 per token, row and
 64-group) and the quantised activations are bit-exact; the dequantised fp32
 GEMV/GEMM outputs are bit-exact too, because the kernels reproduce the
 reference's per-group FMA chain (gemma4.c:218); RMSNorm outputs are within

@@ -39,6 +39,7 @@
 // both fragment layouts), so each MMA pair sums exactly the group's products.
 #include <cuda.h>
 
+#include "../../include/g4cuda.h"
 #include "g4_common.cuh"
 #include "g4_internal.h"
 
@@ -283,6 +284,40 @@ void pick_tiling(int N, int T, int sms, int *wm_out, int *nt_out) {
     *nt_out = nt;
 }
 
+// Launch geometry of an N x K GEMM over T token rows (wm, nt: 0 = chosen from
+// the shape): tiling, staged layout and ring depth into p, threads per CTA,
+// dynamic shared memory. False when the combination does not fit.
+bool plan(int N, int K, int T, int sms, int wm, int nt, SkArgs &p, int &threads, int &smem) {
+    if (T < 1 || T > G4_SKINNY_MAX_T || K % 256 || N % 16) return false;
+    if (wm <= 0 || nt <= 0) {
+        int w, n;
+        pick_tiling(N, T, sms, &w, &n);
+        if (wm <= 0) wm = w;
+        if (nt <= 0) nt = n;
+    }
+    if (nt != 1 && nt != 2 && nt != 4) return false;
+    const int wt = (T + 8 * nt - 1) / (8 * nt);
+    if (wm * wt > kMaxWarps || N % (16 * wm)) return false;
+    p.T = T;
+    p.N = N;
+    p.K = K;
+    p.tp = wt * 8 * nt;
+    p.wm = wm;
+    p.wt = wt;
+    const int RB = 16 * wm;
+    p.gs = K % (64 * kMaxGS) == 0 ? kMaxGS : 4;
+    const int RW = 64 * p.gs;
+    p.off_x = (uint32_t)(RB * RW);
+    p.off_ws = p.off_x + (uint32_t)(p.tp * RW);
+    p.off_xs = p.off_ws + (uint32_t)(p.gs * RB * 4);
+    p.stage_bytes = p.off_xs + (uint32_t)(p.gs * p.tp * 4);
+    const int stages = kStageBudget / (int)p.stage_bytes;
+    p.stages = stages < 2 ? 2 : stages > 8 ? 8 : stages;
+    threads = 32 * (p.wm * p.wt + 1);
+    smem = p.stages * (int)p.stage_bytes + 2 * p.stages * 8 + 128;
+    return smem <= kSmemMax;
+}
+
 template <int NT>
 cudaError_t launch_nt(const CUtensorMap (&maps)[4], const SkArgs &p, int blocks, cudaStream_t st, bool pdl) {
     const int threads = 32 * (p.wm * p.wt + 1);
@@ -315,31 +350,11 @@ bool g4_gemm_skinny_preferred(const GemmArgs &a) {
 
 cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, int wm, int nt) {
     if (!g4_gemm_skinny_supported(a)) return cudaErrorNotSupported;
-    if (wm <= 0 || nt <= 0) {
-        int w, n;
-        pick_tiling(a.m.N, a.T, g4_device_sms(), &w, &n);
-        if (wm <= 0) wm = w;
-        if (nt <= 0) nt = n;
-    }
-    if (nt != 1 && nt != 2 && nt != 4) return cudaErrorInvalidValue;
-    const int wt = (a.T + 8 * nt - 1) / (8 * nt);
-    if (wm * wt > kMaxWarps || a.m.N % (16 * wm)) return cudaErrorInvalidValue;
     SkArgs p{};
-    p.T = a.T;
-    p.N = a.m.N;
-    p.K = a.m.K;
-    p.tp = wt * 8 * nt;
-    p.wm = wm;
-    p.wt = wt;
-    const int RB = 16 * wm, G = a.m.K / 64;
-    p.gs = a.m.K % (64 * kMaxGS) == 0 ? kMaxGS : 4;
-    const int RW = 64 * p.gs;
-    p.off_x = (uint32_t)(RB * RW);
-    p.off_ws = p.off_x + (uint32_t)(p.tp * RW);
-    p.off_xs = p.off_ws + (uint32_t)(p.gs * RB * 4);
-    p.stage_bytes = p.off_xs + (uint32_t)(p.gs * p.tp * 4);
-    int stages = kStageBudget / (int)p.stage_bytes;
-    p.stages = stages < 2 ? 2 : stages > 8 ? 8 : stages;
+    int threads = 0, smem = 0;
+    if (!plan(a.m.N, a.m.K, a.T, g4_device_sms(), wm, nt, p, threads, smem)) return cudaErrorInvalidValue;
+    nt = p.tp / (8 * p.wt);
+    const int RB = 16 * p.wm, G = a.m.K / 64, RW = 64 * p.gs;
     p.epi = a.epi;
     p.out = a.out;
     p.out_stride = a.out_stride;
@@ -361,4 +376,18 @@ cudaError_t g4_launch_gemm_skinny(const GemmArgs &a, cudaStream_t st, bool pdl, 
     case 2: return launch_nt<2>(maps, p, blocks, st, pdl);
     default: return launch_nt<1>(maps, p, blocks, st, pdl);
     }
+}
+
+// Launch geometry of the small-batch GEMM for an N x K matrix over T token rows
+// as the engine would run it (host only: no CUDA call beyond the SM count).
+extern "C" int g4_skinny_plan(int N, int K, int T, int *wm, int *nt, int *stages, int *threads, int *smem_bytes) {
+    SkArgs p{};
+    int th = 0, sm = 0;
+    if (!plan(N, K, T, g4_device_sms(), 0, 0, p, th, sm)) return G4_ERR_INVALID;
+    if (wm) *wm = p.wm;
+    if (nt) *nt = p.tp / (8 * p.wt);
+    if (stages) *stages = p.stages;
+    if (threads) *threads = th;
+    if (smem_bytes) *smem_bytes = sm;
+    return G4_OK;
 }

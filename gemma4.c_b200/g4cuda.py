@@ -79,6 +79,7 @@ def load(path=LIB_PATH):
     L.g4_bench_gemm.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
                                 C.POINTER(C.c_double)]
     L.g4_bench_mma_i8.argtypes = [C.c_int, C.POINTER(C.c_float), C.POINTER(C.c_double)]
+    L.g4_skinny_plan.argtypes = [C.c_int] * 3 + [C.POINTER(C.c_int)] * 5
     L.g4_bench_gemv.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_float),
                                 C.POINTER(C.c_double)]
     L.g4k_attention.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _f32p, vp, vp, _f32p,
@@ -319,6 +320,14 @@ def bench_gemm(N, K, T, path=3, iters=20):
     ms, ops = C.c_float(), C.c_double()
     _check(L.g4_bench_gemm(N, K, T, path, iters, C.byref(ms), C.byref(ops)))
     return ms.value, ops.value
+
+
+def skinny_plan(N, K, T):
+    """Launch geometry of the small-batch GEMM: dict(wm, nt, stages, threads, smem)."""
+    L = load()
+    v = [C.c_int() for _ in range(5)]
+    _check(L.g4_skinny_plan(N, K, T, *[C.byref(x) for x in v]))
+    return dict(zip(("wm", "nt", "stages", "threads", "smem"), (x.value for x in v)))
 
 
 def bench_mma_i8(iters=20000):

@@ -224,6 +224,12 @@ int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch,
  * T <= 64) on T x N x K: average
  * launch duration and int8 operations (2 T N K) per launch. */
 int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch, double *ops_per_launch);
+/* Launch geometry the small-batch GEMM (T <= 64 token rows) would use for an
+ * N x K matrix (no reference counterpart; host-side planning, no kernel runs):
+ * output rows per unit / 16 (wm), 8-token tiles per warp (nt), ring stages,
+ * threads per CTA and dynamic shared memory. G4_ERR_INVALID when the shape is
+ * not supported or does not fit. */
+int g4_skinny_plan(int N, int K, int T, int *wm, int *nt, int *stages, int *threads, int *smem_bytes);
 /* Measured int8 tensor-core peak of this GPU (no reference counterpart: the
  * denominator of the prefill GEMM's roofline): `iters` back-to-back tcgen05
  * kind::i8 MMAs (M 128, N 256, K 32) on every SM; duration of one launch and

@@ -94,3 +94,30 @@ def test_library_has_no_cpu_fallback(g4):
     out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=120)
     rc = int(out.stdout.strip().splitlines()[-1])
     assert rc in (-2, -3)   # format error (zero records) or CUDA unavailable — never success
+
+
+# every (N, K) the engine runs through the small-batch GEMM (o/down with both
+# head and MLP widths, q/k/v fused and q-only, gate/up, PLE, model projection, lm_head)
+_SKINNY_SHAPES = [(2560, 1536), (5120, 1536), (2048, 1536), (4096, 1536), (1536, 2048), (1536, 4096),
+                  (12288, 1536), (24576, 1536), (1536, 6144), (1536, 12288), (256, 1536), (1536, 256),
+                  (8960, 1536), (262144, 1536)]
+
+
+def test_skinny_plan_fits_every_shape(g4):
+    """The small-batch GEMM's launch geometry (host-side planning, the same
+    function the launcher uses) fits the 200 KB shared-memory opt-in and the
+    15 consumer warps for every model shape at every row count 1..64, covers
+    each unit's token rows, and picks the measured tiling on known shapes."""
+    for N, K in _SKINNY_SHAPES:
+        for T in range(1, 65):
+            pl = g4.skinny_plan(N, K, T)
+            warps = pl["threads"] // 32 - 1
+            assert 1 <= warps <= 15 and pl["smem"] <= 200 * 1024 and 2 <= pl["stages"] <= 8
+            assert N % (16 * pl["wm"]) == 0
+            assert warps % pl["wm"] == 0 and (warps // pl["wm"]) * 8 * pl["nt"] >= T   # token rows covered
+    assert (g4.skinny_plan(1536, 12288, 32)["wm"], g4.skinny_plan(1536, 12288, 32)["nt"]) == (1, 1)
+    assert (g4.skinny_plan(12288, 1536, 8)["wm"], g4.skinny_plan(12288, 1536, 8)["nt"]) == (8, 1)
+    assert (g4.skinny_plan(2560, 1536, 31)["wm"], g4.skinny_plan(2560, 1536, 31)["nt"]) == (2, 2)
+    for bad in ((1536, 1536, 65), (1536, 1536, 0), (1536, 100, 8), (1540, 1536, 8)):
+        with pytest.raises(g4.G4Error):
+            g4.skinny_plan(*bad)

@@ -229,6 +229,8 @@ struct Pre {
         return s >= pre[j] ? 2 * b : 2 * b + 1;
     }
 };
+static_assert(Pre<256>::kSmem <= 227 * 1024 && Pre<512>::kSmem <= 227 * 1024,
+              "shared memory budget of the prefill attention CTA");
 
 // Quantise (gemma4.c:265-279) one 64-wide group held as 4 values in each of 16
 // consecutive lanes: the group's max |x| over the 16 lanes, then scale and

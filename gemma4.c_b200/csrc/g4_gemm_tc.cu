@@ -73,6 +73,10 @@ struct TcCfg {
                                        ((uint32_t)(kBM >> 4) << 24);
 };
 
+static_assert(TcCfg<128>::kSmemBytes <= 227 * 1024 && TcCfg<64>::kSmemBytes <= 227 * 1024 &&
+                  TcCfg<32>::kSmemBytes <= 227 * 1024,
+              "shared memory budget of the GEMM tiles");
+
 G4_DEV void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(

@@ -42,6 +42,18 @@ INT8_DENSE_TOPS = 4500.0       # B200 datasheet dense int8 (reported beside the 
 PREFILL_SHAPES = ((2560, 1536, 12), (5120, 1536, 3), (2048, 1536, 16), (4096, 1536, 4),
                   (1536, 2048, 28), (1536, 4096, 7), (12288, 1536, 15), (24576, 1536, 20),
                   (1536, 6144, 15), (1536, 12288, 20), (256, 1536, 35), (1536, 256, 35), (8960, 1536, 1))
+# benchmark config 2: every projection shape of one layer (both head widths and
+# MLP widths), the fused shapes the engine streams, and the lm_head
+GEMV_SHAPES = (("q_sliding", 2048, 1536), ("q_global", 4096, 1536), ("kv_sliding", 256, 1536),
+               ("kv_global", 512, 1536), ("qkv_fused_sliding", 2560, 1536), ("o_sliding", 1536, 2048),
+               ("o_global", 1536, 4096), ("gate_up_6144", 6144, 1536), ("gate_up_12288", 12288, 1536),
+               ("gate_up_fused_24576", 24576, 1536), ("down_6144", 1536, 6144), ("down_12288", 1536, 12288),
+               ("ple_gate", 256, 1536), ("ple_proj", 1536, 256), ("per_layer_model_proj", 8960, 1536),
+               ("lm_head", 262144, 1536))
+# benchmark config 3: the projection shapes of one layer on the tensor cores
+GEMM_SHAPES = (("qkv_sliding", 2560, 1536), ("q_global", 4096, 1536), ("o_sliding", 1536, 2048),
+               ("gate_up_12288", 12288, 1536), ("gate_up_24576", 24576, 1536), ("down_6144", 1536, 6144),
+               ("down_12288", 1536, 12288), ("ple_gate", 256, 1536), ("ple_proj", 1536, 256))
 PREFILL = 512
 CTX_LONG = 16384
 # nominal FP32 FMA peak: 148 SMs x 128 lanes x 2 FLOP x 1.965 GHz (no measured figure on this pool)
@@ -96,6 +108,16 @@ class Dist:
                               device="cuda" if self.backend == "nccl" else "cpu")
         self.dist.all_reduce(t, op=self.dist.ReduceOp.MAX)
         return float(t.item())
+
+    def gather(self, v):
+        """[v of rank 0, v of rank 1, ...] on every rank."""
+        if not self.pg:
+            return [float(v)]
+        t = self.torch.zeros(self.world, dtype=self.torch.float64,
+                             device="cuda" if self.backend == "nccl" else "cpu")
+        t[self.rank] = float(v)
+        self.dist.all_reduce(t, op=self.dist.ReduceOp.SUM)
+        return [float(x) for x in t.tolist()]
 
     def close(self):
         if self.pg:
@@ -154,6 +176,15 @@ class Clocks:
         return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def workload_config(world):
+    """The `config` both arms print (the driver compares them)."""
+    return {"workload": "decode after a 512-token prefill (gemma4.c --bench 512 K); one step = "
+                        "forward(1 token) + logits",
+            "model": "gemma4-E2B random-init (.bin layout, seed 0)", "global_batch": world,
+            "seq_len": PREFILL, "parallelism": f"replicas x{world}",
+            "l2": "weights streamed per step (2.35 GB) exceed L2 (126 MB)"}
+
+
 def prompt_ids(n, seed=0):
     return np.random.default_rng(seed).integers(0, 262144, size=n).astype(np.int32)
 
@@ -163,6 +194,7 @@ def cpu_reference_decode(img, max_seconds=10.0, max_steps=256, prompt=PREFILL):
     tokens, then decode until max_seconds or max_steps. Returns a dict."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     from oracle import Reference
+    Reference.use_all_cores()
     ref = Reference()
     m = ref.open_model(img)
     try:
@@ -187,14 +219,18 @@ def cpu_reference_decode(img, max_seconds=10.0, max_steps=256, prompt=PREFILL):
 
 def run_reference_arm(args, dist):
     """--impl reference: the reference's own CPU implementation of the path on
-    this host's cores (rank 0 only), same metric and workload."""
+    this host's cores (rank 0 only), same metric and workload. Only the
+    reference library (oracle/_ref, which also carries the synthetic-model
+    writer) is loaded; its OpenMP team is the reference's default, one thread
+    per physical core (gemma4.c:182-188), whatever OMP_NUM_THREADS a launcher
+    exported."""
     if dist.rank != 0:
         return
-    import g4cuda as g4
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     from oracle import Reference
-    img = g4.synth_image(seed=0, flags=0)
+    Reference.use_all_cores()
     ref = Reference()
+    img = ref.synth_image(seed=0, flags=0)
     m = ref.open_model(img)
     ids = prompt_ids(PREFILL)
     m.forward(ids, 0)
@@ -216,11 +252,10 @@ def run_reference_arm(args, dist):
         "impl": "reference", "metric": "decode tok/s @ctx 512", "value": v, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": v / PUBLISHED_DECODE_512, "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "decode after a 512-token prefill (gemma4.c --bench 512 K)",
-                   "model": "gemma4-E2B random-init (.bin layout, seed 0)", "global_batch": 1, "seq_len": PREFILL,
-                   "parallelism": "host cores"},
+        "config": workload_config(dist.world),
         "cpu_baseline": {"value": v, "unit": "tok/s", "cores": ref.threads(), "kind": "reference",
-                         "sample": f"{args.steps} decode steps after a {PREFILL}-token prefill ({ref.variant} build)"},
+                         "sample": f"{args.steps} decode steps after a {PREFILL}-token prefill ({ref.variant} build, "
+                                   f"{ref.threads()} OpenMP threads: the reference's default of one per core)"},
         "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     m.close()
@@ -322,19 +357,27 @@ def batched_serving(m, dist, seqs=64, profile_step=None):
         steps += 1
         generated += act.size
     m.mark(8)
-    pre_ms = dist.max(m.elapsed(6, 7))
-    dec_ms = dist.max(m.elapsed(7, 8))
+    pre_ms_r, dec_ms_r = m.elapsed(6, 7), m.elapsed(7, 8)
     weights = 2350706688.0
-    total_prompt = int(plen.sum())
+    # whole-job aggregates: every rank's own tokens, over the slowest rank's time
+    prompts_r = dist.gather(int(plen.sum()))
+    gen_r = dist.gather(generated)
+    newtok_r = dist.gather(int(dlen.sum()))
+    pre_r, dec_r = dist.gather(pre_ms_r), dist.gather(dec_ms_r)
+    steps_r = dist.gather(steps)
+    hbm_r = dist.gather((steps * weights + kv_bytes) / (dec_ms_r / 1e3) / 1e9)
+    pre_ms, dec_ms = max(pre_r), max(dec_r)
     return {
-        "workload": f"{seqs} sequences per GPU, prompts log-uniform [128, 8192] (sum {total_prompt}), "
-                    f"decode lengths U[32, 512] (sum {int(dlen.sum())}), greedy, seed 2+rank",
-        "prefill_tok_s": dist.world * total_prompt / (pre_ms / 1e3),
-        "decode_tok_s": dist.world * generated / (dec_ms / 1e3),
-        "total_tok_s": dist.world * (total_prompt + int(dlen.sum())) / ((pre_ms + dec_ms) / 1e3),
-        "decode_steps": steps,
-        "decode_hbm_gbs_per_gpu": (steps * weights + kv_bytes) / (dec_ms / 1e3) / 1e9,
+        "workload": f"{seqs} sequences per GPU, prompts log-uniform [128, 8192], decode lengths U[32, 512], "
+                    f"greedy, seed 2+rank",
+        "prefill_tok_s": sum(prompts_r) / (pre_ms / 1e3),
+        "decode_tok_s": sum(gen_r) / (dec_ms / 1e3),
+        "total_tok_s": (sum(prompts_r) + sum(newtok_r)) / ((pre_ms + dec_ms) / 1e3),
+        "decode_hbm_gbs_per_gpu": hbm_r,
         "prefill_s": pre_ms / 1e3, "decode_s": dec_ms / 1e3,
+        "per_rank": {"prompt_tokens": [int(x) for x in prompts_r], "new_tokens": [int(x) for x in newtok_r],
+                     "decode_steps": [int(x) for x in steps_r],
+                     "prefill_s": [x / 1e3 for x in pre_r], "decode_s": [x / 1e3 for x in dec_r]},
     }
 
 
@@ -437,6 +480,19 @@ def run_ours(args, dist):
             gemm_ms += cnt * ms_g
             gemm_ops += cnt * ops_g
     gemm_tops = gemm_ops / (gemm_ms / 1e3) / 1e12 if gemm_ms else 0.0
+    # benchmark config 3: M in {512, 2048, 8192, 16384} over one layer's projection shapes
+    gemm_sweep = None
+    if not args.short:
+        gemm_sweep = {}
+        for M in (512, 2048, 8192, 16384):
+            row, ops_m, ms_m = {}, 0.0, 0.0
+            for name, N, K in GEMM_SHAPES:
+                ms_g, ops_g = g4.bench_gemm(N, K, M, 3, iters=3 if M > 2048 else 10)
+                row[name] = ops_g / (ms_g / 1e3) / 1e12
+                ops_m += ops_g
+                ms_m += ms_g
+            row["all_tops"] = ops_m / (ms_m / 1e3) / 1e12
+            gemm_sweep[f"M{M}"] = row
     # measured int8 tensor peak of this GPU (back-to-back tcgen05 kind::i8 MMAs on every SM)
     try:
         ms_p, ops_p = g4.bench_mma_i8(20000)
@@ -447,24 +503,45 @@ def run_ours(args, dist):
     batched = batched_serving(m, dist, profile_step=20 if args.profile_range else None) if not args.no_batched else None
     attention = attention_bench(g4, hbm_peak) if not args.no_attention else None
 
-    # long context: prefill 16384 then decode
+    # the other contexts of the reference's README table (pp / tg128 @ d2048, 8192, 16384)
     long = {}
     if not args.short:
-        pre_long, _ = prefill_timed(m, CTX_LONG, 0, dist)
-        ms_l, _, _ = decode_timed(m, CTX_LONG, max(8, args.steps // 2), 2, dist)
-        long = {"prefill_tok_s_16384": dist.world * pre_long,
-                "decode_tok_s_16384": dist.world * max(8, args.steps // 2) / (ms_l / 1e3)}
+        for ctx in (2048, 8192, CTX_LONG):
+            pre_c, _ = prefill_timed(m, ctx, 0, dist)
+            n_dec = max(8, args.steps // 4)
+            ms_c, _, _ = decode_timed(m, ctx, n_dec, 3, dist)
+            long[f"prefill_tok_s_{ctx}"] = dist.world * pre_c
+            long[f"decode_tok_s_{ctx}"] = dist.world * n_dec / (ms_c / 1e3)
+            kv = 28 * min(ctx, 512) * 256 * 8 + 7 * ctx * 512 * 8
+            long[f"decode_frac_hbm_{ctx}"] = (2350706688.0 + kv) / (ms_c / n_dec / 1e3) / 1e9 / hbm_peak
+
+    # strict mode (reference-order reductions: the bit-exact configuration), decode at ctx 512
+    strict = None
+    if not args.short:
+        pre_s, _ = prefill_timed(m, PREFILL, 0, dist)
+        m.set_option(5, 1)   # G4_OPT_STRICT
+        n_s = 8
+        ms_s, _, _ = decode_timed(m, PREFILL, n_s, 3, dist)
+        m.set_option(5, 0)
+        strict = {"decode_tok_s_512": dist.world * n_s / (ms_s / 1e3), "ms_per_step": ms_s / n_s,
+                  "note": "G4_OPT_STRICT: RMSNorm sums, attention scores, softmax and value sums in gemma4.c's "
+                          "sequential order with the host libm's expf; bit-identical residual stream"}
+
+    # benchmark config 2: the decode GEMV (M = 1) on every projection shape and the lm_head
+    gemv_sweep = None
+    if not args.short:
+        gemv_sweep = {}
+        for name, N, K in GEMV_SHAPES:
+            ms_v, by = g4.bench_gemv(N, K, 1, iters=50)
+            gemv_sweep[name] = {"N": N, "K": K, "us": ms_v * 1e3, "gbs": by / (ms_v / 1e3) / 1e9,
+                                "frac_hbm": by / (ms_v / 1e3) / 1e9 / hbm_peak}
 
     line = {
         "metric": "decode tok/s @ctx 512", "value": value, "unit": "tok/s", "n_gpus": dist.world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": per_step, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": value / PUBLISHED_DECODE_512,
         "dtype": "int8", "data": "synthetic",
-        "config": {"workload": "decode after a 512-token prefill (gemma4.c --bench 512 K); one step = "
-                               "forward(1 token) + logits",
-                   "model": "gemma4-E2B random-init (.bin layout, seed 0)", "global_batch": dist.world,
-                   "seq_len": PREFILL, "parallelism": f"replicas x{dist.world}",
-                   "l2": "weights streamed per step (2.35 GB) exceed L2 (126 MB)"},
+        "config": workload_config(dist.world),
         "e2e": {"value": e2e, "unit": "tok/s", "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4},
         "gpu_launches": args.steps * m.launches_per_token(),
         "roofline": {"bound": "hbm", "achieved": dec_gbs, "peak": hbm_peak, "unit": "GB/s",
@@ -472,7 +549,10 @@ def run_ours(args, dist):
                      "kernel": "k_decode: persistent single-token step (all int8 GEMVs incl. lm_head, "
                                "attention, norms) = the only launch per step", "peak_kind": peak_kind},
         "profile_ms": {"gemv": prof_ms[0], "attention": prof_ms[1], "other": prof_ms[2],
-                       "ops": prof_n, "source": "device timeline of one k_decode launch"},
+                       "ops": prof_n, "source": "device timeline of one traced k_decode launch (op end minus "
+                                                "the previous barrier exit, %globaltimer); the tracing itself "
+                                                "lengthens that launch, so the classes sum to more than "
+                                                "ms_per_step"},
         "prefill_roofline": {"bound": "tensor", "achieved": gemm_tops, "peak": int8_peak,
                              "unit": "TOP/s", "frac": gemm_tops / int8_peak,
                              "peak_nominal": INT8_DENSE_TOPS, "frac_nominal": gemm_tops / INT8_DENSE_TOPS,
@@ -482,6 +562,12 @@ def run_ours(args, dist):
         "prefill_tok_s_512": dist.world * pre512,
     }
     line.update(long)
+    if strict:
+        line["strict"] = strict
+    if gemv_sweep:
+        line["decode_gemv_sweep"] = gemv_sweep
+    if gemm_sweep:
+        line["prefill_gemm_sweep"] = gemm_sweep
     if batched:
         line["batched"] = batched
     if attention:

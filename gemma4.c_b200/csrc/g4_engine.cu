@@ -202,25 +202,71 @@ int get_vec(g4_ctx *c, const uint8_t *img, uint64_t bytes, const Rec *r, int idx
     return G4_OK;
 }
 
-// Copy a packed host matrix into row-major device form, in chunks of whole
-// 16-row blocks through a staging buffer.
-int upload_mat(g4_ctx *c, const HostMat &hm, DMat dst, int row_offset, int row_mul, uint8_t *stage, size_t stage_bytes) {
-    const int K = hm.K, G = K / 64;
-    size_t per_row = (size_t)K + (size_t)G * 2;
-    int rows = (int)(stage_bytes / per_row) / 16 * 16;
-    if (rows < 16) return fail(c, G4_ERR_INVALID, "staging buffer too small");
-    uint8_t *sw = stage;
-    uint16_t *ss = (uint16_t *)(stage + (((size_t)rows * K + 255) & ~(size_t)255));
-    for (int r0 = 0; r0 < hm.N; r0 += rows) {
-        int nr = hm.N - r0 < rows ? hm.N - r0 : rows;
-        CK(cudaMemcpyAsync(sw, hm.w + (size_t)r0 * K, (size_t)nr * K, cudaMemcpyDefault, c->st));
-        CK(cudaMemcpyAsync(ss, hm.s + (size_t)r0 * G, (size_t)nr * G * 2, cudaMemcpyDefault, c->st));
-        CK(g4_launch_repack((const int8_t *)sw, ss, nr, K, (int8_t *)dst.w, (uint16_t *)dst.s, row_offset + r0 * row_mul,
-                            row_mul, c->st));
-        CK(cudaStreamSynchronize(c->st));
+// Load-time repacking: packed matrix pieces (whole 16-row blocks) are gathered
+// into one staging buffer (host images), or used where they lie (device
+// images), and every fill is repacked by ONE launch of k_repack_jobs.
+struct Uploader {
+    static constexpr int kMaxJobs = 512;
+    g4_ctx *c = nullptr;
+    bool device_src = false;
+    uint8_t *stage = nullptr;
+    size_t stage_bytes = 0, used = 0;
+    RepackJob *jobs_dev = nullptr;
+    std::vector<RepackJob> jobs;
+
+    ~Uploader() {
+        if (stage) cudaFree(stage);
+        if (jobs_dev) cudaFree(jobs_dev);
     }
-    return G4_OK;
-}
+    int flush() {
+        if (jobs.empty()) return G4_OK;
+        CK(cudaMemcpyAsync(jobs_dev, jobs.data(), jobs.size() * sizeof(RepackJob), cudaMemcpyHostToDevice, c->st));
+        CK(g4_launch_repack_jobs(jobs_dev, (int)jobs.size(), c->st));
+        CK(cudaStreamSynchronize(c->st));   // the staging buffer and the job list are reused
+        jobs.clear();
+        used = 0;
+        return G4_OK;
+    }
+    int add(const HostMat &hm, DMat dst, int row_offset, int row_mul) {
+        const int K = hm.K, G = K / 64;
+        const size_t per_row = (size_t)K + (size_t)G * 2;
+        for (int r0 = 0; r0 < hm.N;) {
+            int nr = hm.N - r0;
+            RepackJob j{};
+            if (device_src) {
+                j.src_w = hm.w + (size_t)r0 * K;
+                j.src_s = hm.s + (size_t)r0 * G;
+            } else {
+                int fit = (int)((stage_bytes - used) / (per_row + 1)) / 16 * 16 - 16;
+                if (fit < 16 || (fit < nr && used > 0)) {
+                    if (int rc = flush()) return rc;
+                    fit = (int)(stage_bytes / (per_row + 1)) / 16 * 16 - 16;
+                    if (fit < 16) return fail(c, G4_ERR_INVALID, "staging buffer too small");
+                }
+                nr = nr < fit ? nr : fit;
+                uint8_t *w = stage + used;
+                const size_t wb = ((size_t)nr * K + 255) & ~(size_t)255;
+                uint8_t *sc = w + wb;
+                CK(cudaMemcpyAsync(w, hm.w + (size_t)r0 * K, (size_t)nr * K, cudaMemcpyDefault, c->st));
+                CK(cudaMemcpyAsync(sc, hm.s + (size_t)r0 * G, (size_t)nr * G * 2, cudaMemcpyDefault, c->st));
+                used += wb + (((size_t)nr * G * 2 + 255) & ~(size_t)255);
+                j.src_w = (const int8_t *)w;
+                j.src_s = (const uint16_t *)sc;
+            }
+            j.dst_w = (int8_t *)dst.w;
+            j.dst_s = (uint16_t *)dst.s;
+            j.N = nr;
+            j.K = K;
+            j.row_offset = row_offset + r0 * row_mul;
+            j.row_mul = row_mul;
+            jobs.push_back(j);
+            r0 += nr;
+            if ((int)jobs.size() >= kMaxJobs)
+                if (int rc = flush()) return rc;
+        }
+        return G4_OK;
+    }
+};
 
 DMat alloc_mat(g4_ctx *c, int N, int K) {
     DMat m{};
@@ -342,29 +388,32 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes, const uint8_t *hdr 
     if (!c->embed.w || !c->L[G4_NUM_LAYERS - 1].plep.s) return fail(c, G4_ERR_NOMEM, "weight arena too small");
 
     // ---- upload + repack ----
-    const size_t stage_bytes = 256u << 20;
-    uint8_t *stage = nullptr;
-    CK(cudaMalloc(&stage, stage_bytes));
-    auto up = [&](const HostMat &hm, DMat d, int off, int mul) { return upload_mat(c, hm, d, off, mul, stage, stage_bytes); };
-    rc = up(embed, c->embed, 0, 1);
-    if (!rc) rc = up(eple, c->embed_ple, 0, 1);
-    if (!rc) rc = up(pmp, c->pmp, 0, 1);
+    Uploader upl;
+    upl.c = c;
+    upl.device_src = hdr != nullptr;   // the image is already in device memory (g4_open_file)
+    upl.stage_bytes = upl.device_src ? 0 : (size_t)256 << 20;
+    if (upl.stage_bytes) CK(cudaMalloc(&upl.stage, upl.stage_bytes));
+    CK(cudaMalloc(&upl.jobs_dev, Uploader::kMaxJobs * sizeof(RepackJob)));
+    rc = upl.add(embed, c->embed, 0, 1);
+    if (!rc) rc = upl.add(eple, c->embed_ple, 0, 1);
+    if (!rc) rc = upl.add(pmp, c->pmp, 0, 1);
     for (int l = 0; l < G4_NUM_LAYERS && !rc; l++) {
         Layer &Y = c->L[l];
         HL &x = hl[l];
-        rc = up(x.q, Y.qkv, 0, 1);
-        if (!rc && Y.has_kv) rc = up(x.k, Y.qkv, Y.qw, 1);
-        if (!rc && Y.has_kv) rc = up(x.v, Y.qkv, Y.qw + Y.hd, 1);
-        if (!rc) rc = up(x.o, Y.o, 0, 1);
-        if (!rc) rc = up(x.gate, Y.gu, 0, 2);
-        if (!rc) rc = up(x.up, Y.gu, 1, 2);
-        if (!rc) rc = up(x.down, Y.down, 0, 1);
-        if (!rc) rc = up(x.pleg, Y.pleg, 0, 1);
-        if (!rc) rc = up(x.plep, Y.plep, 0, 1);
+        rc = upl.add(x.q, Y.qkv, 0, 1);
+        if (!rc && Y.has_kv) rc = upl.add(x.k, Y.qkv, Y.qw, 1);
+        if (!rc && Y.has_kv) rc = upl.add(x.v, Y.qkv, Y.qw + Y.hd, 1);
+        if (!rc) rc = upl.add(x.o, Y.o, 0, 1);
+        if (!rc) rc = upl.add(x.gate, Y.gu, 0, 2);
+        if (!rc) rc = upl.add(x.up, Y.gu, 1, 2);
+        if (!rc) rc = upl.add(x.down, Y.down, 0, 1);
+        if (!rc) rc = upl.add(x.pleg, Y.pleg, 0, 1);
+        if (!rc) rc = upl.add(x.plep, Y.plep, 0, 1);
     }
-    cudaFree(stage);
+    if (!rc) rc = upl.flush();
     if (rc) return rc;
-    // group-major fp32 copies of the layer and per-layer-projection scales (tensor-core GEMM)
+    // group-major fp32 copies of the layer and per-layer-projection scales
+    // (tensor-core GEMM), all in one launch
     {
         std::vector<DMat *> mats;
         mats.push_back(&c->pmp);
@@ -375,13 +424,19 @@ int open_impl(g4_ctx *c, const uint8_t *img, uint64_t bytes, const uint8_t *hdr 
         size_t bytes = 0;
         for (DMat *m : mats) bytes += ((size_t)m->N * (m->K / 64) * 4 + 255) & ~(size_t)255;
         CK(cudaMalloc(&c->scales_t, bytes));
+        std::vector<ScalesJob> sj;
         size_t off = 0;
         for (DMat *m : mats) {
             float *d = (float *)((uint8_t *)c->scales_t + off);
-            CK(g4_launch_scales_t(m->s, m->N, m->K, d, c->st));
+            sj.push_back(ScalesJob{m->s, d, m->N, m->K / 64});
             m->sT = d;
             off += ((size_t)m->N * (m->K / 64) * 4 + 255) & ~(size_t)255;
         }
+        static_assert(sizeof(ScalesJob) <= sizeof(RepackJob), "scale jobs reuse the repack job buffer");
+        if (sj.size() > (size_t)Uploader::kMaxJobs) return fail(c, G4_ERR_INVALID, "too many scale jobs");
+        CK(cudaMemcpyAsync(upl.jobs_dev, sj.data(), sj.size() * sizeof(ScalesJob), cudaMemcpyHostToDevice, c->st));
+        CK(g4_launch_scales_t_jobs((const ScalesJob *)upl.jobs_dev, (int)sj.size(), c->st));
+        CK(cudaStreamSynchronize(c->st));
         c->scales_t_bytes = bytes;
     }
     int vr = G4_OK;
@@ -1358,6 +1413,29 @@ int g4_read_cache(g4_ctx *c, int layer, int which, int slot0, int nslots, float 
     if (rc) return rc;
     const float *src = (which ? Y.vcache : Y.kcache) + (size_t)slot0 * Y.hd;
     CK(cudaMemcpyAsync(out, src, (size_t)nslots * Y.hd * 4, cudaMemcpyDeviceToHost, c->st));
+    return check_device_error(c);
+}
+
+int g4_read_ple(g4_ctx *c, size_t rows, float *out) {
+    if (!c || !out || rows > (size_t)kMaxT) return G4_ERR_INVALID;
+    cudaSetDevice(c->device);
+    int rc = flush_pending(c);
+    if (rc) return rc;
+    CK(cudaMemcpyAsync(out, c->ple_u, rows * G4_NUM_LAYERS * G4_PLE * 4, cudaMemcpyDeviceToHost, c->st));
+    return check_device_error(c);
+}
+
+int g4_read_seq_cache(g4_ctx *c, int seq, int layer, int which, int slot0, int nslots, float *out) {
+    if (!c || !out || layer < 0 || layer >= G4_NUM_LAYERS || nslots < 0 || seq < 0 || seq >= c->max_seqs)
+        return G4_ERR_INVALID;
+    const int ring = c->bring[layer], hd = c->L[layer].hd;
+    if (slot0 < 0 || slot0 + nslots > ring) return G4_ERR_INVALID;
+    cudaSetDevice(c->device);
+    int rc = flush_pending(c);
+    if (rc) return rc;
+    const size_t stride = (size_t)2 * ring * hd;   // one sequence's K ring then V ring
+    const float *src = (which ? c->bv[layer] : c->bk[layer]) + (size_t)seq * stride + (size_t)slot0 * hd;
+    CK(cudaMemcpyAsync(out, src, (size_t)nslots * hd * 4, cudaMemcpyDeviceToHost, c->st));
     return check_device_error(c);
 }
 

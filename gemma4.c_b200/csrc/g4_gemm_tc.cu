@@ -161,7 +161,8 @@ G4_DEV void chain(uint64_t *acc, const int (&d)[CW], const float *ws, float xv) 
 
 struct TcArgs {
     int T, N, K;
-    const float *xsT;       // [K/64][G4_XST_STRIDE] activation scales, group-major
+    const float *xsT;       // [K/64][xs_stride] activation scales, group-major
+    int xs_stride;          // row stride of xsT (and qsT), >= T
     const float *wsT;       // [K/64][N] weight scales, fp32
     int epi;
     float *out;
@@ -241,7 +242,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // per group: BN column scales then 128 row scales (weight / activation,
                 // or activation / weight when swapped)
                 const float *colT = p.swap ? p.xsT + rb : p.wsT + rb, *rowT = p.swap ? p.wsT + ra : p.xsT + ra;
-                const size_t colS = p.swap ? G4_XST_STRIDE : p.N, rowS = p.swap ? p.N : G4_XST_STRIDE;
+                const size_t colS = p.swap ? (size_t)p.xs_stride : p.N, rowS = p.swap ? p.N : (size_t)p.xs_stride;
                 for (int ks = 0; ks < steps; ks++, k++) {
                     const int s = k % kStages, use = k / kStages;
                     if (use > 0 &&
@@ -427,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     *(uint4 *)(p.qout + (size_t)t * K2 + (nb >> 1)) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
                     if (cb == 0) {
                         p.qs[(size_t)t * (K2 / 64) + g] = sc;
-                        if (p.qsT) p.qsT[(size_t)g * G4_XST_STRIDE + t] = sc;
+                        if (p.qsT) p.qsT[(size_t)g * p.xs_stride + t] = sc;
                     }
                 }
               }
@@ -595,7 +596,8 @@ cudaError_t launch_bn(const CUtensorMap &ma, const CUtensorMap &mb, const TcArgs
 void *g4_tmap_encoder() { return (void *)encode_fn(); }
 
 bool g4_gemm_tc_supported(const GemmArgs &a) {
-    return a.m.sT != nullptr && a.xsT != nullptr && a.T <= G4_XST_STRIDE && a.m.K % kBK == 0 && a.m.N % 32 == 0 &&
+    const int xs_stride = a.xs_stride > 0 ? a.xs_stride : G4_XST_STRIDE;
+    return a.m.sT != nullptr && a.xsT != nullptr && a.T <= xs_stride && a.m.K % kBK == 0 && a.m.N % 32 == 0 &&
            a.T >= 1 && encode_fn() != nullptr && (a.epi == EPI_STORE || a.epi == EPI_GEGLU_PAIR || a.epi == EPI_PLE) &&
            a.dots_out == nullptr;
 }
@@ -633,6 +635,7 @@ cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
     p.N = a.m.N;
     p.K = a.m.K;
     p.xsT = a.xsT;
+    p.xs_stride = a.xs_stride > 0 ? a.xs_stride : G4_XST_STRIDE;
     p.wsT = a.m.sT;
     p.epi = a.epi;
     p.out = a.out;

@@ -88,6 +88,9 @@ struct GemvArgs {
 
 // ---- GEMM (prefill, T > 4) -------------------------------------------------
 constexpr int G4_XST_STRIDE = G4_BATCH;
+// token rows of one tensor-core GEMM outside the engine (kernel tests and the
+// prefill-GEMM sweep of benchmark config 3)
+constexpr int G4_GEMM_MAX_T = 16384;
 // one prefill-attention partial: rows x (hd outputs) + row max + row sum, for
 // 64 rows at hd 256 (32 rows at hd 512 need less)
 constexpr int G4_PRE_PART_SLOT = 64 * (256 + 2);   // row stride of group-major activation scales
@@ -97,7 +100,8 @@ struct GemmArgs {
     int T;
     const int8_t *xq;       // [T][K]
     const float *xs;        // [T][K/64]
-    const float *xsT;       // [K/64][G4_XST_STRIDE] the same scales group-major (tensor-core path), or NULL
+    const float *xsT;       // [K/64][xs_stride] the same scales group-major (tensor-core path), or NULL
+    int xs_stride;          // row stride of xsT / qsT; 0 = G4_XST_STRIDE (the engine's 512-row chunks)
     int epi;                // GemvEpi subset: STORE, GEGLU_PAIR, PLE
     float *out;
     int out_stride;
@@ -239,6 +243,22 @@ cudaError_t g4_launch_attn_strict(const AttnArgs &a, cudaStream_t st, bool pdl);
 
 cudaError_t g4_launch_repack(const int8_t *packed_w, const uint16_t *packed_s, int N, int K, int8_t *w, uint16_t *s,
                              int row_offset, int row_stride_mul, cudaStream_t st);
+// Load-time repacking of many matrices per launch (the model upload): one job
+// per packed matrix piece (whole 16-row blocks) already in device memory.
+struct RepackJob {
+    const int8_t *src_w;      // packed [N/16][K/64][16][16][4]
+    const uint16_t *src_s;    // packed [N/16][K/64][16]
+    int8_t *dst_w;            // row-major destination matrix
+    uint16_t *dst_s;
+    int N, K, row_offset, row_mul;
+};
+struct ScalesJob {
+    const uint16_t *s;        // [N][G] fp16
+    float *sT;                // [G][N] fp32
+    int N, G;
+};
+cudaError_t g4_launch_repack_jobs(const RepackJob *jobs_dev, int njobs, cudaStream_t st);
+cudaError_t g4_launch_scales_t_jobs(const ScalesJob *jobs_dev, int njobs, cudaStream_t st);
 cudaError_t g4_launch_rows_embed(const int *tokens, int T, DMat embed, DMat embed_ple, float mult, float ple_mult,
                                  float *res, float *ple_emb, int *err, cudaStream_t st, bool pdl);
 // xsT (optional): the scales again, group-major [K/64][G4_XST_STRIDE] (tensor-core GEMM)

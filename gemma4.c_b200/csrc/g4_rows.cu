@@ -38,6 +38,44 @@ __global__ void k_repack_s(const uint16_t *__restrict__ src, int N, int K, uint1
     }
 }
 
+// Every matrix of one staging fill in one launch: CTAs walk the jobs in order,
+// each job's words and scales grid-stride (the per-element mapping of
+// k_repack_w / k_repack_s above).
+__global__ void __launch_bounds__(256) k_repack_jobs(const RepackJob *__restrict__ jobs, int njobs) {
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nthr = (size_t)gridDim.x * blockDim.x;
+    for (int j = 0; j < njobs; j++) {
+        const RepackJob J = jobs[j];
+        const int G = J.K / 64;
+        const size_t words = (size_t)J.N * J.K / 4, per_block = (size_t)G * 256;
+        const uint32_t *src = (const uint32_t *)J.src_w;
+        for (size_t wi = tid; wi < words; wi += nthr) {
+            const size_t rb = wi / per_block, rem = wi - rb * per_block;
+            const int g = (int)(rem >> 8), c = (int)((rem >> 4) & 15), r = (int)(rem & 15);
+            const size_t drow = (size_t)J.row_offset + (rb * 16 + r) * J.row_mul;
+            *(uint32_t *)(J.dst_w + drow * J.K + g * 64 + c * 4) = src[wi];
+        }
+        const size_t count = (size_t)J.N * G;
+        for (size_t si = tid; si < count; si += nthr) {
+            const size_t rb = si / ((size_t)G * 16);
+            const int g = (int)((si / 16) % G), r = (int)(si & 15);
+            J.dst_s[((size_t)J.row_offset + (rb * 16 + r) * J.row_mul) * G + g] = J.src_s[si];
+        }
+    }
+}
+
+// Group-major fp32 scales of many matrices in one launch (k_scales_t per job).
+__global__ void __launch_bounds__(256) k_scales_t_jobs(const ScalesJob *__restrict__ jobs, int njobs) {
+    const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x, nthr = (size_t)gridDim.x * blockDim.x;
+    for (int j = 0; j < njobs; j++) {
+        const ScalesJob J = jobs[j];
+        const size_t n = (size_t)J.N * J.G;
+        for (size_t i = tid; i < n; i += nthr) {
+            const int g = (int)(i / J.N), r = (int)(i % J.N);
+            J.sT[i] = h2f(J.s[(size_t)r * J.G + g]);
+        }
+    }
+}
+
 __device__ float block_sum256(float v, float *red) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     v = warp_sum(v);
@@ -242,6 +280,18 @@ cudaError_t g4_launch_repack(const int8_t *packed_w, const uint16_t *packed_s, i
     if (N % 16 || K % 64) return cudaErrorInvalidValue;
     k_repack_w<<<1184, 256, 0, st>>>((const uint32_t *)packed_w, N, K, w, row_offset, row_mul);
     k_repack_s<<<592, 256, 0, st>>>(packed_s, N, K, s, row_offset, row_mul);
+    return cudaGetLastError();
+}
+
+cudaError_t g4_launch_repack_jobs(const RepackJob *jobs_dev, int njobs, cudaStream_t st) {
+    if (njobs < 1) return cudaSuccess;
+    k_repack_jobs<<<2 * g4_device_sms() * 4, 256, 0, st>>>(jobs_dev, njobs);
+    return cudaGetLastError();
+}
+
+cudaError_t g4_launch_scales_t_jobs(const ScalesJob *jobs_dev, int njobs, cudaStream_t st) {
+    if (njobs < 1) return cudaSuccess;
+    k_scales_t_jobs<<<2 * g4_device_sms() * 4, 256, 0, st>>>(jobs_dev, njobs);
     return cudaGetLastError();
 }
 

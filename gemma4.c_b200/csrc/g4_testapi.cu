@@ -251,7 +251,7 @@ int g4k_rmsnorm_quant(const float *x, int rows, const float *w, float eps, float
 int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, const int8_t *xq, const float *xs,
                int T, int path, float *out, int32_t *dots) {
     if (!w_packed || !s_packed || !xq || !xs || !out || N < 16 || N % 16 || K < 256 || K % 256 || T < 1 ||
-        T > G4_BATCH)
+        T > (path == 3 ? G4_GEMM_MAX_T : G4_BATCH))
         return G4_ERR_INVALID;
     if (path == 0) path = T <= 4 ? 1 : 2;
     if (path == 1 && T > 4) return G4_ERR_INVALID;
@@ -274,14 +274,16 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
     TK(g4_launch_repack((const int8_t *)pw.p, (const uint16_t *)ps.p, N, K, (int8_t *)w.p, (uint16_t *)s.p, 0, 1, 0));
     DMat m{(const int8_t *)w.p, (const uint16_t *)s.p, nullptr, N, K};
     DevBuf sT, xsT;
+    // group-major activation scales: the engine's 512-row stride, or T rounded up
+    // to whole 128-row tiles for the longer tensor-core problems
+    const int xs_stride = T <= G4_XST_STRIDE ? G4_XST_STRIDE : (T + 127) / 128 * 128;
     if (path == 3 || path == 4) {
-        if (T > G4_XST_STRIDE) return G4_ERR_INVALID;
         TK(sT.alloc((size_t)N * G * 4));
         TK(g4_launch_scales_t(m.s, N, K, (float *)sT.p, 0));
         m.sT = (const float *)sT.p;
-        std::vector<float> h((size_t)G * G4_XST_STRIDE, 0.0f);   // group-major activation scales
+        std::vector<float> h((size_t)G * xs_stride, 0.0f);
         for (int t = 0; t < T; t++)
-            for (int g = 0; g < G; g++) h[(size_t)g * G4_XST_STRIDE + t] = xs[(size_t)t * G + g];
+            for (int g = 0; g < G; g++) h[(size_t)g * xs_stride + t] = xs[(size_t)t * G + g];
         TK(xsT.alloc(h.size() * 4));
         TK(cudaMemcpy(xsT.p, h.data(), h.size() * 4, cudaMemcpyHostToDevice));
     }
@@ -306,6 +308,7 @@ int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, c
         a.xq = (const int8_t *)dxq.p;
         a.xs = (const float *)dxs.p;
         a.xsT = (const float *)xsT.p;
+        a.xs_stride = xs_stride;
         a.epi = EPI_STORE;
         a.out = (float *)dout.p;
         a.out_stride = N;
@@ -600,10 +603,11 @@ int g4_bench_mma_i8(int iters, float *ms_per_launch, double *ops_per_launch) {
 // report the average launch duration and the int8 operations per launch
 // (2 T N K).
 int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch, double *ops_per_launch) {
-    if (N < 128 || N % 128 || K % 256 || T < 1 || T > G4_BATCH || iters < 1 || !ms_per_launch || path < 2 ||
-        path > 4 || (path == 4 && T > G4_SKINNY_MAX_T))
+    if (N < 128 || N % 128 || K % 256 || T < 1 || T > (path == 3 ? G4_GEMM_MAX_T : G4_BATCH) || iters < 1 ||
+        !ms_per_launch || path < 2 || path > 4 || (path == 4 && T > G4_SKINNY_MAX_T))
         return G4_ERR_INVALID;
     const int G = K / 64;
+    const int xs_stride = T <= G4_XST_STRIDE ? G4_XST_STRIDE : (T + 127) / 128 * 128;
     const size_t wbytes = (size_t)N * K + (size_t)N * G * 2;
     const size_t tbytes = (size_t)N * G * 4;
     int copies = (int)((512ull << 20) / wbytes) + 1;
@@ -611,8 +615,8 @@ int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch
     DevBuf w, sT, xq, xs, xsT, out, err;
     TK(w.alloc(wbytes * copies));
     TK(sT.alloc(tbytes));
-    TK(xsT.alloc((size_t)G * G4_XST_STRIDE * 4));
-    TK(cudaMemset(xsT.p, 0, (size_t)G * G4_XST_STRIDE * 4));
+    TK(xsT.alloc((size_t)G * xs_stride * 4));
+    TK(cudaMemset(xsT.p, 0, (size_t)G * xs_stride * 4));
     TK(xq.alloc((size_t)T * K));
     TK(xs.alloc((size_t)T * G * 4));
     TK(out.alloc((size_t)T * N * 4));
@@ -633,6 +637,7 @@ int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch
         a.xq = (const int8_t *)xq.p;
         a.xs = (const float *)xs.p;
         a.xsT = (const float *)xsT.p;
+        a.xs_stride = xs_stride;
         a.epi = EPI_STORE;
         a.out = (float *)out.p;
         a.out_stride = N;

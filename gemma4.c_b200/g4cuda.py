@@ -67,6 +67,8 @@ def load(path=LIB_PATH):
     L.g4_set_option.argtypes = [vp, C.c_int, C.c_int]
     L.g4_read_residual.argtypes = [vp, C.c_size_t, _f32p]
     L.g4_read_cache.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
+    L.g4_read_ple.argtypes = [vp, C.c_size_t, _f32p]
+    L.g4_read_seq_cache.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
     L.g4_stream.argtypes = [vp]
     L.g4_stream.restype = vp
     L.g4_device_bytes.argtypes = [vp, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)]
@@ -201,6 +203,17 @@ class Model:
     def cache(self, layer, which, slot0, nslots, head_dim):
         out = np.empty((nslots, head_dim), np.float32)
         _check(self.L.g4_read_cache(self.h, layer, which, slot0, nslots, out), self.h)
+        return out
+
+    def ple(self, rows):
+        """Per-layer inputs of the last forward's rows, [rows][35][256]."""
+        out = np.empty((rows, NUM_LAYERS, 256), np.float32)
+        _check(self.L.g4_read_ple(self.h, rows, out), self.h)
+        return out
+
+    def seq_cache(self, seq, layer, which, slot0, nslots, head_dim):
+        out = np.empty((nslots, head_dim), np.float32)
+        _check(self.L.g4_read_seq_cache(self.h, seq, layer, which, slot0, nslots, out), self.h)
         return out
 
     def stream(self):

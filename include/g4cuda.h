@@ -171,6 +171,12 @@ int g4_logits_batch(g4_ctx *ctx, int *argmax, float *logits);
 int g4_read_residual(g4_ctx *ctx, size_t rows, float *out);          /* [rows][1536] */
 /* `nslots` ring slots of the K (which=0) or V (which=1) cache `layer` reads. */
 int g4_read_cache(g4_ctx *ctx, int layer, int which, int slot0, int nslots, float *out);
+/* The per-layer inputs of the last forward's rows ([rows][35][256]: the
+ * token-conditioned input each layer's gate multiplies, gemma4.c:468-477). */
+int g4_read_ple(g4_ctx *ctx, size_t rows, float *out);
+/* Ring slots of sequence `seq`'s K (which=0) / V (which=1) cache that `layer`
+ * reads (multi-sequence serving, after g4_seq_alloc). */
+int g4_read_seq_cache(g4_ctx *ctx, int seq, int layer, int which, int slot0, int nslots, float *out);
 void *g4_stream(g4_ctx *ctx);                 /* the context's cudaStream_t */
 /* Open (1) / close (0) the profiler capture range (ncu --profile-from-start off). */
 int g4_profiler_range(int on);
@@ -213,15 +219,15 @@ int g4k_quantize(const float *x, int rows, int width, int8_t *q, float *s);
  * out[T][N]; `dots` (may be NULL) receives the int32 of every (t, n, 64-group)
  * as [T][N][K/64]. path: 0 auto, 1 decode GEMV (T <= 4), 2 SIMT GEMM,
  * 3 tcgen05 GEMM, 4 small-batch mma GEMM (T <= 64); paths 3 and 4 do not
- * return dots. */
+ * return dots. T <= 512 (the reference's chunk), except path 3: T <= 16384. */
 int g4k_linear(const int8_t *w_packed, const uint16_t *s_packed, int N, int K, const int8_t *xq, const float *xs,
                int T, int path, float *out, int32_t *dots);
 /* Average duration of the decode GEMV on an N x K int8 matrix over `iters`
  * launches (weights cycled through enough copies to exceed L2), and the
  * algorithmic bytes (int8 weights + FP16 scales) one launch streams. */
 int g4_bench_gemv(int N, int K, int T, int iters, int pdl, float *ms_per_launch, double *bytes_per_launch);
-/* Prefill GEMM timing (path 2 SIMT dp4a, 3 tcgen05, 4 small-batch mma with
- * T <= 64) on T x N x K: average
+/* Prefill GEMM timing (path 2 SIMT dp4a with T <= 512, 3 tcgen05 with
+ * T <= 16384, 4 small-batch mma with T <= 64) on T x N x K: average
  * launch duration and int8 operations (2 T N K) per launch. */
 int g4_bench_gemm(int N, int K, int T, int path, int iters, float *ms_per_launch, double *ops_per_launch);
 /* Launch geometry the small-batch GEMM (T <= 64 token rows) would use for an

@@ -12,7 +12,8 @@
  *   - fmaf() appears exactly where the reference uses an FMA intrinsic (the
  *     per-group dequant chain, attention scores, the weighted value sum).
  * With the same libm (expf, tanhf, sqrtf) the whole forward is then bit-for-bit
- * the reference's, which tests/test_oracle_vs_reference.py checks.
+ * the reference's: tests/test_oracle_golden.py checks it against golden vectors
+ * that the reference itself produced (tests/golden/make_golden.py).
  *
  * OpenMP parallelises over independent outputs only, so results do not depend
  * on the thread count.
@@ -255,6 +256,7 @@ void or_attend(float *out, const float *q, const float *kc, const float *vc,
 
 /* gemma4.c:519 */
 void or_softcap(float *x, size_t n) {
+    #pragma omp parallel for schedule(static)
     for (size_t i = 0; i < n; i++) x[i] = 30.0f * tanhf(x[i] / 30.0f);
 }
 
@@ -453,12 +455,13 @@ void or_forward(const or_model *m, or_state *s, const int *tokens, size_t T, int
     or_forward_layers(m, s, tokens, T, start_pos, NL);
 }
 
-/* forward restricted to the first `layers` layers (a testing aid for
- * bisecting mismatches; layers = 35 is the reference's forward). */
-void or_forward_layers(const or_model *m, or_state *s, const int *tokens, size_t T, int start_pos, int layers) {
+/* The token-conditioned inputs of every layer (gemma4.c:468-477): the scaled
+ * token embedding into the residual stream, and the per-layer inputs (model
+ * projection of the embedding, RMSNorm, plus the per-layer embedding, times
+ * 1/sqrt(2)). */
+void or_prologue(const or_model *m, or_state *s, const int *tokens, size_t T) {
     const tens *E = &m->t[0], *EP = &m->t[1];
-    const tens *norm_ple = &m->t[2 + NL * 19 + 2], *pmp = &m->t[2 + NL * 19 + 1], *gelu = &m->t[2 + NL * 19 + 3];
-    const float *gt = (const float *)gelu->data;
+    const tens *norm_ple = &m->t[2 + NL * 19 + 2], *pmp = &m->t[2 + NL * 19 + 1];
     int plw = norm_ple->shape[0];
 
     or_embedding(s->residual, (const int8_t *)E->data, E->scales, E->shape[1], tokens, T, sqrtf((float)HID));
@@ -467,32 +470,60 @@ void or_forward_layers(const or_model *m, or_state *s, const int *tokens, size_t
     or_rmsnorm(s->ple, s->ple, (const float *)norm_ple->data, plw, 1e-6f * HID, T * NL);
     or_embedding(s->hidden, (const int8_t *)EP->data, EP->scales, EP->shape[1], tokens, T, sqrtf((float)plw));
     or_add_scale(s->ple, s->hidden, T * NL * (size_t)plw, 1.0f / sqrtf(2.0f));
+}
 
-    for (int l = 0; l < layers; l++) {
-        const tens *L = &m->t[L_(l, 0)];
-        or_rmsnorm(s->hidden, s->residual, (const float *)L[0].data, HID, 1e-6f, T);
-        attention_layer(m, s, l, start_pos, T);
-        or_rmsnorm(s->hidden, s->hidden, (const float *)L[3].data, HID, 1e-6f, T);
-        or_add_scale(s->residual, s->hidden, T * HID, 1.0f);
+/* One decoder layer (the loop body of gemma4.c:479-507) on the T residual rows
+ * in the state, at positions start_pos.., with the per-layer inputs in the
+ * state: attention (writing this layer's K/V when it owns a cache), the
+ * feed-forward block and the per-layer-input gate, each added back onto the
+ * residual stream. */
+void or_layer(const or_model *m, or_state *s, int l, int start_pos, size_t T) {
+    const tens *gelu = &m->t[2 + NL * 19 + 3];
+    const float *gt = (const float *)gelu->data;
+    const int plw = m->t[2 + NL * 19 + 2].shape[0];
+    const tens *L = &m->t[L_(l, 0)];
+    or_rmsnorm(s->hidden, s->residual, (const float *)L[0].data, HID, 1e-6f, T);
+    attention_layer(m, s, l, start_pos, T);
+    or_rmsnorm(s->hidden, s->hidden, (const float *)L[3].data, HID, 1e-6f, T);
+    or_add_scale(s->residual, s->hidden, T * HID, 1.0f);
 
-        or_rmsnorm(s->hidden, s->residual, (const float *)L[2].data, HID, 1e-6f, T);
-        or_quantize(s->q, s->qs, s->hidden, T, (size_t)L[14].shape[1]);
-        lin(s->hidden, s, &L[14], T);
-        lin(s->aux, s, &L[15], T);
-        or_geglu(s->hidden, s->aux, (int)T, L[14].shape[0], L[14].shape[0], gt, gelu->shape[0], gelu->shape[1], gelu->shape[2]);
-        or_quantize(s->q, s->qs, s->hidden, T, (size_t)L[16].shape[1]);
-        lin(s->hidden, s, &L[16], T);
-        or_rmsnorm(s->hidden, s->hidden, (const float *)L[4].data, HID, 1e-6f, T);
-        or_add_scale(s->residual, s->hidden, T * HID, 1.0f);
+    or_rmsnorm(s->hidden, s->residual, (const float *)L[2].data, HID, 1e-6f, T);
+    or_quantize(s->q, s->qs, s->hidden, T, (size_t)L[14].shape[1]);
+    lin(s->hidden, s, &L[14], T);
+    lin(s->aux, s, &L[15], T);
+    or_geglu(s->hidden, s->aux, (int)T, L[14].shape[0], L[14].shape[0], gt, gelu->shape[0], gelu->shape[1], gelu->shape[2]);
+    or_quantize(s->q, s->qs, s->hidden, T, (size_t)L[16].shape[1]);
+    lin(s->hidden, s, &L[16], T);
+    or_rmsnorm(s->hidden, s->hidden, (const float *)L[4].data, HID, 1e-6f, T);
+    or_add_scale(s->residual, s->hidden, T * HID, 1.0f);
 
-        or_quantize(s->q, s->qs, s->residual, T, HID);
-        lin(s->hidden, s, &L[6], T);
-        or_geglu(s->hidden, s->ple + (size_t)l * plw, (int)T, plw, NL * plw, gt, gelu->shape[0], gelu->shape[1], gelu->shape[2]);
-        or_quantize(s->q, s->qs, s->hidden, T, (size_t)L[7].shape[1]);
-        lin(s->hidden, s, &L[7], T);
-        or_rmsnorm(s->hidden, s->hidden, (const float *)L[5].data, HID, 1e-6f, T);
-        or_add_scale(s->residual, s->hidden, T * HID, ((const float *)L[1].data)[0]);
-    }
+    or_quantize(s->q, s->qs, s->residual, T, HID);
+    lin(s->hidden, s, &L[6], T);
+    or_geglu(s->hidden, s->ple + (size_t)l * plw, (int)T, plw, NL * plw, gt, gelu->shape[0], gelu->shape[1], gelu->shape[2]);
+    or_quantize(s->q, s->qs, s->hidden, T, (size_t)L[7].shape[1]);
+    lin(s->hidden, s, &L[7], T);
+    or_rmsnorm(s->hidden, s->hidden, (const float *)L[5].data, HID, 1e-6f, T);
+    or_add_scale(s->residual, s->hidden, T * HID, ((const float *)L[1].data)[0]);
+}
+
+/* forward restricted to the first `layers` layers (a testing aid for
+ * bisecting mismatches; layers = 35 is the reference's forward). */
+void or_forward_layers(const or_model *m, or_state *s, const int *tokens, size_t T, int start_pos, int layers) {
+    or_prologue(m, s, tokens, T);
+    for (int l = 0; l < layers; l++) or_layer(m, s, l, start_pos, T);
+}
+
+float *or_state_ple(or_state *s) { return s->ple; }
+
+/* logits() (gemma4.c:512-522) of the first `rows` (<= 512) residual rows at
+ * once, into out[rows][262144]: the same per-row arithmetic as or_logits, with
+ * the lm_head matrix read once for all rows. */
+void or_logits_rows(const or_model *m, or_state *s, size_t rows, float *out) {
+    const tens *E = &m->t[0], *norm = &m->t[2 + NL * 19];
+    or_rmsnorm(s->hidden, s->residual, (const float *)norm->data, HID, 1e-6f, rows);
+    or_quantize(s->q, s->qs, s->hidden, rows, HID);
+    or_linear(out, s->q, s->qs, rows, (const int8_t *)E->data, E->scales, E->shape[0], E->shape[1]);
+    or_softcap(out, rows * (size_t)E->shape[0]);
 }
 
 /* gemma4.c:512-522 logits: final norm of one residual row, quantise, tied

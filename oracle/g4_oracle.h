@@ -50,7 +50,15 @@ void or_state_free(or_state *s);
 void or_forward(const or_model *m, or_state *s, const int *tokens, size_t count, int start_pos);
 void or_forward_layers(const or_model *m, or_state *s, const int *tokens, size_t count, int start_pos, int layers);
 float *or_logits(const or_model *m, or_state *s, size_t row);
+/* Teacher-forced pieces of forward: the per-layer inputs of T tokens, and one
+ * layer applied to the residual rows (and per-layer inputs) in the state. */
+void or_prologue(const or_model *m, or_state *s, const int *tokens, size_t T);
+void or_layer(const or_model *m, or_state *s, int layer, int start_pos, size_t T);
 float *or_state_residual(or_state *s);
+/* Per-layer inputs [512 rows][35][256]. */
+float *or_state_ple(or_state *s);
+/* logits of residual rows [0, rows) into out[rows][262144]. */
+void or_logits_rows(const or_model *m, or_state *s, size_t rows, float *out);
 /* Key (which=0) or value (which=1) cache that `layer` reads. */
 float *or_state_cache(or_state *s, int layer, int which);
 int or_num_threads(void);

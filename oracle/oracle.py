@@ -79,6 +79,11 @@ class Oracle:
         L.or_state_residual.restype = C.POINTER(C.c_float)
         L.or_state_cache.argtypes = [C.c_void_p, C.c_int, C.c_int]
         L.or_state_cache.restype = C.POINTER(C.c_float)
+        L.or_state_ple.argtypes = [C.c_void_p]
+        L.or_state_ple.restype = C.POINTER(C.c_float)
+        L.or_prologue.argtypes = [C.c_void_p, C.c_void_p, _i32p, C.c_size_t]
+        L.or_layer.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_size_t]
+        L.or_logits_rows.argtypes = [C.c_void_p, C.c_void_p, C.c_size_t, _f32p]
         L.or_num_threads.restype = C.c_int
 
     # kernels ---------------------------------------------------------------
@@ -213,6 +218,35 @@ class OracleModel:
         p = self.o.lib.or_state_cache(self.state, layer, which)
         return np.ctypeslib.as_array(p, shape=(slots, head_dim)).copy()
 
+    # teacher forcing: state views the tests write into, and one layer at a time
+    def residual_view(self, rows):
+        """Writable view of the first `rows` residual rows of the state."""
+        p = self.o.lib.or_state_residual(self.state)
+        return np.ctypeslib.as_array(p, shape=(rows, 1536))
+
+    def ple_view(self, rows):
+        """Writable view of the per-layer inputs [rows][35][256] of the state."""
+        p = self.o.lib.or_state_ple(self.state)
+        return np.ctypeslib.as_array(p, shape=(rows, 35, 256))
+
+    def cache_view(self, layer, which, slots, head_dim):
+        """Writable view of the K (0) / V (1) ring that `layer` reads."""
+        p = self.o.lib.or_state_cache(self.state, layer, which)
+        return np.ctypeslib.as_array(p, shape=(slots, head_dim))
+
+    def prologue(self, tokens):
+        tokens = np.ascontiguousarray(tokens, np.int32)
+        self.o.lib.or_prologue(self.h, self.state, tokens, len(tokens))
+
+    def layer(self, layer, start_pos, rows):
+        self.o.lib.or_layer(self.h, self.state, layer, start_pos, rows)
+
+    def logits_rows(self, rows):
+        """logits() of residual rows [0, rows) of the state, [rows][262144]."""
+        out = np.empty((rows, 262144), np.float32)
+        self.o.lib.or_logits_rows(self.h, self.state, rows, out)
+        return out
+
     def close(self):
         if self.state:
             self.o.lib.or_state_free(self.state)
@@ -254,6 +288,29 @@ class Reference:
         L.softmax.argtypes = [_f32p, C.c_int]
         L.sample.argtypes = [_f32p, C.c_int, C.c_float]
         L.sample.restype = C.c_int
+        L.g4synth_image_bytes.restype = C.c_uint64
+        L.g4synth_fill.argtypes = [C.c_void_p, C.c_uint64, C.c_uint64, C.c_uint]
+        L.g4synth_fill.restype = C.c_int
+
+    def synth_image(self, seed=0, flags=0):
+        """The seeded synthetic model image (the same bytes as g4cuda.synth_image),
+        written by the copy of the synthetic-model writer linked into this
+        library, so the reference leg loads no other shared object."""
+        n = self.lib.g4synth_image_bytes()
+        raw = np.empty(n + 4096, np.uint8)
+        off = (-raw.ctypes.data) % 4096
+        img = raw[off:off + n]
+        if self.lib.g4synth_fill(img.ctypes.data, n, seed, flags) != 0:
+            raise RuntimeError("g4synth_fill failed")
+        return img
+
+    @staticmethod
+    def use_all_cores():
+        """The reference sizes its OpenMP team from OMP_NUM_THREADS when that is
+        set, else one thread per physical core (gemma4.c:182-188). Launchers such
+        as torchrun export OMP_NUM_THREADS=1; dropping it restores the
+        reference's own default. Returns the value removed (or None)."""
+        return os.environ.pop("OMP_NUM_THREADS", None)
 
     def threads(self):
         return self.lib.g4ref_threads()

@@ -42,6 +42,10 @@ constexpr int kAttnBytes = cmax(decode_smem_floats(256, kKT256), decode_smem_flo
 constexpr int kGemvScratch = kMaxK + (kMaxK / 64) * 4 + G4_HIDDEN * 4;   // xq + xs + vec bytes
 constexpr int kDotsBytes = 32 * (kMaxK / 64) * 4;   // group-parallel dots: [G][32 rows] int32
 constexpr int kScratchBytes = cmax(cmax(kAttnBytes, kGemvScratch + kDotsBytes), (512 + 16) * 4);
+// the GELU table's copy sits in the group-parallel dots region past the dots of
+// K <= 1536 ([24 groups][32 rows] int32); GEGLU GEMVs have K = 1536
+constexpr int kGeluOff = 8192;
+static_assert(kGeluOff >= 32 * (1536 / 64) * 4 && kGeluOff + 4096 * 4 <= kDotsBytes, "GELU table copy");
 
 constexpr int kOffRing = 0;
 constexpr int kOffFull = kOffRing + (int)kRingBytes;
@@ -195,16 +199,18 @@ G4_DEV float scale_at(uint2 s4, int k) {
 
 // Per-row epilogue of a finished row (lane = row within the stage). GEGLU
 // pairs are lanes (2i, 2i + 1) of the same warp, so every lane of the warp
-// must call it.
-G4_DEV void row_epilogue(const GemvArgs &a, int epi, int n, float acc, bool active, float &best_v, int &best_i) {
+// must call it. gelu: the GELU table (shared memory); u: the row's per-layer
+// input (EPI_PLE), loaded before the row's dots so its latency is hidden.
+G4_DEV void row_epilogue(const GemvArgs &a, int epi, int n, float acc, bool active, const float *gelu, float u,
+                         float &best_v, int &best_i) {
     const float up = __shfl_down_sync(0xffffffffu, acc, 1);
     if (!active) return;
     if (epi == EPI_STORE) {
         a.out[n] = acc;
     } else if (epi == EPI_GEGLU_PAIR) {
-        if ((n & 1) == 0) a.out[n >> 1] = geglu_one(acc, up, a.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+        if ((n & 1) == 0) a.out[n >> 1] = geglu_one(acc, up, gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
     } else if (epi == EPI_PLE) {
-        a.out[n] = geglu_one(acc, a.ple_u[n], a.gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
+        a.out[n] = geglu_one(acc, u, gelu, 4096, -8.0f, 8.0f, 4095.0f / 16.0f);
     } else {
         const float sv = __fmul_rn(30.0f, tanhf(__fdiv_rn(acc, 30.0f)));   // gemma4.c:519
         a.out[n] = sv;
@@ -234,8 +240,20 @@ G4_DEV __noinline__ void gemv_op(const GemvArgs &a, const CtaRows cr, int pro, i
     float *vec = (float *)(smem + kOffScratch + kMaxK + (kMaxK / 64) * 4);
     float *red = (float *)(smem + kOffRed);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // GEGLU epilogues look their GELU values up in a shared-memory copy of the
+    // table, copied in while the prologue runs (past the group dots of K <= 1536)
+    float *gelu_s = (float *)(smem + kOffScratch + kGemvScratch + kGeluOff);
+    const bool geglu = epi == EPI_GEGLU_PAIR || epi == EPI_PLE;
+    if (geglu) {
+        for (int i = tid; i < 4096 / 4; i += kConsumers) cp_async16(gelu_s + 4 * i, a.gelu + 4 * i);
+        cp_async_commit();
+    }
+    // the per-layer input of warp 0's rows (group-parallel EPI_PLE), early
+    float u0 = 0.0f;
+    if (epi == EPI_PLE && warp == 0 && lane < cr.rows) u0 = a.ple_u[cr.n0 + lane];
 
     decode_prologue(a, pro, xq, xs, vec, red);
+    if (geglu) cp_async_wait<0>();
     csync();
     if (tr && tid == 0) atomicMax(tr, (unsigned long long)g4_globaltimer());
     float best_v = -INFINITY;
@@ -268,6 +286,7 @@ G4_DEV __noinline__ void gemv_op(const GemvArgs &a, const CtaRows cr, int pro, i
             }
             const int nr = stage_nr(cr, j);
             const int r = lane < nr ? lane : nr - 1;   // idle lanes re-read the last row
+            const float u = epi == EPI_PLE ? a.ple_u[cr.n0 + j * cr.R + r] : 0.0f;
             const uint8_t *sb = ring + st % kRingBytes;
             const uint8_t *wr = sb + (size_t)r * K;
             const uint16_t *sr = (const uint16_t *)(sb + (size_t)nr * K) + r * G;
@@ -285,7 +304,7 @@ G4_DEV __noinline__ void gemv_op(const GemvArgs &a, const CtaRows cr, int pro, i
             }
             __syncwarp();
             if (lane == 0) atomicAdd(&done[(cs + j) % kFifo], 1);   // the stage is no longer read
-            row_epilogue(a, epi, cr.n0 + j * cr.R + lane, acc, lane < nr, best_v, best_i);
+            row_epilogue(a, epi, cr.n0 + j * cr.R + lane, acc, lane < nr, gelu_s, u, best_v, best_i);
         }
     } else {
         // ---- group-parallel: (row, group) dots of every stage spread over all
@@ -332,7 +351,7 @@ G4_DEV __noinline__ void gemv_op(const GemvArgs &a, const CtaRows cr, int pro, i
                 acc = chain_step(acc, D[(g + 2) * 32 + r], scale_at(s4, 2), x4.z);
                 acc = chain_step(acc, D[(g + 3) * 32 + r], scale_at(s4, 3), x4.w);
             }
-            row_epilogue(a, epi, cr.n0 + lane, acc, lane < cr.rows, best_v, best_i);
+            row_epilogue(a, epi, cr.n0 + lane, acc, lane < cr.rows, gelu_s, u0, best_v, best_i);
         }
     }
     // every warp leaves with the ring position after the op's last stage

@@ -76,9 +76,10 @@ __device__ float row_sumsq(const float (&v)[PER], bool strict, float *vec, float
 // (gemma4.c:265-279). All consumer threads work: thread t takes the float4s at
 // t + 256 j, so each 64-value group is one half-warp's 16 float4s; the group
 // maximum is a 4-step shuffle reduction (exact in any order). Loads are issued
-// U float4s ahead, so a global source costs ceil(K / (4 * 256 * U)) round trips.
+// U float4s ahead, so a global source costs ceil(K / (4 * 256 * U)) round trips:
+// one for every row width of the model (K <= 12288).
 __device__ __noinline__ void quantize_row(const float *src, int K, int8_t *xq, float *xs) {
-    constexpr int U = 4;
+    constexpr int U = 12;
     const int tid = threadIdx.x, n4 = K >> 2;   // K % 128 == 0: a warp is all in or all out
     const float4 *s4 = (const float4 *)src;
     for (int i0 = tid; i0 < n4; i0 += kConsumers * U) {

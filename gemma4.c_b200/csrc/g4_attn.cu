@@ -77,6 +77,8 @@ struct DecodeCfg {
     static constexpr int KT = DecodeKT<HD>::value;
     static constexpr size_t smem = (size_t)decode_smem_floats(HD, KT) * 4;
 };
+static_assert(DecodeCfg<256>::smem <= 227 * 1024 && DecodeCfg<512>::smem <= 227 * 1024,
+              "shared memory budget of the decode / batch-row attention CTAs");
 
 template <int HD>
 __global__ void __launch_bounds__(256) k_attn_decode(const AttnArgs a, int splits) {

@@ -456,6 +456,10 @@ G4_DEV void produce(const DecodeParams &P, uint8_t *smem, volatile int *fail, in
     const uint64_t pol = l2_policy_evict_first();
     unsigned head = 0, tail = 0;   // monotonic ring positions: next free byte, end of released space
     int cs = 0, oldest = 0;        // next stage to issue, oldest stage not yet released
+    if (P.starve) {                // test aid: nothing is issued, every stage wait runs out
+        *issued = 0;
+        return;
+    }
     for (int o = 0; o < P.nops && !*fail; o++) {
         const DecodeOp &op = P.ops[o];
         if (op.type != OP_GEMV) continue;

@@ -122,6 +122,7 @@ struct g4_ctx {
     cudaEvent_t dump_done[2] = {nullptr, nullptr}, dump_copied[2] = {nullptr, nullptr};
     std::vector<int> blast;          // last row of each sequence of the last batch
     bool pending = false;            // a single-token forward waiting to be launched
+    bool starve_next = false;        // g4_test_starve_next_step
     DecodeOp *dec_fwd = nullptr, *dec_fwdlog = nullptr;
     int n_fwd = 0, n_fwdlog = 0, dec_cur = 0, dec_layers = 0;
     unsigned long long *bar = nullptr, *bar_base = nullptr;
@@ -1012,6 +1013,8 @@ cudaError_t launch_decode(g4_ctx *c, bool with_logits, unsigned long long *trace
     p.bar = c->bar;
     p.bar_base = c->bar_base;
     p.err = c->err;
+    p.starve = c->starve_next ? 1 : 0;
+    c->starve_next = false;
     return g4_launch_decode(p, c->num_sms, c->st);
 }
 
@@ -1556,6 +1559,13 @@ int g4_profile_decode(g4_ctx *c, int token, int pos, float ms[3], double bytes[3
     for (int i = 0; i <= Prof::kMax; i++) cudaEventDestroy(pr->ev[i]);
     delete pr;
     return rc ? rc : check_device_error(c);
+}
+
+int g4_test_starve_next_step(g4_ctx *c) {
+    if (!c) return G4_ERR_INVALID;
+    if (!c->persistent || c->strict) return fail(c, G4_ERR_STATE, "starve: persistent decode is off");
+    c->starve_next = true;
+    return G4_OK;
 }
 
 int g4_launches_per_token(g4_ctx *c, int *n) {

@@ -202,6 +202,8 @@ struct DecodeParams {
     unsigned long long *bar;          // grid-barrier arrival counter (monotonic)
     unsigned long long *bar_base;     // its value when this launch starts
     int *err;
+    int starve;                       // test aid: the producer issues no weight copy, so the
+                                      // consumers' bounded waits run out (G4D_TIMEOUT_FULL)
     // optional timeline (zeroed by the host): [0] latest CTA start, then per op o
     // at 1+6o: latest prologue end (GEMV), latest op end, latest barrier exit,
     // longest stage wait of a consumer warp (ns), latest issue of the op's

@@ -208,12 +208,17 @@ int g4_topk_noalloc(const float *logits, int n, int k, float *values, int *ids, 
     NoAllocScratch s;
     if (noalloc_scratch(dev, &s) != cudaSuccess) return G4_ERR_CUDA;
     // pass 1 writes blocks * k candidates and pass 2 reads exactly those, so
-    // nothing in the shared scratch has to start at zero
+    // nothing in the shared scratch has to start at zero. Each launch reports
+    // its own status (an earlier, unrelated error pending on this thread is
+    // neither returned nor cleared here).
     const cudaStream_t st = (cudaStream_t)stream;
     const int blocks = (n + kNoAllocSlice - 1) / kNoAllocSlice;
-    k_topk_pass<kNoAllocSlice><<<blocks, kTopkThreads, 0, st>>>(logits, nullptr, n, k, s.v, s.i);
-    k_topk_pass<kTopkSlice><<<1, kTopkThreads, 0, st>>>(s.v, s.i, blocks * k, k, values, ids);
-    return cudaGetLastError() == cudaSuccess ? G4_OK : G4_ERR_CUDA;
+    cudaError_t e = g4_launch(k_topk_pass<kNoAllocSlice>, dim3(blocks), dim3(kTopkThreads), 0, st, false, logits,
+                              (const int *)nullptr, n, k, s.v, s.i);
+    if (e == cudaSuccess)
+        e = g4_launch(k_topk_pass<kTopkSlice>, dim3(1), dim3(kTopkThreads), 0, st, false, (const float *)s.v,
+                      (const int *)s.i, blocks * k, k, values, ids);
+    return e == cudaSuccess ? G4_OK : G4_ERR_CUDA;
 }
 
 int g4k_quantize(const float *x, int rows, int width, int8_t *q, float *s) {

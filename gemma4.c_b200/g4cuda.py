@@ -67,6 +67,7 @@ def load(path=LIB_PATH):
     L.g4_set_option.argtypes = [vp, C.c_int, C.c_int]
     L.g4_read_residual.argtypes = [vp, C.c_size_t, _f32p]
     L.g4_read_cache.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
+    L.g4_test_starve_next_step.argtypes = [vp]
     L.g4_read_ple.argtypes = [vp, C.c_size_t, _f32p]
     L.g4_read_seq_cache.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, _f32p]
     L.g4_stream.argtypes = [vp]

@@ -102,9 +102,12 @@ int g4_set_seed(g4_ctx *ctx, uint64_t seed);
  * image, which every GPU that loads the library keeps until exit; n above
  * 262144 or k above 64 is rejected with G4_ERR_INVALID. The first call on a
  * device looks up that array's device address, so make it before capturing a
- * stream. All calls share the array: calls whose kernels overlap on the GPU
+ * stream. The looked-up address is kept for the life of the process: after
+ * cudaDeviceReset on a device, restart the process before calling this again.
+ * All calls share the array: calls whose kernels overlap on the GPU
  * (different streams, no ordering between them) race on it. Asynchronous: no
- * synchronisation, results valid once the stream reaches them. */
+ * synchronisation, results valid once the stream reaches them; a launch error
+ * of its own two kernels is returned as G4_ERR_CUDA. */
 int g4_topk_noalloc(const float *logits, int n, int k, float *values, int *ids, void *stream);
 
 /* Wait for queued work; returns any device-side error. */
@@ -204,6 +207,12 @@ int g4_profile_decode(g4_ctx *ctx, int token, int pos, float ms[3], double bytes
 int g4_trace_decode(g4_ctx *ctx, int token, int pos, int cap, int *types, double *t_ns, int *nops);
 /* Kernels one single-token decode step (forward + logits) launches. */
 int g4_launches_per_token(g4_ctx *ctx, int *n);
+/* Failure-path test aid (no reference counterpart): the next persistent
+ * single-token step's weight producers issue no copies, so every consumer's
+ * bounded wait (2 s) runs out; the step then reports G4_ERR_DEVICE at the next
+ * synchronising call, the context resets its error word and barrier counters,
+ * and later steps run normally. G4_ERR_STATE when persistent decode is off. */
+int g4_test_starve_next_step(g4_ctx *ctx);
 
 /* ---- synthetic model images (benchmarks and parity tests) ----
  * A seeded random-init Gemma 4 E2B in the exact .bin layout gemma4.c reads. */

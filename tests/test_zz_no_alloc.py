@@ -46,3 +46,29 @@ def test_topk_noalloc_matches_g4_topk(g4, image):
                                  None) == -1
         assert L.g4_topk_noalloc(big, g4.VOCAB, 65, C.c_void_p(d_vals.data_ptr()), C.c_void_p(d_ids.data_ptr()),
                                  None) == -1
+
+
+def test_topk_noalloc_ragged_sizes(g4):
+    """Sizes that are not whole 4096-value slices (a short last slice padded
+    inside the selection, a single slice, k close to n), two calls in a row
+    per size, against a stable host sort: value descending, ties to the lower
+    index (the reference's candidate order, gemma4.c:544-551)."""
+    torch = pytest.importorskip("torch")
+    L = g4.load()
+    rng = np.random.default_rng(22)
+    for n in (64, 4097, 5000):
+        x = rng.standard_normal(n).astype(np.float32)
+        x[rng.integers(0, n, size=8)] = x[0]          # a few exact ties
+        d_x = torch.from_numpy(x).to("cuda:0")
+        order = np.lexsort((np.arange(n), -x.astype(np.float64)))
+        for k in (1, min(64, n)):
+            for _ in range(2):
+                d_vals = torch.empty(k, dtype=torch.float32, device="cuda:0")
+                d_ids = torch.empty(k, dtype=torch.int32, device="cuda:0")
+                torch.cuda.synchronize()
+                rc = L.g4_topk_noalloc(C.c_void_p(d_x.data_ptr()), n, k, C.c_void_p(d_vals.data_ptr()),
+                                       C.c_void_p(d_ids.data_ptr()), None)
+                assert rc == 0
+                torch.cuda.synchronize()
+                assert np.array_equal(d_ids.cpu().numpy(), order[:k].astype(np.int32)), (n, k)
+                assert np.array_equal(d_vals.cpu().numpy(), x[order[:k]]), (n, k)

@@ -308,19 +308,37 @@ def prefill_timed(m, n, reps, dist):
     return n / (np.mean(times) / 1e3), float(np.mean(times))
 
 
+def pack_sequences(plen, world, per_gpu):
+    """Bin-pack sequences over `world` replicas, `per_gpu` each: longest prompt
+    first onto the replica with the fewest prompt tokens so far (prefill time
+    follows prompt tokens; every replica then finishes together)."""
+    load, members = [0] * world, [[] for _ in range(world)]
+    for i in np.argsort(-plen, kind="stable"):
+        r = min((r for r in range(world) if len(members[r]) < per_gpu), key=lambda r: load[r])
+        members[r].append(int(i))
+        load[r] += int(plen[i])
+    return [sorted(mb) for mb in members]
+
+
 def batched_serving(m, dist, seqs=64, profile_step=None):
-    """Benchmark config 5 (multi-sequence serving) on this GPU: 64 independent sequences, prompts
-    log-uniform in [128, 8192], decode lengths uniform in [32, 512], ids
-    uniform (seed 2 + rank). Each prompt is prefilled (512-token chunks) and its
-    first token sampled; then all unfinished sequences decode together, one
-    token per sequence per step, greedy, through g4_forward_batch /
-    g4_logits_batch (argmax read back every step). Times: CUDA events on the
-    library stream, max over ranks."""
+    """Benchmark config 5 (multi-sequence serving): one ragged batch of 64 x N
+    independent sequences (prompts log-uniform in [128, 8192], decode lengths
+    uniform in [32, 512], ids uniform, seed 2), bin-packed by prompt length
+    onto the N replicas, 64 sequences each (N = 1: all 64 in draw order). Each
+    prompt is prefilled (512-token chunks) and its first token sampled; then
+    all unfinished sequences of a replica decode together, one token per
+    sequence per step, greedy, through g4_forward_batch / g4_logits_batch
+    (argmax read back every step). Times: CUDA events on the library stream,
+    max over ranks."""
     import g4cuda as g4
-    rng = np.random.default_rng(2 + dist.rank)
-    plen = np.exp(rng.uniform(np.log(128), np.log(8192), seqs)).astype(np.int64)
-    dlen = rng.integers(32, 513, seqs)
-    prompts = [rng.integers(0, g4.VOCAB, size=int(n)).astype(np.int32) for n in plen]
+    rng = np.random.default_rng(2)
+    total = seqs * dist.world
+    plen_all = np.exp(rng.uniform(np.log(128), np.log(8192), total)).astype(np.int64)
+    dlen_all = rng.integers(32, 513, total)
+    mine = pack_sequences(plen_all, dist.world, seqs)[dist.rank]
+    plen, dlen = plen_all[mine], dlen_all[mine]
+    prompts_all = [rng.integers(0, g4.VOCAB, size=int(n)).astype(np.int32) for n in plen_all]
+    prompts = [prompts_all[i] for i in mine]
     m.seq_alloc(seqs, int(plen.max() + dlen.max()))
     m.sync()
     dist.barrier()
@@ -368,8 +386,8 @@ def batched_serving(m, dist, seqs=64, profile_step=None):
     hbm_r = dist.gather((steps * weights + kv_bytes) / (dec_ms_r / 1e3) / 1e9)
     pre_ms, dec_ms = max(pre_r), max(dec_r)
     return {
-        "workload": f"{seqs} sequences per GPU, prompts log-uniform [128, 8192], decode lengths U[32, 512], "
-                    f"greedy, seed 2+rank",
+        "workload": f"{seqs} x {dist.world} sequences (seed 2), prompts log-uniform [128, 8192], decode lengths "
+                    f"U[32, 512], greedy; bin-packed by prompt length, {seqs} per GPU",
         "prefill_tok_s": sum(prompts_r) / (pre_ms / 1e3),
         "decode_tok_s": sum(gen_r) / (dec_ms / 1e3),
         "total_tok_s": (sum(prompts_r) + sum(newtok_r)) / ((pre_ms + dec_ms) / 1e3),

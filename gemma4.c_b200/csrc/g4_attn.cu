@@ -234,22 +234,6 @@ struct Pre {
 static_assert(Pre<256>::kSmem <= 227 * 1024 && Pre<512>::kSmem <= 227 * 1024,
               "shared memory budget of the prefill attention CTA");
 
-// Quantise (gemma4.c:265-279) one 64-wide group held as 4 values in each of 16
-// consecutive lanes: the group's max |x| over the 16 lanes, then scale and
-// rounded int8 values exactly as quantize(). All 32 lanes must call it.
-G4_DEV void quant_lanes16(float4 v, int8_t *q, float *xs, float *xsT, bool leader) {
-    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
-#pragma unroll
-    for (int off = 1; off < 16; off <<= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    const float sc = quant_scale(m), inv = quant_inv(sc);
-    *(char4 *)q = make_char4((signed char)quant_one(v.x, inv), (signed char)quant_one(v.y, inv),
-                             (signed char)quant_one(v.z, inv), (signed char)quant_one(v.w, inv));
-    if (leader) {
-        *xs = sc;
-        if (xsT) *xsT = sc;
-    }
-}
-
 // Stage BK key rows [kt, kt + nt) of a ring into shared memory (row stride
 // dstride); rows past nt are zero.
 template <int HD>

@@ -1,0 +1,681 @@
+// g4_attn_tc.cu — prefill attention on the 5th-generation tensor cores.
+//
+// Reference: attention (gemma4.c:411-461) for a chunk of T tokens: per query
+// head, unscaled scores q.k over the visible keys (attention_scores,
+// :281-294), softmax (:400-408) and the probability-weighted sum of the values
+// (weighted_value_sum, :296-307). Same semantics as the CUDA-core kernel of
+// g4_attn.cu (8 query heads on one KV head, causal, sliding window on the
+// 256-wide layers), different floating-point order: outputs agree within fp32
+// rounding, not bit for bit.
+//
+// Both contractions are tcgen05.mma kind::tf32 with the 3xTF32 split: every
+// fp32 operand x is stored as hi = tf32(x) and lo = tf32(x - hi) (round to
+// nearest), and each K step issues hi.hi + hi.lo + lo.hi into one fp32 TMEM
+// accumulator. The dropped lo.lo term and the roundings leave a relative
+// error near 2^-21 per product (an fp32 FMA: 2^-24).
+//
+// The chunk's R = 8T query rows (row r = token r / 8, head r % 8) form 128-row
+// tiles of 16 tokens. Five launches:
+//   1. k_tc_split   Q rows, the chunk's keys [kbase, npos) and their values as
+//                   hi/lo pairs; V transposed to [HD][keys] so that both GEMMs
+//                   read K-major tiles;
+//   2. k_tc_gemm<0> S = Q K^T per 128-row x 256-key tile (K = HD), only tiles
+//                   that hold a visible key; the epilogue stores S and every
+//                   row's max over the visible keys of each 128-key half tile;
+//   3. k_tc_soft    per row: m = max of its half-tile maxima, p = exp(s - m) on
+//                   visible keys (0 elsewhere), l = sum p; p stored as hi (over
+//                   S) and lo;
+//   4. k_tc_gemm<1> O = P V per 128-row x 256-dim tile over one piece of the
+//                   row tile's keys (split K, so every SM has work), partial
+//                   tiles stored;
+//   5. k_tc_out     O = (sum of the pieces, in order) / l per token, stored and
+//                   quantised for o_proj (gemma4.c:459).
+// The schedule depends only on (T, start position, SM count): deterministic.
+//
+// GEMM roles (10 warps, one CTA per SM, persistent over units):
+//   warp 0      TMA producer: per stage the 32-wide K slice of A hi/lo (128
+//               rows) and B hi/lo (256 rows) with the 128-byte swizzle;
+//   warp 1      allocates 512 TMEM columns (two 256-column accumulators, so a
+//               unit's epilogue overlaps the next unit's MMAs); one lane issues
+//               3 x 4 MMAs (M 128, N 256, K 8) per stage;
+//   warps 2-9   epilogue: thread = row (TMEM lane), two warps per lane quadrant
+//               with 128 columns each.
+// Waits are bounded (mbar_wait); on a timeout every role leaves its loop, the
+// CTA waits (bounded) for its copies and MMAs in flight, and frees TMEM.
+#include <cuda.h>
+
+#include "g4_attn_dev.cuh"
+#include "g4_tc.cuh"
+
+namespace {
+
+constexpr int kTM = 128;                  // query rows per tile (16 tokens x 8 heads)
+constexpr int kTN = 256;                  // keys (S) or value dimensions (O) per tile
+constexpr int kTK = 32;                   // fp32 K elements per stage: one 128-byte row
+constexpr int kTStages = 2;
+constexpr int kTileA = kTM * kTK * 4;     // 16 KB
+constexpr int kTileB = kTN * kTK * 4;     // 32 KB
+constexpr int kStageBytes = 2 * kTileA + 2 * kTileB;   // hi and lo of both operands
+constexpr int kEpiWarps = 8;
+constexpr int kThreads = 64 + 32 * kEpiWarps;
+constexpr int kOffBar = kTStages * kStageBytes;
+constexpr int kSmem = kOffBar + 128 + 1024;          // + barriers, + 1 KB for alignment
+constexpr int kTokTile = kTM / kHeads;                // 16 tokens per row tile
+constexpr int kMaxRowTiles = G4_BATCH / kTokTile;     // 32
+constexpr int kMinPiece = 16;                         // K stages per O unit, at least
+#ifndef G4_TC_SPLIT_ACC
+#define G4_TC_SPLIT_ACC 1
+#endif
+// The accumulator adds every MMA's products with rounding toward zero at its own
+// magnitude, so its error grows with the number of MMAs landing at the full
+// magnitude: the hi.hi products go to one accumulator and the two correction
+// products (2^-11 smaller) to a second one, summed in fp32 by the epilogue.
+constexpr bool kSplitAcc = G4_TC_SPLIT_ACC != 0;
+constexpr int kBufs = kSplitAcc ? 1 : 2;              // accumulator (pairs) in TMEM
+// D fp32, A and B tf32, both K-major, N = 256 (>> 3), M = 128 (>> 4)
+constexpr uint32_t kIdesc =
+    (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kTN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
+static_assert(kSmem <= 227 * 1024, "shared memory budget of the attention GEMM CTA");
+static_assert(kMaxRowTiles <= 32, "the unit prefix is one warp scan");
+
+enum : int { kCodeFull = 0xa01, kCodeEmpty = 0xa02, kCodeTfull = 0xa03, kCodeTempty = 0xa04 };
+
+// The chunk's schedule, computed the same way on the host and the device.
+struct TcPlan {
+    int T, sp, window, hd;
+    int R, mt;        // query rows, 128-row tiles
+    int kbase, nk;    // the workspace holds keys [kbase, kbase + nk)
+    int kpad;         // row stride (keys) of S, P and V^T: nk rounded up to 256
+    int nd;           // 256-wide value-dimension tiles: hd / 256
+    int piece;        // O units: K stages (32 keys) per unit
+};
+
+__host__ __device__ inline int tc_first_key(int p, int window) { return (window && p + 1 > window) ? p + 1 - window : 0; }
+__host__ __device__ inline int imin(int a, int b) { return a < b ? a : b; }
+
+// Visible keys of row tile m relative to kbase: [kb, ke) (the first token's
+// first key to the last token's position).
+__host__ __device__ inline void tile_keys(const TcPlan &p, int m, int *kb, int *ke) {
+    const int t0 = m * kTokTile, t1 = imin(p.T, t0 + kTokTile) - 1;
+    *kb = tc_first_key(p.sp + t0, p.window) - p.kbase;
+    *ke = p.sp + t1 + 1 - p.kbase;
+}
+// S units of row tile m: its 256-key tiles holding a visible key
+__host__ __device__ inline int units_s(const TcPlan &p, int m) {
+    int kb, ke;
+    tile_keys(p, m, &kb, &ke);
+    return (ke + kTN - 1) / kTN - kb / kTN;
+}
+// O units of row tile m: value-dimension tiles x pieces of its K stages
+__host__ __device__ inline int pieces_o(const TcPlan &p, int m) {
+    int kb, ke;
+    tile_keys(p, m, &kb, &ke);
+    const int c0 = kb / kTK, c1 = (ke + kTK - 1) / kTK;
+    return (c1 - c0 + p.piece - 1) / p.piece;
+}
+__host__ __device__ inline int units_o(const TcPlan &p, int m) { return p.nd * pieces_o(p, m); }
+
+struct TcAttnArgs {
+    TcPlan p;
+    const float *qkv;
+    int qkv_stride;
+    const float *kcache, *vcache;
+    int mask;
+    float *qh, *ql;       // [R][HD]
+    float *kh, *kl;       // [nk][HD]
+    float *vh, *vl;       // [HD][kpad]
+    float *s, *pl;        // [R][kpad]: S, then P hi over it; P lo
+    float *smax;          // [R][kpad / 128]
+    float *lsum;          // [R]
+    float *opart;         // [O units][128][256]
+    float *out;           // [T][8 HD]
+    int8_t *xq;
+    float *xs, *xsT;
+    int quant_out;
+    int *err;
+};
+
+// Round to the nearest tf32 value (10 explicit mantissa bits; ties away from zero).
+G4_DEV float tf32_rn(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
+G4_DEV void split_tf32(float x, float &hi, float &lo) {
+    hi = tf32_rn(x);
+    lo = tf32_rn(__fsub_rn(x, hi));   // x - hi is exact
+}
+G4_DEV void split4(float4 x, float4 &h, float4 &l) {
+    split_tf32(x.x, h.x, l.x);
+    split_tf32(x.y, h.y, l.y);
+    split_tf32(x.z, h.z, l.z);
+    split_tf32(x.w, h.w, l.w);
+}
+
+// pre[0..mt] = prefix sums of the units of each row tile (warp 0; mt <= 32)
+template <int MODE>
+G4_DEV void unit_prefix(const TcPlan &p, int *pre) {
+    const int lane = threadIdx.x & 31;
+    int v = lane < p.mt ? (MODE == 0 ? units_s(p, lane) : units_o(p, lane)) : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += n;
+    }
+    if (lane == 0) pre[0] = 0;
+    if (lane < p.mt) pre[lane + 1] = v;
+}
+
+struct Unit {
+    int m, n;     // row tile; key tile (S) or value-dimension tile (O)
+    int c0, c1;   // K stages [c0, c1)
+};
+template <int MODE, int HD>
+G4_DEV Unit unit_of(const TcPlan &p, const int *pre, int u) {
+    Unit x;
+    int m = 0;
+    while (pre[m + 1] <= u) m++;
+    const int v = u - pre[m];
+    int kb, ke;
+    tile_keys(p, m, &kb, &ke);
+    x.m = m;
+    if (MODE == 0) {
+        x.n = kb / kTN + v;
+        x.c0 = 0;
+        x.c1 = HD / kTK;
+    } else {
+        const int c0 = kb / kTK, c1 = (ke + kTK - 1) / kTK, np = (c1 - c0 + p.piece - 1) / p.piece;
+        x.n = v / np;
+        x.c0 = c0 + (v % np) * p.piece;
+        x.c1 = imin(c1, x.c0 + p.piece);
+    }
+    return x;
+}
+
+// ---------------------------------------------------------------------------
+// 1. hi/lo operands. grid (blocks, 3): y = 0 Q rows, 1 key rows, 2 V^T tiles.
+template <int HD>
+__global__ void __launch_bounds__(256) k_tc_split(const TcAttnArgs a) {
+    __shared__ float tile[32][33];
+    const TcPlan &p = a.p;
+    const int job = blockIdx.y;
+    if (job < 2) {
+        const long long n4 = (long long)(job == 0 ? p.R : p.nk) * (HD / 4);
+        for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < n4; i += (long long)gridDim.x * 256) {
+            const int r = (int)(i / (HD / 4)), c4 = (int)(i % (HD / 4));
+            const float *src = job == 0 ? a.qkv + (size_t)(r >> 3) * a.qkv_stride + (r & 7) * HD + c4 * 4
+                                        : a.kcache + (size_t)((p.kbase + r) & a.mask) * HD + c4 * 4;
+            float4 h, l;
+            split4(*(const float4 *)src, h, l);
+            const size_t o = (size_t)r * HD + c4 * 4;
+            *(float4 *)((job == 0 ? a.qh : a.kh) + o) = h;
+            *(float4 *)((job == 0 ? a.ql : a.kl) + o) = l;
+        }
+        return;
+    }
+    // V^T through shared memory, 32 keys x 32 dimensions per tile
+    const int kt = (p.nk + 31) / 32, ntiles = kt * (HD / 32);
+    for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
+        const int k0 = (ti / (HD / 32)) * 32, d0 = (ti % (HD / 32)) * 32;
+        for (int i = threadIdx.x; i < 32 * 32; i += 256) {
+            const int kr = i >> 5, dc = i & 31;
+            tile[kr][dc] = k0 + kr < p.nk ? a.vcache[(size_t)((p.kbase + k0 + kr) & a.mask) * HD + d0 + dc] : 0.0f;
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < 32 * 32; i += 256) {
+            const int dr = i >> 5, kc = i & 31;
+            if (k0 + kc < p.nk) {
+                float h, l;
+                split_tf32(tile[kc][dr], h, l);
+                const size_t o = (size_t)(d0 + dr) * p.kpad + k0 + kc;
+                a.vh[o] = h;
+                a.vl[o] = l;
+            }
+        }
+        __syncthreads();
+    }
+}
+
+// 32 columns of this lane's accumulator (plus its correction accumulator, 256
+// columns on, when split), as fp32 bits.
+G4_DEV void load_acc(uint32_t taddr, int (&v)[32]) {
+    tmem_ld32(taddr, v);
+    if constexpr (kSplitAcc) {
+        int w[32];
+        tmem_ld32(taddr + kTN, w);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = __float_as_int(__fadd_rn(__int_as_float(v[j]), __int_as_float(w[j])));
+    } else {
+        tmem_wait_ld();
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 2 and 4. The 3xTF32 GEMMs. MODE 0: A = Q, B = K, units (row tile, key tile);
+// MODE 1: A = P, B = V^T, units (row tile, dimension tile, piece of keys).
+template <int MODE, int HD>
+__global__ void __launch_bounds__(kThreads, 1)
+    k_tc_gemm(const __grid_constant__ CUtensorMap map_ah, const __grid_constant__ CUtensorMap map_al,
+              const __grid_constant__ CUtensorMap map_bh, const __grid_constant__ CUtensorMap map_bl,
+              const TcAttnArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = (uint8_t *)(((uintptr_t)smem_raw + 1023) & ~(uintptr_t)1023);
+    uint64_t *full = (uint64_t *)(smem + kOffBar);
+    uint64_t *empty = full + kTStages;
+    uint64_t *tfull = empty + kTStages;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_slot = (uint32_t *)(drain + 1);
+    __shared__ int pre[kMaxRowTiles + 1];
+    __shared__ int fail, issued;
+    const TcPlan &p = a.p;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    if (warp == 0) unit_prefix<MODE>(p, pre);
+    if (tid == 32) {
+        for (int s = 0; s < kTStages; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < kBufs; b++) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], kEpiWarps);
+        }
+        mbar_init(drain, 1);
+        mbar_fence_init();
+        fail = 0;
+        issued = 0;
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                     "r"(2 * kTN)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const int units = pre[p.mt];
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int k = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
+                const Unit x = unit_of<MODE, HD>(p, pre, u);
+                const int ay = x.m * kTM, by = x.n * kTN;
+                for (int c = x.c0; c < x.c1; c++, k++) {
+                    const int s = k % kTStages, use = k / kTStages;
+                    if (use > 0 && !mbar_wait(&empty[s], (use - 1) & 1, a.err, G4D_TIMEOUT_EMPTY | (kCodeEmpty << 8))) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *st = smem + s * kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d(st, &map_ah, c * kTK, ay, &full[s]);
+                    tma_load_2d(st + kTileA, &map_al, c * kTK, ay, &full[s]);
+                    tma_load_2d(st + 2 * kTileA, &map_bh, c * kTK, by, &full[s]);
+                    tma_load_2d(st + 2 * kTileA + kTileB, &map_bl, c * kTK, by, &full[s]);
+                }
+            }
+            if (!ok) fail = 1;
+            issued = k;
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint64_t d0 = umma_desc(smem, 0);
+            int k = 0, i = 0;
+            bool ok = true;
+            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, i++) {
+                const Unit x = unit_of<MODE, HD>(p, pre, u);
+                const int buf = i % kBufs, use = i / kBufs;
+                if (use > 0 && !mbar_wait(&tempty[buf], (use - 1) & 1, a.err, G4D_TIMEOUT_EMPTY | (kCodeTempty << 8))) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t td = tmem + (uint32_t)(buf * kTN), tcr = kSplitAcc ? tmem + kTN : td;
+                for (int c = x.c0; c < x.c1; c++, k++) {
+                    const int s = k % kTStages;
+                    if (!mbar_wait(&full[s], (k / kTStages) & 1, a.err, G4D_TIMEOUT_FULL | (kCodeFull << 8))) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    // stage tiles: A hi, A lo, B hi, B lo (start-address field in 16-byte units)
+                    const uint64_t ah = d0 + (uint64_t)((s * kStageBytes) >> 4);
+                    const uint64_t al = ah + (uint64_t)(kTileA >> 4);
+                    const uint64_t bh = ah + (uint64_t)((2 * kTileA) >> 4);
+                    const uint64_t bl = bh + (uint64_t)(kTileB >> 4);
+#pragma unroll
+                    for (int kk = 0; kk < kTK / 8; kk++) {
+                        const uint64_t o = (uint64_t)((kk * 32) >> 4);   // 8 tf32 = 32 bytes per MMA
+                        const bool acc = c > x.c0 || kk > 0;
+                        mma_tf32(td, ah + o, bh + o, kIdesc, acc);
+                        mma_tf32(tcr, ah + o, bl + o, kIdesc, kSplitAcc ? acc : true);
+                        mma_tf32(tcr, al + o, bh + o, kIdesc, true);
+                    }
+                    mma_commit(&empty[s]);
+                }
+                if (!ok) break;
+                mma_commit(&tfull[buf]);
+            }
+            if (!ok) fail = 1;
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const int e = warp - 2, q = warp & 3, ch = e >> 2;
+        const int row = q * 32 + lane;
+        int i = 0;
+        for (int u = blockIdx.x; u < units; u += gridDim.x, i++) {
+            const Unit x = unit_of<MODE, HD>(p, pre, u);
+            const int buf = i % kBufs;
+            const bool got = mbar_wait(&tfull[buf], (i / kBufs) & 1, a.err, G4D_TIMEOUT_FULL | (kCodeTfull << 8));
+            if (!__all_sync(0xffffffffu, got)) {
+                if (lane == 0) fail = 1;
+                break;
+            }
+            tc_fence_after();
+            const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kTN + ch * 128);
+            const int rg = x.m * kTM + row;
+            if (MODE == 0) {
+                const int t = rg >> 3;
+                const int kmin = tc_first_key(p.sp + t, p.window) - p.kbase, kmax = p.sp + t - p.kbase;
+                const int j0 = x.n * kTN + ch * 128;
+                float *dst = a.s + (size_t)rg * p.kpad + j0;
+                float mx = -INFINITY;
+#pragma unroll 1
+                for (int c = 0; c < 4; c++) {
+                    int v[32];
+                    load_acc(ta + (uint32_t)(c * 32), v);
+                    if (c == 3) {   // the accumulator is read: free it for the unit after next
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[buf]);
+                    }
+                    if (rg < p.R) {
+                        const int jb = j0 + c * 32;
+#pragma unroll
+                        for (int j = 0; j < 32; j++) {
+                            const int key = jb + j;
+                            if (key >= kmin && key <= kmax) mx = fmaxf(mx, __int_as_float(v[j]));
+                        }
+#pragma unroll
+                        for (int j = 0; j < 32; j += 4)
+                            *(float4 *)(dst + c * 32 + j) = make_float4(__int_as_float(v[j]), __int_as_float(v[j + 1]),
+                                                                        __int_as_float(v[j + 2]), __int_as_float(v[j + 3]));
+                    }
+                }
+                if (rg < p.R) a.smax[(size_t)rg * (p.kpad / 128) + j0 / 128] = mx;
+            } else {
+                float *dst = a.opart + ((size_t)u * kTM + row) * kTN + ch * 128;
+#pragma unroll 1
+                for (int c = 0; c < 4; c++) {
+                    int v[32];
+                    load_acc(ta + (uint32_t)(c * 32), v);
+                    if (c == 3) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[buf]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 32; j += 4)
+                        *(float4 *)(dst + c * 32 + j) = make_float4(__int_as_float(v[j]), __int_as_float(v[j + 1]),
+                                                                    __int_as_float(v[j + 2]), __int_as_float(v[j + 3]));
+                }
+            }
+        }
+    }
+
+    // ---------------- teardown ----------------
+    __syncwarp();
+    tc_fence_before();
+    __syncthreads();
+    if (tid == 32) {
+        // every MMA this lane issued has retired (bounded: after a failure some never ran)
+        mma_commit(drain);
+        mbar_wait(drain, 0, nullptr, 0);
+    }
+    if (fail && tid == 0) {
+        // copies in flight still write shared memory: let them land
+        const uint64_t t0n = g4_globaltimer();
+        for (int k = issued > kTStages ? issued - kTStages : 0; k < issued; k++)
+            while (!mbar_try_wait(&full[k % kTStages], (k / kTStages) & 1) && g4_globaltimer() - t0n < G4_WAIT_NS) {
+            }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * kTN) : "memory");
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 3. Softmax numerators: one CTA per query row.
+__global__ void __launch_bounds__(256) k_tc_soft(const TcAttnArgs a) {
+    __shared__ float red[8];
+    const TcPlan &p = a.p;
+    const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const int m = r / kTM, t = r >> 3;
+    int kb, ke;
+    tile_keys(p, m, &kb, &ke);
+    const int kmin = tc_first_key(p.sp + t, p.window) - p.kbase, kmax = p.sp + t - p.kbase;
+    const int h0 = (kb / kTN) * 2, h1 = ((ke + kTN - 1) / kTN) * 2;
+    float mx = -INFINITY;
+    for (int h = h0 + tid; h < h1; h += 256) mx = fmaxf(mx, a.smax[(size_t)r * (p.kpad / 128) + h]);
+    mx = warp_max(mx);
+    if (lane == 0) red[w] = mx;
+    __syncthreads();
+    mx = red[0];
+#pragma unroll
+    for (int i = 1; i < 8; i++) mx = fmaxf(mx, red[i]);
+    __syncthreads();
+    float *srow = a.s + (size_t)r * p.kpad, *lrow = a.pl + (size_t)r * p.kpad;
+    const int j0 = (kb / kTK) * kTK, j1 = ((ke + kTK - 1) / kTK) * kTK;
+    float sum = 0.0f;
+    for (int j = j0 + 4 * tid; j < j1; j += 1024) {
+        const float4 sv = *(const float4 *)(srow + j);
+        const float x[4] = {sv.x, sv.y, sv.z, sv.w};
+        float hi[4], lo[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const float e = (j + i >= kmin && j + i <= kmax) ? expf(x[i] - mx) : 0.0f;
+            sum += e;
+            split_tf32(e, hi[i], lo[i]);
+        }
+        *(float4 *)(srow + j) = make_float4(hi[0], hi[1], hi[2], hi[3]);
+        *(float4 *)(lrow + j) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) red[w] = sum;
+    __syncthreads();
+    if (tid == 0) {
+        float l = 0.0f;
+        for (int i = 0; i < 8; i++) l += red[i];
+        a.lsum[r] = l;
+    }
+}
+
+// ---------------------------------------------------------------------------
+// 5. Output rows: one CTA per token (its 8 heads), pieces summed in order.
+template <int HD>
+__global__ void __launch_bounds__(256) k_tc_out(const TcAttnArgs a) {
+    __shared__ int pre[kMaxRowTiles + 1];
+    __shared__ float inv[kHeads];
+    const TcPlan &p = a.p;
+    const int t = blockIdx.x, tid = threadIdx.x;
+    if (tid < 32) unit_prefix<1>(p, pre);
+    if (tid < kHeads) inv[tid] = 1.0f / a.lsum[(size_t)t * kHeads + tid];
+    __syncthreads();
+    const int m = t / kTokTile, np = pieces_o(p, m);
+    constexpr int W = kHeads * HD;
+    for (int idx = tid; idx < W / 4; idx += 256) {
+        const int h = idx / (HD / 4), c4 = idx % (HD / 4), d = c4 * 4;
+        const int n = d / kTN, dl = d % kTN, rl = (t * kHeads + h) % kTM;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int pc = 0; pc < np; pc++) {
+            const float4 v = *(const float4 *)(a.opart + ((size_t)(pre[m] + n * np + pc) * kTM + rl) * kTN + dl);
+            acc.x += v.x;
+            acc.y += v.y;
+            acc.z += v.z;
+            acc.w += v.w;
+        }
+        const float s = inv[h];
+        acc = make_float4(acc.x * s, acc.y * s, acc.z * s, acc.w * s);
+        const int col = h * HD + d;
+        *(float4 *)(a.out + (size_t)t * W + col) = acc;
+        if (a.quant_out)   // 16 consecutive lanes hold one 64-wide group
+            quant_lanes16(acc, a.xq + (size_t)t * W + col, a.xs + (size_t)t * (W / 64) + col / 64,
+                          a.xsT ? a.xsT + (size_t)(col / 64) * G4_XST_STRIDE + t : nullptr, (c4 & 15) == 0);
+    }
+}
+
+// ---- host side ----------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// fp32 [rows][cols] (row stride `stride` bytes), boxes of box_rows x 32 with
+// the 128-byte swizzle; elements outside [rows][cols] read as zero.
+bool make_map_f32(CUtensorMap *m, const float *base, int cols, int rows, size_t stride, int box_rows) {
+    EncodeTiledFn fn = (EncodeTiledFn)g4_tmap_encoder();
+    if (!fn || ((uintptr_t)base & 15) || (stride & 15) || cols < 1 || rows < 1) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)stride};
+    const cuuint32_t box[2] = {(cuuint32_t)kTK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+TcPlan make_plan(const AttnArgs &a, int sms, int *nunits_s, int *nunits_o) {
+    TcPlan p{};
+    p.T = a.T;
+    p.sp = a.start_pos;
+    p.window = a.window;
+    p.hd = a.hd;
+    p.R = kHeads * a.T;
+    p.mt = (p.R + kTM - 1) / kTM;
+    p.kbase = tc_first_key(a.start_pos, a.window);
+    p.nk = a.start_pos + a.T - p.kbase;
+    p.kpad = (p.nk + kTN - 1) / kTN * kTN;
+    p.nd = a.hd / kTN;
+    // pieces of about total / (2 SMs) stages, so the O units fill the SMs twice
+    long long stages = 0;
+    int us = 0;
+    for (int m = 0; m < p.mt; m++) {
+        int kb, ke;
+        tile_keys(p, m, &kb, &ke);
+        stages += (long long)p.nd * ((ke + kTK - 1) / kTK - kb / kTK);
+        us += units_s(p, m);
+    }
+    const long long want = (stages + 2LL * sms - 1) / (2LL * sms);
+    p.piece = want < kMinPiece ? kMinPiece : (int)want;
+    int uo = 0;
+    for (int m = 0; m < p.mt; m++) uo += units_o(p, m);
+    *nunits_s = us;
+    *nunits_o = uo;
+    return p;
+}
+
+// Workspace pieces, 1 KB aligned (float offsets).
+struct TcWs {
+    size_t qh, ql, kh, kl, vh, vl, s, pl, smax, lsum, opart, total;
+};
+TcWs ws_layout(const TcPlan &p, int nunits_o) {
+    TcWs w{};
+    size_t off = 0;
+    auto take = [&](size_t floats) {
+        const size_t o = off;
+        off += (floats + 255) / 256 * 256;
+        return o;
+    };
+    const size_t R = (size_t)p.R, HD = (size_t)p.hd, kp = (size_t)p.kpad;
+    w.qh = take(R * HD);
+    w.ql = take(R * HD);
+    w.kh = take((size_t)p.nk * HD);
+    w.kl = take((size_t)p.nk * HD);
+    w.vh = take(HD * kp);
+    w.vl = take(HD * kp);
+    w.s = take(R * kp);
+    w.pl = take(R * kp);
+    w.smax = take(R * (kp / 128));
+    w.lsum = take(R);
+    w.opart = take((size_t)nunits_o * kTM * kTN);
+    w.total = off * 4;
+    return w;
+}
+
+bool tc_args_ok(const AttnArgs &a) {
+    return (a.hd == 256 || a.hd == 512) && a.T >= 1 && a.T <= G4_BATCH && !a.row_seq && !a.strict &&
+           a.start_pos >= 0 && a.qkv && a.kcache && a.vcache && a.out &&
+           // the keys of the chunk must not wrap around the ring
+           a.start_pos + a.T - tc_first_key(a.start_pos, a.window) <= a.mask + 1;
+}
+
+template <int HD>
+cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st) {
+    const int sms = g4_device_sms();
+    int nus = 0, nuo = 0;
+    const TcPlan p = make_plan(a, sms, &nus, &nuo);
+    const TcWs w = ws_layout(p, nuo);
+    if (!ws || ws_bytes < w.total || ((uintptr_t)ws & 255)) return cudaErrorInvalidValue;
+    float *f = (float *)ws;
+    TcAttnArgs x{};
+    x.p = p;
+    x.qkv = a.qkv;
+    x.qkv_stride = a.qkv_stride;
+    x.kcache = a.kcache;
+    x.vcache = a.vcache;
+    x.mask = a.mask;
+    x.qh = f + w.qh;
+    x.ql = f + w.ql;
+    x.kh = f + w.kh;
+    x.kl = f + w.kl;
+    x.vh = f + w.vh;
+    x.vl = f + w.vl;
+    x.s = f + w.s;
+    x.pl = f + w.pl;
+    x.smax = f + w.smax;
+    x.lsum = f + w.lsum;
+    x.opart = f + w.opart;
+    x.out = a.out;
+    x.quant_out = a.quant_out;
+    x.xq = a.xq;
+    x.xs = a.xs;
+    x.xsT = a.xsT;
+    x.err = a.err;
+    if (a.quant_out && (!a.xq || !a.xs)) return cudaErrorInvalidValue;
+    CUtensorMap qh, ql, kh, kl, ph, pl, vh, vl;
+    const size_t rs = (size_t)HD * 4, ks = (size_t)p.kpad * 4;
+    if (!make_map_f32(&qh, x.qh, HD, p.R, rs, kTM) || !make_map_f32(&ql, x.ql, HD, p.R, rs, kTM) ||
+        !make_map_f32(&kh, x.kh, HD, p.nk, rs, kTN) || !make_map_f32(&kl, x.kl, HD, p.nk, rs, kTN) ||
+        !make_map_f32(&ph, x.s, p.kpad, p.R, ks, kTM) || !make_map_f32(&pl, x.pl, p.kpad, p.R, ks, kTM) ||
+        !make_map_f32(&vh, x.vh, p.nk, HD, ks, kTN) || !make_map_f32(&vl, x.vl, p.nk, HD, ks, kTN))
+        return cudaErrorInvalidValue;
+    cudaError_t e = g4_smem_optin((const void *)k_tc_gemm<0, HD>, kSmem);
+    if (e == cudaSuccess) e = g4_smem_optin((const void *)k_tc_gemm<1, HD>, kSmem);
+    if (e) return e;
+    k_tc_split<HD><<<dim3(4 * sms, 3), 256, 0, st>>>(x);
+    k_tc_gemm<0, HD><<<nus < sms ? nus : sms, kThreads, kSmem, st>>>(qh, ql, kh, kl, x);
+    k_tc_soft<<<p.R, 256, 0, st>>>(x);
+    k_tc_gemm<1, HD><<<nuo < sms ? nuo : sms, kThreads, kSmem, st>>>(ph, pl, vh, vl, x);
+    k_tc_out<HD><<<p.T, 256, 0, st>>>(x);
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+size_t g4_attn_tc_ws_bytes(const AttnArgs &a) {
+    if (!tc_args_ok(a)) return 0;
+    int nus = 0, nuo = 0;
+    const TcPlan p = make_plan(a, g4_device_sms(), &nus, &nuo);
+    return ws_layout(p, nuo).total;
+}
+
+cudaError_t g4_launch_attn_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st) {
+    if (!tc_args_ok(a) || !g4_tmap_encoder()) return cudaErrorInvalidValue;
+    if (a.hd == 256) return launch_tc<256>(a, ws, ws_bytes, st);
+    return launch_tc<512>(a, ws, ws_bytes, st);
+}

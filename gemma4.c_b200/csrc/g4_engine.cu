@@ -89,6 +89,10 @@ struct g4_ctx {
     bool strict = false;          // reference-order reductions (bit-exact forward)
     float *scores = nullptr;      // strict attention scratch
     size_t scores_cap = 0;
+    // tensor-core prefill attention: path option and its workspace (grown on demand)
+    int attn_path = 0;
+    void *tc_ws = nullptr;
+    size_t tc_ws_cap = 0;
     cudaGraphExec_t g_decode = nullptr;
     int graph_cur = 0;
     bool decode_warm = false;
@@ -843,6 +847,43 @@ struct BatchPlan {
     int seq;
 };
 
+// Prefill attention on the tensor cores for this layer kind and chunk size
+// (G4_OPT_ATTN_PATH); the CUDA-core kernel otherwise.
+constexpr int kTcMinTokens = 64;
+bool attn_on_tensor_cores(const g4_ctx *c, bool global, int T) {
+    if (c->strict || c->attn_path == 1) return false;
+    return c->attn_path == 2 || (global && T >= kTcMinTokens);
+}
+
+// Grow the tensor-core attention workspace for a chunk of T tokens at
+// start_pos (before any launch of the chunk: freeing waits for the stream).
+int ensure_tc_ws(g4_ctx *c, int T, int start_pos, int ring_global) {
+    size_t need = 0;
+    for (int global = 0; global < 2; global++) {
+        if (!attn_on_tensor_cores(c, global != 0, T)) continue;
+        AttnArgs a{};
+        a.hd = global ? 512 : 256;
+        a.window = global ? 0 : G4_SLIDING_WINDOW;
+        a.mask = (global ? ring_global : 1024) - 1;
+        a.T = T;
+        a.start_pos = start_pos;
+        a.qkv = a.kcache = a.vcache = a.out = (float *)c;   // non-null placeholders: only the size is asked
+        const size_t b = g4_attn_tc_ws_bytes(a);
+        if (!b) return fail(c, G4_ERR_INVALID, "tensor-core attention cannot run T %d at %d", T, start_pos);
+        need = b > need ? b : need;
+    }
+    if (need <= c->tc_ws_cap) return G4_OK;
+    CK(cudaStreamSynchronize(c->st));
+    if (c->tc_ws) cudaFree(c->tc_ws);
+    c->tc_ws = nullptr;
+    c->tc_ws_cap = 0;
+    // a quarter more than asked, so a growing context reallocates rarely
+    const size_t want = need + need / 4;
+    CK(cudaMalloc(&c->tc_ws, want));
+    c->tc_ws_cap = want;
+    return G4_OK;
+}
+
 cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp = nullptr) {
     Seq q{c, c->use_pdl};
     int cur = 0;
@@ -894,10 +935,13 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp
             q.ck(g4_launch_attn_rows(at, sp, c->st, q.pdl));
         }
         else if (!c->strict) {
-            // the tiled kernel also quantises its output rows for o_proj
+            // the tiled kernels also quantise their output rows for o_proj
             at.quant_out = 1;
             at.xsT = c->xsT;
-            q.ck(g4_launch_attn_prefill(at, c->st, q.pdl));
+            if (attn_on_tensor_cores(c, Y.global, T))
+                q.ck(g4_launch_attn_tc(at, c->tc_ws, c->tc_ws_cap, c->st));
+            else
+                q.ck(g4_launch_attn_prefill(at, c->st, q.pdl));
         } else
             q.ck(g4_launch_attn_strict(at, c->st, q.pdl));
         if (!at.quant_out) q.ck(g4_launch_rows_quant(c->attn, Y.qw, T, Y.qw, c->xq, c->xs, c->st, q.pdl, c->xsT));
@@ -1195,6 +1239,7 @@ int g4_close(g4_ctx *c) {
     if (c->state) cudaFree(c->state);
     if (c->kv) cudaFree(c->kv);
     if (c->scores) cudaFree(c->scores);
+    if (c->tc_ws) cudaFree(c->tc_ws);
     if (c->st) cudaStreamDestroy(c->st);
     delete c;
     return G4_OK;
@@ -1217,6 +1262,10 @@ int g4_set_option(g4_ctx *c, int option, int value) {
         if (c->g_decode) { cudaGraphExecDestroy(c->g_decode); c->g_decode = nullptr; }
         break;
     case G4_OPT_GEMM_PATH: c->gemm_path = value; break;
+    case G4_OPT_ATTN_PATH:
+        if (value < 0 || value > 2) return fail(c, G4_ERR_INVALID, "attention path %d out of range", value);
+        c->attn_path = value;
+        break;
     case G4_OPT_STRICT: c->strict = value != 0; break;
     case G4_OPT_LAYERS:
         if (value < 1 || value > G4_NUM_LAYERS) return fail(c, G4_ERR_INVALID, "layers %d out of range", value);
@@ -1294,6 +1343,8 @@ int g4_forward(g4_ctx *c, const int *tokens, size_t count, int start_pos) {
         e = enqueue_small(c, T, start_pos, nullptr);
         if (e) return fail(c, G4_ERR_CUDA, "decode launch: %s", cudaGetErrorString(e));
     } else {
+        rc = ensure_tc_ws(c, T, start_pos, G4_MAX_CONTEXT);
+        if (rc) return rc;
         e = enqueue_prefill(c, T, start_pos);
         if (e) return fail(c, G4_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e));
     }
@@ -1725,6 +1776,9 @@ int g4_forward_batch(g4_ctx *c, int n, const int *seq_ids, const int *tokens, co
             c->rows_warm[T]++;
         }
     } else {
+        // layer 4 is the first global layer (gemma4.c:417-419): its batch ring
+        const int rc = ensure_tc_ws(c, T, start_pos[0], c->bring[4]);
+        if (rc) return rc;
         cudaError_t e = enqueue_prefill(c, T, start_pos[0], &bp);
         if (e) return fail(c, G4_ERR_CUDA, "forward_batch launch: %s", cudaGetErrorString(e));
     }

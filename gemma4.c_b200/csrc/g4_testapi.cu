@@ -344,12 +344,12 @@ int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, 
                   const float *q_norm, const float *k_norm, const float *rope_cos, const float *rope_sin,
                   float *kring, float *vring, float *out, int8_t *xq, float *xs, int iters, float *ms_per_call) {
     if ((hd != 256 && hd != 512) || ring < 1024 || (ring & (ring - 1)) || T < 1 || T > G4_BATCH ||
-        start_pos < 0 || mode < 0 || mode > 3 || !qkv || !rope_cos || !rope_sin || !kring || !vring || !out ||
+        start_pos < 0 || mode < 0 || mode > 4 || !qkv || !rope_cos || !rope_sin || !kring || !vring || !out ||
         iters < 0 || (iters > 0 && !ms_per_call))
         return G4_ERR_INVALID;
     if ((mode == 2 || mode == 3) && (splits < 1 || splits > 256)) return G4_ERR_INVALID;
     if (mode == 2 && T != 1) return G4_ERR_INVALID;
-    if ((xq || xs) && (mode != 0 || !xq || !xs)) return G4_ERR_INVALID;
+    if ((xq || xs) && ((mode != 0 && mode != 4) || !xq || !xs)) return G4_ERR_INVALID;
     const int window = hd == 256 ? G4_SLIDING_WINDOW : 0;
     const int pairs = hd == 256 ? 128 : 64;
     const int npos = start_pos + T;
@@ -357,7 +357,7 @@ int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, 
     if ((window ? (T - 1 + window) : npos) > ring) return G4_ERR_INVALID;
     const int stride = 10 * hd;
     const int sms = num_sms();
-    DevBuf dqkv, dqn, dkn, dcos, dsin, dk, dv, dout, dpart, dpre, dscores, derr, drs, drp, dxq, dxs;
+    DevBuf dqkv, dqn, dkn, dcos, dsin, dk, dv, dout, dpart, dpre, dscores, derr, drs, drp, dxq, dxs, dws;
     TK(dqkv.alloc((size_t)T * stride * 4));
     TK(dqn.alloc((size_t)hd * 4));
     TK(dkn.alloc((size_t)hd * 4));
@@ -420,12 +420,19 @@ int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, 
         a.row_seq = (const int *)drs.p;
         a.row_pos = (const int *)drp.p;
     }
+    size_t ws_bytes = 0;
+    if (mode == 4) {   // the tensor-core path's workspace
+        ws_bytes = g4_attn_tc_ws_bytes(a);
+        if (!ws_bytes) return G4_ERR_INVALID;
+        TK(dws.alloc(ws_bytes));
+    }
     // q/k/v post-processing (decode does its own inside the split kernel)
     if (mode != 2) TK(g4_launch_qkv_post(a, 0, false));
     auto attend = [&]() -> cudaError_t {
         switch (mode) {
         case 0: return g4_launch_attn_prefill(a, 0, false);
         case 1: return g4_launch_attn_strict(a, 0, false);
+        case 4: return g4_launch_attn_tc(a, dws.p, ws_bytes, 0);
         case 2: {
             cudaError_t e = g4_launch_attn_decode(a, splits, 0, false);
             return e ? e : g4_launch_attn_combine(a, splits, 0, false);

@@ -360,7 +360,7 @@ def bench_gemv(N, K, T=1, iters=200, pdl=True):
     return ms.value, by.value
 
 
-ATTN_PREFILL, ATTN_STRICT, ATTN_DECODE, ATTN_ROWS = 0, 1, 2, 3
+ATTN_PREFILL, ATTN_STRICT, ATTN_DECODE, ATTN_ROWS, ATTN_PREFILL_TC = 0, 1, 2, 3, 4
 
 
 def attention(qkv, hd, kring, vring, start_pos, cos_t, sin_t, mode=ATTN_PREFILL, splits=148, q_norm=None,
@@ -368,7 +368,7 @@ def attention(qkv, hd, kring, vring, start_pos, cos_t, sin_t, mode=ATTN_PREFILL,
     """One attention sub-layer on the GPU (g4k_attention). qkv[T][10*hd] raw
     q | k | v; kring / vring [ring][hd] are updated in place with the chunk's
     keys and values. Returns (out[T][8*hd], ms per call or None), and with
-    quant=True (prefill mode) also the kernel's quantised rows (xq, xs)."""
+    quant=True (prefill modes) also the kernel's quantised rows (xq, xs)."""
     L = load()
     qkv = np.ascontiguousarray(qkv, np.float32)
     T = qkv.shape[0]

@@ -142,6 +142,13 @@ const char *g4_strerror(int code);
  * decoding that sequence alone (other values change only the attention's
  * floating-point summation order). */
 #define G4_OPT_BATCH_SPLITS 7
+/* Prefill attention of a chunk (g4_forward / one-sequence g4_forward_batch):
+ * 0 (default) auto = tensor cores (3xTF32 tcgen05 GEMMs for Q K^T and P V) on
+ * the global layers for chunks of >= 64 tokens, CUDA cores elsewhere; 1 CUDA
+ * cores everywhere; 2 tensor cores everywhere. The paths differ in
+ * floating-point order only (outputs agree to fp32 rounding). Not used in
+ * strict mode. */
+#define G4_OPT_ATTN_PATH 8
 int g4_set_option(g4_ctx *ctx, int option, int value);
 
 /* ---- multi-sequence serving (ragged batches of independent sequences) ----
@@ -259,9 +266,10 @@ int g4_bench_mma_i8(int iters, float *ms_per_launch, double *ops_per_launch);
  * mode 0: prefill fast path (q/k/v post-processing + tiled kernel); 1: strict
  * (the reference's floating-point order); 2: single-token decode (split-KV
  * over `splits` CTAs + combine, T == 1); 3: batched-row decode path (one row
- * per token at start_pos + t, `splits` key splits). iters > 0: the attention
+ * per token at start_pos + t, `splits` key splits); 4: prefill on the tensor
+ * cores (3xTF32 tcgen05 GEMMs for Q K^T and P V). iters > 0: the attention
  * kernels (without post-processing) are then repeated `iters` times and the
- * average duration per call is written to ms_per_call. xq / xs (mode 0, both
+ * average duration per call is written to ms_per_call. xq / xs (mode 0 or 4, both
  * or neither): the output rows as the kernel quantises them for o_proj
  * (quantize, gemma4.c:265-279): xq[T][8*hd], xs[T][8*hd/64]. */
 int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, const float *qkv,

@@ -13,7 +13,11 @@ normalised vectors already in the ring.
     expf; the oracle itself is within ~2e-5 of a float64 evaluation), ring
     contents within 1e-5;
   - the fast prefill is deterministic (same bits on a second call), and its
-    fused quantisation of the output rows equals quantize() of them.
+    fused quantisation of the output rows equals quantize() of them;
+  - the tensor-core prefill (3xTF32 tcgen05 GEMMs) meets the same 2e-4 bound
+    (each product carries a relative error near 2^-21 against the CUDA-core
+    path's 2^-24: scores of |s| <= ~70 move by ~1e-5), is deterministic, and
+    its quantised rows equal quantize() of its output rows.
 """
 import numpy as np
 import pytest
@@ -67,6 +71,24 @@ def test_prefill_fast_tracks_oracle(g4, oracle, hd, T, start_pos, ring):
     out2, _, xq, xs = g4.attention(qkv, hd, k2, v2, start_pos, cos_t, sin_t, mode=g4.ATTN_PREFILL, quant=True)
     assert np.array_equal(out.view(np.uint32), out2.view(np.uint32))
     # the fused quantisation for o_proj is quantize() of those rows
+    eq, es = oracle.quantize(out2)
+    assert np.array_equal(xq, eq) and np.array_equal(xs.view(np.uint32), es.view(np.uint32))
+
+
+TC_CASES = CASES + [(256, 300, 700, 1024), (512, 17, 1000, 4096), (512, 48, 12000, 16384)]
+
+
+@pytest.mark.parametrize("hd,T,start_pos,ring", TC_CASES)
+def test_prefill_tensor_cores_track_oracle(g4, oracle, hd, T, start_pos, ring):
+    (qkv, k, v, cos_t, sin_t), (eo, ek, ev) = _oracle(oracle, hd, T, start_pos, ring, 600 + T + start_pos)
+    k1, v1 = k.copy(), v.copy()
+    out, _ = g4.attention(qkv, hd, k1, v1, start_pos, cos_t, sin_t, mode=g4.ATTN_PREFILL_TC)
+    assert np.abs(k1 - ek).max() <= RING_ATOL and np.abs(v1 - ev).max() <= RING_ATOL
+    err = np.abs(out - eo).max()
+    assert err <= OUT_ATOL, f"max abs error {err}"
+    out2, _, xq, xs = g4.attention(qkv, hd, k.copy(), v.copy(), start_pos, cos_t, sin_t, mode=g4.ATTN_PREFILL_TC,
+                                   quant=True)
+    assert np.array_equal(out.view(np.uint32), out2.view(np.uint32))
     eq, es = oracle.quantize(out2)
     assert np.array_equal(xq, eq) and np.array_equal(xs.view(np.uint32), es.view(np.uint32))
 

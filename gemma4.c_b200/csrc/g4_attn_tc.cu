@@ -8,23 +8,31 @@
 // 256-wide layers), different floating-point order: outputs agree within fp32
 // rounding, not bit for bit.
 //
-// Both contractions are tcgen05.mma kind::tf32 with the 3xTF32 split: every
-// fp32 operand x is stored as hi = tf32(x) and lo = tf32(x - hi) (round to
-// nearest), and each K step issues hi.hi + hi.lo + lo.hi into one fp32 TMEM
-// accumulator. The dropped lo.lo term and the roundings leave a relative
-// error near 2^-21 per product (an fp32 FMA: 2^-24).
+// Both contractions are tcgen05.mma kind::f16 on split operands: every fp32
+// operand x is scaled by an exact power of two c (so |x c| < 2^15) and stored
+// as hi = fp16(x c) and lo = fp16(x c - hi), round to nearest; each K step
+// issues hi.hi into one fp32 TMEM accumulator and hi.lo + lo.hi into a second
+// one (the accumulators add with rounding toward zero at their own magnitude,
+// so the 2^-11 smaller correction products get their own), and the epilogue
+// adds the two and removes the scales. 22 significant bits per operand: the
+// dropped lo.lo term and the roundings leave a relative error near 2^-21 per
+// product (an fp32 FMA: 2^-24). Scales: per row for Q and K (from the row's
+// max |x|: q/k norm weights are unbounded), 2^15 for P (0 < p <= 1) and a
+// fixed 2^(15 - ceil(log2 sqrt(HD))) for V (RMS-normalised without a weight,
+// so |v| <= sqrt(HD)).
 //
 // The chunk's R = 8T query rows (row r = token r / 8, head r % 8) form 128-row
 // tiles of 16 tokens. Five launches:
 //   1. k_tc_split   Q rows, the chunk's keys [kbase, npos) and their values as
-//                   hi/lo pairs; V transposed to [HD][keys] so that both GEMMs
-//                   read K-major tiles;
+//                   scaled fp16 hi/lo pairs (with the Q and K row scales); V
+//                   transposed to [HD][keys] so that both GEMMs read K-major
+//                   tiles;
 //   2. k_tc_gemm<0> S = Q K^T per 128-row x 256-key tile (K = HD), only tiles
 //                   that hold a visible key; the epilogue stores S and every
 //                   row's max over the visible keys of each 128-key half tile;
 //   3. k_tc_soft    per row: m = max of its half-tile maxima, p = exp(s - m) on
-//                   visible keys (0 elsewhere), l = sum p; p stored as hi (over
-//                   S) and lo;
+//                   visible keys (0 elsewhere), l = sum p; p stored as scaled
+//                   fp16 hi and lo;
 //   4. k_tc_gemm<1> O = P V per 128-row x 256-dim tile over one piece of the
 //                   row tile's keys (split K, so every SM has work), partial
 //                   tiles stored;
@@ -33,11 +41,11 @@
 // The schedule depends only on (T, start position, SM count): deterministic.
 //
 // GEMM roles (10 warps, one CTA per SM, persistent over units):
-//   warp 0      TMA producer: per stage the 32-wide K slice of A hi/lo (128
+//   warp 0      TMA producer: per stage the 64-wide K slice of A hi/lo (128
 //               rows) and B hi/lo (256 rows) with the 128-byte swizzle;
-//   warp 1      allocates 512 TMEM columns (two 256-column accumulators, so a
-//               unit's epilogue overlaps the next unit's MMAs); one lane issues
-//               3 x 4 MMAs (M 128, N 256, K 8) per stage;
+//   warp 1      allocates 512 TMEM columns (the hi.hi and the correction
+//               accumulator, 256 columns each); one lane issues 3 x 4 MMAs
+//               (M 128, N 256, K 16) per stage;
 //   warps 2-9   epilogue: thread = row (TMEM lane), two warps per lane quadrant
 //               with 128 columns each.
 // Waits are bounded (mbar_wait); on a timeout every role leaves its loop, the
@@ -51,10 +59,10 @@ namespace {
 
 constexpr int kTM = 128;                  // query rows per tile (16 tokens x 8 heads)
 constexpr int kTN = 256;                  // keys (S) or value dimensions (O) per tile
-constexpr int kTK = 32;                   // fp32 K elements per stage: one 128-byte row
+constexpr int kTK = 64;                   // fp16 K elements per stage: one 128-byte row
 constexpr int kTStages = 2;
-constexpr int kTileA = kTM * kTK * 4;     // 16 KB
-constexpr int kTileB = kTN * kTK * 4;     // 32 KB
+constexpr int kTileA = kTM * kTK * 2;     // 16 KB
+constexpr int kTileB = kTN * kTK * 2;     // 32 KB
 constexpr int kStageBytes = 2 * kTileA + 2 * kTileB;   // hi and lo of both operands
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
@@ -62,19 +70,11 @@ constexpr int kOffBar = kTStages * kStageBytes;
 constexpr int kSmem = kOffBar + 128 + 1024;          // + barriers, + 1 KB for alignment
 constexpr int kTokTile = kTM / kHeads;                // 16 tokens per row tile
 constexpr int kMaxRowTiles = G4_BATCH / kTokTile;     // 32
-constexpr int kMinPiece = 16;                         // K stages per O unit, at least
-#ifndef G4_TC_SPLIT_ACC
-#define G4_TC_SPLIT_ACC 1
-#endif
-// The accumulator adds every MMA's products with rounding toward zero at its own
-// magnitude, so its error grows with the number of MMAs landing at the full
-// magnitude: the hi.hi products go to one accumulator and the two correction
-// products (2^-11 smaller) to a second one, summed in fp32 by the epilogue.
-constexpr bool kSplitAcc = G4_TC_SPLIT_ACC != 0;
-constexpr int kBufs = kSplitAcc ? 1 : 2;              // accumulator (pairs) in TMEM
-// D fp32, A and B tf32, both K-major, N = 256 (>> 3), M = 128 (>> 4)
-constexpr uint32_t kIdesc =
-    (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(kTN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
+constexpr int kMinPiece = 8;                          // K stages per O unit, at least
+constexpr int kBufs = 1;                              // accumulator pairs in TMEM
+constexpr float kPScale = 32768.0f;                   // 2^15: p in (0, 1]
+// D fp32, A and B f16, both K-major, N = 256 (>> 3), M = 128 (>> 4)
+constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kTN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
 static_assert(kSmem <= 227 * 1024, "shared memory budget of the attention GEMM CTA");
 static_assert(kMaxRowTiles <= 32, "the unit prefix is one warp scan");
 
@@ -87,7 +87,8 @@ struct TcPlan {
     int kbase, nk;    // the workspace holds keys [kbase, kbase + nk)
     int kpad;         // row stride (keys) of S, P and V^T: nk rounded up to 256
     int nd;           // 256-wide value-dimension tiles: hd / 256
-    int piece;        // O units: K stages (32 keys) per unit
+    int piece;        // O units: K stages (64 keys) per unit
+    float vscale;     // V scale 2^(15 - ceil(log2 sqrt(hd)))
 };
 
 __host__ __device__ inline int tc_first_key(int p, int window) { return (window && p + 1 > window) ? p + 1 - window : 0; }
@@ -121,10 +122,12 @@ struct TcAttnArgs {
     int qkv_stride;
     const float *kcache, *vcache;
     int mask;
-    float *qh, *ql;       // [R][HD]
-    float *kh, *kl;       // [nk][HD]
-    float *vh, *vl;       // [HD][kpad]
-    float *s, *pl;        // [R][kpad]: S, then P hi over it; P lo
+    __half *qh, *ql;      // [R][HD] scaled
+    __half *kh, *kl;      // [nk][HD] scaled
+    __half *vh, *vl;      // [HD][kpad] scaled
+    float *qinv, *kinv;   // [R], [nk]: 1 / the row's scale
+    float *s;             // [R][kpad] scores
+    __half *ph, *pl;      // [R][kpad] 2^15 p
     float *smax;          // [R][kpad / 128]
     float *lsum;          // [R]
     float *opart;         // [O units][128][256]
@@ -135,17 +138,17 @@ struct TcAttnArgs {
     int *err;
 };
 
-// Round to the nearest tf32 value (10 explicit mantissa bits; ties away from zero).
-G4_DEV float tf32_rn(float x) { return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u); }
-G4_DEV void split_tf32(float x, float &hi, float &lo) {
-    hi = tf32_rn(x);
-    lo = tf32_rn(__fsub_rn(x, hi));   // x - hi is exact
+// x (already scaled, |x| < 2^15) as fp16 hi + lo, round to nearest; x - hi is exact.
+G4_DEV void split_f16(float x, __half &hi, __half &lo) {
+    hi = __float2half_rn(x);
+    lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
 }
-G4_DEV void split4(float4 x, float4 &h, float4 &l) {
-    split_tf32(x.x, h.x, l.x);
-    split_tf32(x.y, h.y, l.y);
-    split_tf32(x.z, h.z, l.z);
-    split_tf32(x.w, h.w, l.w);
+// The power of two c with max_abs * c in [2^14, 2^15) (1 for a zero row).
+G4_DEV float row_scale(float max_abs) {
+    if (!(max_abs > 0.0f)) return 1.0f;
+    int e;
+    frexpf(max_abs, &e);   // max_abs in [2^(e-1), 2^e)
+    return ldexpf(1.0f, 15 - e);
 }
 
 // pre[0..mt] = prefix sums of the units of each row tile (warp 0; mt <= 32)
@@ -189,27 +192,50 @@ G4_DEV Unit unit_of(const TcPlan &p, const int *pre, int u) {
 }
 
 // ---------------------------------------------------------------------------
-// 1. hi/lo operands. grid (blocks, 3): y = 0 Q rows, 1 key rows, 2 V^T tiles.
+// 1. hi/lo operands. grid (blocks, 3): y = 0 Q rows, 1 key rows (one warp per
+// row, scaled by the row's own power of two), 2 V^T tiles (fixed scale).
+G4_DEV uint32_t pack2(__half a, __half b) {
+    const __half2 h = __halves2half2(a, b);
+    return *reinterpret_cast<const uint32_t *>(&h);
+}
+G4_DEV void store_split4(float4 x, float c, __half *dh, __half *dl) {
+    __half h[4], l[4];
+    split_f16(x.x * c, h[0], l[0]);
+    split_f16(x.y * c, h[1], l[1]);
+    split_f16(x.z * c, h[2], l[2]);
+    split_f16(x.w * c, h[3], l[3]);
+    *(uint2 *)dh = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
+    *(uint2 *)dl = make_uint2(pack2(l[0], l[1]), pack2(l[2], l[3]));
+}
+
 template <int HD>
 __global__ void __launch_bounds__(256) k_tc_split(const TcAttnArgs a) {
     __shared__ float tile[32][33];
     const TcPlan &p = a.p;
     const int job = blockIdx.y;
     if (job < 2) {
-        const long long n4 = (long long)(job == 0 ? p.R : p.nk) * (HD / 4);
-        for (long long i = (long long)blockIdx.x * 256 + threadIdx.x; i < n4; i += (long long)gridDim.x * 256) {
-            const int r = (int)(i / (HD / 4)), c4 = (int)(i % (HD / 4));
-            const float *src = job == 0 ? a.qkv + (size_t)(r >> 3) * a.qkv_stride + (r & 7) * HD + c4 * 4
-                                        : a.kcache + (size_t)((p.kbase + r) & a.mask) * HD + c4 * 4;
-            float4 h, l;
-            split4(*(const float4 *)src, h, l);
-            const size_t o = (size_t)r * HD + c4 * 4;
-            *(float4 *)((job == 0 ? a.qh : a.kh) + o) = h;
-            *(float4 *)((job == 0 ? a.ql : a.kl) + o) = l;
+        constexpr int V4 = HD / 128;   // float4s per lane
+        const int lane = threadIdx.x & 31, rows = job == 0 ? p.R : p.nk;
+        for (int r = blockIdx.x * 8 + (threadIdx.x >> 5); r < rows; r += gridDim.x * 8) {
+            const float4 *src = (const float4 *)(job == 0 ? a.qkv + (size_t)(r >> 3) * a.qkv_stride + (r & 7) * HD
+                                                          : a.kcache + (size_t)((p.kbase + r) & a.mask) * HD);
+            float4 x[V4];
+            float m = 0.0f;
+#pragma unroll
+            for (int i = 0; i < V4; i++) {
+                x[i] = src[lane + 32 * i];
+                m = fmaxf(m, fmaxf(fmaxf(fabsf(x[i].x), fabsf(x[i].y)), fmaxf(fabsf(x[i].z), fabsf(x[i].w))));
+            }
+            const float c = row_scale(warp_max(m));
+            __half *dh = (job == 0 ? a.qh : a.kh) + (size_t)r * HD, *dl = (job == 0 ? a.ql : a.kl) + (size_t)r * HD;
+#pragma unroll
+            for (int i = 0; i < V4; i++) store_split4(x[i], c, dh + 4 * (lane + 32 * i), dl + 4 * (lane + 32 * i));
+            if (lane == 0) (job == 0 ? a.qinv : a.kinv)[r] = 1.0f / c;   // a power of two: exact
         }
         return;
     }
     // V^T through shared memory, 32 keys x 32 dimensions per tile
+    const float c = p.vscale;
     const int kt = (p.nk + 31) / 32, ntiles = kt * (HD / 32);
     for (int ti = blockIdx.x; ti < ntiles; ti += gridDim.x) {
         const int k0 = (ti / (HD / 32)) * 32, d0 = (ti % (HD / 32)) * 32;
@@ -221,8 +247,8 @@ __global__ void __launch_bounds__(256) k_tc_split(const TcAttnArgs a) {
         for (int i = threadIdx.x; i < 32 * 32; i += 256) {
             const int dr = i >> 5, kc = i & 31;
             if (k0 + kc < p.nk) {
-                float h, l;
-                split_tf32(tile[kc][dr], h, l);
+                __half h, l;
+                split_f16(tile[kc][dr] * c, h, l);
                 const size_t o = (size_t)(d0 + dr) * p.kpad + k0 + kc;
                 a.vh[o] = h;
                 a.vl[o] = l;
@@ -232,19 +258,16 @@ __global__ void __launch_bounds__(256) k_tc_split(const TcAttnArgs a) {
     }
 }
 
-// 32 columns of this lane's accumulator (plus its correction accumulator, 256
-// columns on, when split), as fp32 bits.
+// ---------------------------------------------------------------------------
+// 32 columns of this lane's hi.hi accumulator plus its correction accumulator
+// (256 columns on), as fp32 bits.
 G4_DEV void load_acc(uint32_t taddr, int (&v)[32]) {
+    int w[32];
     tmem_ld32(taddr, v);
-    if constexpr (kSplitAcc) {
-        int w[32];
-        tmem_ld32(taddr + kTN, w);
-        tmem_wait_ld();
+    tmem_ld32(taddr + kTN, w);
+    tmem_wait_ld();
 #pragma unroll
-        for (int j = 0; j < 32; j++) v[j] = __float_as_int(__fadd_rn(__int_as_float(v[j]), __int_as_float(w[j])));
-    } else {
-        tmem_wait_ld();
-    }
+    for (int j = 0; j < 32; j++) v[j] = __float_as_int(__fadd_rn(__int_as_float(v[j]), __int_as_float(w[j])));
 }
 
 // ---------------------------------------------------------------------------
@@ -334,7 +357,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     break;
                 }
                 tc_fence_after();
-                const uint32_t td = tmem + (uint32_t)(buf * kTN), tcr = kSplitAcc ? tmem + kTN : td;
+                const uint32_t td = tmem + (uint32_t)(buf * kTN), tcr = td + kTN;
                 for (int c = x.c0; c < x.c1; c++, k++) {
                     const int s = k % kTStages;
                     if (!mbar_wait(&full[s], (k / kTStages) & 1, a.err, G4D_TIMEOUT_FULL | (kCodeFull << 8))) {
@@ -348,12 +371,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const uint64_t bh = ah + (uint64_t)((2 * kTileA) >> 4);
                     const uint64_t bl = bh + (uint64_t)(kTileB >> 4);
 #pragma unroll
-                    for (int kk = 0; kk < kTK / 8; kk++) {
-                        const uint64_t o = (uint64_t)((kk * 32) >> 4);   // 8 tf32 = 32 bytes per MMA
+                    for (int kk = 0; kk < kTK / 16; kk++) {
+                        const uint64_t o = (uint64_t)((kk * 32) >> 4);   // 16 fp16 = 32 bytes per MMA
                         const bool acc = c > x.c0 || kk > 0;
-                        mma_tf32(td, ah + o, bh + o, kIdesc, acc);
-                        mma_tf32(tcr, ah + o, bl + o, kIdesc, kSplitAcc ? acc : true);
-                        mma_tf32(tcr, al + o, bh + o, kIdesc, true);
+                        mma_f16(td, ah + o, bh + o, kIdesc, acc);
+                        mma_f16(tcr, ah + o, bl + o, kIdesc, acc);
+                        mma_f16(tcr, al + o, bh + o, kIdesc, true);
                     }
                     mma_commit(&empty[s]);
                 }
@@ -383,6 +406,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int kmin = tc_first_key(p.sp + t, p.window) - p.kbase, kmax = p.sp + t - p.kbase;
                 const int j0 = x.n * kTN + ch * 128;
                 float *dst = a.s + (size_t)rg * p.kpad + j0;
+                const float qi = rg < p.R ? a.qinv[rg] : 0.0f;
                 float mx = -INFINITY;
 #pragma unroll 1
                 for (int c = 0; c < 4; c++) {
@@ -398,7 +422,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int j = 0; j < 32; j++) {
                             const int key = jb + j;
-                            if (key >= kmin && key <= kmax) mx = fmaxf(mx, __int_as_float(v[j]));
+                            // the row and key scales are powers of two: exact
+                            const float sv = __int_as_float(v[j]) * qi * (key < p.nk ? a.kinv[key] : 0.0f);
+                            v[j] = __float_as_int(sv);
+                            if (key >= kmin && key <= kmax) mx = fmaxf(mx, sv);
                         }
 #pragma unroll
                         for (int j = 0; j < 32; j += 4)
@@ -470,21 +497,22 @@ __global__ void __launch_bounds__(256) k_tc_soft(const TcAttnArgs a) {
 #pragma unroll
     for (int i = 1; i < 8; i++) mx = fmaxf(mx, red[i]);
     __syncthreads();
-    float *srow = a.s + (size_t)r * p.kpad, *lrow = a.pl + (size_t)r * p.kpad;
+    const float *srow = a.s + (size_t)r * p.kpad;
+    __half *hrow = a.ph + (size_t)r * p.kpad, *lrow = a.pl + (size_t)r * p.kpad;
     const int j0 = (kb / kTK) * kTK, j1 = ((ke + kTK - 1) / kTK) * kTK;
     float sum = 0.0f;
     for (int j = j0 + 4 * tid; j < j1; j += 1024) {
         const float4 sv = *(const float4 *)(srow + j);
         const float x[4] = {sv.x, sv.y, sv.z, sv.w};
-        float hi[4], lo[4];
+        __half hi[4], lo[4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
             const float e = (j + i >= kmin && j + i <= kmax) ? expf(x[i] - mx) : 0.0f;
             sum += e;
-            split_tf32(e, hi[i], lo[i]);
+            split_f16(e * kPScale, hi[i], lo[i]);
         }
-        *(float4 *)(srow + j) = make_float4(hi[0], hi[1], hi[2], hi[3]);
-        *(float4 *)(lrow + j) = make_float4(lo[0], lo[1], lo[2], lo[3]);
+        *(uint2 *)(hrow + j) = make_uint2(pack2(hi[0], hi[1]), pack2(hi[2], hi[3]));
+        *(uint2 *)(lrow + j) = make_uint2(pack2(lo[0], lo[1]), pack2(lo[2], lo[3]));
     }
     sum = warp_sum(sum);
     if (lane == 0) red[w] = sum;
@@ -505,7 +533,8 @@ __global__ void __launch_bounds__(256) k_tc_out(const TcAttnArgs a) {
     const TcPlan &p = a.p;
     const int t = blockIdx.x, tid = threadIdx.x;
     if (tid < 32) unit_prefix<1>(p, pre);
-    if (tid < kHeads) inv[tid] = 1.0f / a.lsum[(size_t)t * kHeads + tid];
+    // 1 / l, then the P and V scales (powers of two: exact)
+    if (tid < kHeads) inv[tid] = (1.0f / a.lsum[(size_t)t * kHeads + tid]) * (1.0f / (kPScale * p.vscale));
     __syncthreads();
     const int m = t / kTokTile, np = pieces_o(p, m);
     constexpr int W = kHeads * HD;
@@ -535,16 +564,16 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// fp32 [rows][cols] (row stride `stride` bytes), boxes of box_rows x 32 with
+// fp16 [rows][cols] (row stride `stride` bytes), boxes of box_rows x 64 with
 // the 128-byte swizzle; elements outside [rows][cols] read as zero.
-bool make_map_f32(CUtensorMap *m, const float *base, int cols, int rows, size_t stride, int box_rows) {
+bool make_map_f16(CUtensorMap *m, const __half *base, int cols, int rows, size_t stride, int box_rows) {
     EncodeTiledFn fn = (EncodeTiledFn)g4_tmap_encoder();
     if (!fn || ((uintptr_t)base & 15) || (stride & 15) || cols < 1 || rows < 1) return false;
     const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     const cuuint64_t strides[1] = {(cuuint64_t)stride};
     const cuuint32_t box[2] = {(cuuint32_t)kTK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
-    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void *)base, dims, strides, box, estr,
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)base, dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -561,6 +590,11 @@ TcPlan make_plan(const AttnArgs &a, int sms, int *nunits_s, int *nunits_o) {
     p.nk = a.start_pos + a.T - p.kbase;
     p.kpad = (p.nk + kTN - 1) / kTN * kTN;
     p.nd = a.hd / kTN;
+    {   // |v| <= sqrt(hd): the largest power of two c with sqrt(hd) c < 2^15
+        int e;
+        frexpf(sqrtf((float)a.hd), &e);
+        p.vscale = ldexpf(1.0f, 15 - e);
+    }
     // pieces of about total / (2 SMs) stages, so the O units fill the SMs twice
     long long stages = 0;
     int us = 0;
@@ -580,30 +614,33 @@ TcPlan make_plan(const AttnArgs &a, int sms, int *nunits_s, int *nunits_o) {
 }
 
 // Workspace pieces, 1 KB aligned (float offsets).
-struct TcWs {
-    size_t qh, ql, kh, kl, vh, vl, s, pl, smax, lsum, opart, total;
+struct TcWs {   // byte offsets
+    size_t qh, ql, kh, kl, vh, vl, qinv, kinv, s, ph, pl, smax, lsum, opart, total;
 };
 TcWs ws_layout(const TcPlan &p, int nunits_o) {
     TcWs w{};
     size_t off = 0;
-    auto take = [&](size_t floats) {
+    auto take = [&](size_t bytes) {
         const size_t o = off;
-        off += (floats + 255) / 256 * 256;
+        off += (bytes + 1023) / 1024 * 1024;
         return o;
     };
-    const size_t R = (size_t)p.R, HD = (size_t)p.hd, kp = (size_t)p.kpad;
-    w.qh = take(R * HD);
-    w.ql = take(R * HD);
-    w.kh = take((size_t)p.nk * HD);
-    w.kl = take((size_t)p.nk * HD);
-    w.vh = take(HD * kp);
-    w.vl = take(HD * kp);
-    w.s = take(R * kp);
-    w.pl = take(R * kp);
-    w.smax = take(R * (kp / 128));
-    w.lsum = take(R);
-    w.opart = take((size_t)nunits_o * kTM * kTN);
-    w.total = off * 4;
+    const size_t R = (size_t)p.R, HD = (size_t)p.hd, kp = (size_t)p.kpad, nk = (size_t)p.nk;
+    w.qh = take(R * HD * 2);
+    w.ql = take(R * HD * 2);
+    w.kh = take(nk * HD * 2);
+    w.kl = take(nk * HD * 2);
+    w.vh = take(HD * kp * 2);
+    w.vl = take(HD * kp * 2);
+    w.qinv = take(R * 4);
+    w.kinv = take(nk * 4);
+    w.s = take(R * kp * 4);
+    w.ph = take(R * kp * 2);
+    w.pl = take(R * kp * 2);
+    w.smax = take(R * (kp / 128) * 4);
+    w.lsum = take(R * 4);
+    w.opart = take((size_t)nunits_o * kTM * kTN * 4);
+    w.total = off;
     return w;
 }
 
@@ -621,7 +658,7 @@ cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t
     const TcPlan p = make_plan(a, sms, &nus, &nuo);
     const TcWs w = ws_layout(p, nuo);
     if (!ws || ws_bytes < w.total || ((uintptr_t)ws & 255)) return cudaErrorInvalidValue;
-    float *f = (float *)ws;
+    uint8_t *b = (uint8_t *)ws;
     TcAttnArgs x{};
     x.p = p;
     x.qkv = a.qkv;
@@ -629,17 +666,20 @@ cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t
     x.kcache = a.kcache;
     x.vcache = a.vcache;
     x.mask = a.mask;
-    x.qh = f + w.qh;
-    x.ql = f + w.ql;
-    x.kh = f + w.kh;
-    x.kl = f + w.kl;
-    x.vh = f + w.vh;
-    x.vl = f + w.vl;
-    x.s = f + w.s;
-    x.pl = f + w.pl;
-    x.smax = f + w.smax;
-    x.lsum = f + w.lsum;
-    x.opart = f + w.opart;
+    x.qh = (__half *)(b + w.qh);
+    x.ql = (__half *)(b + w.ql);
+    x.kh = (__half *)(b + w.kh);
+    x.kl = (__half *)(b + w.kl);
+    x.vh = (__half *)(b + w.vh);
+    x.vl = (__half *)(b + w.vl);
+    x.qinv = (float *)(b + w.qinv);
+    x.kinv = (float *)(b + w.kinv);
+    x.s = (float *)(b + w.s);
+    x.ph = (__half *)(b + w.ph);
+    x.pl = (__half *)(b + w.pl);
+    x.smax = (float *)(b + w.smax);
+    x.lsum = (float *)(b + w.lsum);
+    x.opart = (float *)(b + w.opart);
     x.out = a.out;
     x.quant_out = a.quant_out;
     x.xq = a.xq;
@@ -648,11 +688,11 @@ cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t
     x.err = a.err;
     if (a.quant_out && (!a.xq || !a.xs)) return cudaErrorInvalidValue;
     CUtensorMap qh, ql, kh, kl, ph, pl, vh, vl;
-    const size_t rs = (size_t)HD * 4, ks = (size_t)p.kpad * 4;
-    if (!make_map_f32(&qh, x.qh, HD, p.R, rs, kTM) || !make_map_f32(&ql, x.ql, HD, p.R, rs, kTM) ||
-        !make_map_f32(&kh, x.kh, HD, p.nk, rs, kTN) || !make_map_f32(&kl, x.kl, HD, p.nk, rs, kTN) ||
-        !make_map_f32(&ph, x.s, p.kpad, p.R, ks, kTM) || !make_map_f32(&pl, x.pl, p.kpad, p.R, ks, kTM) ||
-        !make_map_f32(&vh, x.vh, p.nk, HD, ks, kTN) || !make_map_f32(&vl, x.vl, p.nk, HD, ks, kTN))
+    const size_t rs = (size_t)HD * 2, ks = (size_t)p.kpad * 2;
+    if (!make_map_f16(&qh, x.qh, HD, p.R, rs, kTM) || !make_map_f16(&ql, x.ql, HD, p.R, rs, kTM) ||
+        !make_map_f16(&kh, x.kh, HD, p.nk, rs, kTN) || !make_map_f16(&kl, x.kl, HD, p.nk, rs, kTN) ||
+        !make_map_f16(&ph, x.ph, p.kpad, p.R, ks, kTM) || !make_map_f16(&pl, x.pl, p.kpad, p.R, ks, kTM) ||
+        !make_map_f16(&vh, x.vh, p.nk, HD, ks, kTN) || !make_map_f16(&vl, x.vl, p.nk, HD, ks, kTN))
         return cudaErrorInvalidValue;
     cudaError_t e = g4_smem_optin((const void *)k_tc_gemm<0, HD>, kSmem);
     if (e == cudaSuccess) e = g4_smem_optin((const void *)k_tc_gemm<1, HD>, kSmem);

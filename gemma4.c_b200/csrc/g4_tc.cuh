@@ -33,12 +33,11 @@ G4_DEV void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, bo
         "l"(da), "l"(db), "r"(idesc), "r"((uint32_t)accumulate)
         : "memory");
 }
-// D (fp32, TMEM) (+)= A B^T on tf32 operands (the top 19 bits of each fp32
-// word of the shared-memory tiles); same descriptor forms as mma_i8.
-G4_DEV void mma_tf32(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, bool accumulate) {
+// D (fp32, TMEM) (+)= A B^T on fp16 operands; same descriptor forms as mma_i8.
+G4_DEV void mma_f16(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, bool accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
         "l"(da), "l"(db), "r"(idesc), "r"((uint32_t)accumulate)
         : "memory");
 }

@@ -28,26 +28,35 @@
 //                   transposed to [HD][keys] so that both GEMMs read K-major
 //                   tiles;
 //   2. k_tc_gemm<0> S = Q K^T per 128-row x 256-key tile (K = HD), only tiles
-//                   that hold a visible key; the epilogue stores S and every
-//                   row's max over the visible keys of each 128-key half tile;
-//   3. k_tc_soft    per row: m = max of its half-tile maxima, p = exp(s - m) on
-//                   visible keys (0 elsewhere), l = sum p; p stored as scaled
-//                   fp16 hi and lo;
-//   4. k_tc_gemm<1> O = P V per 128-row x 256-dim tile over one piece of the
-//                   row tile's keys (split K, so every SM has work), partial
-//                   tiles stored;
-//   5. k_tc_out     O = (sum of the pieces, in order) / l per token, stored and
+//                   that hold a visible key; the epilogue stores S tile-major
+//                   ([row tile][key tile][key][row]: each warp store is 128
+//                   contiguous bytes) and every row's max over the visible keys
+//                   of each 128-key half tile;
+//   3. k_tc_rowmax  per row: m = the max of its half-tile maxima;
+//   4. k_tc_gemm<1> O = P V per 128-row x 256-dim tile; the K stages of all
+//                   (row tile, dimension tile) pairs, in order, are cut into
+//                   one even run per CTA (a CTA's run may end or start inside
+//                   a pair: split K, balanced to one stage): each
+//                   stage's S block (64 keys x 128 rows, one bulk copy) becomes
+//                   p = exp(s - m) on visible keys (0 elsewhere) as scaled fp16
+//                   hi/lo A tiles in shared memory, in place, by the epilogue
+//                   warps (exp by the hardware ex2 approximation, relative
+//                   error ~1e-6); partial O tiles and partial sums l = sum p
+//                   stored per (pair, CTA) slot;
+//   5. k_tc_out     O = (sum of the slots, in CTA order) / l per token, stored and
 //                   quantised for o_proj (gemma4.c:459).
 // The schedule depends only on (T, start position, SM count): deterministic.
 //
 // GEMM roles (10 warps, one CTA per SM, persistent over units):
 //   warp 0      TMA producer: per stage the 64-wide K slice of A hi/lo (128
-//               rows) and B hi/lo (256 rows) with the 128-byte swizzle;
+//               rows; for O the raw S block instead) and B hi/lo (256 rows)
+//               with the 128-byte swizzle;
 //   warp 1      allocates 512 TMEM columns (the hi.hi and the correction
 //               accumulator, 256 columns each); one lane issues 3 x 4 MMAs
 //               (M 128, N 256, K 16) per stage;
 //   warps 2-9   epilogue: thread = row (TMEM lane), two warps per lane quadrant
-//               with 128 columns each.
+//               with 128 columns each; for O also the per-stage transform of S
+//               into P (thread = row x 32 keys).
 // Waits are bounded (mbar_wait); on a timeout every role leaves its loop, the
 // CTA waits (bounded) for its copies and MMAs in flight, and frees TMEM.
 #include <cuda.h>
@@ -70,7 +79,6 @@ constexpr int kOffBar = kTStages * kStageBytes;
 constexpr int kSmem = kOffBar + 128 + 1024;          // + barriers, + 1 KB for alignment
 constexpr int kTokTile = kTM / kHeads;                // 16 tokens per row tile
 constexpr int kMaxRowTiles = G4_BATCH / kTokTile;     // 32
-constexpr int kMinPiece = 8;                          // K stages per O unit, at least
 constexpr int kBufs = 1;                              // accumulator pairs in TMEM
 constexpr float kPScale = 32768.0f;                   // 2^15: p in (0, 1]
 // D fp32, A and B f16, both K-major, N = 256 (>> 3), M = 128 (>> 4)
@@ -87,7 +95,9 @@ struct TcPlan {
     int kbase, nk;    // the workspace holds keys [kbase, kbase + nk)
     int kpad;         // row stride (keys) of S, P and V^T: nk rounded up to 256
     int nd;           // 256-wide value-dimension tiles: hd / 256
-    int piece;        // O units: K stages (64 keys) per unit
+    int npairs;       // O: (row tile, dimension tile) pairs, row-tile major
+    int u1;           // O: K stages (64 keys) of all pairs
+    int g1;           // O: CTAs (each an even run of the stages)
     float vscale;     // V scale 2^(15 - ceil(log2 sqrt(hd)))
 };
 
@@ -107,14 +117,16 @@ __host__ __device__ inline int units_s(const TcPlan &p, int m) {
     tile_keys(p, m, &kb, &ke);
     return (ke + kTN - 1) / kTN - kb / kTN;
 }
-// O units of row tile m: value-dimension tiles x pieces of its K stages
-__host__ __device__ inline int pieces_o(const TcPlan &p, int m) {
+// O: K stages of row tile m (each of its dimension tiles has them all)
+__host__ __device__ inline int stages_o(const TcPlan &p, int m) {
     int kb, ke;
     tile_keys(p, m, &kb, &ke);
-    const int c0 = kb / kTK, c1 = (ke + kTK - 1) / kTK;
-    return (c1 - c0 + p.piece - 1) / p.piece;
+    return (ke + kTK - 1) / kTK - kb / kTK;
 }
-__host__ __device__ inline int units_o(const TcPlan &p, int m) { return p.nd * pieces_o(p, m); }
+// O: the CTA whose run holds stage s (CTA b runs [u1 b / g1, u1 (b + 1) / g1))
+__host__ __device__ inline int cta_of_stage(const TcPlan &p, long long s) {
+    return (int)(((s + 1) * p.g1 + p.u1 - 1) / p.u1) - 1;
+}
 
 struct TcAttnArgs {
     TcPlan p;
@@ -126,11 +138,11 @@ struct TcAttnArgs {
     __half *kh, *kl;      // [nk][HD] scaled
     __half *vh, *vl;      // [HD][kpad] scaled
     float *qinv, *kinv;   // [R], [nk]: 1 / the row's scale
-    float *s;             // [R][kpad] scores
-    __half *ph, *pl;      // [R][kpad] 2^15 p
+    float *s;             // [mt][kpad / 256][256 keys][128 rows] scores, tile-major
     float *smax;          // [R][kpad / 128]
-    float *lsum;          // [R]
-    float *opart;         // [O units][128][256]
+    float *rmax;          // [R]
+    float *lpart;         // [O slots][2][128] partial sums of p (pairs of dimension tile 0)
+    float *opart;         // [O slots][128][256]; slot = pair + CTA
     float *out;           // [T][8 HD]
     int8_t *xq;
     float *xs, *xsT;
@@ -151,11 +163,10 @@ G4_DEV float row_scale(float max_abs) {
     return ldexpf(1.0f, 15 - e);
 }
 
-// pre[0..mt] = prefix sums of the units of each row tile (warp 0; mt <= 32)
-template <int MODE>
-G4_DEV void unit_prefix(const TcPlan &p, int *pre) {
+// S: pre[0..mt] = prefix sums of the units of each row tile (warp 0; mt <= 32)
+G4_DEV void unit_prefix_s(const TcPlan &p, int *pre) {
     const int lane = threadIdx.x & 31;
-    int v = lane < p.mt ? (MODE == 0 ? units_s(p, lane) : units_o(p, lane)) : 0;
+    int v = lane < p.mt ? units_s(p, lane) : 0;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const int n = __shfl_up_sync(0xffffffffu, v, o);
@@ -164,31 +175,47 @@ G4_DEV void unit_prefix(const TcPlan &p, int *pre) {
     if (lane == 0) pre[0] = 0;
     if (lane < p.mt) pre[lane + 1] = v;
 }
+// O: pre[0..npairs] = prefix sums of the K stages of each pair (one thread)
+G4_DEV void pair_prefix_o(const TcPlan &p, int *pre) {
+    pre[0] = 0;
+    for (int i = 0; i < p.npairs; i++) pre[i + 1] = pre[i] + stages_o(p, i / p.nd);
+}
 
 struct Unit {
     int m, n;     // row tile; key tile (S) or value-dimension tile (O)
     int c0, c1;   // K stages [c0, c1)
+    int slot;     // O: partial slot (pair + CTA)
 };
+// The idx-th unit of this CTA (false: none left). S: units blockIdx.x, + gridDim.x, ...;
+// O: the pairs overlapping this CTA's run of stages, from pair i0 on.
 template <int MODE, int HD>
-G4_DEV Unit unit_of(const TcPlan &p, const int *pre, int u) {
-    Unit x;
-    int m = 0;
-    while (pre[m + 1] <= u) m++;
-    const int v = u - pre[m];
-    int kb, ke;
-    tile_keys(p, m, &kb, &ke);
-    x.m = m;
+G4_DEV bool unit_at(const TcPlan &p, const int *pre, int idx, int i0, Unit &x) {
     if (MODE == 0) {
-        x.n = kb / kTN + v;
+        const int u = blockIdx.x + idx * gridDim.x;
+        if (u >= pre[p.mt]) return false;
+        int m = 0;
+        while (pre[m + 1] <= u) m++;
+        int kb, ke;
+        tile_keys(p, m, &kb, &ke);
+        x.m = m;
+        x.n = kb / kTN + (u - pre[m]);
         x.c0 = 0;
         x.c1 = HD / kTK;
-    } else {
-        const int c0 = kb / kTK, c1 = (ke + kTK - 1) / kTK, np = (c1 - c0 + p.piece - 1) / p.piece;
-        x.n = v / np;
-        x.c0 = c0 + (v % np) * p.piece;
-        x.c1 = imin(c1, x.c0 + p.piece);
+        x.slot = u;
+        return true;
     }
-    return x;
+    const int i = i0 + idx;
+    const long long s0 = (long long)p.u1 * blockIdx.x / p.g1, s1 = (long long)p.u1 * (blockIdx.x + 1) / p.g1;
+    if (i >= p.npairs || pre[i] >= s1) return false;
+    int kb, ke;
+    x.m = i / p.nd;
+    x.n = i % p.nd;
+    tile_keys(p, x.m, &kb, &ke);
+    const int st = (int)(s0 > pre[i] ? s0 : pre[i]), en = (int)(s1 < pre[i + 1] ? s1 : pre[i + 1]);
+    x.c0 = kb / kTK + (st - pre[i]);
+    x.c1 = x.c0 + (en - st);
+    x.slot = i + blockIdx.x;
+    return true;
 }
 
 // ---------------------------------------------------------------------------
@@ -271,8 +298,9 @@ G4_DEV void load_acc(uint32_t taddr, int (&v)[32]) {
 }
 
 // ---------------------------------------------------------------------------
-// 2 and 4. The 3xTF32 GEMMs. MODE 0: A = Q, B = K, units (row tile, key tile);
-// MODE 1: A = P, B = V^T, units (row tile, dimension tile, piece of keys).
+// 2 and 4. The split-operand GEMMs. MODE 0: A = Q, B = K, units (row tile, key
+// tile); MODE 1: A = P (made from S in shared memory), B = V^T, units (pair,
+// this CTA's share of its K stages).
 template <int MODE, int HD>
 __global__ void __launch_bounds__(kThreads, 1)
     k_tc_gemm(const __grid_constant__ CUtensorMap map_ah, const __grid_constant__ CUtensorMap map_al,
@@ -285,13 +313,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *tfull = empty + kTStages;
     uint64_t *tempty = tfull + 2;
     uint64_t *drain = tempty + 2;
-    uint32_t *tmem_slot = (uint32_t *)(drain + 1);
-    __shared__ int pre[kMaxRowTiles + 1];
-    __shared__ int fail, issued;
+    uint64_t *xready = drain + 1;   // O: the stage's P tiles are written
+    uint32_t *tmem_slot = (uint32_t *)(xready + kTStages);
+    __shared__ int pre[2 * kMaxRowTiles + 1];
+    __shared__ int fail, issued, xfail, ipair0;
     const TcPlan &p = a.p;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-    if (warp == 0) unit_prefix<MODE>(p, pre);
+    if (MODE == 0 && warp == 0) unit_prefix_s(p, pre);
+    if (MODE == 1 && tid == 0) {
+        pair_prefix_o(p, pre);
+        const long long s0 = (long long)p.u1 * blockIdx.x / p.g1;
+        int i = 0;
+        while (pre[i + 1] <= s0) i++;   // the pair holding this CTA's first stage
+        ipair0 = i;
+    }
     if (tid == 32) {
         for (int s = 0; s < kTStages; s++) {
             mbar_init(&full[s], 1);
@@ -302,9 +338,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&tempty[b], kEpiWarps);
         }
         mbar_init(drain, 1);
+        for (int s = 0; s < kTStages; s++) mbar_init(&xready[s], kEpiWarps);
         mbar_fence_init();
         fail = 0;
         issued = 0;
+        xfail = 0;
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -316,15 +354,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    const int units = pre[p.mt];
+    const int ntk = p.kpad / kTN;   // key tiles per row tile in the S layout
+    const int i0 = MODE == 1 ? ipair0 : 0;
+    Unit x;
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             int k = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < units && ok; u += gridDim.x) {
-                const Unit x = unit_of<MODE, HD>(p, pre, u);
+            for (int idx = 0; ok && unit_at<MODE, HD>(p, pre, idx, i0, x); idx++) {
                 const int ay = x.m * kTM, by = x.n * kTN;
                 for (int c = x.c0; c < x.c1; c++, k++) {
                     const int s = k % kTStages, use = k / kTStages;
@@ -334,8 +373,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                     uint8_t *st = smem + s * kStageBytes;
                     mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    tma_load_2d(st, &map_ah, c * kTK, ay, &full[s]);
-                    tma_load_2d(st + kTileA, &map_al, c * kTK, ay, &full[s]);
+                    if (MODE == 0) {
+                        tma_load_2d(st, &map_ah, c * kTK, ay, &full[s]);
+                        tma_load_2d(st + kTileA, &map_al, c * kTK, ay, &full[s]);
+                    } else {   // the S block of keys [64 c, 64 c + 64): 64 x 128 fp32, contiguous
+                        bulk_g2s_plain(st, a.s + (((size_t)x.m * ntk + c / 4) * kTN + (c % 4) * kTK) * kTM,
+                                       2 * kTileA, &full[s]);
+                    }
                     tma_load_2d(st + 2 * kTileA, &map_bh, c * kTK, by, &full[s]);
                     tma_load_2d(st + 2 * kTileA + kTileB, &map_bl, c * kTK, by, &full[s]);
                 }
@@ -349,8 +393,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t d0 = umma_desc(smem, 0);
             int k = 0, i = 0;
             bool ok = true;
-            for (int u = blockIdx.x; u < units && ok; u += gridDim.x, i++) {
-                const Unit x = unit_of<MODE, HD>(p, pre, u);
+            for (; ok && unit_at<MODE, HD>(p, pre, i, i0, x); i++) {
                 const int buf = i % kBufs, use = i / kBufs;
                 if (use > 0 && !mbar_wait(&tempty[buf], (use - 1) & 1, a.err, G4D_TIMEOUT_EMPTY | (kCodeTempty << 8))) {
                     ok = false;
@@ -360,7 +403,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t td = tmem + (uint32_t)(buf * kTN), tcr = td + kTN;
                 for (int c = x.c0; c < x.c1; c++, k++) {
                     const int s = k % kTStages;
-                    if (!mbar_wait(&full[s], (k / kTStages) & 1, a.err, G4D_TIMEOUT_FULL | (kCodeFull << 8))) {
+                    if (!mbar_wait(MODE == 0 ? &full[s] : &xready[s], (k / kTStages) & 1, a.err,
+                                   G4D_TIMEOUT_FULL | (kCodeFull << 8))) {
                         ok = false;
                         break;
                     }
@@ -386,17 +430,74 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (!ok) fail = 1;
         }
     } else {
-        // ---------------- epilogue ----------------
+        // ---------------- epilogue (and, for O, the S -> P transform) ----------------
         const int e = warp - 2, q = warp & 3, ch = e >> 2;
         const int row = q * 32 + lane;
-        int i = 0;
-        for (int u = blockIdx.x; u < units; u += gridDim.x, i++) {
-            const Unit x = unit_of<MODE, HD>(p, pre, u);
+        int i = 0, k = 0;
+        for (; unit_at<MODE, HD>(p, pre, i, i0, x); i++) {
+            if (MODE == 1) {
+                // thread = row trow x keys [32 kh, 32 kh + 32) of each stage
+                const int te = tid - 64, trow = te & 127, kh = te >> 7;
+                const int rg = x.m * kTM + trow, t = rg >> 3;
+                const bool live = rg < p.R;
+                const int kmin = tc_first_key(p.sp + t, p.window) - p.kbase, kmax = p.sp + t - p.kbase;
+                const float mr = live ? a.rmax[rg] : 0.0f;
+                float lsum = 0.0f;
+                for (int c = x.c0; c < x.c1; c++, k++) {
+                    const int s = k % kTStages;
+                    const bool got = mbar_wait(&full[s], (k / kTStages) & 1, a.err, G4D_TIMEOUT_FULL | (kCodeFull << 8));
+                    float v[32];
+                    if (got) {
+                        const float *raw = (const float *)(smem + s * kStageBytes);
+#pragma unroll
+                        for (int j = 0; j < 32; j++) v[j] = raw[(kh * 32 + j) * kTM + trow];
+                    } else {
+                        xfail = 1;
+                        fail = 1;
+                    }
+                    // every thread of the transform has read the block before any writes over it
+                    // (a wait that gave up still arrives here: the decision to leave is uniform)
+                    bar_sync(1, 32 * kEpiWarps);
+                    if (xfail) break;
+                    const int kb0 = c * kTK + kh * 32;
+                    uint32_t hw[16], lw[16];
+#pragma unroll
+                    for (int j = 0; j < 32; j += 2) {
+                        const float p0 = live && kb0 + j >= kmin && kb0 + j <= kmax ? __expf(v[j] - mr) : 0.0f;
+                        const float p1 = live && kb0 + j + 1 >= kmin && kb0 + j + 1 <= kmax ? __expf(v[j + 1] - mr) : 0.0f;
+                        lsum += p0;
+                        lsum += p1;
+                        __half h0, l0, h1, l1;
+                        split_f16(p0 * kPScale, h0, l0);
+                        split_f16(p1 * kPScale, h1, l1);
+                        hw[j / 2] = pack2(h0, h1);
+                        lw[j / 2] = pack2(l0, l1);
+                    }
+                    // K-major fp16 rows of 128 bytes with the 128-byte swizzle: logical 16-byte
+                    // chunk j of row r sits at chunk j ^ (r % 8)
+                    uint8_t *th = smem + s * kStageBytes, *tl = th + kTileA;
+#pragma unroll
+                    for (int c4 = 0; c4 < 4; c4++) {
+                        const int off = trow * 128 + (((4 * kh + c4) ^ (trow & 7)) << 4);
+                        *(uint4 *)(th + off) = make_uint4(hw[4 * c4], hw[4 * c4 + 1], hw[4 * c4 + 2], hw[4 * c4 + 3]);
+                        *(uint4 *)(tl + off) = make_uint4(lw[4 * c4], lw[4 * c4 + 1], lw[4 * c4 + 2], lw[4 * c4 + 3]);
+                    }
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // visible to the tensor core
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&xready[s]);
+                }
+                if (xfail) break;
+                if (x.n == 0) a.lpart[((size_t)x.slot * 2 + kh) * kTM + trow] = lsum;
+            }
             const int buf = i % kBufs;
             const bool got = mbar_wait(&tfull[buf], (i / kBufs) & 1, a.err, G4D_TIMEOUT_FULL | (kCodeTfull << 8));
             if (!__all_sync(0xffffffffu, got)) {
-                if (lane == 0) fail = 1;
-                break;
+                if (lane == 0) {
+                    fail = 1;
+                    xfail = 1;   // the others leave at their next transform barrier
+                }
+                if (MODE == 0) break;
+                continue;
             }
             tc_fence_after();
             const uint32_t ta = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * kTN + ch * 128);
@@ -405,7 +506,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int t = rg >> 3;
                 const int kmin = tc_first_key(p.sp + t, p.window) - p.kbase, kmax = p.sp + t - p.kbase;
                 const int j0 = x.n * kTN + ch * 128;
-                float *dst = a.s + (size_t)rg * p.kpad + j0;
+                float *blk = a.s + ((size_t)x.m * ntk + x.n) * kTN * kTM;   // [256 keys][128 rows]
                 const float qi = rg < p.R ? a.qinv[rg] : 0.0f;
                 float mx = -INFINITY;
 #pragma unroll 1
@@ -417,25 +518,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&tempty[buf]);
                     }
-                    if (rg < p.R) {
-                        const int jb = j0 + c * 32;
+                    const int jb = j0 + c * 32;
 #pragma unroll
-                        for (int j = 0; j < 32; j++) {
-                            const int key = jb + j;
-                            // the row and key scales are powers of two: exact
-                            const float sv = __int_as_float(v[j]) * qi * (key < p.nk ? a.kinv[key] : 0.0f);
-                            v[j] = __float_as_int(sv);
-                            if (key >= kmin && key <= kmax) mx = fmaxf(mx, sv);
-                        }
-#pragma unroll
-                        for (int j = 0; j < 32; j += 4)
-                            *(float4 *)(dst + c * 32 + j) = make_float4(__int_as_float(v[j]), __int_as_float(v[j + 1]),
-                                                                        __int_as_float(v[j + 2]), __int_as_float(v[j + 3]));
+                    for (int j = 0; j < 32; j++) {
+                        const int key = jb + j;
+                        // the row and key scales are powers of two: exact
+                        const float sv = __int_as_float(v[j]) * qi * (key < p.nk ? a.kinv[key] : 0.0f);
+                        if (key >= kmin && key <= kmax) mx = fmaxf(mx, sv);
+                        blk[(size_t)(ch * 128 + c * 32 + j) * kTM + row] = sv;   // the warp: 128 contiguous bytes
                     }
                 }
                 if (rg < p.R) a.smax[(size_t)rg * (p.kpad / 128) + j0 / 128] = mx;
             } else {
-                float *dst = a.opart + ((size_t)u * kTM + row) * kTN + ch * 128;
+                float *dst = a.opart + ((size_t)x.slot * kTM + row) * kTN + ch * 128;
 #pragma unroll 1
                 for (int c = 0; c < 4; c++) {
                     int v[32];
@@ -478,72 +573,59 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
-// 3. Softmax numerators: one CTA per query row.
-__global__ void __launch_bounds__(256) k_tc_soft(const TcAttnArgs a) {
-    __shared__ float red[8];
+// 3. Row maxima of the scores: one warp per query row.
+__global__ void __launch_bounds__(256) k_tc_rowmax(const TcAttnArgs a) {
     const TcPlan &p = a.p;
-    const int r = blockIdx.x, tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-    const int m = r / kTM, t = r >> 3;
+    const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    if (r >= p.R) return;
     int kb, ke;
-    tile_keys(p, m, &kb, &ke);
-    const int kmin = tc_first_key(p.sp + t, p.window) - p.kbase, kmax = p.sp + t - p.kbase;
+    tile_keys(p, r / kTM, &kb, &ke);
     const int h0 = (kb / kTN) * 2, h1 = ((ke + kTN - 1) / kTN) * 2;
     float mx = -INFINITY;
-    for (int h = h0 + tid; h < h1; h += 256) mx = fmaxf(mx, a.smax[(size_t)r * (p.kpad / 128) + h]);
+    for (int h = h0 + lane; h < h1; h += 32) mx = fmaxf(mx, a.smax[(size_t)r * (p.kpad / 128) + h]);
     mx = warp_max(mx);
-    if (lane == 0) red[w] = mx;
-    __syncthreads();
-    mx = red[0];
-#pragma unroll
-    for (int i = 1; i < 8; i++) mx = fmaxf(mx, red[i]);
-    __syncthreads();
-    const float *srow = a.s + (size_t)r * p.kpad;
-    __half *hrow = a.ph + (size_t)r * p.kpad, *lrow = a.pl + (size_t)r * p.kpad;
-    const int j0 = (kb / kTK) * kTK, j1 = ((ke + kTK - 1) / kTK) * kTK;
-    float sum = 0.0f;
-    for (int j = j0 + 4 * tid; j < j1; j += 1024) {
-        const float4 sv = *(const float4 *)(srow + j);
-        const float x[4] = {sv.x, sv.y, sv.z, sv.w};
-        __half hi[4], lo[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const float e = (j + i >= kmin && j + i <= kmax) ? expf(x[i] - mx) : 0.0f;
-            sum += e;
-            split_f16(e * kPScale, hi[i], lo[i]);
-        }
-        *(uint2 *)(hrow + j) = make_uint2(pack2(hi[0], hi[1]), pack2(hi[2], hi[3]));
-        *(uint2 *)(lrow + j) = make_uint2(pack2(lo[0], lo[1]), pack2(lo[2], lo[3]));
-    }
-    sum = warp_sum(sum);
-    if (lane == 0) red[w] = sum;
-    __syncthreads();
-    if (tid == 0) {
-        float l = 0.0f;
-        for (int i = 0; i < 8; i++) l += red[i];
-        a.lsum[r] = l;
-    }
+    if (lane == 0) a.rmax[r] = mx;
 }
 
 // ---------------------------------------------------------------------------
 // 5. Output rows: one CTA per token (its 8 heads), pieces summed in order.
 template <int HD>
 __global__ void __launch_bounds__(256) k_tc_out(const TcAttnArgs a) {
-    __shared__ int pre[kMaxRowTiles + 1];
+    __shared__ int pre[2 * kMaxRowTiles + 1];
+    __shared__ int bfirst[2], blast[2];
     __shared__ float inv[kHeads];
     const TcPlan &p = a.p;
     const int t = blockIdx.x, tid = threadIdx.x;
-    if (tid < 32) unit_prefix<1>(p, pre);
-    // 1 / l, then the P and V scales (powers of two: exact)
-    if (tid < kHeads) inv[tid] = (1.0f / a.lsum[(size_t)t * kHeads + tid]) * (1.0f / (kPScale * p.vscale));
+    const int m = t / kTokTile;
+    if (tid == 0) {
+        pair_prefix_o(p, pre);
+        for (int n = 0; n < p.nd; n++) {   // the CTAs whose runs cover pair (m, n)
+            const int i = m * p.nd + n;
+            bfirst[n] = cta_of_stage(p, pre[i]);
+            blast[n] = cta_of_stage(p, pre[i + 1] - 1);
+        }
+    }
     __syncthreads();
-    const int m = t / kTokTile, np = pieces_o(p, m);
+    if (tid < kHeads) {
+        // l = the partial sums of the CTAs in order; 1 / l, then the P and V scales
+        // (powers of two: exact)
+        const int rl = (t * kHeads + tid) % kTM, i = m * p.nd;
+        float l = 0.0f;
+        for (int b = bfirst[0]; b <= blast[0]; b++) {
+            const size_t sl = (size_t)(i + b);
+            l += a.lpart[(sl * 2) * kTM + rl];
+            l += a.lpart[(sl * 2 + 1) * kTM + rl];
+        }
+        inv[tid] = (1.0f / l) * (1.0f / (kPScale * p.vscale));
+    }
+    __syncthreads();
     constexpr int W = kHeads * HD;
     for (int idx = tid; idx < W / 4; idx += 256) {
         const int h = idx / (HD / 4), c4 = idx % (HD / 4), d = c4 * 4;
         const int n = d / kTN, dl = d % kTN, rl = (t * kHeads + h) % kTM;
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int pc = 0; pc < np; pc++) {
-            const float4 v = *(const float4 *)(a.opart + ((size_t)(pre[m] + n * np + pc) * kTM + rl) * kTN + dl);
+        for (int b = bfirst[n]; b <= blast[n]; b++) {
+            const float4 v = *(const float4 *)(a.opart + ((size_t)(m * p.nd + n + b) * kTM + rl) * kTN + dl);
             acc.x += v.x;
             acc.y += v.y;
             acc.z += v.z;
@@ -595,27 +677,22 @@ TcPlan make_plan(const AttnArgs &a, int sms, int *nunits_s, int *nunits_o) {
         frexpf(sqrtf((float)a.hd), &e);
         p.vscale = ldexpf(1.0f, 15 - e);
     }
-    // pieces of about total / (2 SMs) stages, so the O units fill the SMs twice
-    long long stages = 0;
-    int us = 0;
+    int us = 0, u1 = 0;
     for (int m = 0; m < p.mt; m++) {
-        int kb, ke;
-        tile_keys(p, m, &kb, &ke);
-        stages += (long long)p.nd * ((ke + kTK - 1) / kTK - kb / kTK);
         us += units_s(p, m);
+        u1 += p.nd * stages_o(p, m);
     }
-    const long long want = (stages + 2LL * sms - 1) / (2LL * sms);
-    p.piece = want < kMinPiece ? kMinPiece : (int)want;
-    int uo = 0;
-    for (int m = 0; m < p.mt; m++) uo += units_o(p, m);
+    p.npairs = p.mt * p.nd;
+    p.u1 = u1;
+    p.g1 = u1 < sms ? u1 : sms;
     *nunits_s = us;
-    *nunits_o = uo;
+    *nunits_o = p.npairs + p.g1;   // O partial slots (pair + CTA)
     return p;
 }
 
 // Workspace pieces, 1 KB aligned (float offsets).
 struct TcWs {   // byte offsets
-    size_t qh, ql, kh, kl, vh, vl, qinv, kinv, s, ph, pl, smax, lsum, opart, total;
+    size_t qh, ql, kh, kl, vh, vl, qinv, kinv, s, smax, rmax, lpart, opart, total;
 };
 TcWs ws_layout(const TcPlan &p, int nunits_o) {
     TcWs w{};
@@ -634,11 +711,10 @@ TcWs ws_layout(const TcPlan &p, int nunits_o) {
     w.vl = take(HD * kp * 2);
     w.qinv = take(R * 4);
     w.kinv = take(nk * 4);
-    w.s = take(R * kp * 4);
-    w.ph = take(R * kp * 2);
-    w.pl = take(R * kp * 2);
+    w.s = take((size_t)p.mt * kTM * kp * 4);
     w.smax = take(R * (kp / 128) * 4);
-    w.lsum = take(R * 4);
+    w.rmax = take(R * 4);
+    w.lpart = take((size_t)nunits_o * 2 * kTM * 4);
     w.opart = take((size_t)nunits_o * kTM * kTN * 4);
     w.total = off;
     return w;
@@ -675,10 +751,9 @@ cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t
     x.qinv = (float *)(b + w.qinv);
     x.kinv = (float *)(b + w.kinv);
     x.s = (float *)(b + w.s);
-    x.ph = (__half *)(b + w.ph);
-    x.pl = (__half *)(b + w.pl);
     x.smax = (float *)(b + w.smax);
-    x.lsum = (float *)(b + w.lsum);
+    x.rmax = (float *)(b + w.rmax);
+    x.lpart = (float *)(b + w.lpart);
     x.opart = (float *)(b + w.opart);
     x.out = a.out;
     x.quant_out = a.quant_out;
@@ -687,11 +762,10 @@ cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t
     x.xsT = a.xsT;
     x.err = a.err;
     if (a.quant_out && (!a.xq || !a.xs)) return cudaErrorInvalidValue;
-    CUtensorMap qh, ql, kh, kl, ph, pl, vh, vl;
+    CUtensorMap qh, ql, kh, kl, vh, vl;
     const size_t rs = (size_t)HD * 2, ks = (size_t)p.kpad * 2;
     if (!make_map_f16(&qh, x.qh, HD, p.R, rs, kTM) || !make_map_f16(&ql, x.ql, HD, p.R, rs, kTM) ||
         !make_map_f16(&kh, x.kh, HD, p.nk, rs, kTN) || !make_map_f16(&kl, x.kl, HD, p.nk, rs, kTN) ||
-        !make_map_f16(&ph, x.ph, p.kpad, p.R, ks, kTM) || !make_map_f16(&pl, x.pl, p.kpad, p.R, ks, kTM) ||
         !make_map_f16(&vh, x.vh, p.nk, HD, ks, kTN) || !make_map_f16(&vl, x.vl, p.nk, HD, ks, kTN))
         return cudaErrorInvalidValue;
     cudaError_t e = g4_smem_optin((const void *)k_tc_gemm<0, HD>, kSmem);
@@ -699,8 +773,9 @@ cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t
     if (e) return e;
     k_tc_split<HD><<<dim3(4 * sms, 3), 256, 0, st>>>(x);
     k_tc_gemm<0, HD><<<nus < sms ? nus : sms, kThreads, kSmem, st>>>(qh, ql, kh, kl, x);
-    k_tc_soft<<<p.R, 256, 0, st>>>(x);
-    k_tc_gemm<1, HD><<<nuo < sms ? nuo : sms, kThreads, kSmem, st>>>(ph, pl, vh, vl, x);
+    k_tc_rowmax<<<(p.R + 7) / 8, 256, 0, st>>>(x);
+    // the A maps are unused for O (its A tiles are made from S in shared memory)
+    k_tc_gemm<1, HD><<<p.g1, kThreads, kSmem, st>>>(vh, vl, vh, vl, x);
     k_tc_out<HD><<<p.T, 256, 0, st>>>(x);
     return cudaGetLastError();
 }

@@ -847,12 +847,23 @@ struct BatchPlan {
     int seq;
 };
 
-// Prefill attention on the tensor cores for this layer kind and chunk size
-// (G4_OPT_ATTN_PATH); the CUDA-core kernel otherwise.
-constexpr int kTcMinTokens = 64;
-bool attn_on_tensor_cores(const g4_ctx *c, bool global, int T) {
+// Prefill attention on the tensor cores for this layer kind and chunk
+// (G4_OPT_ATTN_PATH); the CUDA-core kernel otherwise. Auto: by the chunk's
+// work W = sum over its tokens of the keys each sees. The tensor path has a
+// fixed cost of ~45 us (five launches, TMEM and pipeline set-up) and then
+// ~0.06 ns per unit of W, the CUDA-core kernel ~0.8 ns (global, 512-wide
+// heads) or ~0.35 ns (sliding) per unit (B200): they cross near W = 56k and
+// 157k.
+constexpr long long kTcMinWorkGlobal = 64 * 1024, kTcMinWorkSliding = 160 * 1024;
+bool attn_on_tensor_cores(const g4_ctx *c, bool global, int T, int start_pos) {
     if (c->strict || c->attn_path == 1) return false;
-    return c->attn_path == 2 || (global && T >= kTcMinTokens);
+    if (c->attn_path == 2) return true;
+    long long w = 0;
+    for (int t = 0; t < T; t++) {
+        const int p = start_pos + t;
+        w += global || p + 1 <= G4_SLIDING_WINDOW ? p + 1 : G4_SLIDING_WINDOW;
+    }
+    return w >= (global ? kTcMinWorkGlobal : kTcMinWorkSliding);
 }
 
 // Grow the tensor-core attention workspace for a chunk of T tokens at
@@ -860,7 +871,7 @@ bool attn_on_tensor_cores(const g4_ctx *c, bool global, int T) {
 int ensure_tc_ws(g4_ctx *c, int T, int start_pos, int ring_global) {
     size_t need = 0;
     for (int global = 0; global < 2; global++) {
-        if (!attn_on_tensor_cores(c, global != 0, T)) continue;
+        if (!attn_on_tensor_cores(c, global != 0, T, start_pos)) continue;
         AttnArgs a{};
         a.hd = global ? 512 : 256;
         a.window = global ? 0 : G4_SLIDING_WINDOW;
@@ -938,7 +949,7 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp
             // the tiled kernels also quantise their output rows for o_proj
             at.quant_out = 1;
             at.xsT = c->xsT;
-            if (attn_on_tensor_cores(c, Y.global, T))
+            if (attn_on_tensor_cores(c, Y.global, T, start_pos))
                 q.ck(g4_launch_attn_tc(at, c->tc_ws, c->tc_ws_cap, c->st));
             else
                 q.ck(g4_launch_attn_prefill(at, c->st, q.pdl));

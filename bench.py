@@ -430,15 +430,16 @@ def attention_bench(g4, hbm_peak, prefill_iters=10, decode_iters=50):
                                    iters=prefill_iters)
             _, ms_t = g4.attention(qkv, hd, k.copy(), v.copy(), start, cos_t, sin_t, mode=g4.ATTN_PREFILL_TC,
                                    iters=prefill_iters)
-            # the path the engine takes for a 512-token chunk (G4_OPT_ATTN_PATH 0)
-            ms_p = ms_t if hd == 512 else ms_c
+            # the path the engine takes for this chunk (G4_OPT_ATTN_PATH 0: by the keys its tokens see)
+            on_tc = float(keys.sum()) >= (64 * 1024 if hd == 512 else 160 * 1024)
+            ms_p = ms_t if on_tc else ms_c
             _, ms_d = g4.attention(qkv[:1], hd, k, v, ctx - 1, cos_t, sin_t, mode=g4.ATTN_DECODE, splits=148,
                                    iters=decode_iters)
             dbytes = float(keys[-1]) * hd * 8                 # fp32 K and V rows read by one decode token
             tfl = flops / (ms_p / 1e3) / 1e12
             gbs = dbytes / (ms_d / 1e3) / 1e9
             row[kind] = {"prefill_chunk_us": ms_p * 1e3, "prefill_tflops": tfl,
-                         "prefill_path": "tensor cores" if hd == 512 else "cuda cores",
+                         "prefill_path": "tensor cores" if on_tc else "cuda cores",
                          "prefill_cuda_core_us": ms_c * 1e3, "prefill_tensor_core_us": ms_t * 1e3,
                          "prefill_cuda_core_frac_fp32_peak": flops / (ms_c / 1e3) / 1e12 / FP32_TFLOPS,
                          "decode_us": ms_d * 1e3,
@@ -447,8 +448,9 @@ def attention_bench(g4, hbm_peak, prefill_iters=10, decode_iters=50):
                                             for k in ("sliding", "global")) / 1e3
         row["model_decode_us"] = sum(row[k]["decode_us"] * row[k]["layers"] for k in ("sliding", "global"))
         res[f"ctx{ctx}"] = row
-    res["note"] = ("prefill: the engine's path for a 512-token chunk (tensor cores on global layers: 3xTF32 "
-                   "tcgen05 GEMMs k_tc_*; CUDA cores on sliding layers: k_attn_prefill + merge), both timed; "
+    res["note"] = ("prefill: the engine's path for a 512-token chunk (tensor cores: tcgen05 GEMMs on fp16 hi/lo "
+                   "operands, k_tc_*, where the chunk's key work is >= 64k global / 160k sliding; else CUDA cores: "
+                   "k_attn_prefill + merge), both timed; "
                    "TFLOP/s count the attention's own FLOPs (q.k and p.v), the CUDA-core frac is of the nominal "
                    f"FP32 FMA peak {FP32_TFLOPS:.1f} TFLOP/s; decode: split-KV kernel + combine standalone (inside k_decode "
                    "the same code runs as one phase), frac of the measured HBM copy bandwidth")

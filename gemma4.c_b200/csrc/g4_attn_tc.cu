@@ -175,10 +175,27 @@ G4_DEV void unit_prefix_s(const TcPlan &p, int *pre) {
     if (lane == 0) pre[0] = 0;
     if (lane < p.mt) pre[lane + 1] = v;
 }
-// O: pre[0..npairs] = prefix sums of the K stages of each pair (one thread)
+// O: pre[0..npairs] = prefix sums of the K stages of each pair (one warp, two
+// pairs a lane; npairs <= 64)
 G4_DEV void pair_prefix_o(const TcPlan &p, int *pre) {
-    pre[0] = 0;
-    for (int i = 0; i < p.npairs; i++) pre[i + 1] = pre[i] + stages_o(p, i / p.nd);
+    const int lane = threadIdx.x & 31, i0 = 2 * lane, i1 = i0 + 1;
+    const int v0 = i0 < p.npairs ? stages_o(p, i0 / p.nd) : 0, v1 = i1 < p.npairs ? stages_o(p, i1 / p.nd) : 0;
+    int inc = v0 + v1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += n;
+    }
+    const int exc = inc - v0 - v1;
+    if (lane == 0) pre[0] = 0;
+    if (i0 < p.npairs) pre[i0 + 1] = exc + v0;
+    if (i1 < p.npairs) pre[i1 + 1] = inc;
+}
+// O: the pair holding stage s (one warp, after pair_prefix_o): the count of pairs i >= 1 with pre[i] <= s
+G4_DEV int pair_of_stage(const TcPlan &p, const int *pre, long long s) {
+    const int lane = threadIdx.x & 31;
+    const bool a = lane + 1 <= p.npairs && pre[lane + 1] <= s, b = lane + 33 <= p.npairs && pre[lane + 33] <= s;
+    return __popc(__ballot_sync(0xffffffffu, a)) + __popc(__ballot_sync(0xffffffffu, b));
 }
 
 struct Unit {
@@ -321,12 +338,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
     if (MODE == 0 && warp == 0) unit_prefix_s(p, pre);
-    if (MODE == 1 && tid == 0) {
+    if (MODE == 1 && warp == 0) {
         pair_prefix_o(p, pre);
-        const long long s0 = (long long)p.u1 * blockIdx.x / p.g1;
-        int i = 0;
-        while (pre[i + 1] <= s0) i++;   // the pair holding this CTA's first stage
-        ipair0 = i;
+        __syncwarp();
+        // the pair holding this CTA's first stage
+        const int i = pair_of_stage(p, pre, (long long)p.u1 * blockIdx.x / p.g1);
+        if (lane == 0) ipair0 = i;
     }
     if (tid == 32) {
         for (int s = 0; s < kTStages; s++) {
@@ -597,12 +614,13 @@ __global__ void __launch_bounds__(256) k_tc_out(const TcAttnArgs a) {
     const TcPlan &p = a.p;
     const int t = blockIdx.x, tid = threadIdx.x;
     const int m = t / kTokTile;
-    if (tid == 0) {
+    if (tid < 32) {
         pair_prefix_o(p, pre);
-        for (int n = 0; n < p.nd; n++) {   // the CTAs whose runs cover pair (m, n)
-            const int i = m * p.nd + n;
-            bfirst[n] = cta_of_stage(p, pre[i]);
-            blast[n] = cta_of_stage(p, pre[i + 1] - 1);
+        __syncwarp();
+        if (tid < p.nd) {   // the CTAs whose runs cover pair (m, n)
+            const int i = m * p.nd + tid;
+            bfirst[tid] = cta_of_stage(p, pre[i]);
+            blast[tid] = cta_of_stage(p, pre[i + 1] - 1);
         }
     }
     __syncthreads();
@@ -684,6 +702,10 @@ TcPlan make_plan(const AttnArgs &a, int sms, int *nunits_s, int *nunits_o) {
     }
     p.npairs = p.mt * p.nd;
     p.u1 = u1;
+    // one run per SM even when runs are short: a unit's epilogue and pipeline
+    // refill (~6-8 us: the two accumulators fill TMEM, so nothing overlaps
+    // them) cost more in sequence on fewer SMs (measured: 36 runs of 8 stages
+    // 71 us, 148 runs of 2 stages 25 us, global chunk at position 0)
     p.g1 = u1 < sms ? u1 : sms;
     *nunits_s = us;
     *nunits_o = p.npairs + p.g1;   // O partial slots (pair + CTA)

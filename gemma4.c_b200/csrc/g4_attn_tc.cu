@@ -37,7 +37,7 @@
 //                   (row tile, dimension tile) pairs, in order, are cut into
 //                   one even run per CTA (a CTA's run may end or start inside
 //                   a pair: split K, balanced to one stage): each
-//                   stage's S block (64 keys x 128 rows, one bulk copy) becomes
+//                   stage's S block (32 keys x 128 rows, one bulk copy) becomes
 //                   p = exp(s - m) on visible keys (0 elsewhere) as scaled fp16
 //                   hi/lo A tiles in shared memory, in place, by the epilogue
 //                   warps (exp by the hardware ex2 approximation, relative
@@ -48,11 +48,11 @@
 // The schedule depends only on (T, start position, SM count): deterministic.
 //
 // GEMM roles (10 warps, one CTA per SM, persistent over units):
-//   warp 0      TMA producer: per stage the 64-wide K slice of A hi/lo (128
+//   warp 0      TMA producer: per stage the 32-wide K slice of A hi/lo (128
 //               rows; for O the raw S block instead) and B hi/lo (256 rows)
-//               with the 128-byte swizzle;
+//               with the 64-byte swizzle, four stages of 48 KB in flight;
 //   warp 1      allocates 512 TMEM columns (the hi.hi and the correction
-//               accumulator, 256 columns each); one lane issues 3 x 4 MMAs
+//               accumulator, 256 columns each); one lane issues 3 x 2 MMAs
 //               (M 128, N 256, K 16) per stage;
 //   warps 2-9   epilogue: thread = row (TMEM lane), two warps per lane quadrant
 //               with 128 columns each; for O also the per-stage transform of S
@@ -68,11 +68,11 @@ namespace {
 
 constexpr int kTM = 128;                  // query rows per tile (16 tokens x 8 heads)
 constexpr int kTN = 256;                  // keys (S) or value dimensions (O) per tile
-constexpr int kTK = 64;                   // fp16 K elements per stage: one 128-byte row
-constexpr int kTStages = 2;
-constexpr int kTileA = kTM * kTK * 2;     // 16 KB
-constexpr int kTileB = kTN * kTK * 2;     // 32 KB
-constexpr int kStageBytes = 2 * kTileA + 2 * kTileB;   // hi and lo of both operands
+constexpr int kTK = 32;                   // fp16 K elements per stage: one 64-byte row
+constexpr int kTStages = 4;
+constexpr int kTileA = kTM * kTK * 2;     // 8 KB
+constexpr int kTileB = kTN * kTK * 2;     // 16 KB
+constexpr int kStageBytes = 2 * kTileA + 2 * kTileB;   // hi and lo of both operands: 48 KB
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kOffBar = kTStages * kStageBytes;
@@ -96,7 +96,7 @@ struct TcPlan {
     int kpad;         // row stride (keys) of S, P and V^T: nk rounded up to 256
     int nd;           // 256-wide value-dimension tiles: hd / 256
     int npairs;       // O: (row tile, dimension tile) pairs, row-tile major
-    int u1;           // O: K stages (64 keys) of all pairs
+    int u1;           // O: K stages (32 keys) of all pairs
     int g1;           // O: CTAs (each an even run of the stages)
     float vscale;     // V scale 2^(15 - ceil(log2 sqrt(hd)))
 };
@@ -393,8 +393,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (MODE == 0) {
                         tma_load_2d(st, &map_ah, c * kTK, ay, &full[s]);
                         tma_load_2d(st + kTileA, &map_al, c * kTK, ay, &full[s]);
-                    } else {   // the S block of keys [64 c, 64 c + 64): 64 x 128 fp32, contiguous
-                        bulk_g2s_plain(st, a.s + (((size_t)x.m * ntk + c / 4) * kTN + (c % 4) * kTK) * kTM,
+                    } else {   // the S block of keys [32 c, 32 c + 32): 32 x 128 fp32, contiguous
+                        constexpr int per = kTN / kTK;   // blocks per key tile
+                        bulk_g2s_plain(st, a.s + (((size_t)x.m * ntk + c / per) * kTN + (c % per) * kTK) * kTM,
                                        2 * kTileA, &full[s]);
                     }
                     tma_load_2d(st + 2 * kTileA, &map_bh, c * kTK, by, &full[s]);
@@ -407,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            const uint64_t d0 = umma_desc(smem, 0);
+            const uint64_t d0 = umma_desc_sw64(smem, 0);
             int k = 0, i = 0;
             bool ok = true;
             for (; ok && unit_at<MODE, HD>(p, pre, i, i0, x); i++) {
@@ -453,7 +454,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int i = 0, k = 0;
         for (; unit_at<MODE, HD>(p, pre, i, i0, x); i++) {
             if (MODE == 1) {
-                // thread = row trow x keys [32 kh, 32 kh + 32) of each stage
+                // thread = row trow x keys [16 kh, 16 kh + 16) of each stage
                 const int te = tid - 64, trow = te & 127, kh = te >> 7;
                 const int rg = x.m * kTM + trow, t = rg >> 3;
                 const bool live = rg < p.R;
@@ -463,11 +464,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                 for (int c = x.c0; c < x.c1; c++, k++) {
                     const int s = k % kTStages;
                     const bool got = mbar_wait(&full[s], (k / kTStages) & 1, a.err, G4D_TIMEOUT_FULL | (kCodeFull << 8));
-                    float v[32];
+                    float v[kTK / 2];
                     if (got) {
                         const float *raw = (const float *)(smem + s * kStageBytes);
 #pragma unroll
-                        for (int j = 0; j < 32; j++) v[j] = raw[(kh * 32 + j) * kTM + trow];
+                        for (int j = 0; j < kTK / 2; j++) v[j] = raw[(kh * (kTK / 2) + j) * kTM + trow];
                     } else {
                         xfail = 1;
                         fail = 1;
@@ -476,10 +477,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // (a wait that gave up still arrives here: the decision to leave is uniform)
                     bar_sync(1, 32 * kEpiWarps);
                     if (xfail) break;
-                    const int kb0 = c * kTK + kh * 32;
-                    uint32_t hw[16], lw[16];
+                    const int kb0 = c * kTK + kh * (kTK / 2);
+                    uint32_t hw[kTK / 4], lw[kTK / 4];
 #pragma unroll
-                    for (int j = 0; j < 32; j += 2) {
+                    for (int j = 0; j < kTK / 2; j += 2) {
                         const float p0 = live && kb0 + j >= kmin && kb0 + j <= kmax ? __expf(v[j] - mr) : 0.0f;
                         const float p1 = live && kb0 + j + 1 >= kmin && kb0 + j + 1 <= kmax ? __expf(v[j + 1] - mr) : 0.0f;
                         lsum += p0;
@@ -490,12 +491,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                         hw[j / 2] = pack2(h0, h1);
                         lw[j / 2] = pack2(l0, l1);
                     }
-                    // K-major fp16 rows of 128 bytes with the 128-byte swizzle: logical 16-byte
-                    // chunk j of row r sits at chunk j ^ (r % 8)
+                    // K-major fp16 rows of 64 bytes with the 64-byte swizzle: logical 16-byte
+                    // chunk j of row r sits at chunk j ^ ((r / 2) % 4)
                     uint8_t *th = smem + s * kStageBytes, *tl = th + kTileA;
 #pragma unroll
-                    for (int c4 = 0; c4 < 4; c4++) {
-                        const int off = trow * 128 + (((4 * kh + c4) ^ (trow & 7)) << 4);
+                    for (int c4 = 0; c4 < kTK / 16; c4++) {
+                        const int off = trow * (kTK * 2) + ((((kTK / 16) * kh + c4) ^ ((trow >> 1) & 3)) << 4);
                         *(uint4 *)(th + off) = make_uint4(hw[4 * c4], hw[4 * c4 + 1], hw[4 * c4 + 2], hw[4 * c4 + 3]);
                         *(uint4 *)(tl + off) = make_uint4(lw[4 * c4], lw[4 * c4 + 1], lw[4 * c4 + 2], lw[4 * c4 + 3]);
                     }
@@ -664,8 +665,8 @@ typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t
                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
 
-// fp16 [rows][cols] (row stride `stride` bytes), boxes of box_rows x 64 with
-// the 128-byte swizzle; elements outside [rows][cols] read as zero.
+// fp16 [rows][cols] (row stride `stride` bytes), boxes of box_rows x 32 with
+// the 64-byte swizzle; elements outside [rows][cols] read as zero.
 bool make_map_f16(CUtensorMap *m, const __half *base, int cols, int rows, size_t stride, int box_rows) {
     EncodeTiledFn fn = (EncodeTiledFn)g4_tmap_encoder();
     if (!fn || ((uintptr_t)base & 15) || (stride & 15) || cols < 1 || rows < 1) return false;
@@ -674,7 +675,7 @@ bool make_map_f16(CUtensorMap *m, const __half *base, int cols, int rows, size_t
     const cuuint32_t box[2] = {(cuuint32_t)kTK, (cuuint32_t)box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, (void *)base, dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

@@ -26,6 +26,13 @@ G4_DEV uint64_t umma_desc(const void *tile, int kbyte) {
     const uint32_t a = smem_u32(tile) + (uint32_t)kbyte;
     return (uint64_t)((a >> 4) & 0x3FFF) | ((uint64_t)(1024 >> 4) << 32) | (1ull << 46) | (2ull << 61);
 }
+// The same for rows of 64 bytes with the 64-byte swizzle: 8-row atoms of 512
+// bytes (stride byte offset), layout SWIZZLE_64B; 16-byte chunk j of row r sits
+// at chunk j ^ ((r / 2) % 4).
+G4_DEV uint64_t umma_desc_sw64(const void *tile, int kbyte) {
+    const uint32_t a = smem_u32(tile) + (uint32_t)kbyte;
+    return (uint64_t)((a >> 4) & 0x3FFF) | ((uint64_t)(512 >> 4) << 32) | (1ull << 46) | (4ull << 61);
+}
 G4_DEV void mma_i8(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t idesc, bool accumulate) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"

@@ -22,17 +22,22 @@ namespace {
 // ---------------------------------------------------------------------------
 // q/k/v post-processing for a chunk of T tokens (prefill and small-T decode):
 // q heads normalised + rotated in place; k, v normalised (+k rotated) and
-// written to their ring slots. grid (T, heads [+2]), one warp per vector.
+// written to their ring slots. One warp per vector, kQkvWarps vectors per CTA
+// (vector v: token v / W, which = v % W with W = heads [+2]).
+constexpr int kQkvWarps = 8;
 template <int HD>
-__global__ void __launch_bounds__(32) k_qkv_post(const AttnArgs a) {
-    __shared__ float x[HD];
+__global__ void __launch_bounds__(32 * kQkvWarps) k_qkv_post(const AttnArgs a, int W) {
+    __shared__ float xs_[kQkvWarps][HD];
     griddep_launch();
     griddep_wait();
-    const int t = blockIdx.x, which = blockIdx.y;   // 0..7 q heads, 8 = k, 9 = v
+    const int vi = blockIdx.x * kQkvWarps + (threadIdx.x >> 5);
+    if (vi >= a.T * W) return;   // whole warps: the vector index is warp-uniform
+    float *x = xs_[threadIdx.x >> 5];
+    const int t = vi / W, which = vi - t * W;   // 0..7 q heads, 8 = k, 9 = v
     const int p = a.row_pos ? a.row_pos[t] : a.start_pos + t;
     const size_t so = a.row_seq ? (size_t)a.row_seq[t] * a.seq_stride : 0;
     float *src = a.qkv + (size_t)t * a.qkv_stride + which * HD;
-    const int lane = threadIdx.x;
+    const int lane = threadIdx.x & 31;
     for (int i = lane; i < HD; i += 32) x[i] = src[i];
     __syncwarp();
     const float *cosr = a.rope_cos + (size_t)p * a.pairs, *sinr = a.rope_sin + (size_t)p * a.pairs;
@@ -588,9 +593,10 @@ cudaError_t launch_prefill(const AttnArgs &a, cudaStream_t st, bool pdl) {
 }  // namespace
 
 cudaError_t g4_launch_qkv_post(const AttnArgs &a, cudaStream_t st, bool pdl) {
-    dim3 grid(a.T, kHeads + (a.has_kv ? 2 : 0));
-    if (a.hd == 256) return g4_launch(k_qkv_post<256>, grid, dim3(32), 0, st, pdl, a);
-    if (a.hd == 512) return g4_launch(k_qkv_post<512>, grid, dim3(32), 0, st, pdl, a);
+    const int W = kHeads + (a.has_kv ? 2 : 0);
+    const dim3 grid((a.T * W + kQkvWarps - 1) / kQkvWarps), block(32 * kQkvWarps);
+    if (a.hd == 256) return g4_launch(k_qkv_post<256>, grid, block, 0, st, pdl, a, W);
+    if (a.hd == 512) return g4_launch(k_qkv_post<512>, grid, block, 0, st, pdl, a, W);
     return cudaErrorInvalidValue;
 }
 

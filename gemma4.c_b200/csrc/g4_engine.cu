@@ -866,9 +866,9 @@ bool attn_on_tensor_cores(const g4_ctx *c, bool global, int T, int start_pos) {
     return w >= (global ? kTcMinWorkGlobal : kTcMinWorkSliding);
 }
 
-// Grow the tensor-core attention workspace for a chunk of T tokens at
-// start_pos (before any launch of the chunk: freeing waits for the stream).
-int ensure_tc_ws(g4_ctx *c, int T, int start_pos, int ring_global) {
+// Tensor-core attention workspace bytes for a chunk of T tokens at start_pos
+// (the larger of the two layer kinds that take that path); 0 if neither does.
+size_t tc_ws_need(const g4_ctx *c, int T, int start_pos, int ring_global, bool *bad) {
     size_t need = 0;
     for (int global = 0; global < 2; global++) {
         if (!attn_on_tensor_cores(c, global != 0, T, start_pos)) continue;
@@ -880,17 +880,37 @@ int ensure_tc_ws(g4_ctx *c, int T, int start_pos, int ring_global) {
         a.start_pos = start_pos;
         a.qkv = a.kcache = a.vcache = a.out = (float *)c;   // non-null placeholders: only the size is asked
         const size_t b = g4_attn_tc_ws_bytes(a);
-        if (!b) return fail(c, G4_ERR_INVALID, "tensor-core attention cannot run T %d at %d", T, start_pos);
+        if (!b) *bad = true;
         need = b > need ? b : need;
     }
+    return need;
+}
+
+// Grow the tensor-core attention workspace for a chunk of T tokens at
+// start_pos (before any launch of the chunk: freeing waits for the stream).
+// A growth costs a stream drain and a large allocation (~15 ms), so it
+// provisions ahead: for the last chunk of the whole context range when the
+// device has four times that much memory free (2.7 GB at 131072 positions),
+// else for twice the need.
+int ensure_tc_ws(g4_ctx *c, int T, int start_pos, int ring_global) {
+    bool bad = false;
+    const size_t need = tc_ws_need(c, T, start_pos, ring_global, &bad);
+    if (bad) return fail(c, G4_ERR_INVALID, "tensor-core attention cannot run T %d at %d", T, start_pos);
     if (need <= c->tc_ws_cap) return G4_OK;
     CK(cudaStreamSynchronize(c->st));
     if (c->tc_ws) cudaFree(c->tc_ws);
     c->tc_ws = nullptr;
     c->tc_ws_cap = 0;
-    // a quarter more than asked, so a growing context reallocates rarely
-    const size_t want = need + need / 4;
-    CK(cudaMalloc(&c->tc_ws, want));
+    bool bad_full = false;
+    const size_t full = tc_ws_need(c, G4_BATCH, ring_global - G4_BATCH, ring_global, &bad_full);
+    size_t free_b = 0, total_b = 0;
+    size_t want = 2 * need;
+    if (!bad_full && full >= need && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess && free_b / 4 > full) want = full;
+    if (cudaMalloc(&c->tc_ws, want) != cudaSuccess) {
+        cudaGetLastError();   // not sticky: retry at the exact need
+        want = need;
+        CK(cudaMalloc(&c->tc_ws, want));
+    }
     c->tc_ws_cap = want;
     return G4_OK;
 }

@@ -170,20 +170,29 @@ __global__ void __launch_bounds__(256) k_rows_norm(int mode, const float *src, c
     constexpr int PER = G4_HIDDEN / 256;
     const int t = blockIdx.x, tid = threadIdx.x;
     const float *h = src + (size_t)t * G4_HIDDEN;
-    float v[PER];
+    // every global operand of the row is loaded up front (one round trip, not
+    // one per reduction); the arithmetic below is unchanged
+    float v[PER], rin[PER], wq[PER], wp[PER];
+    const bool has_res = mode != 0, has_pre = mode == 0 || mode == 1;
 #pragma unroll
-    for (int i = 0; i < PER; i++) v[i] = h[tid + 256 * i];
+    for (int i = 0; i < PER; i++) {
+        const int e = tid + 256 * i;
+        v[i] = h[e];
+        rin[i] = has_res ? res_in[(size_t)t * G4_HIDDEN + e] : 0.0f;
+        wq[i] = has_res ? w_post[e] : 0.0f;
+        wp[i] = has_pre ? w_pre[e] : 0.0f;
+    }
+    const float sc = mode != 0 && scalar ? *scalar : 1.0f;
     const float ss = sumsq_row<PER>(v, strict, y, red);
     const float inv = rms_inv(ss, (float)G4_HIDDEN, eps);
     if (mode == 0) {
 #pragma unroll
-        for (int i = 0; i < PER; i++) v[i] = rms_apply(v[i], inv, w_pre[tid + 256 * i]);
+        for (int i = 0; i < PER; i++) v[i] = rms_apply(v[i], inv, wp[i]);
     } else {
-        const float sc = scalar ? *scalar : 1.0f;
 #pragma unroll
         for (int i = 0; i < PER; i++) {
             const int e = tid + 256 * i;
-            float r = __fadd_rn(res_in[(size_t)t * G4_HIDDEN + e], rms_apply(v[i], inv, w_post[e]));
+            float r = __fadd_rn(rin[i], rms_apply(v[i], inv, wq[i]));
             if (scalar) r = __fmul_rn(r, sc);
             res_out[(size_t)t * G4_HIDDEN + e] = r;
             v[i] = r;
@@ -193,7 +202,7 @@ __global__ void __launch_bounds__(256) k_rows_norm(int mode, const float *src, c
             const float ss2 = sumsq_row<PER>(v, strict, y, red);
             const float inv2 = rms_inv(ss2, (float)G4_HIDDEN, eps);
 #pragma unroll
-            for (int i = 0; i < PER; i++) v[i] = rms_apply(v[i], inv2, w_pre[tid + 256 * i]);
+            for (int i = 0; i < PER; i++) v[i] = rms_apply(v[i], inv2, wp[i]);
         }
     }
 #pragma unroll

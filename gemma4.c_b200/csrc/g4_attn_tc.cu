@@ -794,7 +794,8 @@ cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t
     cudaError_t e = g4_smem_optin((const void *)k_tc_gemm<0, HD>, kSmem);
     if (e == cudaSuccess) e = g4_smem_optin((const void *)k_tc_gemm<1, HD>, kSmem);
     if (e) return e;
-    k_tc_split<HD><<<dim3(4 * sms, 3), 256, 0, st>>>(x);
+    // job 0 splits Q; jobs 1 and 2 K and V, unless the workspace holds them already
+    k_tc_split<HD><<<dim3(4 * sms, a.reuse_kv ? 1 : 3), 256, 0, st>>>(x);
     k_tc_gemm<0, HD><<<nus < sms ? nus : sms, kThreads, kSmem, st>>>(qh, ql, kh, kl, x);
     k_tc_rowmax<<<(p.R + 7) / 8, 256, 0, st>>>(x);
     // the A maps are unused for O (its A tiles are made from S in shared memory)

@@ -89,10 +89,11 @@ struct g4_ctx {
     bool strict = false;          // reference-order reductions (bit-exact forward)
     float *scores = nullptr;      // strict attention scratch
     size_t scores_cap = 0;
-    // tensor-core prefill attention: path option and its workspace (grown on demand)
+    // tensor-core prefill attention: path option and its workspace (grown on
+    // demand): the global layers' region, then the sliding layers' region
     int attn_path = 0;
     void *tc_ws = nullptr;
-    size_t tc_ws_cap = 0;
+    size_t tc_ws_gcap = 0, tc_ws_scap = 0;
     cudaGraphExec_t g_decode = nullptr;
     int graph_cur = 0;
     bool decode_warm = false;
@@ -866,58 +867,73 @@ bool attn_on_tensor_cores(const g4_ctx *c, bool global, int T, int start_pos) {
     return w >= (global ? kTcMinWorkGlobal : kTcMinWorkSliding);
 }
 
-// Tensor-core attention workspace bytes for a chunk of T tokens at start_pos
-// (the larger of the two layer kinds that take that path); 0 if neither does.
-size_t tc_ws_need(const g4_ctx *c, int T, int start_pos, int ring_global, bool *bad) {
-    size_t need = 0;
-    for (int global = 0; global < 2; global++) {
-        if (!attn_on_tensor_cores(c, global != 0, T, start_pos)) continue;
-        AttnArgs a{};
-        a.hd = global ? 512 : 256;
-        a.window = global ? 0 : G4_SLIDING_WINDOW;
-        a.mask = (global ? ring_global : 1024) - 1;
-        a.T = T;
-        a.start_pos = start_pos;
-        a.qkv = a.kcache = a.vcache = a.out = (float *)c;   // non-null placeholders: only the size is asked
-        const size_t b = g4_attn_tc_ws_bytes(a);
-        if (!b) *bad = true;
-        need = b > need ? b : need;
-    }
-    return need;
+// Tensor-core attention workspace bytes of one layer kind for a chunk of T
+// tokens at start_pos; 0 if that kind does not take the path.
+size_t tc_ws_need(const g4_ctx *c, bool global, int T, int start_pos, int ring_global, bool *bad) {
+    if (!attn_on_tensor_cores(c, global, T, start_pos)) return 0;
+    AttnArgs a{};
+    a.hd = global ? 512 : 256;
+    a.window = global ? 0 : G4_SLIDING_WINDOW;
+    a.mask = (global ? ring_global : 1024) - 1;
+    a.T = T;
+    a.start_pos = start_pos;
+    a.qkv = a.kcache = a.vcache = a.out = (float *)c;   // non-null placeholders: only the size is asked
+    const size_t b = g4_attn_tc_ws_bytes(a);
+    if (!b) *bad = true;
+    return b;
 }
 
 // Grow the tensor-core attention workspace for a chunk of T tokens at
 // start_pos (before any launch of the chunk: freeing waits for the stream).
+// The global and the sliding layers get separate regions, so that a layer that
+// reads another layer's cache can reuse that layer's K/V split of the chunk.
 // A growth costs a stream drain and a large allocation (~15 ms), so it
-// provisions ahead: for the last chunk of the whole context range when the
-// device has four times that much memory free (2.7 GB at 131072 positions),
-// else for twice the need.
+// provisions ahead: the global region for the last chunk of the whole context
+// range when the device has four times that much memory free (2.7 GB at
+// 131072 positions), else for twice the need; the sliding region for its
+// largest chunk (the window bounds it).
 int ensure_tc_ws(g4_ctx *c, int T, int start_pos, int ring_global) {
     bool bad = false;
-    const size_t need = tc_ws_need(c, T, start_pos, ring_global, &bad);
+    const size_t ng = tc_ws_need(c, true, T, start_pos, ring_global, &bad);
+    const size_t ns = tc_ws_need(c, false, T, start_pos, ring_global, &bad);
     if (bad) return fail(c, G4_ERR_INVALID, "tensor-core attention cannot run T %d at %d", T, start_pos);
-    if (need <= c->tc_ws_cap) return G4_OK;
+    if (ng <= c->tc_ws_gcap && ns <= c->tc_ws_scap) return G4_OK;
     CK(cudaStreamSynchronize(c->st));
     if (c->tc_ws) cudaFree(c->tc_ws);
     c->tc_ws = nullptr;
-    c->tc_ws_cap = 0;
-    bool bad_full = false;
-    const size_t full = tc_ws_need(c, G4_BATCH, ring_global - G4_BATCH, ring_global, &bad_full);
-    size_t free_b = 0, total_b = 0;
-    size_t want = 2 * need;
-    if (!bad_full && full >= need && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess && free_b / 4 > full) want = full;
-    if (cudaMalloc(&c->tc_ws, want) != cudaSuccess) {
-        cudaGetLastError();   // not sticky: retry at the exact need
-        want = need;
-        CK(cudaMalloc(&c->tc_ws, want));
+    size_t wg = c->tc_ws_gcap, ws = c->tc_ws_scap;
+    c->tc_ws_gcap = c->tc_ws_scap = 0;
+    if (ng > wg) {
+        bool bad_full = false;
+        const size_t full = tc_ws_need(c, true, G4_BATCH, ring_global - G4_BATCH, ring_global, &bad_full);
+        size_t free_b = 0, total_b = 0;
+        wg = 2 * ng;
+        if (!bad_full && full >= ng && cudaMemGetInfo(&free_b, &total_b) == cudaSuccess && free_b / 4 > full) wg = full;
     }
-    c->tc_ws_cap = want;
+    {   // the sliding region at its largest with the first growth of either
+        bool bad_s = false;
+        const size_t smax = tc_ws_need(c, false, G4_BATCH, 4 * G4_SLIDING_WINDOW, ring_global, &bad_s);
+        ws = !bad_s && smax > ws ? smax : ws;
+        ws = ns > ws ? ns : ws;
+    }
+    wg = (wg + 1023) / 1024 * 1024;
+    if (cudaMalloc(&c->tc_ws, wg + ws) != cudaSuccess) {
+        cudaGetLastError();   // not sticky: retry at the exact needs
+        wg = (ng + 1023) / 1024 * 1024;
+        ws = ns;
+        CK(cudaMalloc(&c->tc_ws, wg + ws));
+    }
+    c->tc_ws_gcap = wg;
+    c->tc_ws_scap = ws;
     return G4_OK;
 }
 
 cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp = nullptr) {
     Seq q{c, c->use_pdl};
     int cur = 0;
+    // per layer kind (sliding, global): the cache whose K/V split of this chunk
+    // the tensor-core workspace region holds
+    const float *tc_split_of[2] = {nullptr, nullptr};
     q.ck(g4_launch_rows_embed(c->tokens_d, T, c->embed, c->embed_ple, sqrtf((float)G4_HIDDEN), sqrtf((float)G4_PLE),
                               c->res[0], c->ple_emb, c->err, c->st, q.pdl));
     q.ck(g4_launch_rows_quant(c->res[0], G4_HIDDEN, T, G4_HIDDEN, c->xq, c->xs, c->st, q.pdl, c->xsT));
@@ -969,9 +985,13 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp
             // the tiled kernels also quantise their output rows for o_proj
             at.quant_out = 1;
             at.xsT = c->xsT;
-            if (attn_on_tensor_cores(c, Y.global, T, start_pos))
-                q.ck(g4_launch_attn_tc(at, c->tc_ws, c->tc_ws_cap, c->st));
-            else
+            if (attn_on_tensor_cores(c, Y.global, T, start_pos)) {
+                const int kind = Y.global ? 1 : 0;
+                at.reuse_kv = !Y.has_kv && tc_split_of[kind] == at.kcache;
+                uint8_t *ws = (uint8_t *)c->tc_ws + (kind ? 0 : c->tc_ws_gcap);
+                q.ck(g4_launch_attn_tc(at, ws, kind ? c->tc_ws_gcap : c->tc_ws_scap, c->st));
+                tc_split_of[kind] = at.kcache;
+            } else
                 q.ck(g4_launch_attn_prefill(at, c->st, q.pdl));
         } else
             q.ck(g4_launch_attn_strict(at, c->st, q.pdl));

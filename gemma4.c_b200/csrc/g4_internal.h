@@ -166,6 +166,9 @@ struct AttnArgs {
     // into xq [T][8*hd], xs [T][8*hd/64] and, when set, xsT (group-major)
     int quant_out;
     float *xsT;
+    // tensor-core prefill: the workspace already holds this chunk's K/V split
+    // of the same cache (a layer that reads another layer's cache)
+    int reuse_kv;
 };
 
 // ---- persistent decode step (g4_decode.cu) ---------------------------------

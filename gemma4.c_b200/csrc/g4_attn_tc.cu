@@ -525,10 +525,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const int kmin = tc_first_key(p.sp + t, p.window) - p.kbase, kmax = p.sp + t - p.kbase;
                 const int j0 = x.n * kTN + ch * 128;
                 float *blk = a.s + ((size_t)x.m * ntk + x.n) * kTN * kTM;   // [256 keys][128 rows]
-                const float qi = rg < p.R ? a.qinv[rg] : 0.0f;
+                const float qi = rg < p.R ? __ldg(a.qinv + rg) : 0.0f;
                 float mx = -INFINITY;
 #pragma unroll 1
                 for (int c = 0; c < 4; c++) {
+                    const int jb = j0 + c * 32;
+                    // the chunk's key scales, loaded before the accumulator read (one
+                    // round trip, not one per key between the stores below)
+                    float kv[32];
+#pragma unroll
+                    for (int j = 0; j < 32; j++) kv[j] = jb + j < p.nk ? __ldg(a.kinv + jb + j) : 0.0f;
                     int v[32];
                     load_acc(ta + (uint32_t)(c * 32), v);
                     if (c == 3) {   // the accumulator is read: free it for the unit after next
@@ -536,12 +542,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&tempty[buf]);
                     }
-                    const int jb = j0 + c * 32;
 #pragma unroll
                     for (int j = 0; j < 32; j++) {
                         const int key = jb + j;
                         // the row and key scales are powers of two: exact
-                        const float sv = __int_as_float(v[j]) * qi * (key < p.nk ? a.kinv[key] : 0.0f);
+                        const float sv = __int_as_float(v[j]) * qi * kv[j];
                         if (key >= kmin && key <= kmax) mx = fmaxf(mx, sv);
                         blk[(size_t)(ch * 128 + c * 32 + j) * kTM + row] = sv;   // the warp: 128 contiguous bytes
                     }

@@ -61,6 +61,9 @@
 // CTA waits (bounded) for its copies and MMAs in flight, and frees TMEM.
 #include <cuda.h>
 
+#include <vector>
+
+#include "../../include/g4cuda.h"
 #include "g4_attn_dev.cuh"
 #include "g4_tc.cuh"
 
@@ -810,6 +813,77 @@ cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t
 }
 
 }  // namespace
+
+// Host check of the tensor-core attention schedule for a chunk (no GPU work):
+// every S unit's key tile inside the workspace and every row tile's visible
+// keys inside its units; the P V stages of every (row tile, dimension tile)
+// pair covered exactly once by the CTA runs; partial slots distinct and below
+// npairs + g1; the combine's CTA range of each pair equal to the CTAs that ran
+// it. Returns 0, or the number of the first failed check.
+extern "C" int g4k_attn_tc_plan(int hd, int T, int start_pos, int sms, int *units_s_out, int *stages_o_out,
+                                int *ctas_o_out, unsigned long long *ws_bytes_out) {
+    if ((hd != 256 && hd != 512) || T < 1 || T > G4_BATCH || start_pos < 0 || sms < 1 ||
+        start_pos + T > G4_MAX_CONTEXT)
+        return G4_ERR_INVALID;
+    AttnArgs a{};
+    a.hd = hd;
+    a.window = hd == 256 ? G4_SLIDING_WINDOW : 0;
+    a.mask = (hd == 256 ? 1024 : G4_MAX_CONTEXT) - 1;
+    a.T = T;
+    a.start_pos = start_pos;
+    a.qkv = a.kcache = a.vcache = a.out = (float *)&a;   // placeholders: nothing is read
+    if (!tc_args_ok(a)) return 1;
+    int nus = 0, nslots = 0;
+    const TcPlan p = make_plan(a, sms, &nus, &nslots);
+    if (p.mt > kMaxRowTiles || p.npairs > 2 * kMaxRowTiles || p.kpad % kTN || p.nk < 1 || p.nk > p.kpad) return 2;
+    // S units and row tiles
+    int us = 0;
+    for (int m = 0; m < p.mt; m++) {
+        int kb, ke;
+        tile_keys(p, m, &kb, &ke);
+        if (kb < 0 || kb >= ke || ke > p.nk) return 3;
+        for (int t = m * kTokTile; t < imin(T, m * kTokTile + kTokTile); t++) {
+            const int kmin = tc_first_key(start_pos + t, a.window) - p.kbase, kmax = start_pos + t - p.kbase;
+            if (kmin < kb || kmax >= ke) return 4;
+        }
+        const int n0 = kb / kTN, n1 = (ke + kTN - 1) / kTN;
+        if (n1 * kTN > p.kpad || n1 - n0 != units_s(p, m)) return 5;
+        // the P V stages of the row tile and the S tiles that hold them
+        const int c0 = kb / kTK, c1 = (ke + kTK - 1) / kTK;
+        if (c1 * kTK > p.kpad || c0 * kTK < n0 * kTN || c1 * kTK > n1 * kTN || c1 - c0 != stages_o(p, m)) return 6;
+        us += n1 - n0;
+    }
+    if (us != nus) return 7;
+    // P V runs: CTA b takes stages [u1 b / g1, u1 (b + 1) / g1) of the pairs in order
+    std::vector<int> pre(p.npairs + 1, 0), cover(p.u1, 0), slot_used(p.npairs + p.g1, 0);
+    for (int i = 0; i < p.npairs; i++) pre[i + 1] = pre[i] + stages_o(p, i / p.nd);
+    if (pre[p.npairs] != p.u1 || p.g1 < 1 || p.g1 > sms || p.g1 > p.u1) return 8;
+    std::vector<int> first_cta(p.npairs, -1), last_cta(p.npairs, -1);
+    for (int b = 0; b < p.g1; b++) {
+        const long long s0 = (long long)p.u1 * b / p.g1, s1 = (long long)p.u1 * (b + 1) / p.g1;
+        if (s1 <= s0) return 9;
+        int i = 0;
+        while (pre[i + 1] <= s0) i++;
+        for (; i < p.npairs && pre[i] < s1; i++) {
+            const long long st = s0 > pre[i] ? s0 : pre[i], en = s1 < pre[i + 1] ? s1 : pre[i + 1];
+            if (en <= st) return 10;
+            for (long long s = st; s < en; s++) cover[s]++;
+            const int slot = i + b;
+            if (slot >= p.npairs + p.g1 || slot_used[slot]++) return 11;
+            if (first_cta[i] < 0) first_cta[i] = b;
+            last_cta[i] = b;
+        }
+    }
+    for (int s = 0; s < p.u1; s++)
+        if (cover[s] != 1) return 12;
+    for (int i = 0; i < p.npairs; i++)
+        if (cta_of_stage(p, pre[i]) != first_cta[i] || cta_of_stage(p, pre[i + 1] - 1) != last_cta[i]) return 13;
+    if (units_s_out) *units_s_out = nus;
+    if (stages_o_out) *stages_o_out = p.u1;
+    if (ctas_o_out) *ctas_o_out = p.g1;
+    if (ws_bytes_out) *ws_bytes_out = ws_layout(p, nslots).total;
+    return 0;
+}
 
 size_t g4_attn_tc_ws_bytes(const AttnArgs &a) {
     if (!tc_args_ok(a)) return 0;

@@ -388,6 +388,18 @@ def attention(qkv, hd, kring, vring, start_pos, cos_t, sin_t, mode=ATTN_PREFILL,
     return out, (ms.value if iters else None)
 
 
+def attn_tc_plan(hd, T, start_pos, sms=148):
+    """Host check of the tensor-core attention schedule (g4k_attn_tc_plan, no
+    GPU work): returns (rc, S units, P V stages, P V CTAs, workspace bytes),
+    rc 0 when every check holds."""
+    L = load()
+    f = L.g4k_attn_tc_plan
+    f.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p]
+    us, so, g1, wb = C.c_int(), C.c_int(), C.c_int(), C.c_ulonglong()
+    rc = f(hd, T, start_pos, sms, C.byref(us), C.byref(so), C.byref(g1), C.byref(wb))
+    return rc, us.value, so.value, g1.value, wb.value
+
+
 def sample(logits, temperature, state):
     """Device sample() (g4k_sample) of one logits row; returns (token, state after)."""
     L = load()

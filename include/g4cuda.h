@@ -277,6 +277,14 @@ int g4_bench_mma_i8(int iters, float *ms_per_launch, double *ops_per_launch);
 int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, const float *qkv,
                   const float *q_norm, const float *k_norm, const float *rope_cos, const float *rope_sin,
                   float *kring, float *vring, float *out, int8_t *xq, float *xs, int iters, float *ms_per_call);
+/* The tensor-core prefill attention's schedule for a chunk of T tokens at
+ * start_pos on a GPU with `sms` SMs, checked on the host (no GPU needed): S
+ * tiles inside the workspace, every P V stage covered exactly once by the
+ * per-CTA runs, partial slots distinct, the combine's CTA ranges exact.
+ * Returns 0 (or the number of the first failed check); outputs the S units,
+ * the P V stages, the P V CTAs and the workspace bytes. */
+int g4k_attn_tc_plan(int hd, int T, int start_pos, int sms, int *units_s, int *stages_o, int *ctas_o,
+                     unsigned long long *ws_bytes);
 /* sample (gemma4.c:536-561) of one logits row[n] on the device (top-64 and the
  * draw); *state: the xorshift state before the call, the state after it on return */
 int g4k_sample(const float *logits, int n, float temperature, unsigned long long *state, int *token);

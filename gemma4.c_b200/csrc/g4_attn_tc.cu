@@ -83,6 +83,10 @@ constexpr int kSmem = kOffBar + 128 + 1024;          // + barriers, + 1 KB for a
 constexpr int kTokTile = kTM / kHeads;                // 16 tokens per row tile
 constexpr int kMaxRowTiles = G4_BATCH / kTokTile;     // 32
 constexpr int kBufs = 1;                              // accumulator pairs in TMEM
+// O: up to this many K stages per pair on average, one CTA takes each whole
+// pair and finishes its rows (divide by l, quantise): no partial tiles and no
+// combine launch. Above it the stages are cut evenly over the SMs (split K).
+constexpr int kWholeMaxStages = 24;
 constexpr float kPScale = 32768.0f;                   // 2^15: p in (0, 1]
 // D fp32, A and B f16, both K-major, N = 256 (>> 3), M = 128 (>> 4)
 constexpr uint32_t kIdesc = (1u << 4) | ((uint32_t)(kTN >> 3) << 17) | ((uint32_t)(kTM >> 4) << 24);
@@ -100,7 +104,8 @@ struct TcPlan {
     int nd;           // 256-wide value-dimension tiles: hd / 256
     int npairs;       // O: (row tile, dimension tile) pairs, row-tile major
     int u1;           // O: K stages (32 keys) of all pairs
-    int g1;           // O: CTAs (each an even run of the stages)
+    int g1;           // O: CTAs (each an even run of the stages, or one whole pair)
+    int whole;        // O: one CTA per pair, which finishes its output rows itself
     float vscale;     // V scale 2^(15 - ceil(log2 sqrt(hd)))
 };
 
@@ -224,6 +229,17 @@ G4_DEV bool unit_at(const TcPlan &p, const int *pre, int idx, int i0, Unit &x) {
         x.slot = u;
         return true;
     }
+    if (p.whole) {   // CTA b: pair b, all its stages
+        if (idx > 0) return false;
+        int kb, ke;
+        x.m = blockIdx.x / p.nd;
+        x.n = blockIdx.x % p.nd;
+        tile_keys(p, x.m, &kb, &ke);
+        x.c0 = kb / kTK;
+        x.c1 = (ke + kTK - 1) / kTK;
+        x.slot = blockIdx.x;
+        return true;
+    }
     const int i = i0 + idx;
     const long long s0 = (long long)p.u1 * blockIdx.x / p.g1, s1 = (long long)p.u1 * (blockIdx.x + 1) / p.g1;
     if (i >= p.npairs || pre[i] >= s1) return false;
@@ -337,6 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t *tmem_slot = (uint32_t *)(xready + kTStages);
     __shared__ int pre[2 * kMaxRowTiles + 1];
     __shared__ int fail, issued, xfail, ipair0;
+    __shared__ float lsh[2][kTM];   // O, whole pairs: the row sums of p of the two key halves
     const TcPlan &p = a.p;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -508,7 +525,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (lane == 0) mbar_arrive(&xready[s]);
                 }
                 if (xfail) break;
-                if (x.n == 0) a.lpart[((size_t)x.slot * 2 + kh) * kTM + trow] = lsum;
+                if (p.whole) {
+                    lsh[kh][trow] = lsum;
+                    bar_sync(1, 32 * kEpiWarps);   // every thread of the epilogue is here (no exit between)
+                } else if (x.n == 0) {
+                    a.lpart[((size_t)x.slot * 2 + kh) * kTM + trow] = lsum;
+                }
             }
             const int buf = i % kBufs;
             const bool got = mbar_wait(&tfull[buf], (i / kBufs) & 1, a.err, G4D_TIMEOUT_FULL | (kCodeTfull << 8));
@@ -555,6 +577,54 @@ __global__ void __launch_bounds__(kThreads, 1)
                     }
                 }
                 if (rg < p.R) a.smax[(size_t)rg * (p.kpad / 128) + j0 / 128] = mx;
+            } else if (p.whole) {
+                // the finished rows: O = acc / l with the P and V scales removed (powers of
+                // two: exact), stored and quantised per 64-wide group (quantize,
+                // gemma4.c:265-279) for o_proj; the same arithmetic as k_tc_out's
+                const float inv = (1.0f / (lsh[0][row] + lsh[1][row])) * (1.0f / (kPScale * p.vscale));
+                const int t = rg >> 3;
+#pragma unroll 1
+                for (int c = 0; c < 4; c += 2) {
+                    float o[64];
+                    {
+                        int v[32];
+                        load_acc(ta + (uint32_t)(c * 32), v);
+#pragma unroll
+                        for (int j = 0; j < 32; j++) o[j] = __int_as_float(v[j]) * inv;
+                        load_acc(ta + (uint32_t)(c * 32 + 32), v);
+#pragma unroll
+                        for (int j = 0; j < 32; j++) o[32 + j] = __int_as_float(v[j]) * inv;
+                    }
+                    if (c == 2) {
+                        tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&tempty[buf]);
+                    }
+                    if (rg >= p.R) continue;
+                    const int d0 = x.n * kTN + ch * 128 + c * 32;   // 64-aligned
+                    float *orow = a.out + (size_t)rg * HD + d0;
+#pragma unroll
+                    for (int j = 0; j < 64; j += 4) *(float4 *)(orow + j) = make_float4(o[j], o[j + 1], o[j + 2], o[j + 3]);
+                    if (a.quant_out) {
+                        float mx = 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 64; j++) mx = fmaxf(mx, fabsf(o[j]));
+                        const float sc = quant_scale(mx), qv = quant_inv(sc);
+                        uint32_t w[16];
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            w[j] = (uint32_t)(uint8_t)quant_one(o[4 * j], qv) |
+                                   ((uint32_t)(uint8_t)quant_one(o[4 * j + 1], qv) << 8) |
+                                   ((uint32_t)(uint8_t)quant_one(o[4 * j + 2], qv) << 16) |
+                                   ((uint32_t)(uint8_t)quant_one(o[4 * j + 3], qv) << 24);
+                        uint4 *qrow = (uint4 *)(a.xq + (size_t)rg * HD + d0);
+#pragma unroll
+                        for (int j = 0; j < 4; j++) qrow[j] = make_uint4(w[4 * j], w[4 * j + 1], w[4 * j + 2], w[4 * j + 3]);
+                        const int gcol = ((rg & 7) * HD + d0) / 64;   // the group's column in the token's row
+                        a.xs[(size_t)t * (kHeads * HD / 64) + gcol] = sc;
+                        if (a.xsT) a.xsT[(size_t)gcol * G4_XST_STRIDE + t] = sc;
+                    }
+                }
             } else {
                 float *dst = a.opart + ((size_t)x.slot * kTM + row) * kTN + ch * 128;
 #pragma unroll 1
@@ -711,13 +781,14 @@ TcPlan make_plan(const AttnArgs &a, int sms, int *nunits_s, int *nunits_o) {
     }
     p.npairs = p.mt * p.nd;
     p.u1 = u1;
+    p.whole = u1 <= kWholeMaxStages * p.npairs ? 1 : 0;
     // one run per SM even when runs are short: a unit's epilogue and pipeline
     // refill (~6-8 us: the two accumulators fill TMEM, so nothing overlaps
     // them) cost more in sequence on fewer SMs (measured: 36 runs of 8 stages
     // 71 us, 148 runs of 2 stages 25 us, global chunk at position 0)
-    p.g1 = u1 < sms ? u1 : sms;
+    p.g1 = p.whole ? p.npairs : (u1 < sms ? u1 : sms);
     *nunits_s = us;
-    *nunits_o = p.npairs + p.g1;   // O partial slots (pair + CTA)
+    *nunits_o = p.whole ? 0 : p.npairs + p.g1;   // O partial slots (pair + CTA)
     return p;
 }
 
@@ -808,7 +879,7 @@ cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t
     k_tc_rowmax<<<(p.R + 7) / 8, 256, 0, st>>>(x);
     // the A maps are unused for O (its A tiles are made from S in shared memory)
     k_tc_gemm<1, HD><<<p.g1, kThreads, kSmem, st>>>(vh, vl, vh, vl, x);
-    k_tc_out<HD><<<p.T, 256, 0, st>>>(x);
+    if (!p.whole) k_tc_out<HD><<<p.T, 256, 0, st>>>(x);
     return cudaGetLastError();
 }
 
@@ -857,6 +928,14 @@ extern "C" int g4k_attn_tc_plan(int hd, int T, int start_pos, int sms, int *unit
     // P V runs: CTA b takes stages [u1 b / g1, u1 (b + 1) / g1) of the pairs in order
     std::vector<int> pre(p.npairs + 1, 0), cover(p.u1, 0), slot_used(p.npairs + p.g1, 0);
     for (int i = 0; i < p.npairs; i++) pre[i + 1] = pre[i] + stages_o(p, i / p.nd);
+    if (p.whole) {   // CTA b takes pair b whole and finishes its rows: no slots, no combine
+        if (pre[p.npairs] != p.u1 || p.g1 != p.npairs || nslots != 0 || p.u1 > kWholeMaxStages * p.npairs) return 14;
+        if (units_s_out) *units_s_out = nus;
+        if (stages_o_out) *stages_o_out = p.u1;
+        if (ctas_o_out) *ctas_o_out = p.g1;
+        if (ws_bytes_out) *ws_bytes_out = ws_layout(p, nslots).total;
+        return 0;
+    }
     if (pre[p.npairs] != p.u1 || p.g1 < 1 || p.g1 > sms || p.g1 > p.u1) return 8;
     std::vector<int> first_cta(p.npairs, -1), last_cta(p.npairs, -1);
     for (int b = 0; b < p.g1; b++) {

@@ -40,8 +40,9 @@
 //                   stage's S block (32 keys x 128 rows, one bulk copy) becomes
 //                   p = exp(s - m) on visible keys (0 elsewhere) as scaled fp16
 //                   hi/lo A tiles in shared memory, in place, by the epilogue
-//                   warps (exp by the hardware ex2 approximation, relative
-//                   error ~1e-6); partial O tiles and partial sums l = sum p
+//                   warps (2^(s log2 e - m log2 e) by the hardware ex2
+//                   approximation, relative error ~1e-6; fp16 pairs by packed
+//                   conversions); partial O tiles and partial sums l = sum p
 //                   stored per (pair, CTA) slot;
 //   5. k_tc_out     O = (sum of the slots, in CTA order) / l per token, stored and
 //                   quantised for o_proj (gemma4.c:459).
@@ -163,6 +164,23 @@ G4_DEV void split_f16(float x, __half &hi, __half &lo) {
     hi = __float2half_rn(x);
     lo = __float2half_rn(__fsub_rn(x, __half2float(hi)));
 }
+// Two scaled values as fp16 hi and lo pairs (packed conversions: one
+// instruction converts both); x - hi is exact.
+G4_DEV void split2_f16(float x0, float x1, uint32_t &hi, uint32_t &lo) {
+    const __half2 h = __float22half2_rn(make_float2(x0, x1));
+    const float2 hf = __half22float2(h);
+    const __half2 l = __float22half2_rn(make_float2(__fsub_rn(x0, hf.x), __fsub_rn(x1, hf.y)));
+    hi = *reinterpret_cast<const uint32_t *>(&h);
+    lo = *reinterpret_cast<const uint32_t *>(&l);
+}
+// 2^x by the hardware approximation (ex2.approx, relative error below 2^-22).
+G4_DEV float ex2_approx(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+constexpr float kLog2e = 1.4426950408889634f;
+
 // The power of two c with max_abs * c in [2^14, 2^15) (1 for a zero row).
 G4_DEV float row_scale(float max_abs) {
     if (!(max_abs > 0.0f)) return 1.0f;
@@ -262,13 +280,11 @@ G4_DEV uint32_t pack2(__half a, __half b) {
     return *reinterpret_cast<const uint32_t *>(&h);
 }
 G4_DEV void store_split4(float4 x, float c, __half *dh, __half *dl) {
-    __half h[4], l[4];
-    split_f16(x.x * c, h[0], l[0]);
-    split_f16(x.y * c, h[1], l[1]);
-    split_f16(x.z * c, h[2], l[2]);
-    split_f16(x.w * c, h[3], l[3]);
-    *(uint2 *)dh = make_uint2(pack2(h[0], h[1]), pack2(h[2], h[3]));
-    *(uint2 *)dl = make_uint2(pack2(l[0], l[1]), pack2(l[2], l[3]));
+    uint32_t h0, l0, h1, l1;
+    split2_f16(x.x * c, x.y * c, h0, l0);
+    split2_f16(x.z * c, x.w * c, h1, l1);
+    *(uint2 *)dh = make_uint2(h0, h1);
+    *(uint2 *)dl = make_uint2(l0, l1);
 }
 
 template <int HD>
@@ -480,6 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const bool live = rg < p.R;
                 const int kmin = tc_first_key(p.sp + t, p.window) - p.kbase, kmax = p.sp + t - p.kbase;
                 const float mr = live ? a.rmax[rg] : 0.0f;
+                const float mrl = mr * kLog2e;   // p = 2^(s log2 e - m log2 e)
                 float lsum = 0.0f;
                 for (int c = x.c0; c < x.c1; c++, k++) {
                     const int s = k % kTStages;
@@ -497,19 +514,27 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // (a wait that gave up still arrives here: the decision to leave is uniform)
                     bar_sync(1, 32 * kEpiWarps);
                     if (xfail) break;
-                    const int kb0 = c * kTK + kh * (kTK / 2);
+                    const int kb0 = c * kTK + kh * (kTK / 2), kb1 = kb0 + kTK / 2 - 1;
+                    // this thread's keys all visible (the common case), none, or some
+                    const bool all_vis = live && kb0 >= kmin && kb1 <= kmax;
+                    const bool none_vis = !live || kb0 > kmax || kb1 < kmin;
                     uint32_t hw[kTK / 4], lw[kTK / 4];
 #pragma unroll
                     for (int j = 0; j < kTK / 2; j += 2) {
-                        const float p0 = live && kb0 + j >= kmin && kb0 + j <= kmax ? __expf(v[j] - mr) : 0.0f;
-                        const float p1 = live && kb0 + j + 1 >= kmin && kb0 + j + 1 <= kmax ? __expf(v[j + 1] - mr) : 0.0f;
+                        float p0, p1;
+                        if (all_vis) {
+                            p0 = ex2_approx(__fmaf_rn(v[j], kLog2e, -mrl));
+                            p1 = ex2_approx(__fmaf_rn(v[j + 1], kLog2e, -mrl));
+                        } else if (none_vis) {
+                            p0 = p1 = 0.0f;
+                        } else {
+                            p0 = kb0 + j >= kmin && kb0 + j <= kmax ? ex2_approx(__fmaf_rn(v[j], kLog2e, -mrl)) : 0.0f;
+                            p1 = kb0 + j + 1 >= kmin && kb0 + j + 1 <= kmax
+                                     ? ex2_approx(__fmaf_rn(v[j + 1], kLog2e, -mrl)) : 0.0f;
+                        }
                         lsum += p0;
                         lsum += p1;
-                        __half h0, l0, h1, l1;
-                        split_f16(p0 * kPScale, h0, l0);
-                        split_f16(p1 * kPScale, h1, l1);
-                        hw[j / 2] = pack2(h0, h1);
-                        lw[j / 2] = pack2(l0, l1);
+                        split2_f16(p0 * kPScale, p1 * kPScale, hw[j / 2], lw[j / 2]);
                     }
                     // K-major fp16 rows of 64 bytes with the 64-byte swizzle: logical 16-byte
                     // chunk j of row r sits at chunk j ^ ((r / 2) % 4)

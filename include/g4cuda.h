@@ -149,7 +149,11 @@ const char *g4_strerror(int code);
  * one, CUDA cores below; 1 CUDA cores everywhere; 2 tensor cores everywhere.
  * The paths differ in floating-point order only (outputs agree to fp32
  * rounding: a relative error near 2^-21 per product). Not used in strict
- * mode. */
+ * mode. The tensor-core path's device workspace is allocated at the first
+ * chunk that takes it: for the whole context range (about 2.7 GB for global
+ * layers at 131072 positions, plus ~40 MB for sliding ones) when the device
+ * has four times that free, else twice the chunk's need, grown on demand;
+ * g4_close frees it. */
 #define G4_OPT_ATTN_PATH 8
 int g4_set_option(g4_ctx *ctx, int option, int value);
 

@@ -57,7 +57,8 @@
 //               (M 128, N 256, K 16) per stage;
 //   warps 2-9   epilogue: thread = row (TMEM lane), two warps per lane quadrant
 //               with 128 columns each; for O also the per-stage transform of S
-//               into P (thread = row x 32 keys).
+//               into P, by two groups of four warps on alternate stages
+//               (thread = row x the stage's 32 keys).
 // Waits are bounded (mbar_wait); on a timeout every role leaves its loop, the
 // CTA waits (bounded) for its copies and MMAs in flight, and frees TMEM.
 #include <cuda.h>
@@ -80,7 +81,11 @@ constexpr int kStageBytes = 2 * kTileA + 2 * kTileB;   // hi and lo of both oper
 constexpr int kEpiWarps = 8;
 constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kOffBar = kTStages * kStageBytes;
-constexpr int kSmem = kOffBar + 128 + 1024;          // + barriers, + 1 KB for alignment
+// barriers: full, empty, xready [kTStages] each, tfull, tempty [2] each, drain,
+// ldone, then the TMEM address word
+constexpr int kBarBytes = (3 * kTStages + 2 * 2 + 2) * 8 + 4;
+constexpr int kSmem = kOffBar + 256 + 1024;          // + barriers, + 1 KB for alignment
+static_assert(kBarBytes <= 256, "barrier region of the attention GEMM CTA");
 constexpr int kTokTile = kTM / kHeads;                // 16 tokens per row tile
 constexpr int kMaxRowTiles = G4_BATCH / kTokTile;     // 32
 constexpr int kBufs = 1;                              // accumulator pairs in TMEM
@@ -366,10 +371,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint64_t *tempty = tfull + 2;
     uint64_t *drain = tempty + 2;
     uint64_t *xready = drain + 1;   // O: the stage's P tiles are written
-    uint32_t *tmem_slot = (uint32_t *)(xready + kTStages);
+    uint64_t *ldone = xready + kTStages;   // O, whole pairs: both groups' row sums are written
+    uint32_t *tmem_slot = (uint32_t *)(ldone + 1);
     __shared__ int pre[2 * kMaxRowTiles + 1];
-    __shared__ int fail, issued, xfail, ipair0;
-    __shared__ float lsh[2][kTM];   // O, whole pairs: the row sums of p of the two key halves
+    __shared__ int fail, issued, ipair0;
+    __shared__ int xfail_g[2];      // O: a transform group's wait gave up (written by that group only)
+    __shared__ float lsh[2][kTM];   // O, whole pairs: the row sums of p of the two transform groups
     const TcPlan &p = a.p;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -391,11 +398,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_init(&tempty[b], kEpiWarps);
         }
         mbar_init(drain, 1);
-        for (int s = 0; s < kTStages; s++) mbar_init(&xready[s], kEpiWarps);
+        for (int s = 0; s < kTStages; s++) mbar_init(&xready[s], kEpiWarps / 2);
+        mbar_init(ldone, kEpiWarps);
         mbar_fence_init();
         fail = 0;
         issued = 0;
-        xfail = 0;
+        xfail_g[0] = xfail_g[1] = 0;
     }
     if (warp == 1) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
@@ -490,8 +498,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         int i = 0, k = 0;
         for (; unit_at<MODE, HD>(p, pre, i, i0, x); i++) {
             if (MODE == 1) {
-                // thread = row trow x keys [16 kh, 16 kh + 16) of each stage
-                const int te = tid - 64, trow = te & 127, kh = te >> 7;
+                // two transform groups of four warps take alternate stages (stage k:
+                // group k % 2); thread = row trow x the stage's 32 keys. Each group has
+                // its own named barrier and failure flag, so its exits stay uniform.
+                const int g = e >> 2, trow = (e & 3) * 32 + lane;
                 const int rg = x.m * kTM + trow, t = rg >> 3;
                 const bool live = rg < p.R;
                 const int kmin = tc_first_key(p.sp + t, p.window) - p.kbase, kmax = p.sp + t - p.kbase;
@@ -499,28 +509,29 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const float mrl = mr * kLog2e;   // p = 2^(s log2 e - m log2 e)
                 float lsum = 0.0f;
                 for (int c = x.c0; c < x.c1; c++, k++) {
+                    if ((k & 1) != g) continue;   // the other group's stage
                     const int s = k % kTStages;
                     const bool got = mbar_wait(&full[s], (k / kTStages) & 1, a.err, G4D_TIMEOUT_FULL | (kCodeFull << 8));
-                    float v[kTK / 2];
+                    float v[kTK];
                     if (got) {
                         const float *raw = (const float *)(smem + s * kStageBytes);
 #pragma unroll
-                        for (int j = 0; j < kTK / 2; j++) v[j] = raw[(kh * (kTK / 2) + j) * kTM + trow];
+                        for (int j = 0; j < kTK; j++) v[j] = raw[j * kTM + trow];
                     } else {
-                        xfail = 1;
+                        xfail_g[g] = 1;
                         fail = 1;
                     }
-                    // every thread of the transform has read the block before any writes over it
+                    // every thread of the group has read the block before any writes over it
                     // (a wait that gave up still arrives here: the decision to leave is uniform)
-                    bar_sync(1, 32 * kEpiWarps);
-                    if (xfail) break;
-                    const int kb0 = c * kTK + kh * (kTK / 2), kb1 = kb0 + kTK / 2 - 1;
-                    // this thread's keys all visible (the common case), none, or some
+                    bar_sync(1 + g, 32 * kEpiWarps / 2);
+                    if (xfail_g[g]) break;
+                    const int kb0 = c * kTK, kb1 = kb0 + kTK - 1;
+                    // this row's keys all visible (the common case), none, or some
                     const bool all_vis = live && kb0 >= kmin && kb1 <= kmax;
                     const bool none_vis = !live || kb0 > kmax || kb1 < kmin;
-                    uint32_t hw[kTK / 4], lw[kTK / 4];
+                    uint32_t hw[kTK / 2], lw[kTK / 2];
 #pragma unroll
-                    for (int j = 0; j < kTK / 2; j += 2) {
+                    for (int j = 0; j < kTK; j += 2) {
                         float p0, p1;
                         if (all_vis) {
                             p0 = ex2_approx(__fmaf_rn(v[j], kLog2e, -mrl));
@@ -540,8 +551,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                     // chunk j of row r sits at chunk j ^ ((r / 2) % 4)
                     uint8_t *th = smem + s * kStageBytes, *tl = th + kTileA;
 #pragma unroll
-                    for (int c4 = 0; c4 < kTK / 16; c4++) {
-                        const int off = trow * (kTK * 2) + ((((kTK / 16) * kh + c4) ^ ((trow >> 1) & 3)) << 4);
+                    for (int c4 = 0; c4 < kTK / 8; c4++) {
+                        const int off = trow * (kTK * 2) + ((c4 ^ ((trow >> 1) & 3)) << 4);
                         *(uint4 *)(th + off) = make_uint4(hw[4 * c4], hw[4 * c4 + 1], hw[4 * c4 + 2], hw[4 * c4 + 3]);
                         *(uint4 *)(tl + off) = make_uint4(lw[4 * c4], lw[4 * c4 + 1], lw[4 * c4 + 2], lw[4 * c4 + 3]);
                     }
@@ -549,21 +560,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&xready[s]);
                 }
-                if (xfail) break;
-                if (p.whole) {
-                    lsh[kh][trow] = lsum;
-                    bar_sync(1, 32 * kEpiWarps);   // every thread of the epilogue is here (no exit between)
+                if (xfail_g[g]) break;
+                if (p.whole) {   // the row sums of both groups meet in shared memory
+                    lsh[g][trow] = lsum;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(ldone);
                 } else if (x.n == 0) {
-                    a.lpart[((size_t)x.slot * 2 + kh) * kTM + trow] = lsum;
+                    a.lpart[((size_t)x.slot * 2 + g) * kTM + trow] = lsum;
                 }
             }
             const int buf = i % kBufs;
             const bool got = mbar_wait(&tfull[buf], (i / kBufs) & 1, a.err, G4D_TIMEOUT_FULL | (kCodeTfull << 8));
             if (!__all_sync(0xffffffffu, got)) {
-                if (lane == 0) {
-                    fail = 1;
-                    xfail = 1;   // the others leave at their next transform barrier
-                }
+                // (for O the warp goes on to the next unit with its group: its transform
+                // waits then give up on their own, keeping the group's barriers uniform)
+                if (lane == 0) fail = 1;
                 if (MODE == 0) break;
                 continue;
             }
@@ -606,6 +617,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                 // the finished rows: O = acc / l with the P and V scales removed (powers of
                 // two: exact), stored and quantised per 64-wide group (quantize,
                 // gemma4.c:265-279) for o_proj; the same arithmetic as k_tc_out's
+                if (!__all_sync(0xffffffffu, mbar_wait(ldone, 0, a.err, G4D_TIMEOUT_FULL | (kCodeTfull << 8)))) {
+                    if (lane == 0) fail = 1;
+                    continue;
+                }
                 const float inv = (1.0f / (lsh[0][row] + lsh[1][row])) * (1.0f / (kPScale * p.vscale));
                 const int t = rg >> 3;
 #pragma unroll 1

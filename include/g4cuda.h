@@ -151,7 +151,7 @@ const char *g4_strerror(int code);
  * rounding: a relative error near 2^-21 per product). Not used in strict
  * mode. The tensor-core path's device workspace is allocated at the first
  * chunk that takes it: for the whole context range (about 2.7 GB for global
- * layers at 131072 positions, plus ~40 MB for sliding ones) when the device
+ * layers at 131072 positions, plus ~50 MB for sliding ones) when the device
  * has four times that free, else twice the chunk's need, grown on demand;
  * g4_close frees it. */
 #define G4_OPT_ATTN_PATH 8

@@ -431,7 +431,7 @@ def attention_bench(g4, hbm_peak, prefill_iters=10, decode_iters=50):
             _, ms_t = g4.attention(qkv, hd, k.copy(), v.copy(), start, cos_t, sin_t, mode=g4.ATTN_PREFILL_TC,
                                    iters=prefill_iters)
             # the path the engine takes for this chunk (G4_OPT_ATTN_PATH 0: by the keys its tokens see)
-            on_tc = float(keys.sum()) >= (64 * 1024 if hd == 512 else 160 * 1024)
+            on_tc = float(keys.sum()) >= (64 * 1024 if hd == 512 else 128 * 1024)
             ms_p = ms_t if on_tc else ms_c
             _, ms_d = g4.attention(qkv[:1], hd, k, v, ctx - 1, cos_t, sin_t, mode=g4.ATTN_DECODE, splits=148,
                                    iters=decode_iters)
@@ -449,7 +449,7 @@ def attention_bench(g4, hbm_peak, prefill_iters=10, decode_iters=50):
         row["model_decode_us"] = sum(row[k]["decode_us"] * row[k]["layers"] for k in ("sliding", "global"))
         res[f"ctx{ctx}"] = row
     res["note"] = ("prefill: the engine's path for a 512-token chunk (tensor cores: tcgen05 GEMMs on fp16 hi/lo "
-                   "operands, k_tc_*, where the chunk's key work is >= 64k global / 160k sliding; else CUDA cores: "
+                   "operands, k_tc_*, where the chunk's key work is >= 64k global / 128k sliding; else CUDA cores: "
                    "k_attn_prefill + merge), both timed; "
                    "TFLOP/s count the attention's own FLOPs (q.k and p.v), the CUDA-core frac is of the nominal "
                    f"FP32 FMA peak {FP32_TFLOPS:.1f} TFLOP/s; decode: split-KV kernel + combine standalone (inside k_decode "

@@ -851,11 +851,13 @@ struct BatchPlan {
 // Prefill attention on the tensor cores for this layer kind and chunk
 // (G4_OPT_ATTN_PATH); the CUDA-core kernel otherwise. Auto: by the chunk's
 // work W = sum over its tokens of the keys each sees. The tensor path has a
-// fixed cost of ~45 us (five launches, TMEM and pipeline set-up) and then
-// ~0.06 ns per unit of W, the CUDA-core kernel ~0.8 ns (global, 512-wide
-// heads) or ~0.35 ns (sliding) per unit (B200): they cross near W = 56k and
-// 157k.
-constexpr long long kTcMinWorkGlobal = 64 * 1024, kTcMinWorkSliding = 160 * 1024;
+// fixed cost of ~33 us (four or five launches, TMEM and pipeline set-up) and
+// then ~0.06 ns per unit of W, the CUDA-core kernel ~0.8 ns (global,
+// 512-wide heads) or ~0.38 ns (sliding) per unit (B200). Measured: a
+// 512-token chunk at position 0 (W = 131k) takes 52 vs 107 us (global) and
+// 49 vs 52 us (sliding) on the tensor cores; 128 tokens at position 100
+// (W = 21k) 43 vs 39 us (global).
+constexpr long long kTcMinWorkGlobal = 64 * 1024, kTcMinWorkSliding = 128 * 1024;
 bool attn_on_tensor_cores(const g4_ctx *c, bool global, int T, int start_pos) {
     if (c->strict || c->attn_path == 1) return false;
     if (c->attn_path == 2) return true;

@@ -145,7 +145,7 @@ const char *g4_strerror(int code);
 /* Prefill attention of a chunk (g4_forward / one-sequence g4_forward_batch):
  * 0 (default) auto = tensor cores (tcgen05 GEMMs for Q K^T and P V on fp16
  * hi/lo operand pairs, fp32 accumulation) where the chunk's work (the keys its
- * tokens see, summed) is at least 64k on a global layer or 160k on a sliding
+ * tokens see, summed) is at least 64k on a global layer or 128k on a sliding
  * one, CUDA cores below; 1 CUDA cores everywhere; 2 tensor cores everywhere.
  * The paths differ in floating-point order only (outputs agree to fp32
  * rounding: a relative error near 2^-21 per product). Not used in strict

@@ -22,7 +22,7 @@
 // so |v| <= sqrt(HD)).
 //
 // The chunk's R = 8T query rows (row r = token r / 8, head r % 8) form 128-row
-// tiles of 16 tokens. Five launches:
+// tiles of 16 tokens. Five launches (four for short chunks, see 4):
 //   1. k_tc_split   Q rows, the chunk's keys [kbase, npos) and their values as
 //                   scaled fp16 hi/lo pairs (with the Q and K row scales); V
 //                   transposed to [HD][keys] so that both GEMMs read K-major
@@ -43,9 +43,14 @@
 //                   warps (2^(s log2 e - m log2 e) by the hardware ex2
 //                   approximation, relative error ~1e-6; fp16 pairs by packed
 //                   conversions); partial O tiles and partial sums l = sum p
-//                   stored per (pair, CTA) slot;
+//                   stored per (pair, CTA) slot. Short chunks (at most 24
+//                   stages per pair on average) run one CTA per pair instead,
+//                   which divides by l and quantises its rows itself (no
+//                   slots, no step 5);
 //   5. k_tc_out     O = (sum of the slots, in CTA order) / l per token, stored and
 //                   quantised for o_proj (gemma4.c:459).
+// A layer that reads another layer's KV cache can reuse that layer's K/V
+// split of the chunk (AttnArgs::reuse_kv): step 1 then splits only Q.
 // The schedule depends only on (T, start position, SM count): deterministic.
 //
 // GEMM roles (10 warps, one CTA per SM, persistent over units):

@@ -285,10 +285,6 @@ G4_DEV bool unit_at(const TcPlan &p, const int *pre, int idx, int i0, Unit &x) {
 // ---------------------------------------------------------------------------
 // 1. hi/lo operands. grid (blocks, 3): y = 0 Q rows, 1 key rows (one warp per
 // row, scaled by the row's own power of two), 2 V^T tiles (fixed scale).
-G4_DEV uint32_t pack2(__half a, __half b) {
-    const __half2 h = __halves2half2(a, b);
-    return *reinterpret_cast<const uint32_t *>(&h);
-}
 G4_DEV void store_split4(float4 x, float c, __half *dh, __half *dl) {
     uint32_t h0, l0, h1, l1;
     split2_f16(x.x * c, x.y * c, h0, l0);
@@ -301,6 +297,8 @@ template <int HD>
 __global__ void __launch_bounds__(256) k_tc_split(const TcAttnArgs a) {
     __shared__ float tile[32][33];
     const TcPlan &p = a.p;
+    griddep_launch();
+    griddep_wait();   // q/k/v rows come from the previous kernel
     const int job = blockIdx.y;
     if (job < 2) {
         constexpr int V4 = HD / 128;   // float4s per lane
@@ -420,6 +418,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Programmatic dependent launch: the next kernel may be scheduled once
+    // every CTA holds its TMEM columns (a dependent allocation then waits for
+    // this grid, never the reverse); the workspace is read and written only
+    // after the previous kernel has completed (the set-up above reads kernel
+    // parameters only).
+    griddep_launch();
+    griddep_wait();
     const int ntk = p.kpad / kTN;   // key tiles per row tile in the S layout
     const int i0 = MODE == 1 ? ipair0 : 0;
     Unit x;
@@ -718,6 +723,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 __global__ void __launch_bounds__(256) k_tc_rowmax(const TcAttnArgs a) {
     const TcPlan &p = a.p;
     const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+    griddep_launch();
+    griddep_wait();
     if (r >= p.R) return;
     int kb, ke;
     tile_keys(p, r / kTM, &kb, &ke);
@@ -738,6 +745,8 @@ __global__ void __launch_bounds__(256) k_tc_out(const TcAttnArgs a) {
     const TcPlan &p = a.p;
     const int t = blockIdx.x, tid = threadIdx.x;
     const int m = t / kTokTile;
+    griddep_launch();
+    griddep_wait();
     if (tid < 32) {
         pair_prefix_o(p, pre);
         __syncwarp();
@@ -875,7 +884,7 @@ bool tc_args_ok(const AttnArgs &a) {
 }
 
 template <int HD>
-cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st) {
+cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st, bool pdl) {
     const int sms = g4_device_sms();
     int nus = 0, nuo = 0;
     const TcPlan p = make_plan(a, sms, &nus, &nuo);
@@ -919,13 +928,16 @@ cudaError_t launch_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t
     if (e == cudaSuccess) e = g4_smem_optin((const void *)k_tc_gemm<1, HD>, kSmem);
     if (e) return e;
     // job 0 splits Q; jobs 1 and 2 K and V, unless the workspace holds them already
-    k_tc_split<HD><<<dim3(4 * sms, a.reuse_kv ? 1 : 3), 256, 0, st>>>(x);
-    k_tc_gemm<0, HD><<<nus < sms ? nus : sms, kThreads, kSmem, st>>>(qh, ql, kh, kl, x);
-    k_tc_rowmax<<<(p.R + 7) / 8, 256, 0, st>>>(x);
+    e = g4_launch(k_tc_split<HD>, dim3(4 * sms, a.reuse_kv ? 1 : 3), dim3(256), 0, st, pdl, x);
+    if (e == cudaSuccess)
+        e = g4_launch(k_tc_gemm<0, HD>, dim3(nus < sms ? nus : sms), dim3(kThreads), (size_t)kSmem, st, pdl, qh, ql,
+                      kh, kl, x);
+    if (e == cudaSuccess) e = g4_launch(k_tc_rowmax, dim3((p.R + 7) / 8), dim3(256), 0, st, pdl, x);
     // the A maps are unused for O (its A tiles are made from S in shared memory)
-    k_tc_gemm<1, HD><<<p.g1, kThreads, kSmem, st>>>(vh, vl, vh, vl, x);
-    if (!p.whole) k_tc_out<HD><<<p.T, 256, 0, st>>>(x);
-    return cudaGetLastError();
+    if (e == cudaSuccess)
+        e = g4_launch(k_tc_gemm<1, HD>, dim3(p.g1), dim3(kThreads), (size_t)kSmem, st, pdl, vh, vl, vh, vl, x);
+    if (e == cudaSuccess && !p.whole) e = g4_launch(k_tc_out<HD>, dim3(p.T), dim3(256), 0, st, pdl, x);
+    return e;
 }
 
 }  // namespace
@@ -1016,8 +1028,8 @@ size_t g4_attn_tc_ws_bytes(const AttnArgs &a) {
     return ws_layout(p, nuo).total;
 }
 
-cudaError_t g4_launch_attn_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st) {
+cudaError_t g4_launch_attn_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st, bool pdl) {
     if (!tc_args_ok(a) || !g4_tmap_encoder()) return cudaErrorInvalidValue;
-    if (a.hd == 256) return launch_tc<256>(a, ws, ws_bytes, st);
-    return launch_tc<512>(a, ws, ws_bytes, st);
+    if (a.hd == 256) return launch_tc<256>(a, ws, ws_bytes, st, pdl);
+    return launch_tc<512>(a, ws, ws_bytes, st, pdl);
 }

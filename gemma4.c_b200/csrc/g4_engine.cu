@@ -991,7 +991,7 @@ cudaError_t enqueue_prefill(g4_ctx *c, int T, int start_pos, const BatchPlan *bp
                 const int kind = Y.global ? 1 : 0;
                 at.reuse_kv = !Y.has_kv && tc_split_of[kind] == at.kcache;
                 uint8_t *ws = (uint8_t *)c->tc_ws + (kind ? 0 : c->tc_ws_gcap);
-                q.ck(g4_launch_attn_tc(at, ws, kind ? c->tc_ws_gcap : c->tc_ws_scap, c->st));
+                q.ck(g4_launch_attn_tc(at, ws, kind ? c->tc_ws_gcap : c->tc_ws_scap, c->st, q.pdl));
                 tc_split_of[kind] = at.kcache;
             } else
                 q.ck(g4_launch_attn_prefill(at, c->st, q.pdl));

@@ -162,6 +162,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
+    // Programmatic dependent launch. The next kernel may be scheduled from
+    // here: every CTA of this grid holds its TMEM columns already, so a
+    // dependent kernel's allocation can only wait for this one, never the
+    // reverse. Nothing the previous kernel writes or reads is touched before
+    // it has completed (the set-up above reads only the GELU table, a model
+    // constant).
+    griddep_launch();
+    griddep_wait();
 
     if (warp == 0) {
         // ---------------- TMA producer ----------------
@@ -513,14 +521,15 @@ int pick_bn(int N, int mt, int sms) {
 }
 
 template <int BN>
-cudaError_t launch_bn(const CUtensorMap &ma, const CUtensorMap &mb, const TcArgs &p, int sms, cudaStream_t st) {
+cudaError_t launch_bn(const CUtensorMap &ma, const CUtensorMap &mb, const TcArgs &p, int sms, cudaStream_t st,
+                      bool pdl) {
     {
         cudaError_t e = g4_smem_optin((const void *)k_gemm_tc<BN>, TcCfg<BN>::kSmemBytes);
         if (e != cudaSuccess) return e;
     }
     const int tiles = p.swap ? p.N / kBM : (p.N / BN) * ((p.T + kBM - 1) / kBM);
-    k_gemm_tc<BN><<<tiles < sms ? tiles : sms, kThreads, TcCfg<BN>::kSmemBytes, st>>>(ma, mb, p);
-    return cudaGetLastError();
+    return g4_launch(k_gemm_tc<BN>, dim3(tiles < sms ? tiles : sms), dim3(kThreads), (size_t)TcCfg<BN>::kSmemBytes,
+                     st, pdl, ma, mb, p);
 }
 
 }  // namespace
@@ -550,7 +559,6 @@ bool g4_gemm_tc_swapped(const GemmArgs &a) {
 }
 
 cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
-    (void)pdl;
     if (!g4_gemm_tc_supported(a)) return cudaErrorNotSupported;
     const int sms = g4_device_sms();
     const bool swap = g4_gemm_tc_swapped(a);
@@ -581,7 +589,7 @@ cudaError_t g4_launch_gemm_tc(const GemmArgs &a, cudaStream_t st, bool pdl) {
         p.qs = a.qs;
         p.qsT = a.qsT;
     }
-    if (bn == 128) return launch_bn<128>(ma, mb, p, sms, st);
-    if (bn == 64) return launch_bn<64>(ma, mb, p, sms, st);
-    return launch_bn<32>(ma, mb, p, sms, st);
+    if (bn == 128) return launch_bn<128>(ma, mb, p, sms, st, pdl);
+    if (bn == 64) return launch_bn<64>(ma, mb, p, sms, st, pdl);
+    return launch_bn<32>(ma, mb, p, sms, st, pdl);
 }

@@ -245,11 +245,11 @@ int g4_device_sms();
 cudaError_t g4_launch_qkv_post(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_prefill(const AttnArgs &a, cudaStream_t st, bool pdl);
 cudaError_t g4_launch_attn_strict(const AttnArgs &a, cudaStream_t st, bool pdl);
-// Prefill attention on the tensor cores (g4_attn_tc.cu, 3xTF32 tcgen05 GEMMs):
+// Prefill attention on the tensor cores (g4_attn_tc.cu, tcgen05 GEMMs on fp16 hi/lo operand pairs):
 // workspace bytes for the chunk `a` describes (0: the path cannot run it) and
 // the launches into that workspace (256-byte aligned); q/k/v already post-processed.
 size_t g4_attn_tc_ws_bytes(const AttnArgs &a);
-cudaError_t g4_launch_attn_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st);
+cudaError_t g4_launch_attn_tc(const AttnArgs &a, void *ws, size_t ws_bytes, cudaStream_t st, bool pdl);
 
 cudaError_t g4_launch_repack(const int8_t *packed_w, const uint16_t *packed_s, int N, int K, int8_t *w, uint16_t *s,
                              int row_offset, int row_stride_mul, cudaStream_t st);

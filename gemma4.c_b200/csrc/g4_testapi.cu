@@ -432,7 +432,7 @@ int g4k_attention(int hd, int ring, int T, int start_pos, int mode, int splits, 
         switch (mode) {
         case 0: return g4_launch_attn_prefill(a, 0, false);
         case 1: return g4_launch_attn_strict(a, 0, false);
-        case 4: return g4_launch_attn_tc(a, dws.p, ws_bytes, 0);
+        case 4: return g4_launch_attn_tc(a, dws.p, ws_bytes, 0, false);
         case 2: {
             cudaError_t e = g4_launch_attn_decode(a, splits, 0, false);
             return e ? e : g4_launch_attn_combine(a, splits, 0, false);

@@ -110,6 +110,27 @@ def test_prefill_gemm_paths_bitidentical(g4, image):
     assert np.array_equal(lgs[0].view(np.uint32), lgs[1].view(np.uint32))
 
 
+def test_prefill_pdl_on_off_bitidentical(g4, image):
+    """Programmatic dependent launch only lets a kernel start before the
+    previous one ends: each waits for its predecessor before it reads or
+    writes anything the predecessor touches, so three 512-token chunks
+    (tcgen05 GEMMs; tensor-core attention in its whole-pair and split
+    schedules, with and without the K/V split reused) give the same bits with
+    it on and off."""
+    rng = np.random.default_rng(12)
+    toks = rng.integers(0, 262144, size=1536).astype(np.int32)
+    res, lgs = [], []
+    for pdl in (1, 0):
+        with g4.Model(image) as m:
+            m.set_option(g4.OPT_PDL, pdl)
+            for c in range(0, 1536, 512):
+                m.forward(toks[c:c + 512], c)
+            res.append(m.residual(512))
+            lgs.append(m.logits(511)[0])
+    assert np.array_equal(res[0].view(np.uint32), res[1].view(np.uint32))
+    assert np.array_equal(lgs[0].view(np.uint32), lgs[1].view(np.uint32))
+
+
 @pytest.mark.parametrize("T", [20, 64])
 def test_small_batch_gemm_paths_bitidentical(g4, image, T):
     """A chunk of at most 64 rows takes the small-batch mma GEMM by default;

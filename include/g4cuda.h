@@ -273,7 +273,7 @@ int g4_bench_mma_i8(int iters, float *ms_per_launch, double *ops_per_launch);
  * (the reference's floating-point order); 2: single-token decode (split-KV
  * over `splits` CTAs + combine, T == 1); 3: batched-row decode path (one row
  * per token at start_pos + t, `splits` key splits); 4: prefill on the tensor
- * cores (3xTF32 tcgen05 GEMMs for Q K^T and P V). iters > 0: the attention
+ * cores (tcgen05 GEMMs on fp16 hi/lo operand pairs for Q K^T and P V). iters > 0: the attention
  * kernels (without post-processing) are then repeated `iters` times and the
  * average duration per call is written to ms_per_call. xq / xs (mode 0 or 4, both
  * or neither): the output rows as the kernel quantises them for o_proj

@@ -14,7 +14,7 @@ normalised vectors already in the ring.
     contents within 1e-5;
   - the fast prefill is deterministic (same bits on a second call), and its
     fused quantisation of the output rows equals quantize() of them;
-  - the tensor-core prefill (3xTF32 tcgen05 GEMMs) meets the same 2e-4 bound
+  - the tensor-core prefill (tcgen05 GEMMs on fp16 hi/lo operand pairs) meets the same 2e-4 bound
     (each product carries a relative error near 2^-21 against the CUDA-core
     path's 2^-24: scores of |s| <= ~70 move by ~1e-5), is deterministic, and
     its quantised rows equal quantize() of its output rows.

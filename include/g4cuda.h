@@ -193,7 +193,13 @@ int g4_read_ple(g4_ctx *ctx, size_t rows, float *out);
 /* Ring slots of sequence `seq`'s K (which=0) / V (which=1) cache that `layer`
  * reads (multi-sequence serving, after g4_seq_alloc). */
 int g4_read_seq_cache(g4_ctx *ctx, int seq, int layer, int which, int slot0, int nslots, float *out);
-void *g4_stream(g4_ctx *ctx);                 /* the context's cudaStream_t */
+/* The context's cudaStream_t. Copies, events and ordinary launches a host
+ * adds to it are ordered after the library's work as usual. The library's
+ * kernels let programmatic dependents start early, so a kernel launched here
+ * with cudaLaunchAttributeProgrammaticStreamSerialization must call
+ * cudaGridDependencySynchronize() (griddepcontrol.wait) before it touches
+ * anything the library wrote. */
+void *g4_stream(g4_ctx *ctx);
 /* Open (1) / close (0) the profiler capture range (ncu --profile-from-start off). */
 int g4_profiler_range(int on);
 int g4_device_bytes(g4_ctx *ctx, uint64_t *weights, uint64_t *total);
